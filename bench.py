@@ -1,0 +1,445 @@
+"""Gated DeltaNet forward + backward tokens/s on B200 (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c1|c2]
+
+One step is the whole training pass of the recurrence's layer slice over one batch:
+    gate/norm forward (qn, kn, g, beta from q, k, a, b, A_log, dt_bias)
+    -> recurrence forward (y, final state, chunk states saved)
+    -> recurrence backward (dq, dk, dv, dg, dbeta, dh0 given dy)
+    -> gate/norm backward (dq, dk through the norms; da, db; per-head dA_log, ddt_bias)
+    -> when the batch is split over GPUs, one all-reduce of [dA_log | ddt_bias] (NCCL).
+
+Workloads (synthetic, seeded; shapes and value distributions of the measured configurations):
+  c1  Qwen3.5-4B layer: B=1 per GPU, T=2048, Hk=16, Hv=32, Dk=Dv=128, bf16 activations, fp32 g/beta/state.
+      Weak scaling: GPU r runs batch row r (global batch = N).
+  c2  B=8, T=4096, Hk=16, Hv=64 split over the GPUs by (batch x value-head group); strong scaling.
+
+`value` is tokens/s of the whole job (tokens of all ranks / max over ranks of the device time);
+`e2e` is the same metric through the public API with host buffers: every step copies its inputs
+from pinned host memory and its gradients back.  L2 is flushed (a 512 MiB write) before each timed
+step and the flush is outside the step's events.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CHUNK = 64
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="c1", choices=["c1", "c2"])
+    ap.add_argument("--algo", type=int, default=0, help="0 auto, 1 row-parallel, 2 chunked")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ---- algorithmic work (chunk C = 64, dense contractions only; bytes read once, written once) ----
+def fwd_flops_per_token_head(Dk, Dv, C=CHUNK):
+    return (2 * C * C * (3 * Dk + 2 * Dv) + 6 * C * Dk * Dv + (2.0 / 3.0) * C ** 3) / C
+
+
+def bytes_per_token(Hk, Hv, Dk, Dv, act=2):
+    fwd = 2 * Hk * Dk * act + Hv * Dv * act + 2 * Hv * 4 + Hv * Dv * act
+    bwd = (2 * Hk * Dk * act + 2 * Hv * Dv * act + 2 * Hv * 4) + (2 * Hk * Dk * act + Hv * Dv * act + 2 * Hv * 4)
+    return fwd, bwd
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+# ---- clocks during the timed region ----
+class ClockSampler:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        sm.sort()
+        med = sm[len(sm) // 2] if sm else None
+        return {"sm_mhz": med, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---- the step ----
+class Work:
+    """One rank's share of the workload, resident in HBM."""
+
+    def __init__(self, B, T, Hk, Hv, Dk, Dv, seed, device, algo):
+        from quotebound_b200 import synthetic
+        p = synthetic.make(B, T, Hk, Hv, Dk, Dv, seed=seed, device=device)
+        gen = torch.Generator(device=device).manual_seed(seed + 7)
+        # raw (pre-norm) q, k: any positive rescale of the normalised vectors gives the same qn, kn
+        self.q = (p.q * math.sqrt(Dk) * torch.rand(B, T, Hk, 1, generator=gen, device=device).add_(0.5)).to(torch.bfloat16)
+        self.k = (p.k * torch.rand(B, T, Hk, 1, generator=gen, device=device).add_(0.5)).to(torch.bfloat16)
+        self.v = p.v.to(torch.bfloat16)
+        self.a, self.b = p.a.contiguous(), p.b.contiguous()
+        self.A_log, self.dt_bias = p.A_log, p.dt_bias
+        self.dy = p.dy.to(torch.bfloat16)
+        self.shape = (B, T, Hk, Hv, Dk, Dv)
+        self.algo = algo
+
+    def step(self, events=None):
+        """One fwd+bwd pass; returns (grads..., dA_log, ddt_bias).  `events`: list to append (name, ev0, ev1)."""
+        from quotebound_b200 import deltanet, gate
+
+        def op(name, fn):
+            if events is None:
+                return fn()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            out = fn()
+            e1.record()
+            events.append((name, e0, e1))
+            return out
+
+        qn, kn, g, beta = op("gate_fwd", lambda: gate.gate_fwd(self.q, self.k, self.a, self.b, self.A_log,
+                                                                 self.dt_bias))
+        y, hT, saved = op("gdn_fwd", lambda: deltanet.gated_delta_fwd(qn, kn, self.v, g, beta, None, save=True,
+                                                                       algo=self.algo))
+        dqn, dkn, dv, dg, dbeta, _ = op("gdn_bwd", lambda: deltanet.gated_delta_bwd(
+            qn, kn, self.v, g, beta, None, self.dy, None, saved=saved, algo=self.algo))
+        dq, dk, da, db, dA, ddt = op("gate_bwd", lambda: gate.gate_bwd(self.q, self.k, self.a, self.b, self.A_log,
+                                                                        self.dt_bias, dqn, dkn, dg, dbeta))
+        return dq, dk, dv, da, db, dA, ddt
+
+
+def rank_info():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def workload_shape(name, world, rank):
+    """(B, T, Hk, Hv, Dk, Dv, seed, tokens of this rank, description)."""
+    if name == "c1":
+        return 1, 2048, 16, 32, 128, 128, rank, 2048
+    from quotebound_b200 import partition
+    shards = partition.plan(B=8, Hk=16, Hv=64, world=world)
+    s = shards[rank]
+    nb, nhk = s.b1 - s.b0, s.hk1 - s.hk0
+    return nb, 4096, nhk, nhk * 4, 128, 128, 1000 + rank, nb * 4096 * nhk * 4 / 64  # tokens weighted by heads
+
+
+def flush_l2(buf):
+    buf.zero_()
+
+
+def run_ours(args):
+    world, rank, local = rank_info()
+    dist = world > 1
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if dist:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=dev)
+    from quotebound_b200 import _lib, build
+    build.ensure()
+    _lib.load()
+    B, T, Hk, Hv, Dk, Dv, seed, rank_tokens = workload_shape(args.workload, world, rank)
+    W = Work(B, T, Hk, Hv, Dk, Dv, seed, dev, args.algo)
+    flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    red = torch.empty(2 * (64 if args.workload == "c2" else Hv), dtype=torch.float32, device=dev)
+
+    def allreduce(dA, ddt):
+        if not dist:
+            return
+        if args.workload == "c2":
+            from quotebound_b200 import partition
+            s = partition.plan(B=8, Hk=16, Hv=64, world=world)[rank]
+            red.zero_()
+            red[s.hv0:s.hv1] = dA
+            red[64 + s.hv0:64 + s.hv1] = ddt
+        else:
+            red[:Hv] = dA
+            red[Hv:] = ddt
+        torch.distributed.all_reduce(red)
+
+    for _ in range(args.warmup):
+        out = W.step()
+        allreduce(out[5], out[6])
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(local)
+    if dist:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    time.sleep(0.3)
+    n0 = _lib.launches()
+    step_events = []
+    op_events = []
+    for _ in range(args.steps):
+        flush_l2(flush)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        out = W.step(op_events)
+        allreduce(out[5], out[6])
+        e1.record()
+        step_events.append((e0, e1))
+    torch.cuda.synchronize()
+    if dist:
+        torch.distributed.barrier()
+    launches = _lib.launches() - n0
+    clocks = sampler.stop()
+    ms = sum(a.elapsed_time(b) for a, b in step_events) / args.steps
+    per_op = {}
+    for name, a, b in op_events:
+        per_op.setdefault(name, []).append(a.elapsed_time(b))
+    per_op = {k: sum(v) / len(v) for k, v in per_op.items()}
+    ms_max = ms
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms_max = float(t.item())
+    if args.workload == "c1":
+        total_tokens = world * B * T
+        tokens_label = total_tokens
+    else:
+        total_tokens = 8 * 4096
+        tokens_label = total_tokens
+    value = total_tokens / (ms_max / 1e3)
+
+    # e2e through the public API with host buffers (pinned), every step: H2D inputs, D2H gradients
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(W, args, dev, dist, world, allreduce)
+
+    if rank == 0:
+        hbm, tf, src = load_peaks()
+        Hk_, Hv_ = (16, 32) if args.workload == "c1" else (16, 64)
+        fpt = fwd_flops_per_token_head(Dk, Dv)
+        # dominant op of the step and its algorithmic work per launch
+        dom = max(per_op, key=per_op.get)
+        launch_tokens = B * T if args.workload == "c1" else B * T
+        heads = Hv
+        flops = {"gdn_fwd": fpt * launch_tokens * heads, "gdn_bwd": 2 * fpt * launch_tokens * heads}
+        fb, bb = bytes_per_token(Hk, Hv, Dk, Dv)
+        bytes_ = {"gdn_fwd": fb * launch_tokens, "gdn_bwd": bb * launch_tokens,
+                  "gate_fwd": launch_tokens * (2 * Hk * Dk * 2 * 2 + Hv * 4 * 4),
+                  "gate_bwd": launch_tokens * (4 * Hk * Dk * 2 + 2 * Hk * Dk * 2 + Hv * 4 * 6)}
+        dom_ms = per_op[dom]
+        if dom in flops:
+            ach = flops[dom] / (dom_ms / 1e3) / 1e12
+            roof = {"kernel": dom, "bound": "tensor", "achieved": round(ach, 3), "peak": tf, "unit": "TFLOP/s",
+                    "frac": round(ach / tf, 5), "peak_source": src, "traffic": None, "ms_per_launch": round(dom_ms, 4),
+                    "hbm_achieved_gbs": round(bytes_[dom] / (dom_ms / 1e3) / 1e9, 1),
+                    "hbm_frac": round(bytes_[dom] / (dom_ms / 1e3) / 1e9 / hbm, 5)}
+        else:
+            ach = bytes_[dom] / (dom_ms / 1e3) / 1e9
+            roof = {"kernel": dom, "bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+                    "frac": round(ach / hbm, 5), "peak_source": src, "traffic": None, "ms_per_launch": round(dom_ms, 4)}
+        line = {
+            "metric": "GDN fwd+bwd tokens/s at 4B layer shape" if args.workload == "c1"
+            else "GDN fwd+bwd tokens/s, B=8 T=4096 Hv=64 split over GPUs",
+            "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max, 4), "higher_is_better": True,
+            "scaling": "weak" if args.workload == "c1" else "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded; q,k,v,dO ~ N(0,1), q/k normalised, g = exp(-e^A_log softplus(a+dt_bias)))",
+            "config": {"workload": "config1: B=1/GPU T=2048 Hk=16 Hv=32 Dk=Dv=128" if args.workload == "c1"
+                       else "config2: B=8 T=4096 Hk=16 Hv=64 Dk=Dv=128, (batch x head-group) split",
+                       "global_batch": world * B if args.workload == "c1" else 8, "seq_len": T,
+                       "parallelism": f"dp{world}" if args.workload == "c1" else f"bh{world}",
+                       "l2": "flushed before every step (512 MiB write, outside the step events)",
+                       "algo": {0: "auto", 1: "rows", 2: "chunked"}[args.algo],
+                       "step": "gate_fwd + gdn_fwd(save) + gdn_bwd + gate_bwd" + (" + allreduce" if dist else "")},
+            "per_op_ms": {k: round(v, 4) for k, v in per_op.items()},
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+            "roofline": roof,
+            "e2e": e2e,
+        }
+        if not args.no_cpu_baseline and world == 1:
+            line["cpu_baseline"] = cpu_baseline(args.workload)
+        print(json.dumps(line), flush=True)
+    if dist:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def run_e2e(W, args, dev, dist, world, allreduce):
+    """Same step through the public API with host buffers: H2D of the step's inputs from pinned memory,
+    D2H of every gradient, inside the timed region."""
+    host_in = {n: getattr(W, n).cpu().pin_memory() for n in ("q", "k", "v", "a", "b", "dy")}
+    dev_in = {n: torch.empty_like(getattr(W, n)) for n in host_in}
+    outs = W.step()
+    host_out = [o.cpu().pin_memory() for o in outs]
+    h2d = sum(t.numel() * t.element_size() for t in host_in.values())
+    d2h = sum(t.numel() * t.element_size() for t in host_out)
+
+    class HostWork:
+        pass
+
+    hw = HostWork()
+    for n in ("A_log", "dt_bias", "shape", "algo"):
+        setattr(hw, n, getattr(W, n))
+    for n, t in dev_in.items():
+        setattr(hw, n, t)
+
+    def one():
+        for n, t in host_in.items():
+            dev_in[n].copy_(t, non_blocking=True)
+        out = Work.step(hw)
+        allreduce(out[5], out[6])
+        for h, o in zip(host_out, out):
+            h.copy_(o, non_blocking=True)
+
+    for _ in range(max(2, args.warmup)):
+        one()
+    torch.cuda.synchronize()
+    if dist:
+        torch.distributed.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    n = max(3, args.steps // 2)
+    for _ in range(n):
+        one()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / n
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    B, T = W.shape[0], W.shape[1]
+    total = (world * B * T) if args.workload == "c1" else 8 * 4096
+    return {"value": round(total / (ms / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h), "ms_per_step": round(ms, 4), "steps": n}
+
+
+# ---- the CPU side: the oracle on the host cores ----
+def _oracle_sample(T, threads, seconds):
+    """Times the CPU oracle's fwd+bwd on config 1's heads over T steps until `seconds` have passed."""
+    from oracle import oracle
+    import numpy as np
+    from quotebound_b200 import synthetic
+    p = synthetic.make(1, T, 16, 32, 128, 128, seed=0)
+    q = p.q.to(torch.bfloat16).float().numpy()
+    k = p.k.to(torch.bfloat16).float().numpy()
+    v = p.v.to(torch.bfloat16).float().numpy()
+    dy = p.dy.to(torch.bfloat16).float().numpy()
+    g, beta = p.g.numpy(), p.beta.numpy()
+    n, t0 = 0, time.perf_counter()
+    while True:
+        oracle.gated_delta_fwd(q, k, v, g, beta, None, acc64=False, threads=threads)
+        oracle.gated_delta_bwd(q, k, v, g, beta, None, dy, None, acc64=False, threads=threads)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return n * T / el, n, el
+
+
+def cpu_baseline(workload):
+    from oracle import oracle
+    oracle.build()
+    threads = os.cpu_count() or 1
+    T = 256
+    tps, n, el = _oracle_sample(T, threads, 10.0)
+    return {"value": round(tps, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"config1 heads (Hk=16, Hv=32, Dk=Dv=128), T={T} fwd+bwd, float32 C oracle, OpenMP "
+                      f"{threads} threads, {n} passes in {el:.1f} s"}
+
+
+def run_reference(args):
+    """The reference's CPU path for this recurrence (its MLX/Metal build cannot run here): the C oracle
+    restating it, on every host core, same metric and workload shape, bounded samples per step."""
+    world, rank, local = rank_info()
+    if rank != 0:
+        return
+    from oracle import oracle
+    oracle.build()
+    threads = os.cpu_count() or 1
+    T = 256
+    for _ in range(args.warmup):
+        _oracle_sample(T, threads, 0.0)
+    rates = []
+    for _ in range(args.steps):
+        tps, n, el = _oracle_sample(T, threads, 0.0)
+        rates.append(tps)
+    rates.sort()
+    v = rates[len(rates) // 2]
+    line = {"impl": "reference", "metric": "GDN fwd+bwd tokens/s at 4B layer shape", "value": round(v, 1),
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "dtype": "f32",
+            "config": {"workload": "config1 heads: Hk=16 Hv=32 Dk=Dv=128; sampled T=256 per step"},
+            "cpu_baseline": {"value": round(v, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
+                             "sample": f"one fwd+bwd of T={T} steps per timed step (median of {args.steps})"},
+            "e2e": {"value": round(v, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "the reference's recurrence runs on MLX/Metal (macOS only); its CPU restatement is timed"}
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)

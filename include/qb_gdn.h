@@ -1,0 +1,148 @@
+/*
+ * qb_gdn — the Gated DeltaNet recurrence on B200 (sm_100a) behind a C ABI.
+ *
+ * Drop-in for quotebound's recurrence entry points:
+ *   gated_delta(q, k, v, g, beta, state, train)            src/deltanet.h:17-19, src/deltanet.cpp:68-80
+ *   gated_delta_trainable(q, k, v, g, beta, state)         src/delta_grad.h:14-16, src/delta_grad.cpp:201-212
+ *   gated_delta_vjp({q, k, v, g, beta, state}, dy, dstate) src/delta_grad.h:18-20, src/delta_grad.cpp:155-199
+ * plus the per-token path of deltanet(..., rows) (src/deltanet.cpp:122-135, src/exact.cpp:144-159)
+ * and the gate / beta / q-k norm graph around the recurrence (src/deltanet.cpp:22-33, 113-119).
+ *
+ * Conventions (the reference's own C ABI, src/constrain_capi.h:7-9): every call that can fail
+ * returns -1 and writes a NUL-terminated reason into err (cut to errlen); nothing throws across
+ * the boundary.  0 is success.
+ *
+ * Memory: every tensor pointer is DEVICE memory owned by the caller, contiguous, row-major in the
+ * reference's layouts:
+ *   q, k        [B, T, Hk, Dk]         (in_dtype)
+ *   v, dy       [B, T, Hv, Dv]         (in_dtype)
+ *   y, dv       [B, T, Hv, Dv]         (out_dtype);  dq, dk [B, T, Hk, Dk] (out_dtype)
+ *   g, beta     [B, T, Hv]             float32 (and dg, dbeta)
+ *   state       [N, Hv, Dv, Dk]        float32 (h0, hT, dh0, dhT); N = B, or the sequence count
+ * Value head hv reads key head hv / (Hv / Hk) (src/delta_grad.cpp:35).
+ *
+ * Streams: `stream` is a cudaStream_t (NULL = the legacy default stream).  Calls are asynchronous
+ * on it and never synchronise the device.  Host-side validation runs before any launch, so a call
+ * that fails validation has enqueued nothing.
+ *
+ * Workspace: calls that need scratch take (ws, ws_bytes); query the size with
+ * qb_gdn_workspace_bytes.  The same workspace must not be used by two calls in flight at once.
+ */
+#ifndef QB_GDN_H
+#define QB_GDN_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { QB_DTYPE_F32 = 0, QB_DTYPE_BF16 = 1 };
+
+/* Which calls a workspace / saved-state size is asked for. */
+enum { QB_OP_FWD = 0, QB_OP_BWD = 1 };
+
+/* Which kernels run the recurrence.  AUTO takes the tensor-core chunked path where the shape has
+ * one (Dk = Dv = 128) and the row-parallel path elsewhere; the other two force one path (CHUNKED
+ * fails on a shape it does not cover). */
+enum { QB_ALGO_AUTO = 0, QB_ALGO_ROWS = 1, QB_ALGO_CHUNKED = 2 };
+
+/* Shape and dtypes of one recurrence call.
+ * Varlen (new in this build; the reference right-pads, src/data.cpp:24-38): with cu_seqlens the
+ * batch is B = 1, sequence n covers steps [cu[n], cu[n+1]) of T, its state starts from h0[n] (or
+ * zero) and ends in hT[n].  cu_seqlens is the device copy the kernels read; cu_seqlens_host holds
+ * the same n_seqs + 1 offsets on the host for validation and grid sizing.  Both NULL: N = B
+ * sequences of T steps. */
+typedef struct qb_gdn_desc {
+  int32_t B, T, Hk, Hv, Dk, Dv;
+  int32_t n_seqs;
+  const int32_t* cu_seqlens;
+  const int32_t* cu_seqlens_host;
+  int32_t in_dtype;  /* q, k, v, dy: QB_DTYPE_BF16 or QB_DTYPE_F32 */
+  int32_t out_dtype; /* y, dq, dk, dv */
+  int32_t algo;      /* QB_ALGO_*; a training forward and its backward must use the same path */
+} qb_gdn_desc;
+
+/* Library version string; never fails. */
+const char* qb_gdn_version(void);
+
+/* How many kernels this library has launched in this process so far (all devices and streams). */
+int64_t qb_gdn_launches(void);
+
+/* Bytes of workspace `op` needs for this shape (0 is possible); -1 on an invalid shape. */
+int64_t qb_gdn_workspace_bytes(const qb_gdn_desc* d, int32_t op, char* err, int errlen);
+
+/* Bytes of the saved-for-backward buffer (the fp32 chunk-start states, [N_chunks, Hv, Dv, Dk],
+ * the counterpart of src/delta_grad.cpp:172-181's ckpt) that a training forward fills. */
+int64_t qb_gdn_saved_bytes(const qb_gdn_desc* d, char* err, int errlen);
+
+/* gated_delta: y and the final state(s).  h0 NULL = zero initial state; hT NULL = not written.
+ * saved non-NULL (training forward, gated_delta_trainable) also stores the chunk-start states for
+ * qb_gdn_bwd.  Replaces src/deltanet.h:17-19 (gated_delta) and, with saved, src/delta_grad.h:14-16. */
+int qb_gdn_fwd(const qb_gdn_desc* d, const void* q, const void* k, const void* v, const float* g,
+               const float* beta, const float* h0, void* y, float* hT, void* saved, void* ws,
+               int64_t ws_bytes, void* stream, char* err, int errlen);
+
+/* gated_delta_vjp: cotangents of (q, k, v, g, beta, h0) given dy and the final-state cotangent dhT
+ * (NULL = zero).  saved: the buffer a training qb_gdn_fwd filled with the same inputs, or NULL to
+ * recompute it inside (then ws must also cover qb_gdn_saved_bytes).  dh0 NULL = not written.
+ * Replaces src/delta_grad.h:18-20 (same argument order q, k, v, g, beta, state). */
+int qb_gdn_bwd(const qb_gdn_desc* d, const void* q, const void* k, const void* v, const float* g,
+               const float* beta, const float* h0, const void* dy, const float* dhT, const void* saved,
+               void* dq, void* dk, void* dv, float* dg, float* dbeta, float* dh0, void* ws,
+               int64_t ws_bytes, void* stream, char* err, int errlen);
+
+/* One decode step for N independent sequences (gated_delta with T = 1, src/deltanet.cpp:68-80 as
+ * the decode path calls it, src/generate.cpp forward(..., cache)):
+ *   q, k [N, Hk, Dk]; v [N, Hv, Dv]; g, beta [N, Hv]; state_in [N, Hv, Dv, Dk] float32;
+ *   y [N, Hv, Dv] (out_dtype); state_out [N, Hv, Dv, Dk] (may equal state_in). */
+int qb_gdn_step(int32_t N, int32_t Hk, int32_t Hv, int32_t Dk, int32_t Dv, int32_t in_dtype,
+                int32_t out_dtype, const void* q, const void* k, const void* v, const float* g,
+                const float* beta, const float* state_in, void* y, float* state_out, void* stream,
+                char* err, int errlen);
+
+/* Exact speculative verify (deltanet(..., rows), src/deltanet.cpp:122-135; RowStates,
+ * src/model.h:84-89): V tokens of each of N sequences run as V one-token steps, bit for bit equal
+ * to V calls of qb_gdn_step, and every row's state is kept:
+ *   q, k [N, V, Hk, Dk]; v [N, V, Hv, Dv]; g, beta [N, V, Hv]; state_in [N, Hv, Dv, Dk];
+ *   y [N, V, Hv, Dv]; states [N, V, Hv, Dv, Dk] (row j = the state after token j). */
+int qb_gdn_verify(int32_t N, int32_t V, int32_t Hk, int32_t Hv, int32_t Dk, int32_t Dv, int32_t in_dtype,
+                  int32_t out_dtype, const void* q, const void* k, const void* v, const float* g,
+                  const float* beta, const float* state_in, void* y, float* states, void* stream, char* err,
+                  int errlen);
+
+/* keep_rows for the recurrence's cache (src/exact.cpp:151-159): state_out[n] = states[n, keep[n]-1].
+ * keep: device int32 [N], each in [1, V] (a value outside leaves state_out[n] unchanged and sets
+ * status[0] = 1 when status is non-NULL). */
+int qb_gdn_keep_rows(int32_t N, int32_t V, int32_t Hv, int32_t Dk, int32_t Dv, const float* states,
+                     const int32_t* keep, float* state_out, int32_t* status, void* stream, char* err,
+                     int errlen);
+
+/* The gate / beta / q-k norm graph around the recurrence (src/deltanet.cpp:113-119, compute_g
+ * :41-52), forward:
+ *   qn = q * rsqrt(mean(q^2) + 1e-6) / Dk;  kn = k * rsqrt(mean(k^2) + 1e-6) / sqrt(Dk);
+ *   beta = sigmoid(b);  g = exp(-exp(A_log) * softplus(a + dt_bias)).
+ * q, k, qn, kn [P, Hk, Dk] (in_dtype for q, k; out_dtype for qn, kn); a, b, g, beta [P, Hv] float32;
+ * A_log, dt_bias [Hv] float32.  P = B * T tokens. */
+int qb_gdn_gate_fwd(int64_t P, int32_t Hk, int32_t Hv, int32_t Dk, int32_t in_dtype, int32_t out_dtype,
+                    const void* q, const void* k, const float* a, const float* b, const float* A_log,
+                    const float* dt_bias, void* qn, void* kn, float* g, float* beta, void* stream, char* err,
+                    int errlen);
+
+/* Its backward: dq, dk (out_dtype) through the norms from dqn, dkn (in_dtype); da, db [P, Hv]; and
+ * this call's per-head sums dA_log, ddt_bias [Hv] (float32, overwritten; a fixed-order reduction,
+ * no atomics).  Across GPUs that split the batch, sum dA_log and ddt_bias with one all-reduce. */
+int qb_gdn_gate_bwd(int64_t P, int32_t Hk, int32_t Hv, int32_t Dk, int32_t in_dtype, int32_t out_dtype,
+                    const void* q, const void* k, const float* a, const float* b, const float* A_log,
+                    const float* dt_bias, const void* dqn, const void* dkn, const float* dg,
+                    const float* dbeta, void* dq, void* dk, float* da, float* db, float* dA_log,
+                    float* ddt_bias, void* ws, int64_t ws_bytes, void* stream, char* err, int errlen);
+
+/* Workspace bytes qb_gdn_gate_bwd needs for P tokens and Hv heads. */
+int64_t qb_gdn_gate_workspace_bytes(int64_t P, int32_t Hv);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QB_GDN_H */

@@ -1,0 +1,99 @@
+"""ctypes binding of libqb_gdn.so (include/qb_gdn.h).
+
+The library is the product: every compute call below goes through its C ABI.  There is no
+fallback: if the library is missing or a call fails, an exception says why.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libqb_gdn.so")
+
+QB_DTYPE_F32 = 0
+QB_DTYPE_BF16 = 1
+QB_OP_FWD = 0
+QB_OP_BWD = 1
+QB_ALGO_AUTO = 0
+QB_ALGO_ROWS = 1
+QB_ALGO_CHUNKED = 2
+
+# Every extern "C" symbol include/qb_gdn.h declares.
+SYMBOLS = (
+    "qb_gdn_version", "qb_gdn_launches", "qb_gdn_workspace_bytes", "qb_gdn_saved_bytes", "qb_gdn_fwd", "qb_gdn_bwd",
+    "qb_gdn_step", "qb_gdn_verify", "qb_gdn_keep_rows", "qb_gdn_gate_fwd", "qb_gdn_gate_bwd",
+    "qb_gdn_gate_workspace_bytes",
+)
+
+
+class Desc(ctypes.Structure):
+    _fields_ = [
+        ("B", ctypes.c_int32), ("T", ctypes.c_int32), ("Hk", ctypes.c_int32), ("Hv", ctypes.c_int32),
+        ("Dk", ctypes.c_int32), ("Dv", ctypes.c_int32), ("n_seqs", ctypes.c_int32),
+        ("cu_seqlens", ctypes.c_void_p), ("cu_seqlens_host", ctypes.c_void_p),
+        ("in_dtype", ctypes.c_int32), ("out_dtype", ctypes.c_int32), ("algo", ctypes.c_int32),
+    ]
+
+
+class QbError(RuntimeError):
+    pass
+
+
+_lib = None
+
+
+def load():
+    """The loaded library (raises if it was never built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise QbError(f"{LIB_PATH} is missing: build it with `python -m quotebound_b200.build`")
+    L = ctypes.CDLL(LIB_PATH)
+    vp, i32, i64, cp = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_char_p
+    dp = ctypes.POINTER(Desc)
+    L.qb_gdn_version.restype = cp
+    L.qb_gdn_version.argtypes = []
+    L.qb_gdn_launches.restype = i64
+    L.qb_gdn_launches.argtypes = []
+    L.qb_gdn_workspace_bytes.restype = i64
+    L.qb_gdn_workspace_bytes.argtypes = [dp, i32, cp, ctypes.c_int]
+    L.qb_gdn_saved_bytes.restype = i64
+    L.qb_gdn_saved_bytes.argtypes = [dp, cp, ctypes.c_int]
+    L.qb_gdn_fwd.restype = ctypes.c_int
+    L.qb_gdn_fwd.argtypes = [dp] + [vp] * 10 + [i64, vp, cp, ctypes.c_int]
+    L.qb_gdn_bwd.restype = ctypes.c_int
+    L.qb_gdn_bwd.argtypes = [dp] + [vp] * 16 + [i64, vp, cp, ctypes.c_int]
+    L.qb_gdn_step.restype = ctypes.c_int
+    L.qb_gdn_step.argtypes = [i32] * 7 + [vp] * 8 + [vp, cp, ctypes.c_int]
+    L.qb_gdn_verify.restype = ctypes.c_int
+    L.qb_gdn_verify.argtypes = [i32] * 8 + [vp] * 8 + [vp, cp, ctypes.c_int]
+    L.qb_gdn_keep_rows.restype = ctypes.c_int
+    L.qb_gdn_keep_rows.argtypes = [i32] * 5 + [vp] * 4 + [vp, cp, ctypes.c_int]
+    L.qb_gdn_gate_fwd.restype = ctypes.c_int
+    L.qb_gdn_gate_fwd.argtypes = [i64] + [i32] * 5 + [vp] * 10 + [vp, cp, ctypes.c_int]
+    L.qb_gdn_gate_bwd.restype = ctypes.c_int
+    L.qb_gdn_gate_bwd.argtypes = [i64] + [i32] * 5 + [vp] * 16 + [vp, i64, vp, cp, ctypes.c_int]
+    L.qb_gdn_gate_workspace_bytes.restype = i64
+    L.qb_gdn_gate_workspace_bytes.argtypes = [i64, i32]
+    _lib = L
+    return L
+
+
+def err_buf():
+    return ctypes.create_string_buffer(512)
+
+
+def check(rc: int, err) -> None:
+    if rc != 0:
+        raise QbError(err.value.decode(errors="replace") or f"qb_gdn call failed ({rc})")
+
+
+def version() -> str:
+    return load().qb_gdn_version().decode()
+
+
+def launches() -> int:
+    """Kernels the library has launched in this process so far."""
+    return int(load().qb_gdn_launches())

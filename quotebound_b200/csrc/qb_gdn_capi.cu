@@ -1,0 +1,405 @@
+// The C ABI of include/qb_gdn.h: host-side validation, workspace carving and kernel dispatch.
+// Error convention of the reference's C ABI (src/constrain_capi.h:7-9): -1 and a NUL-terminated
+// reason in err; nothing throws across the boundary.  Validation mirrors the spirit of
+// src/delta_grad.cpp:164-170 (name the offending shapes).
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <atomic>
+
+#include "../../include/qb_gdn.h"
+#include "gdn_chunk.cuh"
+#include "gdn_gate.cuh"
+#include "gdn_simt.cuh"
+#include "launch_count.cuh"
+
+using namespace qbgdn;
+
+namespace qbgdn {
+static std::atomic<int64_t> g_launches{0};
+void note_launch(int64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+int64_t launches() { return g_launches.load(std::memory_order_relaxed); }
+}  // namespace qbgdn
+
+namespace {
+
+constexpr int kChunkSteps = 64;
+
+int fail(char* err, int errlen, const char* fmt, ...) {
+  if (err && errlen > 0) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(err, (size_t)errlen, fmt, ap);
+    va_end(ap);
+    err[errlen - 1] = '\0';
+  }
+  return -1;
+}
+
+int cuda_fail(cudaError_t e, const char* what, char* err, int errlen) {
+  return fail(err, errlen, "%s: CUDA error %d (%s)", what, (int)e, cudaGetErrorString(e));
+}
+
+bool aligned(const void* p, size_t a) { return ((uintptr_t)p % a) == 0; }
+bool dtype_ok(int32_t d) { return d == QB_DTYPE_F32 || d == QB_DTYPE_BF16; }
+
+struct Plan {
+  int N;                // sequences
+  int64_t tokens;       // B * T
+  int64_t n_chunks;     // sum over sequences of ceil(len / 64)
+  bool varlen;
+  bool chunked;         // tensor-core chunked path
+  int rpb;              // rows per block (row-parallel path)
+  int NB;               // row blocks (row-parallel backward)
+};
+
+int check_desc(const qb_gdn_desc* d, Plan* p, char* err, int errlen) {
+  if (!d) return fail(err, errlen, "gated delta: null descriptor");
+  if (d->B < 1 || d->T < 0 || d->Hk < 1 || d->Hv < 1 || d->Dk < 1 || d->Dv < 1)
+    return fail(err, errlen, "gated delta: bad shape (B %d, T %d, Hk %d, Hv %d, Dk %d, Dv %d)", d->B, d->T, d->Hk,
+                d->Hv, d->Dk, d->Dv);
+  if (d->Dk != 32 && d->Dk != 64 && d->Dk != 128 && d->Dk != 256)
+    return fail(err, errlen, "gated delta: needs Dk in {32, 64, 128, 256} (Dk %d, Dv %d, Hk %d, Hv %d)", d->Dk, d->Dv,
+                d->Hk, d->Hv);
+  if (d->Hv % d->Hk)
+    return fail(err, errlen, "gated delta: value heads must be a multiple of key heads (Hk %d, Hv %d)", d->Hk,
+                d->Hv);
+  if (!dtype_ok(d->in_dtype) || !dtype_ok(d->out_dtype))
+    return fail(err, errlen, "gated delta: dtypes must be QB_DTYPE_F32 or QB_DTYPE_BF16 (in %d, out %d)",
+                d->in_dtype, d->out_dtype);
+  if (d->algo < QB_ALGO_AUTO || d->algo > QB_ALGO_CHUNKED)
+    return fail(err, errlen, "gated delta: unknown algo %d", d->algo);
+  p->varlen = d->cu_seqlens || d->cu_seqlens_host;
+  p->tokens = (int64_t)d->B * d->T;
+  if (p->varlen) {
+    if (!d->cu_seqlens || !d->cu_seqlens_host)
+      return fail(err, errlen, "gated delta: varlen needs both cu_seqlens (device) and cu_seqlens_host");
+    if (d->B != 1) return fail(err, errlen, "gated delta: varlen needs B == 1 (B %d)", d->B);
+    if (d->n_seqs < 1) return fail(err, errlen, "gated delta: varlen needs n_seqs >= 1 (n_seqs %d)", d->n_seqs);
+    const int32_t* cu = d->cu_seqlens_host;
+    if (cu[0] != 0) return fail(err, errlen, "gated delta: cu_seqlens[0] must be 0 (got %d)", cu[0]);
+    int64_t nc = 0;
+    for (int n = 0; n < d->n_seqs; ++n) {
+      if (cu[n + 1] < cu[n])
+        return fail(err, errlen, "gated delta: cu_seqlens must be non-decreasing (cu[%d] = %d > cu[%d] = %d)", n,
+                    cu[n], n + 1, cu[n + 1]);
+      nc += (cu[n + 1] - cu[n] + kChunkSteps - 1) / kChunkSteps;
+    }
+    if (cu[d->n_seqs] != d->T)
+      return fail(err, errlen, "gated delta: cu_seqlens[%d] = %d must equal T = %d", d->n_seqs, cu[d->n_seqs], d->T);
+    p->N = d->n_seqs;
+    p->n_chunks = nc;
+  } else {
+    p->N = d->B;
+    p->n_chunks = (int64_t)d->B * ((d->T + kChunkSteps - 1) / kChunkSteps);
+  }
+  const bool chunk_ok = chunked_supported(d->Dk, d->Dv);
+  if (d->algo == QB_ALGO_CHUNKED && !chunk_ok)
+    return fail(err, errlen, "gated delta: the chunked path needs Dk = Dv = 128 (Dk %d, Dv %d)", d->Dk, d->Dv);
+  p->chunked = d->algo == QB_ALGO_CHUNKED || (d->algo == QB_ALGO_AUTO && chunk_ok);
+  p->rpb = simt_rows_per_block(d->Dv);
+  p->NB = d->Dv / p->rpb;
+  return 0;
+}
+
+int64_t saved_bytes_of(const qb_gdn_desc* d, const Plan& p) {
+  if (p.chunked) return chunked_saved_bytes(d->Hv, d->Dk, d->Dv, p.n_chunks, p.tokens);
+  return p.n_chunks * d->Hv * (int64_t)d->Dv * d->Dk * 4;
+}
+
+int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
+
+// Row-parallel workspace: [chunk_off (varlen)] [dq_part] [dk_part] [dg_part] [dbeta_part] [saved (recompute)]
+struct SimtWs {
+  int64_t* chunk_off;
+  float *dq_part, *dk_part, *dg_part, *dbeta_part;
+  float* saved;
+};
+
+int64_t simt_ws_bytes(const qb_gdn_desc* d, const Plan& p, int op, bool with_saved, SimtWs* out, char* base) {
+  int64_t off = 0;
+  auto take = [&](int64_t bytes) {
+    char* at = base ? base + off : nullptr;
+    off += align256(bytes);
+    return at;
+  };
+  SimtWs w{};
+  w.chunk_off = (int64_t*)take(p.varlen ? (p.N + 1) * 8 : 0);
+  if (op == QB_OP_BWD) {
+    const int64_t parts = p.tokens * d->Hv * (int64_t)p.NB;
+    w.dq_part = (float*)take(parts * d->Dk * 4);
+    w.dk_part = (float*)take(parts * d->Dk * 4);
+    w.dg_part = (float*)take(parts * 4);
+    w.dbeta_part = (float*)take(parts * 4);
+    if (with_saved) w.saved = (float*)take(saved_bytes_of(d, p));
+  }
+  if (out) *out = w;
+  return off;
+}
+
+int64_t ws_bytes_of(const qb_gdn_desc* d, const Plan& p, int op, bool with_saved) {
+  if (p.chunked) return chunked_ws_bytes(d->Hv, d->Hk, d->Dk, d->Dv, p.N, p.n_chunks, p.tokens, p.varlen, op,
+                                         with_saved);
+  return simt_ws_bytes(d, p, op, with_saved, nullptr, nullptr);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* qb_gdn_version(void) { return "qb_gdn 0.1 (sm_100a)"; }
+
+int64_t qb_gdn_launches(void) { return launches(); }
+
+int64_t qb_gdn_workspace_bytes(const qb_gdn_desc* d, int32_t op, char* err, int errlen) {
+  Plan p;
+  if (check_desc(d, &p, err, errlen)) return -1;
+  if (op != QB_OP_FWD && op != QB_OP_BWD) return fail(err, errlen, "gated delta: unknown op %d", op);
+  // the backward's figure covers recomputing the saved states (saved == NULL)
+  return ws_bytes_of(d, p, op, op == QB_OP_BWD);
+}
+
+int64_t qb_gdn_saved_bytes(const qb_gdn_desc* d, char* err, int errlen) {
+  Plan p;
+  if (check_desc(d, &p, err, errlen)) return -1;
+  return saved_bytes_of(d, p);
+}
+
+int qb_gdn_fwd(const qb_gdn_desc* d, const void* q, const void* k, const void* v, const float* g, const float* beta,
+               const float* h0, void* y, float* hT, void* saved, void* ws, int64_t ws_bytes, void* stream, char* err,
+               int errlen) {
+  Plan p;
+  if (check_desc(d, &p, err, errlen)) return -1;
+  if (!q || !k || !v || !g || !beta || !y)
+    return fail(err, errlen, "gated delta forward: q, k, v, g, beta and y must be non-null");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(y, 16) || (h0 && !aligned(h0, 16)) ||
+      (hT && !aligned(hT, 16)) || (saved && !aligned(saved, 256)))
+    return fail(err, errlen, "gated delta forward: q, k, v, y, h0, hT need 16-byte alignment and saved 256-byte");
+  const int64_t need = ws_bytes_of(d, p, QB_OP_FWD, false);
+  if (need > 0 && (!ws || ws_bytes < need))
+    return fail(err, errlen, "gated delta forward: workspace of %lld bytes needed (got %lld)", (long long)need,
+                (long long)ws_bytes);
+  if (need > 0 && !aligned(ws, 256)) return fail(err, errlen, "gated delta forward: workspace needs 256-byte alignment");
+  if (p.tokens == 0) return 0;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (p.chunked) {
+    ChunkFwdArgs a{};
+    a.B = d->B, a.T = d->T, a.Hk = d->Hk, a.Hv = d->Hv, a.Dk = d->Dk, a.Dv = d->Dv, a.N = p.N;
+    a.n_chunks = p.n_chunks;
+    a.cu = d->cu_seqlens;
+    a.q = q, a.k = k, a.v = v, a.g = g, a.beta = beta, a.h0 = h0, a.y = y, a.hT = hT;
+    a.saved = saved;
+    a.in_bf16 = d->in_dtype == QB_DTYPE_BF16, a.out_bf16 = d->out_dtype == QB_DTYPE_BF16;
+    cudaError_t e = chunked_fwd(a, ws, st);
+    return e == cudaSuccess ? 0 : cuda_fail(e, "gated delta forward (chunked)", err, errlen);
+  }
+  SimtWs w;
+  simt_ws_bytes(d, p, QB_OP_FWD, false, &w, (char*)ws);
+  cudaError_t e;
+  if (p.varlen && saved) {
+    if ((e = launch_chunk_offsets(d->cu_seqlens, p.N, w.chunk_off, st)) != cudaSuccess)
+      return cuda_fail(e, "gated delta forward", err, errlen);
+  }
+  SimtArgs a{};
+  a.T = d->T, a.Hk = d->Hk, a.Hv = d->Hv, a.Dk = d->Dk, a.Dv = d->Dv, a.rows_per_block = p.rpb;
+  a.cu = d->cu_seqlens;
+  a.chunk_off = p.varlen ? w.chunk_off : nullptr;
+  a.q = q, a.k = k, a.v = v, a.g = g, a.beta = beta, a.h0 = h0, a.y = y, a.hT = hT;
+  a.ckpt = (float*)saved;
+  e = simt_launch(SimtKind::Fwd, a, p.N, d->in_dtype == QB_DTYPE_BF16, d->out_dtype == QB_DTYPE_BF16, st);
+  return e == cudaSuccess ? 0 : cuda_fail(e, "gated delta forward", err, errlen);
+}
+
+int qb_gdn_bwd(const qb_gdn_desc* d, const void* q, const void* k, const void* v, const float* g, const float* beta,
+               const float* h0, const void* dy, const float* dhT, const void* saved, void* dq, void* dk, void* dv,
+               float* dg, float* dbeta, float* dh0, void* ws, int64_t ws_bytes, void* stream, char* err,
+               int errlen) {
+  Plan p;
+  if (check_desc(d, &p, err, errlen)) return -1;
+  if (!q || !k || !v || !g || !beta || !dy || !dq || !dk || !dv || !dg || !dbeta)
+    return fail(err, errlen, "gated delta backward: q, k, v, g, beta, dy, dq, dk, dv, dg, dbeta must be non-null");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(dy, 16) || !aligned(dq, 16) ||
+      !aligned(dk, 16) || !aligned(dv, 16) || (h0 && !aligned(h0, 16)) || (dhT && !aligned(dhT, 16)) ||
+      (dh0 && !aligned(dh0, 16)) || (saved && !aligned(saved, 256)))
+    return fail(err, errlen, "gated delta backward: tensors need 16-byte alignment and saved 256-byte");
+  const int64_t need = ws_bytes_of(d, p, QB_OP_BWD, saved == nullptr);
+  if (need > 0 && (!ws || ws_bytes < need))
+    return fail(err, errlen, "gated delta backward: workspace of %lld bytes needed (got %lld)", (long long)need,
+                (long long)ws_bytes);
+  if (need > 0 && !aligned(ws, 256)) return fail(err, errlen, "gated delta backward: workspace needs 256-byte alignment");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (p.tokens == 0) {
+    if (dh0 && dhT) {
+      cudaError_t e = cudaMemcpyAsync(dh0, dhT, (size_t)p.N * d->Hv * d->Dv * d->Dk * 4, cudaMemcpyDeviceToDevice, st);
+      if (e != cudaSuccess) return cuda_fail(e, "gated delta backward", err, errlen);
+    } else if (dh0) {
+      cudaError_t e = cudaMemsetAsync(dh0, 0, (size_t)p.N * d->Hv * d->Dv * d->Dk * 4, st);
+      if (e != cudaSuccess) return cuda_fail(e, "gated delta backward", err, errlen);
+    }
+    return 0;
+  }
+  if (p.chunked) {
+    ChunkBwdArgs a{};
+    a.B = d->B, a.T = d->T, a.Hk = d->Hk, a.Hv = d->Hv, a.Dk = d->Dk, a.Dv = d->Dv, a.N = p.N;
+    a.n_chunks = p.n_chunks;
+    a.cu = d->cu_seqlens;
+    a.q = q, a.k = k, a.v = v, a.g = g, a.beta = beta, a.h0 = h0, a.dy = dy, a.dhT = dhT;
+    a.saved = saved;
+    a.dq = dq, a.dk = dk, a.dv = dv, a.dg = dg, a.dbeta = dbeta, a.dh0 = dh0;
+    a.in_bf16 = d->in_dtype == QB_DTYPE_BF16, a.out_bf16 = d->out_dtype == QB_DTYPE_BF16;
+    cudaError_t e = chunked_bwd(a, ws, st);
+    return e == cudaSuccess ? 0 : cuda_fail(e, "gated delta backward (chunked)", err, errlen);
+  }
+  SimtWs w;
+  simt_ws_bytes(d, p, QB_OP_BWD, saved == nullptr, &w, (char*)ws);
+  const int in_bf16 = d->in_dtype == QB_DTYPE_BF16, out_bf16 = d->out_dtype == QB_DTYPE_BF16;
+  cudaError_t e;
+  if (p.varlen && (e = launch_chunk_offsets(d->cu_seqlens, p.N, w.chunk_off, st)) != cudaSuccess)
+    return cuda_fail(e, "gated delta backward", err, errlen);
+  SimtArgs a{};
+  a.T = d->T, a.Hk = d->Hk, a.Hv = d->Hv, a.Dk = d->Dk, a.Dv = d->Dv, a.rows_per_block = p.rpb;
+  a.cu = d->cu_seqlens;
+  a.chunk_off = p.varlen ? w.chunk_off : nullptr;
+  a.q = q, a.k = k, a.v = v, a.g = g, a.beta = beta, a.h0 = h0;
+  float* ck = (float*)saved;
+  if (!ck) {  // recompute the chunk starts with the forward itself, y discarded into the dv buffer
+    ck = w.saved;
+    SimtArgs f = a;
+    f.y = dv;  // same shape and dtype as y; overwritten by the backward below
+    f.ckpt = ck;
+    if ((e = simt_launch(SimtKind::Fwd, f, p.N, in_bf16, out_bf16, st)) != cudaSuccess)
+      return cuda_fail(e, "gated delta backward (recompute)", err, errlen);
+  }
+  a.ckpt = ck;
+  a.dy = dy, a.dhT = dhT, a.dv = dv, a.dh0 = dh0;
+  a.dq_part = w.dq_part, a.dk_part = w.dk_part, a.dg_part = w.dg_part, a.dbeta_part = w.dbeta_part;
+  if ((e = simt_launch(SimtKind::Bwd, a, p.N, in_bf16, out_bf16, st)) != cudaSuccess)
+    return cuda_fail(e, "gated delta backward", err, errlen);
+  ReduceArgs r{};
+  r.tokens = p.tokens, r.Hk = d->Hk, r.Hv = d->Hv, r.Dk = d->Dk, r.NB = p.NB;
+  r.dq_part = w.dq_part, r.dk_part = w.dk_part, r.dg_part = w.dg_part, r.dbeta_part = w.dbeta_part;
+  r.dq = dq, r.dk = dk, r.dg = dg, r.dbeta = dbeta;
+  if ((e = simt_reduce_parts(r, out_bf16, st)) != cudaSuccess) return cuda_fail(e, "gated delta backward", err, errlen);
+  return 0;
+}
+
+static int check_rows(int32_t N, int32_t V, int32_t Hk, int32_t Hv, int32_t Dk, int32_t Dv, int32_t in_dtype,
+                      int32_t out_dtype, const char* what, char* err, int errlen) {
+  if (N < 0 || V < 1 || Hk < 1 || Hv < 1 || Dv < 1)
+    return fail(err, errlen, "%s: bad shape (N %d, V %d, Hk %d, Hv %d, Dk %d, Dv %d)", what, N, V, Hk, Hv, Dk, Dv);
+  if (Dk != 32 && Dk != 64 && Dk != 128 && Dk != 256)
+    return fail(err, errlen, "%s: needs Dk in {32, 64, 128, 256} (Dk %d)", what, Dk);
+  if (Hv % Hk) return fail(err, errlen, "%s: value heads must be a multiple of key heads (Hk %d, Hv %d)", what, Hk, Hv);
+  if (!dtype_ok(in_dtype) || !dtype_ok(out_dtype))
+    return fail(err, errlen, "%s: dtypes must be QB_DTYPE_F32 or QB_DTYPE_BF16 (in %d, out %d)", what, in_dtype,
+                out_dtype);
+  return 0;
+}
+
+int qb_gdn_step(int32_t N, int32_t Hk, int32_t Hv, int32_t Dk, int32_t Dv, int32_t in_dtype, int32_t out_dtype,
+                const void* q, const void* k, const void* v, const float* g, const float* beta, const float* state_in,
+                void* y, float* state_out, void* stream, char* err, int errlen) {
+  if (check_rows(N, 1, Hk, Hv, Dk, Dv, in_dtype, out_dtype, "gated delta step", err, errlen)) return -1;
+  if (!q || !k || !v || !g || !beta || !state_in || !y || !state_out)
+    return fail(err, errlen, "gated delta step: every pointer must be non-null");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(state_in, 16) || !aligned(state_out, 16))
+    return fail(err, errlen, "gated delta step: q, k and the states need 16-byte alignment");
+  if (N == 0) return 0;
+  SimtArgs a{};
+  a.T = 1, a.Hk = Hk, a.Hv = Hv, a.Dk = Dk, a.Dv = Dv, a.rows_per_block = simt_rows_per_block(Dv);
+  a.q = q, a.k = k, a.v = v, a.g = g, a.beta = beta, a.h0 = state_in, a.y = y, a.hT = state_out;
+  cudaError_t e = simt_launch(SimtKind::Step, a, N, in_dtype == QB_DTYPE_BF16, out_dtype == QB_DTYPE_BF16,
+                              (cudaStream_t)stream);
+  return e == cudaSuccess ? 0 : cuda_fail(e, "gated delta step", err, errlen);
+}
+
+int qb_gdn_verify(int32_t N, int32_t V, int32_t Hk, int32_t Hv, int32_t Dk, int32_t Dv, int32_t in_dtype,
+                  int32_t out_dtype, const void* q, const void* k, const void* v, const float* g, const float* beta,
+                  const float* state_in, void* y, float* states, void* stream, char* err, int errlen) {
+  if (check_rows(N, V, Hk, Hv, Dk, Dv, in_dtype, out_dtype, "gated delta verify", err, errlen)) return -1;
+  if (!q || !k || !v || !g || !beta || !state_in || !y || !states)
+    return fail(err, errlen, "gated delta verify: every pointer must be non-null");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(state_in, 16) || !aligned(states, 16))
+    return fail(err, errlen, "gated delta verify: q, k and the states need 16-byte alignment");
+  if (N == 0) return 0;
+  SimtArgs a{};
+  a.T = V, a.Hk = Hk, a.Hv = Hv, a.Dk = Dk, a.Dv = Dv, a.rows_per_block = simt_rows_per_block(Dv);
+  a.q = q, a.k = k, a.v = v, a.g = g, a.beta = beta, a.h0 = state_in, a.y = y, a.ckpt = states;
+  cudaError_t e = simt_launch(SimtKind::Verify, a, N, in_dtype == QB_DTYPE_BF16, out_dtype == QB_DTYPE_BF16,
+                              (cudaStream_t)stream);
+  return e == cudaSuccess ? 0 : cuda_fail(e, "gated delta verify", err, errlen);
+}
+
+int qb_gdn_keep_rows(int32_t N, int32_t V, int32_t Hv, int32_t Dk, int32_t Dv, const float* states,
+                     const int32_t* keep, float* state_out, int32_t* status, void* stream, char* err, int errlen) {
+  if (N < 0 || V < 1 || Hv < 1 || Dk < 1 || Dv < 1)
+    return fail(err, errlen, "gated delta keep_rows: bad shape (N %d, V %d, Hv %d, Dk %d, Dv %d)", N, V, Hv, Dk, Dv);
+  if (!states || !keep || !state_out) return fail(err, errlen, "gated delta keep_rows: null pointer");
+  if (!aligned(states, 16) || !aligned(state_out, 16) || ((int64_t)Hv * Dv * Dk) % 4)
+    return fail(err, errlen, "gated delta keep_rows: states need 16-byte alignment and Hv*Dv*Dk a multiple of 4");
+  if (N == 0) return 0;
+  cudaError_t e = launch_keep_rows(N, V, (int64_t)Hv * Dv * Dk, states, keep, state_out, status, (cudaStream_t)stream);
+  return e == cudaSuccess ? 0 : cuda_fail(e, "gated delta keep_rows", err, errlen);
+}
+
+int qb_gdn_gate_fwd(int64_t P, int32_t Hk, int32_t Hv, int32_t Dk, int32_t in_dtype, int32_t out_dtype, const void* q,
+                    const void* k, const float* a, const float* b, const float* A_log, const float* dt_bias, void* qn,
+                    void* kn, float* g, float* beta, void* stream, char* err, int errlen) {
+  if (P < 0 || Hk < 1 || Hv < 1 || Hv > 256 || (Dk != 32 && Dk != 64 && Dk != 128 && Dk != 256) ||
+      !dtype_ok(in_dtype) || !dtype_ok(out_dtype))
+    return fail(err, errlen, "gated delta gate: bad arguments (P %lld, Hk %d, Hv %d (<= 256), Dk %d, dtypes %d/%d)",
+                (long long)P, Hk, Hv, Dk, in_dtype, out_dtype);
+  if (!q || !k || !a || !b || !A_log || !dt_bias || !qn || !kn || !g || !beta)
+    return fail(err, errlen, "gated delta gate: every pointer must be non-null");
+  if (!aligned(q, 16) || !aligned(k, 16)) return fail(err, errlen, "gated delta gate: q, k need 16-byte alignment");
+  if (P == 0) return 0;
+  GateArgs ga{};
+  ga.P = P, ga.Hk = Hk, ga.Hv = Hv, ga.Dk = Dk;
+  ga.q = q, ga.k = k, ga.a = a, ga.b = b, ga.A_log = A_log, ga.dt_bias = dt_bias;
+  ga.qn = qn, ga.kn = kn, ga.g = g, ga.beta = beta;
+  cudaError_t e = gate_fwd(ga, in_dtype == QB_DTYPE_BF16, out_dtype == QB_DTYPE_BF16, (cudaStream_t)stream);
+  return e == cudaSuccess ? 0 : cuda_fail(e, "gated delta gate", err, errlen);
+}
+
+int64_t qb_gdn_gate_workspace_bytes(int64_t P, int32_t Hv) {
+  return align256((int64_t)gate_head_blocks(P) * Hv * 2 * 4);
+}
+
+int qb_gdn_gate_bwd(int64_t P, int32_t Hk, int32_t Hv, int32_t Dk, int32_t in_dtype, int32_t out_dtype, const void* q,
+                    const void* k, const float* a, const float* b, const float* A_log, const float* dt_bias,
+                    const void* dqn, const void* dkn, const float* dg, const float* dbeta, void* dq, void* dk,
+                    float* da, float* db, float* dA_log, float* ddt_bias, void* ws, int64_t ws_bytes, void* stream,
+                    char* err, int errlen) {
+  if (P < 0 || Hk < 1 || Hv < 1 || Hv > 256 || (Dk != 32 && Dk != 64 && Dk != 128 && Dk != 256) ||
+      !dtype_ok(in_dtype) || !dtype_ok(out_dtype))
+    return fail(err, errlen, "gated delta gate backward: bad arguments (P %lld, Hk %d, Hv %d (<= 256), Dk %d)",
+                (long long)P, Hk, Hv, Dk);
+  if (!q || !k || !a || !b || !A_log || !dt_bias || !dqn || !dkn || !dg || !dbeta || !dq || !dk || !da || !db ||
+      !dA_log || !ddt_bias)
+    return fail(err, errlen, "gated delta gate backward: every pointer must be non-null");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(dqn, 16) || !aligned(dkn, 16))
+    return fail(err, errlen, "gated delta gate backward: q, k, dqn, dkn need 16-byte alignment");
+  const int64_t need = qb_gdn_gate_workspace_bytes(P, Hv);
+  if (!ws || ws_bytes < need)
+    return fail(err, errlen, "gated delta gate backward: workspace of %lld bytes needed (got %lld)", (long long)need,
+                (long long)ws_bytes);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (P == 0) {
+    cudaError_t e = cudaMemsetAsync(dA_log, 0, Hv * 4, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(ddt_bias, 0, Hv * 4, st);
+    return e == cudaSuccess ? 0 : cuda_fail(e, "gated delta gate backward", err, errlen);
+  }
+  GateArgs ga{};
+  ga.P = P, ga.Hk = Hk, ga.Hv = Hv, ga.Dk = Dk;
+  ga.q = q, ga.k = k, ga.a = a, ga.b = b, ga.A_log = A_log, ga.dt_bias = dt_bias;
+  ga.dqn = dqn, ga.dkn = dkn, ga.dg = dg, ga.dbeta = dbeta;
+  ga.dq = dq, ga.dk = dk, ga.da = da, ga.db = db, ga.dA_log = dA_log, ga.ddt_bias = ddt_bias;
+  cudaError_t e = gate_bwd(ga, in_dtype == QB_DTYPE_BF16, out_dtype == QB_DTYPE_BF16, (float*)ws, st);
+  return e == cudaSuccess ? 0 : cuda_fail(e, "gated delta gate backward", err, errlen);
+}
+
+}  // extern "C"
