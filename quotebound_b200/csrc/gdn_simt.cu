@@ -46,7 +46,7 @@ __global__ void __launch_bounds__(256) gdn_seq_fwd(SimtArgs a) {
 #pragma unroll
     for (int i = 0; i < NPT; ++i) s[i] = 0.f;
   }
-  const int64_t chunk_base = a.chunk_off ? a.chunk_off[n] : 0;
+  const int64_t chunk_base = a.chunk_off ? a.chunk_off[n] : (int64_t)n * ((a.T + kChunk - 1) / kChunk);
   for (int64_t t = sr.t0; t < sr.t1; ++t) {
     if (a.ckpt && ((t - sr.t0) % kChunk) == 0) {
       const int64_t c = chunk_base + (t - sr.t0) / kChunk;
@@ -140,7 +140,7 @@ __global__ void __launch_bounds__(256) gdn_simt_bwd(SimtArgs a) {
   const size_t srow = ((size_t)n * a.Hv + hv) * a.Dv + r;
   const int64_t L = sr.t1 - sr.t0;
   const int64_t NC = (L + kChunk - 1) / kChunk;
-  const int64_t chunk_base = a.chunk_off ? a.chunk_off[n] : 0;
+  const int64_t chunk_base = a.chunk_off ? a.chunk_off[n] : (int64_t)n * ((a.T + kChunk - 1) / kChunk);
   const int W2 = 2 * Dk + 2;
 
   float ds[NPT];

@@ -1,0 +1,216 @@
+// sm_100a building blocks: mbarriers with bounded waits, TMA tile loads, and tcgen05 tensor-core
+// MMAs with TMEM accumulators.  Operand tiles live in shared memory in the 128-byte-swizzled
+// canonical layouts the MMA descriptors describe:
+//
+//  * K-major tile (R rows of M or N, K contiguous): the K extent is cut into 128-byte slabs
+//    (64 bf16 or 32 fp32 elements); slab s holds R rows of 128 bytes, row r at r*128, and the
+//    16-byte chunk j of row r sits at chunk (j ^ (r & 7)).  Slabs follow each other every R*128
+//    bytes.  Descriptor: SBO = 1024 (8 rows), LBO unused; one MMA K-step (32 bytes) advances the
+//    start address by 32 bytes inside a slab.
+//  * MN-major tile (K rows, M or N contiguous): the MN extent is cut into 128-byte slabs; slab s
+//    holds Krows rows of 128 bytes (row = one k), chunk j of row k at chunk (j ^ (k & 7)).
+//    Descriptor: LBO = the slab stride (Krows*128), SBO = 1024 (8 k-rows); one MMA K-step advances
+//    the start by 16 (bf16) or 8 (tf32) rows.
+//
+// Every slab starts on a 1024-byte boundary, so the hardware's address-based swizzle matches.
+// No cluster multicast anywhere: every CTA loads its own tiles.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace qbgdn {
+namespace tc {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---- mbarriers ---------------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for the phase with the given parity to complete.  Gives up after ~2^22 polls (each
+// poll may itself suspend briefly), writes `code` into *err and returns false; the caller then
+// skips its remaining work, frees its TMEM and returns.  Never spins forever, never traps.
+constexpr uint32_t kMaxPolls = 1u << 22;
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  for (uint32_t i = 0; i < kMaxPolls; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  if (err) atomicExch(err, code);
+  return false;
+}
+
+// ---- TMA ----------------------------------------------------------------------------------------
+// 3-D tiled load (no multicast) into shared memory, completing `bytes` on the mbarrier.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                            int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ---- fences -------------------------------------------------------------------------------------
+// Generic-proxy writes to shared memory -> visible to the async proxy (MMA operand reads).
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// ---- TMEM -----------------------------------------------------------------------------------------
+// Executed by one whole warp; the TMEM address lands in *slot (shared memory).
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// 32 lanes x 32 bits, 16 consecutive columns into v (this thread's lane).  Then wait::ld.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+// 32 consecutive columns.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// TMEM address of (lane, column): lane in the high 16 bits.
+__device__ __forceinline__ uint32_t taddr(uint32_t base, uint32_t lane, uint32_t col) {
+  return base + (lane << 16) + col;
+}
+
+// ---- descriptors ---------------------------------------------------------------------------------
+enum Kind { kBF16 = 1, kTF32 = 2 };
+
+// Instruction descriptor of kind::f16 (bf16 inputs) or kind::tf32, fp32 accumulate.
+__host__ __device__ constexpr uint32_t idesc(int kind, int M, int N, bool a_mn_major, bool b_mn_major) {
+  return (1u << 4)                                   // D format: f32
+         | (uint32_t(kind) << 7) | (uint32_t(kind) << 10)  // A, B formats: bf16 = 1, tf32 = 2
+         | (uint32_t(a_mn_major) << 15) | (uint32_t(b_mn_major) << 16) | (uint32_t(N >> 3) << 17) |
+         (uint32_t(M >> 4) << 24);
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle, sm_100 version field.
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  return uint64_t((saddr >> 4) & 0x3FFFu) | (uint64_t((lbo_bytes >> 4) & 0x3FFFu) << 16) |
+         (uint64_t((sbo_bytes >> 4) & 0x3FFFu) << 32) | (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+
+// Descriptor of MMA K-step `ks` over a K-major tile with R rows (32 bytes per step).
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t tile, int R, int ks) {
+  return sdesc(tile + (ks >> 2) * (R * 128) + (ks & 3) * 32, 16, 1024);
+}
+// Descriptor of MMA K-step `ks` over an MN-major tile with Krows k-rows; rows_per_step is 16 for
+// bf16 and 8 for tf32.
+__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t tile, int Krows, int ks, int rows_per_step) {
+  return sdesc(tile + ks * rows_per_step * 128, Krows * 128, 1024);
+}
+
+// Byte offset of element (r, k) in a K-major tile of R rows, element size eb.
+__host__ __device__ __forceinline__ uint32_t off_kmajor(int r, int k, int R, int eb) {
+  const int E = 128 / eb, slab = k / E, kin = k - slab * E;
+  const int chunk = (kin * eb) >> 4, within = (kin * eb) & 15;
+  return slab * (R * 128) + r * 128 + ((chunk ^ (r & 7)) << 4) + within;
+}
+// Byte offset of element (k, r) in an MN-major tile of Krows k-rows.
+__host__ __device__ __forceinline__ uint32_t off_mnmajor(int k, int r, int Krows, int eb) {
+  const int E = 128 / eb, slab = r / E, rin = r - slab * E;
+  const int chunk = (rin * eb) >> 4, within = (rin * eb) & 15;
+  return slab * (Krows * 128) + k * 128 + ((chunk ^ (k & 7)) << 4) + within;
+}
+
+// ---- MMA issue (one thread) ------------------------------------------------------------------------
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t id, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(id), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t id, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(id), "r"(accumulate)
+      : "memory");
+}
+// Arrive once on `bar` when every MMA this thread issued before has completed.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// D[M x N] (+)= A[M x K] * B[N x K]^T over K / kstep MMA instructions.  Operand tiles as above;
+// a_mn / b_mn select MN-major tiles (then a_rows / b_rows are the tile's K row count).
+template <int KIND>
+__device__ __forceinline__ void mma_tile(uint32_t d_tmem, uint32_t a_tile, bool a_mn, int a_rows, uint32_t b_tile,
+                                         bool b_mn, int b_rows, int M, int N, int K, bool accumulate) {
+  const uint32_t id = idesc(KIND, M, N, a_mn, b_mn);
+  const int kstep = KIND == kBF16 ? 16 : 8;
+  for (int ks = 0; ks < K / kstep; ++ks) {
+    const uint64_t a = a_mn ? desc_mnmajor(a_tile, a_rows, ks, kstep) : desc_kmajor(a_tile, a_rows, ks);
+    const uint64_t b = b_mn ? desc_mnmajor(b_tile, b_rows, ks, kstep) : desc_kmajor(b_tile, b_rows, ks);
+    if (KIND == kBF16)
+      mma_bf16(d_tmem, a, b, id, (accumulate || ks > 0) ? 1u : 0u);
+    else
+      mma_tf32(d_tmem, a, b, id, (accumulate || ks > 0) ? 1u : 0u);
+  }
+}
+
+}  // namespace tc
+}  // namespace qbgdn

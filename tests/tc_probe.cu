@@ -1,0 +1,96 @@
+// Test support: one tcgen05 MMA tile D = A * B^T through the same helpers the chunked kernels use
+// (quotebound_b200/csrc/tc_sm100.cuh), for every operand majorness and kind the kernels need.
+// Built by tests/test_gpu_tc.py into tests/_build/libtcprobe.so.
+#include <cuda_bf16.h>
+
+#include "tc_sm100.cuh"
+
+using namespace qbgdn;
+
+__device__ __forceinline__ float to_tf32(float x) {
+  uint32_t u;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u) : "f"(x));
+  return __uint_as_float(u);
+}
+
+// Bytes of an R x K operand tile: whole 128-byte slabs along the contiguous dimension.
+__host__ __device__ inline int tile_bytes(int R, int K, int eb, int mn_major) {
+  const int slabs = mn_major ? (R * eb + 127) / 128 : (K * eb + 127) / 128;
+  return slabs * (mn_major ? K : R) * 128;
+}
+
+// A logical [M][K], B logical [N][K], D [M][N]; fp32 in global.
+__global__ void __launch_bounds__(128) tc_probe_kernel(int M, int N, int K, int kind, int a_mn, int b_mn,
+                                                       const float* A, const float* B, float* D, int* err) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_slot;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int eb = kind == tc::kBF16 ? 2 : 4;
+  uint8_t* a_tile = smem;
+  uint8_t* b_tile = smem + tile_bytes(M, K, eb, a_mn);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  int ncols = 32;
+  while (ncols < N) ncols <<= 1;
+  if (warp == 0) tc::tmem_alloc(&tmem_slot, ncols);
+  if (tid == 0) {
+    tc::mbar_init(&bar, 1);
+    tc::fence_mbar_init();
+  }
+  for (int i = tid; i < M * K; i += blockDim.x) {
+    const int m = i / K, k = i % K;
+    const uint32_t o = a_mn ? tc::off_mnmajor(k, m, K, eb) : tc::off_kmajor(m, k, M, eb);
+    if (eb == 2)
+      *reinterpret_cast<__nv_bfloat16*>(a_tile + o) = __float2bfloat16_rn(A[i]);
+    else
+      *reinterpret_cast<float*>(a_tile + o) = to_tf32(A[i]);
+  }
+  for (int i = tid; i < N * K; i += blockDim.x) {
+    const int n = i / K, k = i % K;
+    const uint32_t o = b_mn ? tc::off_mnmajor(k, n, K, eb) : tc::off_kmajor(n, k, N, eb);
+    if (eb == 2)
+      *reinterpret_cast<__nv_bfloat16*>(b_tile + o) = __float2bfloat16_rn(B[i]);
+    else
+      *reinterpret_cast<float*>(b_tile + o) = to_tf32(B[i]);
+  }
+  tc::fence_async_smem();
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = tmem_slot;
+  if (tid == 0) {
+    if (kind == tc::kBF16)
+      tc::mma_tile<tc::kBF16>(tmem, tc::smem_u32(a_tile), a_mn, a_mn ? K : M, tc::smem_u32(b_tile), b_mn,
+                              b_mn ? K : N, M, N, K, false);
+    else
+      tc::mma_tile<tc::kTF32>(tmem, tc::smem_u32(a_tile), a_mn, a_mn ? K : M, tc::smem_u32(b_tile), b_mn,
+                              b_mn ? K : N, M, N, K, false);
+    tc::mma_commit(&bar);
+  }
+  const bool ok = tc::mbar_wait(&bar, 0, err, 1);
+  tc::fence_after_sync();
+  if (ok) {
+    // M = 128: row m in lane m.  M = 64: rows 16w..16w+15 in lanes 32w..32w+15.
+    const int row = M == 128 ? 32 * warp + lane : 16 * warp + lane;
+    const bool mine = M == 128 || lane < 16;
+    for (int c = 0; c < N; c += 16) {
+      float v[16];
+      tc::tmem_ld16(tc::taddr(tmem, 32 * warp, c), v);
+      if (mine)
+        for (int j = 0; j < 16 && c + j < N; ++j) D[row * N + c + j] = v[j];
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tmem, ncols);
+}
+
+extern "C" int tc_probe_gemm(int M, int N, int K, int kind, int a_mn, int b_mn, const float* A, const float* B,
+                             float* D, int* err) {
+  if ((M != 64 && M != 128) || N < 16 || N > 256 || N % 16 || K < 16 || K > 128 || K % 16) return -1;
+  const int eb = kind == tc::kBF16 ? 2 : 4;
+  const int smem = 1024 + tile_bytes(M, K, eb, a_mn) + tile_bytes(N, K, eb, b_mn);
+  cudaFuncSetAttribute(tc_probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  tc_probe_kernel<<<1, 128, smem>>>(M, N, K, kind, a_mn, b_mn, A, B, D, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}

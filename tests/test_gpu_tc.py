@@ -1,0 +1,62 @@
+"""The tcgen05 building blocks the chunked kernels are made of (GPU only): one MMA tile through the
+shared-memory layouts, descriptors, TMEM allocation and loads of quotebound_b200/csrc/tc_sm100.cuh,
+for bf16 and tf32 operands, M in {64, 128}, every operand majorness, against float64 matmul of the
+same rounded operands."""
+import ctypes
+import itertools
+import os
+import subprocess
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+SO = os.path.join(HERE, "_build", "libtcprobe.so")
+
+
+def build_probe():
+    if not os.path.exists(SO):
+        os.makedirs(os.path.dirname(SO), exist_ok=True)
+        nvcc = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "bin", "nvcc")
+        subprocess.run([nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-O2", "-std=c++17", "-shared",
+                        "-Xcompiler", "-fPIC", "-I" + os.path.join(ROOT, "quotebound_b200", "csrc"),
+                        os.path.join(HERE, "tc_probe.cu"), "-o", SO], check=True)
+    L = ctypes.CDLL(SO)
+    L.tc_probe_gemm.argtypes = [ctypes.c_int] * 6 + [ctypes.c_void_p] * 4
+    return L
+
+
+def tf32(x):
+    u = x.contiguous().view(torch.int32)
+    return ((u + 0x1000) & ~0x1FFF).view(torch.float32)
+
+
+CASES = list(itertools.product((1, 2), (64, 128), (32, 64, 128), (64, 128), (0, 1), (0, 1)))
+
+
+@pytest.fixture(scope="module")
+def L():
+    return build_probe()
+
+
+@pytest.mark.parametrize("kind,M,N,K,a_mn,b_mn", CASES,
+                         ids=lambda v: str(v))
+def test_mma_tile(L, kind, M, N, K, a_mn, b_mn):
+    gen = torch.Generator(device="cuda").manual_seed(M * 1000 + N * 10 + K + a_mn + 2 * b_mn + kind)
+    A = torch.randn(M, K, device="cuda", generator=gen)
+    B = torch.randn(N, K, device="cuda", generator=gen)
+    D = torch.full((M, N), float("nan"), device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    rc = L.tc_probe_gemm(M, N, K, kind, a_mn, b_mn, A.data_ptr(), B.data_ptr(), D.data_ptr(), err.data_ptr())
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0, "mbarrier wait timed out"
+    if kind == 1:
+        Ar, Br = A.to(torch.bfloat16).double(), B.to(torch.bfloat16).double()
+    else:
+        Ar, Br = tf32(A).double(), tf32(B).double()
+    want = Ar @ Br.T
+    rel = ((D.double() - want).norm() / want.norm()).item()
+    assert rel < 1e-5, rel
