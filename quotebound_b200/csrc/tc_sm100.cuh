@@ -8,9 +8,11 @@
 //    bytes.  Descriptor: SBO = 1024 (8 rows), LBO unused; one MMA K-step (32 bytes) advances the
 //    start address by 32 bytes inside a slab.
 //  * MN-major tile (K rows, M or N contiguous): the MN extent is cut into 128-byte slabs; slab s
-//    holds Krows rows of 128 bytes (row = one k), chunk j of row k at chunk (j ^ (k & 7)).
-//    Descriptor: LBO = the slab stride (Krows*128), SBO = 1024 (8 k-rows); one MMA K-step advances
-//    the start by 16 (bf16) or 8 (tf32) rows.
+//    holds Krows rows of 128 bytes (row = one k).  bf16: 128-byte swizzle, 16-byte chunk j of row k
+//    at chunk (j ^ (k & 7)), SBO = 1024 (8 k-rows).  tf32: the 32-byte-atom variant of the 128-byte
+//    swizzle (layout type 1), 32-byte granule j of row k at granule (j ^ (k & 3)), SBO = 512
+//    (4 k-rows).  LBO = the slab stride (Krows*128); one MMA K-step advances the start by 16 (bf16)
+//    or 8 (tf32) rows.
 //
 // Every slab starts on a 1024-byte boundary, so the hardware's address-based swizzle matches.
 // No cluster multicast anywhere: every CTA loads its own tiles.
@@ -145,10 +147,12 @@ __host__ __device__ constexpr uint32_t idesc(int kind, int M, int N, bool a_mn_m
          (uint32_t(M >> 4) << 24);
 }
 
-// Shared-memory matrix descriptor, 128-byte swizzle, sm_100 version field.
-__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+// Shared-memory matrix descriptor, sm_100 version field.  layout: 2 = 128-byte swizzle, 1 = 128-byte
+// swizzle with 32-byte atoms (the tf32 MN-major layout).
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                          uint32_t layout = 2) {
   return uint64_t((saddr >> 4) & 0x3FFFu) | (uint64_t((lbo_bytes >> 4) & 0x3FFFu) << 16) |
-         (uint64_t((sbo_bytes >> 4) & 0x3FFFu) << 32) | (uint64_t(1) << 46) | (uint64_t(2) << 61);
+         (uint64_t((sbo_bytes >> 4) & 0x3FFFu) << 32) | (uint64_t(1) << 46) | (uint64_t(layout) << 61);
 }
 
 // Descriptor of MMA K-step `ks` over a K-major tile with R rows (32 bytes per step).
@@ -158,7 +162,8 @@ __device__ __forceinline__ uint64_t desc_kmajor(uint32_t tile, int R, int ks) {
 // Descriptor of MMA K-step `ks` over an MN-major tile with Krows k-rows; rows_per_step is 16 for
 // bf16 and 8 for tf32.
 __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t tile, int Krows, int ks, int rows_per_step) {
-  return sdesc(tile + ks * rows_per_step * 128, Krows * 128, 1024);
+  return rows_per_step == 16 ? sdesc(tile + ks * 16 * 128, Krows * 128, 1024, 2)
+                             : sdesc(tile + ks * 8 * 128, Krows * 128, 512, 1);
 }
 
 // Byte offset of element (r, k) in a K-major tile of R rows, element size eb.
@@ -167,11 +172,13 @@ __host__ __device__ __forceinline__ uint32_t off_kmajor(int r, int k, int R, int
   const int chunk = (kin * eb) >> 4, within = (kin * eb) & 15;
   return slab * (R * 128) + r * 128 + ((chunk ^ (r & 7)) << 4) + within;
 }
-// Byte offset of element (k, r) in an MN-major tile of Krows k-rows.
+// Byte offset of element (k, r) in an MN-major tile of Krows k-rows (bf16: 16-byte chunks swizzled
+// by k & 7; fp32: 32-byte granules swizzled by k & 3).
 __host__ __device__ __forceinline__ uint32_t off_mnmajor(int k, int r, int Krows, int eb) {
   const int E = 128 / eb, slab = r / E, rin = r - slab * E;
-  const int chunk = (rin * eb) >> 4, within = (rin * eb) & 15;
-  return slab * (Krows * 128) + k * 128 + ((chunk ^ (k & 7)) << 4) + within;
+  const int byte = rin * eb;
+  if (eb == 4) return slab * (Krows * 128) + k * 128 + ((((byte >> 5) ^ (k & 3))) << 5) + (byte & 31);
+  return slab * (Krows * 128) + k * 128 + ((((byte >> 4) ^ (k & 7))) << 4) + (byte & 15);
 }
 
 // ---- MMA issue (one thread) ------------------------------------------------------------------------
