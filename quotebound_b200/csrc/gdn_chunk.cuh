@@ -30,6 +30,9 @@ struct ChunkBwdArgs {
 };
 
 bool chunked_supported(int Dk, int Dv);
+// Whether the backward has its own chunked kernels; until then a chunked forward's saved buffer starts
+// with the row-parallel backward's chunk-start states and that backward runs.
+bool chunked_bwd_ready();
 int64_t chunked_saved_bytes(int Hv, int Dk, int Dv, int64_t n_chunks, int64_t tokens);
 int64_t chunked_ws_bytes(int Hv, int Hk, int Dk, int Dv, int N, int64_t n_chunks, int64_t tokens, bool varlen, int op,
                          bool with_saved);

@@ -97,9 +97,10 @@ int check_desc(const qb_gdn_desc* d, Plan* p, char* err, int errlen) {
     p->N = d->B;
     p->n_chunks = (int64_t)d->B * ((d->T + kChunkSteps - 1) / kChunkSteps);
   }
-  const bool chunk_ok = chunked_supported(d->Dk, d->Dv);
+  const bool chunk_ok = chunked_supported(d->Dk, d->Dv) && d->in_dtype == QB_DTYPE_BF16;
   if (d->algo == QB_ALGO_CHUNKED && !chunk_ok)
-    return fail(err, errlen, "gated delta: the chunked path needs Dk = Dv = 128 (Dk %d, Dv %d)", d->Dk, d->Dv);
+    return fail(err, errlen, "gated delta: the chunked path needs Dk = Dv = 128 and bf16 activations (Dk %d, Dv %d)",
+                d->Dk, d->Dv);
   p->chunked = d->algo == QB_ALGO_CHUNKED || (d->algo == QB_ALGO_AUTO && chunk_ok);
   p->rpb = simt_rows_per_block(d->Dv);
   p->NB = d->Dv / p->rpb;
@@ -118,6 +119,7 @@ struct SimtWs {
   int64_t* chunk_off;
   float *dq_part, *dk_part, *dg_part, *dbeta_part;
   float* saved;
+  char* fwd_ws;
 };
 
 int64_t simt_ws_bytes(const qb_gdn_desc* d, const Plan& p, int op, bool with_saved, SimtWs* out, char* base) {
@@ -135,15 +137,24 @@ int64_t simt_ws_bytes(const qb_gdn_desc* d, const Plan& p, int op, bool with_sav
     w.dk_part = (float*)take(parts * d->Dk * 4);
     w.dg_part = (float*)take(parts * 4);
     w.dbeta_part = (float*)take(parts * 4);
-    if (with_saved) w.saved = (float*)take(saved_bytes_of(d, p));
+    if (with_saved) {
+      w.saved = (float*)take(saved_bytes_of(d, p));
+      // recomputing with the chunked forward needs that forward's own workspace too
+      if (p.chunked)
+        w.fwd_ws = take(chunked_ws_bytes(d->Hv, d->Hk, d->Dk, d->Dv, p.N, p.n_chunks, p.tokens, p.varlen, QB_OP_FWD,
+                                         false));
+    }
   }
   if (out) *out = w;
   return off;
 }
 
+// The backward of a chunked forward runs the row-parallel kernels until the chunked ones exist.
+bool chunked_bwd_of(const Plan& p) { return p.chunked && chunked_bwd_ready(); }
+
 int64_t ws_bytes_of(const qb_gdn_desc* d, const Plan& p, int op, bool with_saved) {
-  if (p.chunked) return chunked_ws_bytes(d->Hv, d->Hk, d->Dk, d->Dv, p.N, p.n_chunks, p.tokens, p.varlen, op,
-                                         with_saved);
+  if (op == QB_OP_FWD ? p.chunked : chunked_bwd_of(p))
+    return chunked_ws_bytes(d->Hv, d->Hk, d->Dk, d->Dv, p.N, p.n_chunks, p.tokens, p.varlen, op, with_saved);
   return simt_ws_bytes(d, p, op, with_saved, nullptr, nullptr);
 }
 
@@ -242,7 +253,7 @@ int qb_gdn_bwd(const qb_gdn_desc* d, const void* q, const void* k, const void* v
     }
     return 0;
   }
-  if (p.chunked) {
+  if (chunked_bwd_of(p)) {
     ChunkBwdArgs a{};
     a.B = d->B, a.T = d->T, a.Hk = d->Hk, a.Hv = d->Hv, a.Dk = d->Dk, a.Dv = d->Dv, a.N = p.N;
     a.n_chunks = p.n_chunks;
@@ -266,13 +277,25 @@ int qb_gdn_bwd(const qb_gdn_desc* d, const void* q, const void* k, const void* v
   a.chunk_off = p.varlen ? w.chunk_off : nullptr;
   a.q = q, a.k = k, a.v = v, a.g = g, a.beta = beta, a.h0 = h0;
   float* ck = (float*)saved;
-  if (!ck) {  // recompute the chunk starts with the forward itself, y discarded into the dv buffer
+  if (!ck) {  // recompute the chunk starts with the same forward, y discarded into the dv buffer
     ck = w.saved;
-    SimtArgs f = a;
-    f.y = dv;  // same shape and dtype as y; overwritten by the backward below
-    f.ckpt = ck;
-    if ((e = simt_launch(SimtKind::Fwd, f, p.N, in_bf16, out_bf16, st)) != cudaSuccess)
-      return cuda_fail(e, "gated delta backward (recompute)", err, errlen);
+    if (p.chunked) {
+      ChunkFwdArgs f{};
+      f.B = d->B, f.T = d->T, f.Hk = d->Hk, f.Hv = d->Hv, f.Dk = d->Dk, f.Dv = d->Dv, f.N = p.N;
+      f.n_chunks = p.n_chunks;
+      f.cu = d->cu_seqlens;
+      f.q = q, f.k = k, f.v = v, f.g = g, f.beta = beta, f.h0 = h0, f.y = dv, f.hT = nullptr;
+      f.saved = ck;
+      f.in_bf16 = in_bf16, f.out_bf16 = out_bf16;
+      if ((e = chunked_fwd(f, w.fwd_ws, st)) != cudaSuccess)
+        return cuda_fail(e, "gated delta backward (recompute)", err, errlen);
+    } else {
+      SimtArgs f = a;
+      f.y = dv;  // same shape and dtype as y; overwritten by the backward below
+      f.ckpt = ck;
+      if ((e = simt_launch(SimtKind::Fwd, f, p.N, in_bf16, out_bf16, st)) != cudaSuccess)
+        return cuda_fail(e, "gated delta backward (recompute)", err, errlen);
+    }
   }
   a.ckpt = ck;
   a.dy = dy, a.dhT = dhT, a.dv = dv, a.dh0 = dh0;
