@@ -141,6 +141,23 @@ int qb_gdn_gate_bwd(int64_t P, int32_t Hk, int32_t Hv, int32_t Dk, int32_t in_dt
 /* Workspace bytes qb_gdn_gate_bwd needs for P tokens and Hv heads. */
 int64_t qb_gdn_gate_workspace_bytes(int64_t P, int32_t Hv);
 
+/* qb_gdn_gate_bwd without a workspace argument, for callers that cannot allocate device memory:
+ * code running inside a fixed memory budget or a pre-allocated pool, plugins handed only their input
+ * and output buffers, and hosts that forbid cudaMalloc / cudaFree on the hot path because those calls
+ * synchronise the device.  It allocates nothing: its partial sums go to a fixed array of 148 x 256 x 2
+ * floats (296 KiB) in the library's own device memory, which every GPU that loads the library holds
+ * until the process exits.  Value heads beyond 256 are refused with an error.  The first call on a
+ * device looks up that array's device address (cudaGetSymbolAddress, with that device current); make
+ * that first call before any stream capture.  All calls share the one array, so two calls that
+ * overlap on the GPU (other streams, other threads) race on it and must be ordered by the caller;
+ * nothing in it needs clearing between calls.  Arguments and results are those of qb_gdn_gate_bwd.
+ * This entry point has no counterpart in the reference. */
+int qb_gdn_gate_bwd_noalloc(int64_t P, int32_t Hk, int32_t Hv, int32_t Dk, int32_t in_dtype, int32_t out_dtype,
+                            const void* q, const void* k, const float* a, const float* b, const float* A_log,
+                            const float* dt_bias, const void* dqn, const void* dkn, const float* dg,
+                            const float* dbeta, void* dq, void* dk, float* da, float* db, float* dA_log,
+                            float* ddt_bias, void* stream, char* err, int errlen);
+
 #ifdef __cplusplus
 }
 #endif

@@ -23,7 +23,7 @@ QB_ALGO_CHUNKED = 2
 SYMBOLS = (
     "qb_gdn_version", "qb_gdn_launches", "qb_gdn_workspace_bytes", "qb_gdn_saved_bytes", "qb_gdn_fwd", "qb_gdn_bwd",
     "qb_gdn_step", "qb_gdn_verify", "qb_gdn_keep_rows", "qb_gdn_gate_fwd", "qb_gdn_gate_bwd",
-    "qb_gdn_gate_workspace_bytes",
+    "qb_gdn_gate_workspace_bytes", "qb_gdn_gate_bwd_noalloc",
 )
 
 
@@ -75,6 +75,8 @@ def load():
     L.qb_gdn_gate_fwd.argtypes = [i64] + [i32] * 5 + [vp] * 10 + [vp, cp, ctypes.c_int]
     L.qb_gdn_gate_bwd.restype = ctypes.c_int
     L.qb_gdn_gate_bwd.argtypes = [i64] + [i32] * 5 + [vp] * 16 + [vp, i64, vp, cp, ctypes.c_int]
+    L.qb_gdn_gate_bwd_noalloc.restype = ctypes.c_int
+    L.qb_gdn_gate_bwd_noalloc.argtypes = [i64] + [i32] * 5 + [vp] * 16 + [vp, cp, ctypes.c_int]
     L.qb_gdn_gate_workspace_bytes.restype = i64
     L.qb_gdn_gate_workspace_bytes.argtypes = [i64, i32]
     _lib = L

@@ -2,6 +2,12 @@
 // :41-52) and its chain rule.  HBM-bound elementwise work: one warp per (token, key head) row of
 // q and k, coalesced 16-byte loads, warp-shuffle reductions; per-head parameter gradients summed
 // in a fixed order (block partials, then one block over the partials) with no atomics.
+#include <stdarg.h>
+#include <stdio.h>
+
+#include <mutex>
+
+#include "../../include/qb_gdn.h"
 #include "gdn_common.cuh"
 #include "gdn_gate.cuh"
 #include "launch_count.cuh"
@@ -178,3 +184,97 @@ cudaError_t gate_bwd(const GateArgs& a, int in_bf16, int out_bf16, float* partia
 }
 
 }  // namespace qbgdn
+
+// ------------------------------------------------------------------------------------------------
+// The gate backward for callers that cannot allocate device memory: its per-block partial sums live
+// in a fixed array in the library's own device memory instead of a caller-provided workspace.
+namespace qbgdn {
+namespace {
+
+// Blocks of gdn_gate_bwd_heads (at most 148) x value heads (at most 256) x 2 sums, float32: 296 KiB,
+// held by every GPU that loads the library until the process exits.
+constexpr int64_t kGateScratchFloats = 148 * 256 * 2;
+static __device__ __align__(256) float g_gate_scratch[kGateScratchFloats];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+float* g_scratch_ptr[kMaxDevices];  // device address of g_gate_scratch, per device
+
+int noalloc_fail(char* err, int errlen, const char* fmt, ...) {
+  if (err && errlen > 0) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(err, (size_t)errlen, fmt, ap);
+    va_end(ap);
+    err[errlen - 1] = '\0';
+  }
+  return -1;
+}
+
+// The device address of the scratch array on the current device, looked up once per device.
+cudaError_t scratch_on_current_device(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_gate_scratch);
+    if (e != cudaSuccess) return e;
+    g_scratch_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_scratch_ptr[dev];
+  return cudaSuccess;
+}
+
+}  // namespace
+}  // namespace qbgdn
+
+extern "C" int qb_gdn_gate_bwd_noalloc(int64_t P, int32_t Hk, int32_t Hv, int32_t Dk, int32_t in_dtype,
+                                       int32_t out_dtype, const void* q, const void* k, const float* a,
+                                       const float* b, const float* A_log, const float* dt_bias, const void* dqn,
+                                       const void* dkn, const float* dg, const float* dbeta, void* dq, void* dk,
+                                       float* da, float* db, float* dA_log, float* ddt_bias, void* stream,
+                                       char* err, int errlen) {
+  using namespace qbgdn;
+  const bool dt_ok = (in_dtype == QB_DTYPE_F32 || in_dtype == QB_DTYPE_BF16) &&
+                     (out_dtype == QB_DTYPE_F32 || out_dtype == QB_DTYPE_BF16);
+  if (P < 0 || Hk < 1 || Hv < 1 || (Dk != 32 && Dk != 64 && Dk != 128 && Dk != 256) || !dt_ok)
+    return noalloc_fail(err, errlen, "gated delta gate backward (no-alloc): bad arguments (P %lld, Hk %d, Hv %d, Dk %d)",
+                        (long long)P, Hk, Hv, Dk);
+  const int64_t need = (int64_t)gate_head_blocks(P) * Hv * 2;
+  if (Hv > 256 || need > kGateScratchFloats)
+    return noalloc_fail(err, errlen,
+                        "gated delta gate backward (no-alloc): Hv = %d needs %lld scratch floats; the fixed scratch "
+                        "holds %lld (at most 256 value heads)",
+                        Hv, (long long)need, (long long)kGateScratchFloats);
+  if (!q || !k || !a || !b || !A_log || !dt_bias || !dqn || !dkn || !dg || !dbeta || !dq || !dk || !da || !db ||
+      !dA_log || !ddt_bias)
+    return noalloc_fail(err, errlen, "gated delta gate backward (no-alloc): every pointer must be non-null");
+  if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)dqn | (uintptr_t)dkn) % 16)
+    return noalloc_fail(err, errlen, "gated delta gate backward (no-alloc): q, k, dqn, dkn need 16-byte alignment");
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t e;
+  if (P == 0) {
+    e = cudaMemsetAsync(dA_log, 0, Hv * 4, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(ddt_bias, 0, Hv * 4, st);
+  } else {
+    float* scratch = nullptr;
+    e = scratch_on_current_device(&scratch);
+    if (e == cudaSuccess) {
+      // Every partial the finishing kernel reads is written first by the heads kernel, so nothing in
+      // the scratch needs clearing between calls.
+      GateArgs ga{};
+      ga.P = P, ga.Hk = Hk, ga.Hv = Hv, ga.Dk = Dk;
+      ga.q = q, ga.k = k, ga.a = a, ga.b = b, ga.A_log = A_log, ga.dt_bias = dt_bias;
+      ga.dqn = dqn, ga.dkn = dkn, ga.dg = dg, ga.dbeta = dbeta;
+      ga.dq = dq, ga.dk = dk, ga.da = da, ga.db = db, ga.dA_log = dA_log, ga.ddt_bias = ddt_bias;
+      e = gate_bwd(ga, in_dtype == QB_DTYPE_BF16, out_dtype == QB_DTYPE_BF16, scratch, st);
+    }
+  }
+  if (e != cudaSuccess)
+    return noalloc_fail(err, errlen, "gated delta gate backward (no-alloc): CUDA error %d (%s)", (int)e,
+                        cudaGetErrorString(e));
+  return 0;
+}
