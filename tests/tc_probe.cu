@@ -94,3 +94,52 @@ extern "C" int tc_probe_gemm(int M, int N, int K, int kind, int a_mn, int b_mn, 
   tc_probe_kernel<<<1, 128, smem>>>(M, N, K, kind, a_mn, b_mn, A, B, D, err);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
+
+// TMA layout probe: one 2-D box of 32 fp32 columns x 64 rows from an [rows][64] fp32 matrix, loaded
+// with the given swizzle (3 = 128B, 4 = 128B with 32-byte atoms), copied back raw so the test can
+// compare every element's position with the layouts tc_sm100.cuh assumes.
+__global__ void __launch_bounds__(128) tc_probe_tma_kernel(const __grid_constant__ CUtensorMap map, int row0,
+                                                           int col0, float* out, int* err) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  __shared__ uint64_t bar;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bar, 1);
+    tc::fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    tc::mbar_arrive_expect_tx(&bar, 8192);
+    tc::tma_load_2d(smem, &map, &bar, col0, row0);
+  }
+  const bool ok = tc::mbar_wait(&bar, 0, err, 1);
+  __syncthreads();
+  if (ok)
+    for (int i = threadIdx.x; i < 2048; i += blockDim.x) out[i] = reinterpret_cast<float*>(smem)[i];
+}
+
+extern "C" int tc_probe_tma(const float* src, int rows, int row0, int col0, int swizzle, float* out, int* err) {
+  using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess)
+    return -3;
+  if (rows < 64 || row0 < 0 || row0 + 64 > rows || (col0 != 0 && col0 != 32)) return -1;
+  CUtensorMap map;
+  cuuint64_t dims[2] = {64, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {64 * 4};
+  cuuint32_t box[2] = {32, 64};
+  cuuint32_t es[2] = {1, 1};
+  CUtensorMapSwizzle sw = swizzle == 4 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
+  if (reinterpret_cast<EncodeTiled>(p)(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(src), dims,
+                                       strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                                       CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+      CUDA_SUCCESS)
+    return -4;
+  cudaFuncSetAttribute(tc_probe_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 8192 + 1024);
+  tc_probe_tma_kernel<<<1, 128, 8192 + 1024>>>(map, row0, col0, out, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}

@@ -60,3 +60,36 @@ def test_mma_tile(L, kind, M, N, K, a_mn, b_mn):
     want = Ar @ Br.T
     rel = ((D.double() - want).norm() / want.norm()).item()
     assert rel < 1e-5, rel
+
+
+def _expect_offsets(kind):
+    """Byte offset of element (row k, column r) of a 64 x 32 fp32 box in the layout tc_sm100.cuh uses:
+    kind 'k' = K-major 128-byte swizzle (16-byte chunks by row & 7), 'mn' = MN-major tf32 (32-byte
+    granules by row & 3)."""
+    off = {}
+    for k in range(64):
+        for r in range(32):
+            b = r * 4
+            if kind == "k":
+                off[(k, r)] = k * 128 + (((b >> 4) ^ (k & 7)) << 4) + (b & 15)
+            else:
+                off[(k, r)] = k * 128 + (((b >> 5) ^ (k & 3)) << 5) + (b & 31)
+    return off
+
+
+@pytest.mark.parametrize("swizzle,kind", [(3, "k"), (4, "mn")])
+@pytest.mark.parametrize("col0", [0, 32])
+def test_tma_box_layout(swizzle, kind, col0):
+    L = build_probe()
+    L.tc_probe_tma.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                               ctypes.c_void_p, ctypes.c_void_p]
+    rows = 256
+    src = torch.arange(rows * 64, dtype=torch.float32, device="cuda").reshape(rows, 64)
+    out = torch.full((2048,), -1.0, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    assert L.tc_probe_tma(src.data_ptr(), rows, 64, col0, swizzle, out.data_ptr(), err.data_ptr()) == 0
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    got = out.cpu()
+    for (k, r), o in _expect_offsets(kind).items():
+        assert got[o // 4].item() == src[64 + k, col0 + r].item(), (k, r)
