@@ -2,26 +2,36 @@
 // sm_100a: TMA tile loads, tcgen05 MMAs with TMEM accumulators, chunk C = 64.
 //
 // Per value head and chunk (local steps i, j < C; b = inclusive cumsum of log g inside the chunk,
-// gamma = exp(b); rows past the sequence end carry k = q = v = 0, beta = 0, log g = 0):
-//   L  = strictly-lower(beta_i exp(b_i - b_j) (K K^T)_ij),   T = (I + L)^-1
-//   P  = lower-incl(exp(b_i - b_j) (Q K^T)_ij)
+// gamma = exp(b), Gamma_ij = exp(b_i - b_j), lambda_i = exp(b_C - b_i); rows past the sequence end
+// carry beta = 0, log g = 0 and zero v / dy):
+//   L  = strict-lower(beta_i Gamma_ij (K K^T)_ij),   T = (I + L)^-1
+//   P  = lower(Gamma_ij (Q K^T)_ij)
 //   E  = diag(beta) (V - diag(gamma) K S^T)                  (S: the chunk-start state, Dv x Dk)
 //   D  = T E                                                  (the chunk's delta rows)
 //   O  = diag(gamma) Q S^T + P D
-//   S' = gamma_C S + (diag(exp(b_C - b)) D)^T K
-// This is the recurrence of src/delta_grad.cpp:13-14 (S~ = g S; u = S~ k; delta = beta (v - u);
-// S = S~ + delta k^T; y = S q) applied to 64 steps at once (the WY / UT form).
+//   S' = gamma_C S + (diag(lambda) D)^T K
+// the recurrence of src/delta_grad.cpp:13-14 (S~ = g S; u = S~ k; delta = beta (v - u);
+// S = S~ + delta k^T; y = S q) over 64 steps at once (the WY / UT form).  Its backward, with dS the
+// cotangent of S' and dO that of O:
+//   dD  = P^T dO + diag(lambda) K dS^T,   F = T^T dD
+//   dS_start = gamma_C dS + (diag(gamma) dO)^T Q - (diag(beta gamma) F)^T K,   dV = diag(beta) F
+//   dQ  = diag(gamma) dO S + dP^ K,   dP^ = lower(Gamma (dO D^T))
+//   dK  = dP^^T Q + diag(lambda) D dS - diag(beta gamma) F S + dKK K + dKK^T K,
+//         dKK = strict-lower(beta_i Gamma_ij (-F D^T)_ij)
+//   d b_i (log-gate cumsum) from every Gamma, gamma and lambda above; d log g = reverse cumsum of d b.
 //
 // Kernels:
-//   gdn_chunk_prep       grid (chunks, Hv): K K^T on the tensor cores, the triangular inverse T by
-//                        forward substitution, the chunk's cumulative log gates.  Fully parallel.
-//   gdn_chunk_fwd_state  grid (Dv/32, Hv, sequences): walks the chunks of a sequence in order with a
-//                        32-row slice of the state in registers; per chunk three tcgen05 rounds
-//                        (K S^T, Q S^T, Q K^T | T E | P D, K^T D~).  Writes y and, for training, the
-//                        chunk-start states (the reference's ckpt, src/delta_grad.cpp:172-181).
-// Operand precision: products of two inputs (K K^T, Q K^T) in bf16 (exact); an input times a computed
-// tile with the computed tile split into bf16 hi + lo (about 16 mantissa bits); two computed tiles
-// in tf32 (round-to-nearest).
+//   gdn_chunk_prep       (chunks, Hv): K K^T and Q K^T on the tensor cores, T by forward substitution;
+//                        writes T, P, Gamma*KK (training) and the gates.  Fully parallel.
+//   gdn_chunk_fwd_state  (Dv/32, Hv, sequences): the chunks of a sequence in order, 32 state rows in
+//                        registers; three tcgen05 rounds per chunk (K S^T, Q S^T | T E | P D, K^T D~).
+//                        Writes y and, for training, the chunk-start states.
+//   gdn_chunk_bwd_state  (Dv/32, Hv, sequences): the chunks in reverse with 32 rows of dS; three rounds
+//                        (K dS^T, P^T dO | T^T dD | Q^T (gamma dO), K^T H).  Writes dv, dS per chunk, dh0.
+//   gdn_chunk_bwd_grad   (chunks, Hk): everything else per chunk, the value heads of a key head in turn
+//                        so dq and dk are summed over the group in TMEM in a fixed order.
+// Operand precision: input x input products in bf16 (exact); input x computed with the computed tile
+// split into bf16 hi + lo (about 16 mantissa bits); computed x computed in tf32 (round to nearest).
 #include <cuda.h>
 #include <cuda_bf16.h>
 
@@ -38,7 +48,7 @@ namespace {
 constexpr int C = kChunk;   // 64
 constexpr int DK = 128;
 constexpr int DV = 128;
-constexpr int DVT = 32;     // value rows of the state per CTA in the state walk
+constexpr int DVT = 32;     // value rows of the state per CTA in the walks; the dv slice in the gradient kernel
 
 __device__ __forceinline__ float tf32_rna(float x) {
   uint32_t u;
@@ -72,6 +82,21 @@ __device__ __forceinline__ void chunk_info(const Geo& g, int64_t c, int& n, int6
   L = (int)min((int64_t)C, (int64_t)g.cu[n + 1] - tok0);
 }
 
+__device__ __forceinline__ void seq_chunks(const Geo& g, int n, int64_t& c_first, int64_t& nchunks, int64_t& seq0,
+                                           int64_t& seq1) {
+  if (g.cu) {
+    c_first = g.chunk_off[n];
+    nchunks = g.chunk_off[n + 1] - c_first;
+    seq0 = g.cu[n];
+    seq1 = g.cu[n + 1];
+  } else {
+    c_first = (int64_t)n * g.ncs;
+    nchunks = g.ncs;
+    seq0 = (int64_t)n * g.T;
+    seq1 = seq0 + g.T;
+  }
+}
+
 // Inclusive prefix sum over 64 values held by threads 0..63 (warps 0 and 1); result in out[64].
 __device__ __forceinline__ void scan64(float x, float* out, float* tmp) {
   const int tid = threadIdx.x, lane = tid & 31;
@@ -86,23 +111,63 @@ __device__ __forceinline__ void scan64(float x, float* out, float* tmp) {
   if (tid < 64) out[tid] = x;
 }
 
+// 32 bf16 activations of one row (zero if !valid) as floats.
+__device__ __forceinline__ void load_row32(const __nv_bfloat16* p, bool valid, float (&v)[32]) {
+  if (valid) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float t8[8];
+      load_vec<8>(p + 8 * q, t8);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[8 * q + e] = t8[e];
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = 0.f;
+  }
+}
+
+template <typename Tout>
+__device__ __forceinline__ void store_row32(Tout* p, const float (&v)[32]);
+template <>
+__device__ __forceinline__ void store_row32<__nv_bfloat16>(__nv_bfloat16* p, const float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    *reinterpret_cast<uint4*>(p + 8 * q) =
+        make_uint4(tc::pack_bf16(v[8 * q], v[8 * q + 1]), tc::pack_bf16(v[8 * q + 2], v[8 * q + 3]),
+                   tc::pack_bf16(v[8 * q + 4], v[8 * q + 5]), tc::pack_bf16(v[8 * q + 6], v[8 * q + 7]));
+}
+template <>
+__device__ __forceinline__ void store_row32<float>(float* p, const float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 8; ++q) *reinterpret_cast<float4*>(p + 4 * q) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+}
+
+__device__ __forceinline__ bool wait_all(uint64_t* bar, uint32_t parity, int* err, int code) {
+  return __syncthreads_and(tc::mbar_wait(bar, parity, err, code)) != 0;
+}
+
 }  // namespace
 
 // ------------------------------------------------------------------------------------------------
-// Per (chunk, value head): T = (I + L)^-1 and the gates (b, beta) of the chunk.
+// Per (chunk, value head): T, P, Gamma*KK and the gates of the chunk.
 struct PrepArgs {
   Geo geo;
   const float *g, *beta;
-  float* Tbuf;      // [chunks, Hv, 64, 64]
-  float* gates;     // [chunks, Hv, 2, 64]: b then beta
+  float* Tbuf;      // [chunks, Hv, 64, 64]  T = (I + L)^-1, tf32-rounded
+  float* Pbuf;      // [chunks, Hv, 64, 64]  P, tf32-rounded
+  float* Lbuf;      // [chunks, Hv, 64, 64]  strict-lower Gamma * K K^T (training only), or null
+  float* gates;     // [chunks, Hv, 2, 64]:  b then beta
   int* err;
 };
 
-__global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CUtensorMap kmap, PrepArgs a) {
+__global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CUtensorMap kmap,
+                                                      const __grid_constant__ CUtensorMap qmap, PrepArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* ktile = smem;                                   // 16 KB bf16, two 64-column slabs
-  float* Lm = reinterpret_cast<float*>(smem + 16384);      // [64][68]
+  uint8_t* ktile = smem;                                   // 16 KB bf16
+  uint8_t* qtile = smem + 16384;                           // 16 KB bf16
+  float* Lm = reinterpret_cast<float*>(smem + 32768);      // [64][68]
   __shared__ float sb[64], sbeta[64], stmp[2];
   __shared__ uint64_t bar_tma, bar_mma;
   __shared__ uint32_t tmem_slot;
@@ -115,7 +180,7 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CU
   int64_t tok0;
   chunk_info(a.geo, c, n, tok0, L);
 
-  if (warp == 0) tc::tmem_alloc(&tmem_slot, 64);
+  if (warp == 0) tc::tmem_alloc(&tmem_slot, 128);
   if (tid == 0) {
     tc::mbar_init(&bar_tma, 1);
     tc::mbar_init(&bar_mma, 1);
@@ -126,9 +191,11 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CU
   tc::fence_after_sync();
   const uint32_t tmem = tmem_slot;
   if (tid == 0) {
-    tc::mbar_arrive_expect_tx(&bar_tma, 16384);
+    tc::mbar_arrive_expect_tx(&bar_tma, 32768);
     tc::tma_load_3d(ktile, &kmap, &bar_tma, 0, hk, (int)tok0);
     tc::tma_load_3d(ktile + 8192, &kmap, &bar_tma, 64, hk, (int)tok0);
+    tc::tma_load_3d(qtile, &qmap, &bar_tma, 0, hk, (int)tok0);
+    tc::tma_load_3d(qtile + 8192, &qmap, &bar_tma, 64, hk, (int)tok0);
   }
   float lg = 0.f, bt = 0.f;
   if (tid < 64 && tid < L) {
@@ -139,27 +206,44 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CU
   if (tid < 64) sbeta[tid] = bt;
   scan64(lg, sb, stmp);
 
-  bool ok = __syncthreads_and(tc::mbar_wait(&bar_tma, 0, a.err, 1)) != 0;
+  bool ok = wait_all(&bar_tma, 0, a.err, 1);
   if (ok && tid == 0) {
     tc::fence_after_sync();
-    tc::mma_tile<tc::kBF16>(tmem, tc::smem_u32(ktile), false, 64, tc::smem_u32(ktile), false, 64, 64, 64, DK, false);
+    const uint32_t kt = tc::smem_u32(ktile), qt = tc::smem_u32(qtile);
+    tc::mma_tile<tc::kBF16>(tmem, kt, false, 64, kt, false, 64, 64, 64, DK, false);        // K K^T
+    tc::mma_tile<tc::kBF16>(tmem + 64, qt, false, 64, kt, false, 64, 64, 64, DK, false);   // Q K^T
     tc::mma_commit(&bar_mma);
   }
   ok = __syncthreads_and(ok && tc::mbar_wait(&bar_mma, 0, a.err, 2)) != 0;
   tc::fence_after_sync();
+  const size_t mat = (size_t)(c * a.geo.Hv + hv) * 4096;
   if (ok) {
     const int i = 16 * warp + (lane & 15);
+    const bool owner = lane < 16;
+    const float bi = sb[i], be = sbeta[i];
     float v[32];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      tc::tmem_ld32(tc::taddr(tmem, 32 * warp, 32 * h), v);
-      if (lane < 16) {
-        const float bi = sb[i], be = sbeta[i];
+      tc::tmem_ld32(tc::taddr(tmem, 32 * warp, 32 * h), v);  // K K^T
+      if (owner) {
+        float lrow[32];
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) {
           const int j = 32 * h + jj;
-          Lm[i * LS + j] = j < i ? be * __expf(bi - sb[j]) * v[jj] : 0.f;
+          const float gk = j < i ? __expf(bi - sb[j]) * v[jj] : 0.f;
+          Lm[i * LS + j] = be * gk;
+          lrow[jj] = gk;
         }
+        if (a.Lbuf) store_row32<float>(a.Lbuf + mat + i * 64 + 32 * h, lrow);
+      }
+      tc::tmem_ld32(tc::taddr(tmem, 32 * warp, 64 + 32 * h), v);  // Q K^T
+      if (owner) {
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+          const int j = 32 * h + jj;
+          v[jj] = tf32_rna(j <= i ? __expf(bi - sb[j]) * v[jj] : 0.f);
+        }
+        store_row32<float>(a.Pbuf + mat + i * 64 + 32 * h, v);
       }
     }
   }
@@ -177,54 +261,51 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CU
       for (int j = 0; j < i; ++j) s = fmaf(-Li[j], t[j], s);
       t[i] = s;
     }
-    // the state walk feeds T to tf32 MMAs: round to nearest here rather than let the operand read drop bits
+    // T feeds tf32 MMAs: round to nearest here rather than let the operand read drop bits
+    float* dst = a.Tbuf + mat;
 #pragma unroll
-    for (int i = 0; i < 64; ++i) t[i] = tf32_rna(t[i]);
-    float* dst = a.Tbuf + ((c * a.geo.Hv + hv) * 64) * 64;
-#pragma unroll
-    for (int i = 0; i < 64; ++i) dst[i * 64 + col] = t[i];
+    for (int i = 0; i < 64; ++i) dst[i * 64 + col] = tf32_rna(t[i]);
     float* gd = a.gates + (c * a.geo.Hv + hv) * 128;
     gd[tid] = sb[tid];
     gd[64 + tid] = sbeta[tid];
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tmem, 64);
+  if (warp == 0) tc::tmem_dealloc(tmem, 128);
 }
 
 // ------------------------------------------------------------------------------------------------
-// The state walk.  One CTA per (32 value rows, value head, sequence); thread t holds column t of
-// the 32 state rows (S^T[t][0..31]) in registers.
+// The forward state walk.  One CTA per (32 value rows, value head, sequence); thread t holds column t
+// of the 32 state rows (S^T[t][0..31]) in registers.
 struct StateArgs {
   Geo geo;
   const void* v;          // [B*T, Hv, Dv] bf16
   const float* gates;     // [chunks, Hv, 2, 64]
   const float* h0;        // [N, Hv, Dv, Dk] or null
-  void* y;                // [B*T, Hv, Dv] (bf16 or fp32)
+  void* y;                // [B*T, Hv, Dv]
   float* hT;              // or null
   float* ckpt;            // [chunks, Hv, Dv, Dk] chunk-start states, or null
-  int out_bf16;
   int* err;
 };
 
-// Shared-memory plan of the state walk (bytes from a 1024-aligned base).
-constexpr int SM_K = 0;            // 2 x 16 KB bf16 K tiles (TMA)
-constexpr int SM_Q = 32768;        // 2 x 16 KB bf16 Q tiles (TMA)
-constexpr int SM_T = 65536;        // 2 x 16 KB fp32 T tiles (TMA)
-constexpr int SM_SHI = 98304;      // 8 KB bf16 state hi, K-major [32][128]
-constexpr int SM_SLO = 106496;     // 8 KB bf16 state lo
-constexpr int SM_E = 114688;       // 8 KB fp32 E, MN-major [64][32]
-constexpr int SM_P = 122880;       // 16 KB fp32 P, K-major [64][64]
-constexpr int SM_D = 139264;       // 8 KB fp32 D, MN-major [64][32]
-constexpr int SM_DHI = 147456;     // 8 KB bf16 D~ hi, MN-major [64][32]
-constexpr int SM_DLO = 155648;     // 8 KB bf16 D~ lo
-constexpr int SM_STATE_BYTES = 163840;
-constexpr int STATE_SMEM = SM_STATE_BYTES + 1024;
+// Shared memory of the forward walk (bytes from a 1024-aligned base).
+constexpr int FW_K = 0;            // 2 x 16 KB bf16 K (TMA)
+constexpr int FW_Q = 32768;        // 2 x 16 KB bf16 Q (TMA)
+constexpr int FW_T = 65536;        // 2 x 16 KB fp32 T, K-major (TMA)
+constexpr int FW_P = 98304;        // 2 x 16 KB fp32 P, K-major (TMA)
+constexpr int FW_SHI = 131072;     // 16 KB bf16 state hi, MN-major [128 dk][32 dv]
+constexpr int FW_SLO = 147456;     // 16 KB bf16 state lo
+constexpr int FW_E = 163840;       // 8 KB fp32 E, MN-major [64][32]
+constexpr int FW_D = 172032;       // 8 KB fp32 D, MN-major [64][32]
+constexpr int FW_DHI = 180224;     // 8 KB bf16 D~ hi, MN-major [64][32]
+constexpr int FW_DLO = 188416;     // 8 KB bf16 D~ lo
+constexpr int FW_SMEM = 196608 + 1024;
 
-template <bool OUT_BF16>
+template <typename Tout>
 __global__ void __launch_bounds__(128, 1) gdn_chunk_fwd_state(const __grid_constant__ CUtensorMap kmap,
                                                               const __grid_constant__ CUtensorMap qmap,
                                                               const __grid_constant__ CUtensorMap tmap,
+                                                              const __grid_constant__ CUtensorMap pmap,
                                                               StateArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -235,19 +316,10 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_fwd_state(const __grid_const
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int dv0 = blockIdx.x * DVT, hv = blockIdx.y, n = blockIdx.z;
   const int Hv = a.geo.Hv, hk = hv / (Hv / a.geo.Hk);
-  int64_t c_first, nchunks;
-  if (a.geo.cu) {
-    c_first = a.geo.chunk_off[n];
-    nchunks = a.geo.chunk_off[n + 1] - c_first;
-  } else {
-    c_first = (int64_t)n * a.geo.ncs;
-    nchunks = a.geo.ncs;
-  }
-  const int64_t seq0 = a.geo.cu ? a.geo.cu[n] : (int64_t)n * a.geo.T;
-  const int64_t seq1 = a.geo.cu ? a.geo.cu[n + 1] : (int64_t)n * a.geo.T + a.geo.T;
+  int64_t c_first, nchunks, seq0, seq1;
+  seq_chunks(a.geo, n, c_first, nchunks, seq0, seq1);
 
-  // TMEM columns
-  const uint32_t cR = 0, cY = 32, cQK = 64, cD = 128, cO = 160, cS = 192;
+  const uint32_t cR = 0, cY = 32, cD = 64, cO = 96, cS = 128;
   if (warp == 0) tc::tmem_alloc(&tmem_slot, 256);
   if (tid == 0) {
     tc::mbar_init(&bar_tma[0], 1);
@@ -257,14 +329,14 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_fwd_state(const __grid_const
     tc::prefetch_tmap(&kmap);
     tc::prefetch_tmap(&qmap);
     tc::prefetch_tmap(&tmap);
+    tc::prefetch_tmap(&pmap);
   }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = tmem_slot;
 
-  // state slice: s[j] = S[dv0 + j][tid]
-  float s[DVT];
+  float s[DVT];  // s[j] = S[dv0 + j][tid]
   {
     const size_t base = ((size_t)n * Hv + hv) * DV * DK;
 #pragma unroll
@@ -273,22 +345,23 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_fwd_state(const __grid_const
 
   auto issue_loads = [&](int64_t jc, int buf) {
     const int64_t tok = seq0 + jc * C;
-    const int64_t cg = c_first + jc;
-    tc::mbar_arrive_expect_tx(&bar_tma[buf], 16384 * 3);
-    tc::tma_load_3d(smem + SM_K + buf * 16384, &kmap, &bar_tma[buf], 0, hk, (int)tok);
-    tc::tma_load_3d(smem + SM_K + buf * 16384 + 8192, &kmap, &bar_tma[buf], 64, hk, (int)tok);
-    tc::tma_load_3d(smem + SM_Q + buf * 16384, &qmap, &bar_tma[buf], 0, hk, (int)tok);
-    tc::tma_load_3d(smem + SM_Q + buf * 16384 + 8192, &qmap, &bar_tma[buf], 64, hk, (int)tok);
-    const int trow = (int)((cg * Hv + hv) * 64);
-    tc::tma_load_2d(smem + SM_T + buf * 16384, &tmap, &bar_tma[buf], 0, trow);
-    tc::tma_load_2d(smem + SM_T + buf * 16384 + 8192, &tmap, &bar_tma[buf], 32, trow);
+    const int mrow = (int)(((c_first + jc) * Hv + hv) * 64);
+    tc::mbar_arrive_expect_tx(&bar_tma[buf], 16384 * 4);
+    tc::tma_load_3d(smem + FW_K + buf * 16384, &kmap, &bar_tma[buf], 0, hk, (int)tok);
+    tc::tma_load_3d(smem + FW_K + buf * 16384 + 8192, &kmap, &bar_tma[buf], 64, hk, (int)tok);
+    tc::tma_load_3d(smem + FW_Q + buf * 16384, &qmap, &bar_tma[buf], 0, hk, (int)tok);
+    tc::tma_load_3d(smem + FW_Q + buf * 16384 + 8192, &qmap, &bar_tma[buf], 64, hk, (int)tok);
+    tc::tma_load_2d(smem + FW_T + buf * 16384, &tmap, &bar_tma[buf], 0, mrow);
+    tc::tma_load_2d(smem + FW_T + buf * 16384 + 8192, &tmap, &bar_tma[buf], 32, mrow);
+    tc::tma_load_2d(smem + FW_P + buf * 16384, &pmap, &bar_tma[buf], 0, mrow);
+    tc::tma_load_2d(smem + FW_P + buf * 16384 + 8192, &pmap, &bar_tma[buf], 32, mrow);
   };
 
   if (nchunks > 0) {
     if (tid == 0) issue_loads(0, 0);
     sg[0][tid] = a.gates[(c_first * Hv + hv) * 128 + tid];
   }
-  uint32_t mma_phase = 0;
+  uint32_t ph = 0;
   bool ok = true;
   const int i_row = 16 * warp + (lane & 15);  // row of the M = 64 accumulators this thread reads
   const bool row_owner = lane < 16;
@@ -299,92 +372,54 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_fwd_state(const __grid_const
     const int64_t tok0 = seq0 + jc * C;
     const int L = (int)min((int64_t)C, seq1 - tok0);
 
-    // 1. the chunk-start state: saved for the backward, and split into the bf16 hi/lo operand
+    // 1. the chunk-start state: saved for the backward, split into the bf16 hi/lo operand (row tid)
     if (a.ckpt) {
       float* dst = a.ckpt + ((cg * Hv + hv) * DV + dv0) * (size_t)DK + tid;
 #pragma unroll
       for (int j = 0; j < DVT; ++j) dst[(size_t)j * DK] = s[j];
     }
-#pragma unroll
-    for (int j = 0; j < DVT; ++j) {
-      const __nv_bfloat16 hi = __float2bfloat16_rn(s[j]);
-      const __nv_bfloat16 lo = __float2bfloat16_rn(s[j] - __bfloat162float(hi));
-      const uint32_t o = tc::off_kmajor(j, tid, DVT, 2);
-      *reinterpret_cast<__nv_bfloat16*>(smem + SM_SHI + o) = hi;
-      *reinterpret_cast<__nv_bfloat16*>(smem + SM_SLO + o) = lo;
-    }
+    tc::st_row_bf16x2_32(smem + FW_SHI, smem + FW_SLO, tid, s);
     // 2. this thread's value row (rows past the end read as zero)
     float vr[DVT];
-    if (row_owner && i_row < L) {
-      const __nv_bfloat16* vp =
-          static_cast<const __nv_bfloat16*>(a.v) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0;
-#pragma unroll
-      for (int q4 = 0; q4 < DVT / 8; ++q4) {
-        float t8[8];
-        load_vec<8>(vp + 8 * q4, t8);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) vr[8 * q4 + e] = t8[e];
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < DVT; ++j) vr[j] = 0.f;
-    }
+    load_row32(static_cast<const __nv_bfloat16*>(a.v) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0,
+               row_owner && i_row < L, vr);
     // 3. tiles of this chunk
     tc::fence_async_smem();
     tc::fence_before_sync();
-    ok = __syncthreads_and(tc::mbar_wait(&bar_tma[buf], (uint32_t)((jc >> 1) & 1), a.err, 10)) != 0;
+    ok = wait_all(&bar_tma[buf], (uint32_t)((jc >> 1) & 1), a.err, 10);
     tc::fence_after_sync();
     if (!ok) break;
-    // prefetch the next chunk into the other buffer (its last readers finished last iteration)
-    if (jc + 1 < nchunks) {
+    if (jc + 1 < nchunks) {  // prefetch the next chunk (its buffer's last readers finished)
       if (tid == 0) issue_loads(jc + 1, buf ^ 1);
       sg[buf ^ 1][tid] = a.gates[((cg + 1) * Hv + hv) * 128 + tid];
     }
-    const uint32_t kt = tc::smem_u32(smem + SM_K + buf * 16384);
-    const uint32_t qt = tc::smem_u32(smem + SM_Q + buf * 16384);
-    const uint32_t tt = tc::smem_u32(smem + SM_T + buf * 16384);
-    // 4. R = K S^T, Y = Q S^T (S split hi + lo), QK = Q K^T
+    const uint32_t kt = tc::smem_u32(smem + FW_K + buf * 16384);
+    const uint32_t qt = tc::smem_u32(smem + FW_Q + buf * 16384);
+    // 4. R = K S^T, Y = Q S^T (S split hi + lo, MN-major: dk rows)
     if (tid == 0) {
-      const uint32_t shi = tc::smem_u32(smem + SM_SHI), slo = tc::smem_u32(smem + SM_SLO);
-      tc::mma_tile<tc::kBF16>(tmem + cR, kt, false, 64, shi, false, DVT, 64, DVT, DK, false);
-      tc::mma_tile<tc::kBF16>(tmem + cR, kt, false, 64, slo, false, DVT, 64, DVT, DK, true);
-      tc::mma_tile<tc::kBF16>(tmem + cY, qt, false, 64, shi, false, DVT, 64, DVT, DK, false);
-      tc::mma_tile<tc::kBF16>(tmem + cY, qt, false, 64, slo, false, DVT, 64, DVT, DK, true);
-      tc::mma_tile<tc::kBF16>(tmem + cQK, qt, false, 64, kt, false, 64, 64, 64, DK, false);
+      const uint32_t shi = tc::smem_u32(smem + FW_SHI), slo = tc::smem_u32(smem + FW_SLO);
+      tc::mma_tile<tc::kBF16>(tmem + cR, kt, false, 64, shi, true, DK, 64, DVT, DK, false);
+      tc::mma_tile<tc::kBF16>(tmem + cR, kt, false, 64, slo, true, DK, 64, DVT, DK, true);
+      tc::mma_tile<tc::kBF16>(tmem + cY, qt, false, 64, shi, true, DK, 64, DVT, DK, false);
+      tc::mma_tile<tc::kBF16>(tmem + cY, qt, false, 64, slo, true, DK, 64, DVT, DK, true);
       tc::mma_commit(&bar_mma);
     }
-    ok = __syncthreads_and(tc::mbar_wait(&bar_mma, mma_phase, a.err, 11)) != 0;
-    mma_phase ^= 1;
+    ok = wait_all(&bar_mma, ph, a.err, 11);
+    ph ^= 1;
     tc::fence_after_sync();
     if (!ok) break;
     const float* gb = sg[buf];
-    const float bi = gb[i_row], be = gb[64 + i_row], gi = __expf(bi);
+    const float bi = gb[i_row], be = gb[64 + i_row], gi = __expf(bi), bC = gb[63];
     float yp[DVT];
     {
       float r[32];
       tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cR), r);
-      if (row_owner) {
 #pragma unroll
-        for (int j = 0; j < DVT; ++j) {
-          const float e = be * (vr[j] - gi * r[j]);
-          *reinterpret_cast<float*>(smem + SM_E + tc::off_mnmajor(i_row, j, 64, 4)) = tf32_rna(e);
-        }
-      }
-      tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cY), r);
+      for (int j = 0; j < DVT; ++j) r[j] = tf32_rna(be * (vr[j] - gi * r[j]));
+      if (row_owner) tc::st_row_mn_f32(smem + FW_E, i_row, r);
+      tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cY), yp);
 #pragma unroll
-      for (int j = 0; j < DVT; ++j) yp[j] = gi * r[j];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cQK + 32 * h), r);
-        if (row_owner) {
-#pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            const int j = 32 * h + jj;
-            const float p = j <= i_row ? __expf(bi - gb[j]) * r[jj] : 0.f;
-            *reinterpret_cast<float*>(smem + SM_P + tc::off_kmajor(i_row, j, 64, 4)) = tf32_rna(p);
-          }
-        }
-      }
+      for (int j = 0; j < DVT; ++j) yp[j] *= gi;
     }
     tc::fence_async_smem();
     tc::fence_before_sync();
@@ -392,29 +427,27 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_fwd_state(const __grid_const
     tc::fence_after_sync();
     // 5. D = T E
     if (tid == 0) {
-      tc::mma_tile<tc::kTF32>(tmem + cD, tt, false, 64, tc::smem_u32(smem + SM_E), true, 64, 64, DVT, C, false);
+      tc::mma_tile<tc::kTF32>(tmem + cD, tc::smem_u32(smem + FW_T + buf * 16384), false, 64,
+                              tc::smem_u32(smem + FW_E), true, 64, 64, DVT, C, false);
       tc::mma_commit(&bar_mma);
     }
-    ok = __syncthreads_and(tc::mbar_wait(&bar_mma, mma_phase, a.err, 12)) != 0;
-    mma_phase ^= 1;
+    ok = wait_all(&bar_mma, ph, a.err, 12);
+    ph ^= 1;
     tc::fence_after_sync();
     if (!ok) break;
-    const float bC = gb[63];
     {
       float d[32];
       tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cD), d);
       if (row_owner) {
         const float sc = __expf(bC - bi);
+        float dd[32];
 #pragma unroll
         for (int j = 0; j < DVT; ++j) {
-          *reinterpret_cast<float*>(smem + SM_D + tc::off_mnmajor(i_row, j, 64, 4)) = tf32_rna(d[j]);
-          const float dt = sc * d[j];
-          const __nv_bfloat16 hi = __float2bfloat16_rn(dt);
-          const __nv_bfloat16 lo = __float2bfloat16_rn(dt - __bfloat162float(hi));
-          const uint32_t o = tc::off_mnmajor(i_row, j, 64, 2);
-          *reinterpret_cast<__nv_bfloat16*>(smem + SM_DHI + o) = hi;
-          *reinterpret_cast<__nv_bfloat16*>(smem + SM_DLO + o) = lo;
+          dd[j] = sc * d[j];
+          d[j] = tf32_rna(d[j]);
         }
+        tc::st_row_mn_f32(smem + FW_D, i_row, d);
+        tc::st_row_bf16x2_32(smem + FW_DHI, smem + FW_DLO, i_row, dd);
       }
     }
     tc::fence_async_smem();
@@ -423,14 +456,14 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_fwd_state(const __grid_const
     tc::fence_after_sync();
     // 6. O2 = P D;  S_upd^T = K^T D~ (K as the MN-major A operand: Dk rows, chunk steps as K)
     if (tid == 0) {
-      tc::mma_tile<tc::kTF32>(tmem + cO, tc::smem_u32(smem + SM_P), false, 64, tc::smem_u32(smem + SM_D), true, 64,
-                              64, DVT, C, false);
-      tc::mma_tile<tc::kBF16>(tmem + cS, kt, true, 64, tc::smem_u32(smem + SM_DHI), true, 64, 128, DVT, C, false);
-      tc::mma_tile<tc::kBF16>(tmem + cS, kt, true, 64, tc::smem_u32(smem + SM_DLO), true, 64, 128, DVT, C, true);
+      tc::mma_tile<tc::kTF32>(tmem + cO, tc::smem_u32(smem + FW_P + buf * 16384), false, 64,
+                              tc::smem_u32(smem + FW_D), true, 64, 64, DVT, C, false);
+      tc::mma_tile<tc::kBF16>(tmem + cS, kt, true, 64, tc::smem_u32(smem + FW_DHI), true, 64, 128, DVT, C, false);
+      tc::mma_tile<tc::kBF16>(tmem + cS, kt, true, 64, tc::smem_u32(smem + FW_DLO), true, 64, 128, DVT, C, true);
       tc::mma_commit(&bar_mma);
     }
-    ok = __syncthreads_and(tc::mbar_wait(&bar_mma, mma_phase, a.err, 13)) != 0;
-    mma_phase ^= 1;
+    ok = wait_all(&bar_mma, ph, a.err, 13);
+    ph ^= 1;
     tc::fence_after_sync();
     if (!ok) break;
     {
@@ -441,26 +474,9 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_fwd_state(const __grid_const
       for (int j = 0; j < DVT; ++j) s[j] = fmaf(gC, s[j], u[j]);
       tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cO), u);
       if (row_owner && i_row < L) {
-        const size_t yo = ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0;
-        if (OUT_BF16) {
-          __nv_bfloat16* yp16 = static_cast<__nv_bfloat16*>(a.y) + yo;
 #pragma unroll
-          for (int q = 0; q < DVT / 8; ++q) {
-            uint4 pk;
-            uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const __nv_bfloat162 h2 =
-                  __floats2bfloat162_rn(yp[8 * q + 2 * e] + u[8 * q + 2 * e], yp[8 * q + 2 * e + 1] + u[8 * q + 2 * e + 1]);
-              w[e] = *reinterpret_cast<const uint32_t*>(&h2);
-            }
-            *reinterpret_cast<uint4*>(yp16 + 8 * q) = pk;
-          }
-        } else {
-          float* yp32 = static_cast<float*>(a.y) + yo;
-#pragma unroll
-          for (int j = 0; j < DVT; ++j) yp32[j] = yp[j] + u[j];
-        }
+        for (int j = 0; j < DVT; ++j) u[j] += yp[j];
+        store_row32<Tout>(static_cast<Tout*>(a.y) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0, u);
       }
     }
     tc::fence_before_sync();
@@ -473,6 +489,580 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_fwd_state(const __grid_const
   tc::fence_before_sync();
   __syncthreads();
   if (warp == 0) tc::tmem_dealloc(tmem, 256);
+}
+
+// ------------------------------------------------------------------------------------------------
+// The backward state walk: chunks in reverse, 32 rows of dS per CTA (thread t holds dS[dv0+j][t]).
+struct BwdStateArgs {
+  Geo geo;
+  const void* dy;         // [B*T, Hv, Dv] bf16
+  const float* gates;
+  const float* dhT;       // [N, Hv, Dv, Dk] or null
+  void* dv;               // [B*T, Hv, Dv]
+  float* dh0;             // or null
+  float* dsbuf;           // [chunks, Hv, Dv, Dk]: cotangent of each chunk's end state
+  int* err;
+};
+
+constexpr int BW_K = 0;            // 2 x 16 KB bf16 K
+constexpr int BW_Q = 32768;        // 2 x 16 KB bf16 Q
+constexpr int BW_T = 65536;        // 2 x 16 KB fp32 T, MN-major tf32 layout (as T^T)
+constexpr int BW_P = 98304;        // 2 x 16 KB fp32 P, MN-major tf32 layout (as P^T)
+constexpr int BW_SHI = 131072;     // 16 KB bf16 dS hi, MN-major [128 dk][32 dv]
+constexpr int BW_SLO = 147456;     // 16 KB bf16 dS lo
+constexpr int BW_DO = 163840;      // 8 KB fp32 dO, MN-major [64][32]
+constexpr int BW_GHI = 172032;     // 8 KB bf16 gamma dO hi, MN-major
+constexpr int BW_GLO = 180224;     // 8 KB bf16 gamma dO lo
+constexpr int BW_DD = 188416;      // 8 KB fp32 dD, MN-major
+constexpr int BW_HHI = 196608;     // 8 KB bf16 H = -beta gamma F hi, MN-major
+constexpr int BW_HLO = 204800;     // 8 KB bf16 H lo
+constexpr int BW_SMEM = 212992 + 1024;
+
+template <typename Tout>
+__global__ void __launch_bounds__(128, 1) gdn_chunk_bwd_state(const __grid_constant__ CUtensorMap kmap,
+                                                              const __grid_constant__ CUtensorMap qmap,
+                                                              const __grid_constant__ CUtensorMap tmap_mn,
+                                                              const __grid_constant__ CUtensorMap pmap_mn,
+                                                              BwdStateArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ float sg[2][128];
+  __shared__ uint64_t bar_tma[2], bar_mma;
+  __shared__ uint32_t tmem_slot;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int dv0 = blockIdx.x * DVT, hv = blockIdx.y, n = blockIdx.z;
+  const int Hv = a.geo.Hv, hk = hv / (Hv / a.geo.Hk);
+  int64_t c_first, nchunks, seq0, seq1;
+  seq_chunks(a.geo, n, c_first, nchunks, seq0, seq1);
+
+  const uint32_t cX = 0, cG = 32, cF = 64, cU = 96;
+  if (warp == 0) tc::tmem_alloc(&tmem_slot, 128);
+  if (tid == 0) {
+    tc::mbar_init(&bar_tma[0], 1);
+    tc::mbar_init(&bar_tma[1], 1);
+    tc::mbar_init(&bar_mma, 1);
+    tc::fence_mbar_init();
+    tc::prefetch_tmap(&kmap);
+    tc::prefetch_tmap(&qmap);
+    tc::prefetch_tmap(&tmap_mn);
+    tc::prefetch_tmap(&pmap_mn);
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = tmem_slot;
+
+  float ds[DVT];  // ds[j] = dS[dv0 + j][tid]
+  {
+    const size_t base = ((size_t)n * Hv + hv) * DV * DK;
+#pragma unroll
+    for (int j = 0; j < DVT; ++j) ds[j] = a.dhT ? a.dhT[base + (size_t)(dv0 + j) * DK + tid] : 0.f;
+  }
+
+  auto issue_loads = [&](int64_t jc, int buf) {
+    const int64_t tok = seq0 + jc * C;
+    const int mrow = (int)(((c_first + jc) * Hv + hv) * 64);
+    tc::mbar_arrive_expect_tx(&bar_tma[buf], 16384 * 4);
+    tc::tma_load_3d(smem + BW_K + buf * 16384, &kmap, &bar_tma[buf], 0, hk, (int)tok);
+    tc::tma_load_3d(smem + BW_K + buf * 16384 + 8192, &kmap, &bar_tma[buf], 64, hk, (int)tok);
+    tc::tma_load_3d(smem + BW_Q + buf * 16384, &qmap, &bar_tma[buf], 0, hk, (int)tok);
+    tc::tma_load_3d(smem + BW_Q + buf * 16384 + 8192, &qmap, &bar_tma[buf], 64, hk, (int)tok);
+    tc::tma_load_2d(smem + BW_T + buf * 16384, &tmap_mn, &bar_tma[buf], 0, mrow);
+    tc::tma_load_2d(smem + BW_T + buf * 16384 + 8192, &tmap_mn, &bar_tma[buf], 32, mrow);
+    tc::tma_load_2d(smem + BW_P + buf * 16384, &pmap_mn, &bar_tma[buf], 0, mrow);
+    tc::tma_load_2d(smem + BW_P + buf * 16384 + 8192, &pmap_mn, &bar_tma[buf], 32, mrow);
+  };
+
+  if (nchunks > 0) {
+    if (tid == 0) issue_loads(nchunks - 1, 0);
+    sg[0][tid] = a.gates[((c_first + nchunks - 1) * Hv + hv) * 128 + tid];
+  }
+  uint32_t ph = 0;
+  bool ok = true;
+  const int i_row = 16 * warp + (lane & 15);
+  const bool row_owner = lane < 16;
+
+  for (int64_t it = 0; it < nchunks && ok; ++it) {
+    const int64_t jc = nchunks - 1 - it;
+    const int buf = (int)(it & 1);
+    const int64_t cg = c_first + jc;
+    const int64_t tok0 = seq0 + jc * C;
+    const int L = (int)min((int64_t)C, seq1 - tok0);
+
+    // 1. dS of this chunk's end: saved for the gradient kernel, split into the hi/lo operand (row tid)
+    {
+      float* dst = a.dsbuf + ((cg * Hv + hv) * DV + dv0) * (size_t)DK + tid;
+#pragma unroll
+      for (int j = 0; j < DVT; ++j) dst[(size_t)j * DK] = ds[j];
+    }
+    tc::st_row_bf16x2_32(smem + BW_SHI, smem + BW_SLO, tid, ds);
+    // 2. dO row (zero past the end) as the fp32 operand of P^T dO, and gamma dO as bf16 hi/lo
+    const float* gb = sg[buf];
+    const float bi = gb[i_row], be = gb[64 + i_row], gi = __expf(bi), bC = gb[63];
+    if (row_owner) {
+      float d[32];
+      load_row32(static_cast<const __nv_bfloat16*>(a.dy) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0,
+                 i_row < L, d);
+      tc::st_row_mn_f32(smem + BW_DO, i_row, d);
+#pragma unroll
+      for (int j = 0; j < DVT; ++j) d[j] *= gi;
+      tc::st_row_bf16x2_32(smem + BW_GHI, smem + BW_GLO, i_row, d);
+    }
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    ok = wait_all(&bar_tma[buf], (uint32_t)((it >> 1) & 1), a.err, 20);
+    tc::fence_after_sync();
+    if (!ok) break;
+    if (jc > 0) {  // prefetch the previous chunk
+      if (tid == 0) issue_loads(jc - 1, buf ^ 1);
+      sg[buf ^ 1][tid] = a.gates[((cg - 1) * Hv + hv) * 128 + tid];
+    }
+    const uint32_t kt = tc::smem_u32(smem + BW_K + buf * 16384);
+    const uint32_t qt = tc::smem_u32(smem + BW_Q + buf * 16384);
+    // 3. X1 = K dS^T (dS split hi + lo), G = P^T dO
+    if (tid == 0) {
+      tc::mma_tile<tc::kBF16>(tmem + cX, kt, false, 64, tc::smem_u32(smem + BW_SHI), true, DK, 64, DVT, DK, false);
+      tc::mma_tile<tc::kBF16>(tmem + cX, kt, false, 64, tc::smem_u32(smem + BW_SLO), true, DK, 64, DVT, DK, true);
+      tc::mma_tile<tc::kTF32>(tmem + cG, tc::smem_u32(smem + BW_P + buf * 16384), true, 64,
+                              tc::smem_u32(smem + BW_DO), true, 64, 64, DVT, C, false);
+      tc::mma_commit(&bar_mma);
+    }
+    ok = wait_all(&bar_mma, ph, a.err, 21);
+    ph ^= 1;
+    tc::fence_after_sync();
+    if (!ok) break;
+    {
+      float x[32], g[32];
+      tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cX), x);
+      tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cG), g);
+      const float lam = __expf(bC - bi);
+#pragma unroll
+      for (int j = 0; j < DVT; ++j) g[j] = tf32_rna(fmaf(lam, x[j], g[j]));
+      if (row_owner) tc::st_row_mn_f32(smem + BW_DD, i_row, g);
+    }
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    // 4. F = T^T dD
+    if (tid == 0) {
+      tc::mma_tile<tc::kTF32>(tmem + cF, tc::smem_u32(smem + BW_T + buf * 16384), true, 64,
+                              tc::smem_u32(smem + BW_DD), true, 64, 64, DVT, C, false);
+      tc::mma_commit(&bar_mma);
+    }
+    ok = wait_all(&bar_mma, ph, a.err, 22);
+    ph ^= 1;
+    tc::fence_after_sync();
+    if (!ok) break;
+    {
+      float f[32];
+      tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cF), f);
+      if (row_owner) {
+        float o[32];
+        if (i_row < L) {
+#pragma unroll
+          for (int j = 0; j < DVT; ++j) o[j] = be * f[j];
+          store_row32<Tout>(static_cast<Tout*>(a.dv) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0, o);
+        }
+        const float h = -be * gi;
+#pragma unroll
+        for (int j = 0; j < DVT; ++j) o[j] = h * f[j];
+        tc::st_row_bf16x2_32(smem + BW_HHI, smem + BW_HLO, i_row, o);
+      }
+    }
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    // 5. U = Q^T (gamma dO) + K^T H (Q, K as MN-major A: Dk rows, chunk steps as K)
+    if (tid == 0) {
+      tc::mma_tile<tc::kBF16>(tmem + cU, qt, true, 64, tc::smem_u32(smem + BW_GHI), true, 64, 128, DVT, C, false);
+      tc::mma_tile<tc::kBF16>(tmem + cU, qt, true, 64, tc::smem_u32(smem + BW_GLO), true, 64, 128, DVT, C, true);
+      tc::mma_tile<tc::kBF16>(tmem + cU, kt, true, 64, tc::smem_u32(smem + BW_HHI), true, 64, 128, DVT, C, true);
+      tc::mma_tile<tc::kBF16>(tmem + cU, kt, true, 64, tc::smem_u32(smem + BW_HLO), true, 64, 128, DVT, C, true);
+      tc::mma_commit(&bar_mma);
+    }
+    ok = wait_all(&bar_mma, ph, a.err, 23);
+    ph ^= 1;
+    tc::fence_after_sync();
+    if (!ok) break;
+    {
+      float u[32];
+      tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cU), u);
+      const float gC = __expf(bC);
+#pragma unroll
+      for (int j = 0; j < DVT; ++j) ds[j] = fmaf(gC, ds[j], u[j]);
+    }
+    tc::fence_before_sync();
+  }
+  if (ok && a.dh0) {
+    float* dst = a.dh0 + (((size_t)n * Hv + hv) * DV + dv0) * DK + tid;
+#pragma unroll
+    for (int j = 0; j < DVT; ++j) dst[(size_t)j * DK] = ds[j];
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tmem, 128);
+}
+
+// ------------------------------------------------------------------------------------------------
+// Per-chunk gradients: one CTA per (chunk, key head); its value heads in turn, Dv in four slices of 32.
+struct GradArgs {
+  Geo geo;
+  const void *v, *dy;       // bf16
+  const float* g;           // [B*T, Hv] (dg = d log g / g)
+  const float* gates;
+  const float* ckpt;        // chunk-start states
+  const float* dsbuf;       // chunk-end state cotangents
+  void *dq, *dk;            // [B*T, Hk, Dk]
+  float *dg, *dbeta;        // [B*T, Hv]
+  int* err;
+};
+
+constexpr int GR_K = 0;         // 16 KB bf16 K (TMA)
+constexpr int GR_Q = 16384;     // 16 KB bf16 Q
+constexpr int GR_TK = 32768;    // 16 KB fp32 T, K-major
+constexpr int GR_TM = 49152;    // 16 KB fp32 T, MN-major (as T^T)
+constexpr int GR_PM = 65536;    // 16 KB fp32 P, MN-major (as P^T)
+constexpr int GR_SHI = 81920;   // 8 KB bf16 S hi, K-major [32 dv][128 dk]      | finalize: Gamma*KK (16 KB)
+constexpr int GR_SLO = 90112;   // 8 KB bf16 S lo
+constexpr int GR_DHI = 98304;   // 8 KB bf16 dS hi                              | finalize: dP^ hi, lo
+constexpr int GR_DLO = 106496;  // 8 KB bf16 dS lo
+constexpr int GR_SM = 114688;   // 16 KB fp32 S, MN-major [32 dv rows][128 dk]   | finalize: dKK hi, lo
+constexpr int GR_DM = 131072;   // 16 KB fp32 dS, MN-major                       | finalize: column-sum scratch
+constexpr int GR_DOM = 147456;  // 8 KB fp32 dO, MN-major [64][32]
+constexpr int GR_DOK = 155648;  // 8 KB fp32 dO, K-major [64][32]
+constexpr int GR_GDO = 163840;  // 8 KB fp32 gamma dO, K-major
+constexpr int GR_E = 172032;    // 8 KB fp32 E, MN-major
+constexpr int GR_DD = 180224;   // 8 KB fp32 dD, MN-major
+constexpr int GR_D = 188416;    // 8 KB fp32 D, K-major
+constexpr int GR_LD = 196608;   // 8 KB fp32 lambda D, K-major
+constexpr int GR_F = 204800;    // 8 KB fp32 F, K-major
+constexpr int GR_NF = 212992;   // 8 KB fp32 -beta gamma F, K-major
+constexpr int GR_SMEM = 221184 + 1024;
+
+template <typename Tout>
+__global__ void __launch_bounds__(128, 1) gdn_chunk_bwd_grad(const __grid_constant__ CUtensorMap kmap,
+                                                             const __grid_constant__ CUtensorMap qmap,
+                                                             const __grid_constant__ CUtensorMap tmap_k,
+                                                             const __grid_constant__ CUtensorMap tmap_mn,
+                                                             const __grid_constant__ CUtensorMap pmap_mn,
+                                                             const __grid_constant__ CUtensorMap lmap_k, GradArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ float sb[64], sbeta[64], sdb[64], scol[64], sred[8];
+  __shared__ uint64_t bar_kq, bar_h, bar_l, bar_mma;
+  __shared__ uint32_t tmem_slot;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t c = blockIdx.x;
+  const int hk = blockIdx.y, Hv = a.geo.Hv, ratio = Hv / a.geo.Hk;
+  int n, L;
+  int64_t tok0;
+  chunk_info(a.geo, c, n, tok0, L);
+  const int i_row = 16 * warp + (lane & 15);
+  const bool row_owner = lane < 16;
+  const bool valid = row_owner && i_row < L;
+
+  // TMEM: R (then D) 0, Y 32, X1 (then F) 64, G 96, dQ 128..255, dK 256..383, dP 384..447, F D^T 448..511
+  const uint32_t cR = 0, cY = 32, cX = 64, cG = 96, cDQ = 128, cDK = 256, cDP = 384, cFD = 448;
+  if (warp == 0) tc::tmem_alloc(&tmem_slot, 512);
+  if (tid == 0) {
+    tc::mbar_init(&bar_kq, 1);
+    tc::mbar_init(&bar_h, 1);
+    tc::mbar_init(&bar_l, 1);
+    tc::mbar_init(&bar_mma, 1);
+    tc::fence_mbar_init();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = tmem_slot;
+  if (tid == 0) {
+    tc::mbar_arrive_expect_tx(&bar_kq, 32768);
+    tc::tma_load_3d(smem + GR_K, &kmap, &bar_kq, 0, hk, (int)tok0);
+    tc::tma_load_3d(smem + GR_K + 8192, &kmap, &bar_kq, 64, hk, (int)tok0);
+    tc::tma_load_3d(smem + GR_Q, &qmap, &bar_kq, 0, hk, (int)tok0);
+    tc::tma_load_3d(smem + GR_Q + 8192, &qmap, &bar_kq, 64, hk, (int)tok0);
+  }
+  uint32_t ph_mma = 0;
+  bool ok = wait_all(&bar_kq, 0, a.err, 30);
+  const uint32_t kt = tc::smem_u32(smem + GR_K), qt = tc::smem_u32(smem + GR_Q);
+
+  for (int r = 0; r < ratio && ok; ++r) {
+    const int hv = hk * ratio + r;
+    const int mrow = (int)((c * Hv + hv) * 64);
+    if (tid == 0) {
+      tc::mbar_arrive_expect_tx(&bar_h, 16384 * 3);
+      tc::tma_load_2d(smem + GR_TK, &tmap_k, &bar_h, 0, mrow);
+      tc::tma_load_2d(smem + GR_TK + 8192, &tmap_k, &bar_h, 32, mrow);
+      tc::tma_load_2d(smem + GR_TM, &tmap_mn, &bar_h, 0, mrow);
+      tc::tma_load_2d(smem + GR_TM + 8192, &tmap_mn, &bar_h, 32, mrow);
+      tc::tma_load_2d(smem + GR_PM, &pmap_mn, &bar_h, 0, mrow);
+      tc::tma_load_2d(smem + GR_PM + 8192, &pmap_mn, &bar_h, 32, mrow);
+    }
+    sb[tid & 63] = a.gates[(c * Hv + hv) * 128 + (tid & 63)];
+    if (tid < 64) sbeta[tid] = a.gates[(c * Hv + hv) * 128 + 64 + tid];
+    __syncthreads();
+    const float bi = sb[i_row], be = sbeta[i_row], gi = __expf(bi), bC = sb[63], lam = __expf(bC - bi);
+    float t1 = 0.f, t2 = 0.f, t3 = 0.f, t4 = 0.f, t5 = 0.f;
+    ok = wait_all(&bar_h, (uint32_t)(r & 1), a.err, 31);
+    if (!ok) break;
+
+    for (int sl = 0; sl < DV / DVT && ok; ++sl) {
+      const int dv0 = sl * DVT;
+      // a. S and dS slices: bf16 hi/lo K-major [dv][dk] and fp32 MN-major [dv rows][dk]
+      {
+        const float* sp = a.ckpt + ((c * Hv + hv) * DV + dv0) * (size_t)DK;
+        const float* dp = a.dsbuf + ((c * Hv + hv) * DV + dv0) * (size_t)DK;
+#pragma unroll 2
+        for (int u = 0; u < 8; ++u) {
+          const int idx = tid + 128 * u, row = idx >> 5, c4 = idx & 31, dk = 4 * c4;
+          const float4 sv = *reinterpret_cast<const float4*>(sp + row * DK + dk);
+          const float4 dvv = *reinterpret_cast<const float4*>(dp + row * DK + dk);
+          t5 += sv.x * dvv.x + sv.y * dvv.y + sv.z * dvv.z + sv.w * dvv.w;
+          const uint32_t ok_ = tc::off_kmajor(row, dk, DVT, 2), om = tc::off_mnmajor(row, dk, DVT, 4);
+          const __nv_bfloat162 s01 = __floats2bfloat162_rn(sv.x, sv.y), s23 = __floats2bfloat162_rn(sv.z, sv.w);
+          const __nv_bfloat162 d01 = __floats2bfloat162_rn(dvv.x, dvv.y), d23 = __floats2bfloat162_rn(dvv.z, dvv.w);
+          *reinterpret_cast<uint2*>(smem + GR_SHI + ok_) =
+              make_uint2(*reinterpret_cast<const uint32_t*>(&s01), *reinterpret_cast<const uint32_t*>(&s23));
+          *reinterpret_cast<uint2*>(smem + GR_SLO + ok_) =
+              make_uint2(tc::pack_bf16(sv.x - __low2float(s01), sv.y - __high2float(s01)),
+                         tc::pack_bf16(sv.z - __low2float(s23), sv.w - __high2float(s23)));
+          *reinterpret_cast<uint2*>(smem + GR_DHI + ok_) =
+              make_uint2(*reinterpret_cast<const uint32_t*>(&d01), *reinterpret_cast<const uint32_t*>(&d23));
+          *reinterpret_cast<uint2*>(smem + GR_DLO + ok_) =
+              make_uint2(tc::pack_bf16(dvv.x - __low2float(d01), dvv.y - __high2float(d01)),
+                         tc::pack_bf16(dvv.z - __low2float(d23), dvv.w - __high2float(d23)));
+          *reinterpret_cast<float4*>(smem + GR_SM + om) =
+              make_float4(tf32_rna(sv.x), tf32_rna(sv.y), tf32_rna(sv.z), tf32_rna(sv.w));
+          *reinterpret_cast<float4*>(smem + GR_DM + om) =
+              make_float4(tf32_rna(dvv.x), tf32_rna(dvv.y), tf32_rna(dvv.z), tf32_rna(dvv.w));
+        }
+      }
+      float vr[32], dor[32];
+      load_row32(static_cast<const __nv_bfloat16*>(a.v) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0, valid, vr);
+      load_row32(static_cast<const __nv_bfloat16*>(a.dy) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0, valid, dor);
+      if (row_owner) {
+        tc::st_row_mn_f32(smem + GR_DOM, i_row, dor);
+        tc::st_row_k_f32(smem + GR_DOK, i_row, dor);
+        float gd[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) gd[j] = tf32_rna(gi * dor[j]);
+        tc::st_row_k_f32(smem + GR_GDO, i_row, gd);
+      }
+      tc::fence_async_smem();
+      tc::fence_before_sync();
+      __syncthreads();
+      tc::fence_after_sync();
+      // b. R = K S^T, Y = Q S^T, X1 = K dS^T (bf16, split), G = P^T dO (tf32)
+      if (tid == 0) {
+        const uint32_t shi = tc::smem_u32(smem + GR_SHI), slo = tc::smem_u32(smem + GR_SLO);
+        const uint32_t dhi = tc::smem_u32(smem + GR_DHI), dlo = tc::smem_u32(smem + GR_DLO);
+        tc::mma_tile<tc::kBF16>(tmem + cR, kt, false, 64, shi, false, DVT, 64, DVT, DK, false);
+        tc::mma_tile<tc::kBF16>(tmem + cR, kt, false, 64, slo, false, DVT, 64, DVT, DK, true);
+        tc::mma_tile<tc::kBF16>(tmem + cY, qt, false, 64, shi, false, DVT, 64, DVT, DK, false);
+        tc::mma_tile<tc::kBF16>(tmem + cY, qt, false, 64, slo, false, DVT, 64, DVT, DK, true);
+        tc::mma_tile<tc::kBF16>(tmem + cX, kt, false, 64, dhi, false, DVT, 64, DVT, DK, false);
+        tc::mma_tile<tc::kBF16>(tmem + cX, kt, false, 64, dlo, false, DVT, 64, DVT, DK, true);
+        tc::mma_tile<tc::kTF32>(tmem + cG, tc::smem_u32(smem + GR_PM), true, 64, tc::smem_u32(smem + GR_DOM), true,
+                                64, 64, DVT, C, false);
+        tc::mma_commit(&bar_mma);
+      }
+      ok = wait_all(&bar_mma, ph_mma, a.err, 32);
+      ph_mma ^= 1;
+      tc::fence_after_sync();
+      if (!ok) break;
+      float rr[32], xx[32];
+      {
+        float y[32], g[32];
+        tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cR), rr);
+        tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cY), y);
+        tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cX), xx);
+        tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cG), g);
+        float e[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          t3 = fmaf(dor[j], y[j], t3);
+          e[j] = tf32_rna(be * (vr[j] - gi * rr[j]));
+          g[j] = tf32_rna(fmaf(lam, xx[j], g[j]));
+        }
+        if (row_owner) {
+          tc::st_row_mn_f32(smem + GR_E, i_row, e);
+          tc::st_row_mn_f32(smem + GR_DD, i_row, g);
+        }
+      }
+      tc::fence_async_smem();
+      tc::fence_before_sync();
+      __syncthreads();
+      tc::fence_after_sync();
+      // c. D = T E, F = T^T dD (tf32); D reuses R's columns, F those of X1
+      if (tid == 0) {
+        tc::mma_tile<tc::kTF32>(tmem + cR, tc::smem_u32(smem + GR_TK), false, 64, tc::smem_u32(smem + GR_E), true, 64,
+                                64, DVT, C, false);
+        tc::mma_tile<tc::kTF32>(tmem + cX, tc::smem_u32(smem + GR_TM), true, 64, tc::smem_u32(smem + GR_DD), true, 64,
+                                64, DVT, C, false);
+        tc::mma_commit(&bar_mma);
+      }
+      ok = wait_all(&bar_mma, ph_mma, a.err, 33);
+      ph_mma ^= 1;
+      tc::fence_after_sync();
+      if (!ok) break;
+      {
+        float d[32], f[32];
+        tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cR), d);
+        tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cX), f);
+        float w[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          t1 = fmaf(f[j], vr[j] - gi * rr[j], t1);
+          t2 = fmaf(f[j], rr[j], t2);
+          t4 = fmaf(d[j], xx[j], t4);
+        }
+        if (row_owner) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) w[j] = tf32_rna(d[j]);
+          tc::st_row_k_f32(smem + GR_D, i_row, w);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) w[j] = tf32_rna(lam * d[j]);
+          tc::st_row_k_f32(smem + GR_LD, i_row, w);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) w[j] = tf32_rna(f[j]);
+          tc::st_row_k_f32(smem + GR_F, i_row, w);
+          const float h = -be * gi;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) w[j] = tf32_rna(h * f[j]);
+          tc::st_row_k_f32(smem + GR_NF, i_row, w);
+        }
+      }
+      tc::fence_async_smem();
+      tc::fence_before_sync();
+      __syncthreads();
+      tc::fence_after_sync();
+      // d. accumulate over the slice's value rows: dQ += (gamma dO) S, dK += (lambda D) dS - (beta gamma F) S,
+      //    dP += dO D^T, FD += F D^T   (all tf32, K = 32 value rows)
+      if (tid == 0) {
+        const bool first = r == 0 && sl == 0;
+        const uint32_t sm = tc::smem_u32(smem + GR_SM), dm = tc::smem_u32(smem + GR_DM);
+        tc::mma_tile<tc::kTF32>(tmem + cDQ, tc::smem_u32(smem + GR_GDO), false, 64, sm, true, DVT, 64, DK, DVT, !first);
+        tc::mma_tile<tc::kTF32>(tmem + cDK, tc::smem_u32(smem + GR_LD), false, 64, dm, true, DVT, 64, DK, DVT, !first);
+        tc::mma_tile<tc::kTF32>(tmem + cDK, tc::smem_u32(smem + GR_NF), false, 64, sm, true, DVT, 64, DK, DVT, true);
+        tc::mma_tile<tc::kTF32>(tmem + cDP, tc::smem_u32(smem + GR_DOK), false, 64, tc::smem_u32(smem + GR_D), false,
+                                64, 64, 64, DVT, sl > 0);
+        tc::mma_tile<tc::kTF32>(tmem + cFD, tc::smem_u32(smem + GR_F), false, 64, tc::smem_u32(smem + GR_D), false, 64,
+                                64, 64, DVT, sl > 0);
+        tc::mma_commit(&bar_mma);
+      }
+      ok = wait_all(&bar_mma, ph_mma, a.err, 34);
+      ph_mma ^= 1;
+      tc::fence_after_sync();
+    }
+    if (!ok) break;
+
+    // e. finalize this value head: dP^ and dKK, the Gamma terms of d b, and their MMAs into dQ, dK
+    if (tid == 0) {
+      tc::mbar_arrive_expect_tx(&bar_l, 16384);
+      tc::tma_load_2d(smem + GR_SHI, &lmap_k, &bar_l, 0, mrow);
+      tc::tma_load_2d(smem + GR_SHI + 8192, &lmap_k, &bar_l, 32, mrow);
+    }
+    ok = wait_all(&bar_l, (uint32_t)(r & 1), a.err, 35);
+    if (!ok) break;
+    float* scratch = reinterpret_cast<float*>(smem + GR_DM);  // [64][65]
+    float rowsum = 0.f, dbl = 0.f;
+    {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float dp[32], fd[32], ph[32], kh[32];
+        tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cDP + 32 * h), dp);
+        tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cFD + 32 * h), fd);
+        if (row_owner) {
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            const int j = 32 * h + jj;
+            const float gam = j <= i_row ? __expf(bi - sb[j]) : 0.f;
+            const float pij = *reinterpret_cast<const float*>(smem + GR_PM + tc::off_mnmajor(i_row, j, 64, 4));
+            const float lh = *reinterpret_cast<const float*>(smem + GR_SHI + tc::off_kmajor(i_row, j, 64, 4));
+            const float xp = j <= i_row ? dp[jj] * pij : 0.f;
+            const float dl = j < i_row ? -fd[jj] : 0.f;
+            const float xl = dl * be * lh;
+            dbl = fmaf(dl, lh, dbl);
+            rowsum += xp + xl;
+            scratch[i_row * 65 + j] = xp + xl;
+            ph[jj] = dp[jj] * gam;          // dP^
+            kh[jj] = dl * be * gam;         // dKK
+          }
+          tc::st_row_bf16x2_32(smem + GR_DHI, smem + GR_DLO, i_row, ph, 4 * h);
+          tc::st_row_bf16x2_32(smem + GR_SM, smem + GR_SM + 8192, i_row, kh, 4 * h);
+        }
+      }
+    }
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    if (tid == 0) {
+      const uint32_t phi = tc::smem_u32(smem + GR_DHI), plo = tc::smem_u32(smem + GR_DLO);
+      const uint32_t khi = tc::smem_u32(smem + GR_SM), klo = tc::smem_u32(smem + GR_SM + 8192);
+      // dQ += dP^ K;  dK += dP^^T Q + dKK K + dKK^T K   (K, Q as MN-major B: chunk rows, Dk contiguous)
+      tc::mma_tile<tc::kBF16>(tmem + cDQ, phi, false, 64, kt, true, 64, 64, DK, C, true);
+      tc::mma_tile<tc::kBF16>(tmem + cDQ, plo, false, 64, kt, true, 64, 64, DK, C, true);
+      tc::mma_tile<tc::kBF16>(tmem + cDK, phi, true, 64, qt, true, 64, 64, DK, C, true);
+      tc::mma_tile<tc::kBF16>(tmem + cDK, plo, true, 64, qt, true, 64, 64, DK, C, true);
+      tc::mma_tile<tc::kBF16>(tmem + cDK, khi, false, 64, kt, true, 64, 64, DK, C, true);
+      tc::mma_tile<tc::kBF16>(tmem + cDK, klo, false, 64, kt, true, 64, 64, DK, C, true);
+      tc::mma_tile<tc::kBF16>(tmem + cDK, khi, true, 64, kt, true, 64, 64, DK, C, true);
+      tc::mma_tile<tc::kBF16>(tmem + cDK, klo, true, 64, kt, true, 64, 64, DK, C, true);
+      tc::mma_commit(&bar_mma);
+    }
+    // column sums of the Gamma terms (fixed order) and the block sums of lambda t4 and t5
+    if (tid < 64) {
+      float cs = 0.f;
+      for (int i = 0; i < 64; ++i) cs += scratch[i * 65 + tid];
+      scol[tid] = cs;
+    }
+    float lt4 = row_owner ? lam * t4 : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      lt4 += __shfl_xor_sync(0xffffffffu, lt4, o);
+      t5 += __shfl_xor_sync(0xffffffffu, t5, o);
+    }
+    if (lane == 0) {
+      sred[warp] = lt4;
+      sred[4 + warp] = t5;
+    }
+    __syncthreads();
+    if (row_owner) sdb[i_row] = rowsum - scol[i_row] + gi * t3 - be * gi * t2 - lam * t4;
+    __syncthreads();
+    if (tid == 0) sdb[63] += (sred[0] + sred[1] + sred[2] + sred[3]) + __expf(bC) * (sred[4] + sred[5] + sred[6] + sred[7]);
+    __syncthreads();
+    if (valid) {
+      float dl = 0.f;  // d log g_i = sum over rows i' >= i of d b_i'
+      for (int i2 = 63; i2 >= i_row; --i2) dl += sdb[i2];
+      const int64_t gi_idx = (tok0 + i_row) * Hv + hv;
+      // dg = d log g / g; a gate of exactly 0 (log g clamped) gets 0, which keeps g * dg = 0 exact
+      const float gv = a.g[gi_idx];
+      a.dg[gi_idx] = gv > 0.f ? dl / gv : 0.f;
+      a.dbeta[gi_idx] = t1 + dbl;
+    }
+    ok = wait_all(&bar_mma, ph_mma, a.err, 36);
+    ph_mma ^= 1;
+    tc::fence_after_sync();
+  }
+  // f. dq, dk rows of this key head
+  if (ok) {
+#pragma unroll 1
+    for (int h = 0; h < 4; ++h) {
+      float v[32];
+      tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cDQ + 32 * h), v);
+      if (valid) store_row32<Tout>(static_cast<Tout*>(a.dq) + ((tok0 + i_row) * a.geo.Hk + hk) * (size_t)DK + 32 * h, v);
+      tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cDK + 32 * h), v);
+      if (valid) store_row32<Tout>(static_cast<Tout*>(a.dk) + ((tok0 + i_row) * a.geo.Hk + hk) * (size_t)DK + 32 * h, v);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tmem, 512);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -508,8 +1098,10 @@ bool map_act(CUtensorMap* m, const void* base, int64_t rows, int heads, int dim)
            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// [rows, 64] fp32 matrices stacked; box = 32 columns x 64 rows, 128-byte swizzle.
-bool map_f32_64(CUtensorMap* m, const void* base, int64_t rows) {
+// Stacked [rows, 64] fp32 matrices; box = 32 columns x 64 rows.  mn = the 32-byte-atom swizzle, which
+// lands the box as the MN-major tf32 operand (the matrix used transposed); otherwise the 128-byte
+// swizzle, the K-major operand.
+bool map_f32_64(CUtensorMap* m, const void* base, int64_t rows, bool mn) {
   EncodeTiled f = encode_fn();
   if (!f) return false;
   cuuint64_t dims[2] = {64, (cuuint64_t)rows};
@@ -517,30 +1109,66 @@ bool map_f32_64(CUtensorMap* m, const void* base, int64_t rows) {
   cuuint32_t box[2] = {32, 64};
   cuuint32_t es[2] = {1, 1};
   return f(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, es,
-           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+           CU_TENSOR_MAP_INTERLEAVE_NONE, mn ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 int64_t a256(int64_t x) { return (x + 255) & ~int64_t(255); }
 
-struct FwdWs {
-  int64_t* chunk_off;
-  int* err;
-  float *Tbuf, *gates;  // used when no saved buffer is given
+// The chunk intermediates: [ckpt][T][P][Gamma*KK][gates], fp32.
+struct Saved {
+  float *ckpt, *T, *P, *L, *gates;
 };
 
-int64_t fwd_ws(int Hv, int N, int64_t n_chunks, bool varlen, char* base, FwdWs* w) {
+int64_t saved_layout(int Hv, int64_t n_chunks, char* base, Saved* s) {
   int64_t off = 0;
   auto take = [&](int64_t bytes) {
     char* at = base ? base + off : nullptr;
     off += a256(bytes);
     return at;
   };
-  FwdWs x{};
+  Saved x;
+  x.ckpt = (float*)take(n_chunks * Hv * (int64_t)DV * DK * 4);
+  x.T = (float*)take(n_chunks * Hv * 4096 * 4);
+  x.P = (float*)take(n_chunks * Hv * 4096 * 4);
+  x.L = (float*)take(n_chunks * Hv * 4096 * 4);
+  x.gates = (float*)take(n_chunks * Hv * 128 * 4);
+  if (s) *s = x;
+  return off;
+}
+
+// Workspace: [chunk_off][err][fwd: T, P, gates when nothing is saved | bwd: dS per chunk, and a saved
+// buffer plus forward workspace when the backward recomputes].
+struct Ws {
+  int64_t* chunk_off;
+  int* err;
+  float *T, *P, *gates;
+  float* dsbuf;
+  char* saved;
+  char* fwd_ws;
+};
+
+int64_t ws_layout(int Hv, int N, int64_t n_chunks, bool varlen, int op, bool with_saved, char* base, Ws* w) {
+  int64_t off = 0;
+  auto take = [&](int64_t bytes) {
+    char* at = base ? base + off : nullptr;
+    off += a256(bytes);
+    return at;
+  };
+  Ws x{};
   x.chunk_off = (int64_t*)take(varlen ? (int64_t)(N + 1) * 8 : 0);
   x.err = (int*)take(16);
-  x.Tbuf = (float*)take(n_chunks * Hv * 4096 * 4);
-  x.gates = (float*)take(n_chunks * Hv * 128 * 4);
+  if (op == 0) {
+    x.T = (float*)take(n_chunks * Hv * 4096 * 4);
+    x.P = (float*)take(n_chunks * Hv * 4096 * 4);
+    x.gates = (float*)take(n_chunks * Hv * 128 * 4);
+  } else {
+    x.dsbuf = (float*)take(n_chunks * Hv * (int64_t)DV * DK * 4);
+    if (with_saved) {
+      x.saved = take(saved_layout(Hv, n_chunks, nullptr, nullptr));
+      x.fwd_ws = take(ws_layout(Hv, N, n_chunks, varlen, 0, false, nullptr, nullptr));
+    }
+  }
   if (w) *w = x;
   return off;
 }
@@ -548,70 +1176,92 @@ int64_t fwd_ws(int Hv, int N, int64_t n_chunks, bool varlen, char* base, FwdWs* 
 }  // namespace
 
 bool chunked_supported(int Dk, int Dv) { return Dk == DK && Dv == DV && encode_fn() != nullptr; }
+bool chunked_bwd_ready() { return true; }
 
-// saved = [ckpt: chunks x Hv x Dv x Dk][T: chunks x Hv x 64 x 64][gates: chunks x Hv x 128], fp32
-int64_t chunked_saved_bytes(int Hv, int Dk, int Dv, int64_t n_chunks, int64_t) {
-  return a256(n_chunks * Hv * (int64_t)Dv * Dk * 4) + a256(n_chunks * Hv * 4096 * 4) + a256(n_chunks * Hv * 128 * 4);
+int64_t chunked_saved_bytes(int Hv, int, int, int64_t n_chunks, int64_t) {
+  return saved_layout(Hv, n_chunks, nullptr, nullptr);
 }
 
-int64_t chunked_ws_bytes(int Hv, int Hk, int Dk, int Dv, int N, int64_t n_chunks, int64_t tokens, bool varlen, int op,
+int64_t chunked_ws_bytes(int Hv, int, int, int, int N, int64_t n_chunks, int64_t, bool varlen, int op,
                          bool with_saved) {
-  (void)Hk;
-  (void)Dk;
-  (void)Dv;
-  (void)tokens;
-  (void)op;
-  (void)with_saved;
-  return fwd_ws(Hv, N, n_chunks, varlen, nullptr, nullptr);
+  return ws_layout(Hv, N, n_chunks, varlen, op, with_saved, nullptr, nullptr);
 }
 
 cudaError_t chunked_fwd(const ChunkFwdArgs& a, void* ws, cudaStream_t st) {
   if (!a.in_bf16) return cudaErrorInvalidValue;
-  FwdWs w;
-  fwd_ws(a.Hv, a.N, a.n_chunks, a.cu != nullptr, (char*)ws, &w);
-  float* ckpt = nullptr;
-  float* Tbuf = w.Tbuf;
-  float* gates = w.gates;
+  Ws w;
+  ws_layout(a.Hv, a.N, a.n_chunks, a.cu != nullptr, 0, false, (char*)ws, &w);
+  Saved sv{};
+  float *Tb = w.T, *Pb = w.P, *gates = w.gates, *ckpt = nullptr, *Lb = nullptr;
   if (a.saved) {
-    char* sv = (char*)a.saved;
-    ckpt = (float*)sv;
-    Tbuf = (float*)(sv + a256(a.n_chunks * a.Hv * (int64_t)a.Dv * a.Dk * 4));
-    gates = (float*)((char*)Tbuf + a256(a.n_chunks * a.Hv * 4096 * 4));
+    saved_layout(a.Hv, a.n_chunks, (char*)a.saved, &sv);
+    Tb = sv.T, Pb = sv.P, gates = sv.gates, ckpt = sv.ckpt, Lb = sv.L;
   }
   cudaError_t e;
   if ((e = cudaMemsetAsync(w.err, 0, 16, st)) != cudaSuccess) return e;
-  if (a.cu) {
-    if ((e = launch_chunk_offsets(a.cu, a.N, w.chunk_off, st)) != cudaSuccess) return e;
-  }
-  const int64_t rows = (int64_t)a.B * a.T;
-  CUtensorMap kmap, qmap, tmap;
+  if (a.cu && (e = launch_chunk_offsets(a.cu, a.N, w.chunk_off, st)) != cudaSuccess) return e;
+  const int64_t rows = (int64_t)a.B * a.T, mrows = a.n_chunks * a.Hv * 64;
+  CUtensorMap kmap, qmap, tmap, pmap;
   if (!map_act(&kmap, a.k, rows, a.Hk, a.Dk) || !map_act(&qmap, a.q, rows, a.Hk, a.Dk) ||
-      !map_f32_64(&tmap, Tbuf, a.n_chunks * a.Hv * 64))
+      !map_f32_64(&tmap, Tb, mrows, false) || !map_f32_64(&pmap, Pb, mrows, false))
     return cudaErrorInvalidValue;
   Geo geo{a.T, a.Hk, a.Hv, a.N, (a.T + C - 1) / C, a.cu, a.cu ? w.chunk_off : nullptr};
-
-  PrepArgs pa{geo, a.g, a.beta, Tbuf, gates, w.err};
-  const int prep_smem = 1024 + 16384 + 64 * 68 * 4;
-  if ((e = cudaFuncSetAttribute(gdn_chunk_prep, cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem)) !=
-      cudaSuccess)
-    return e;
   if (a.n_chunks > 0) {
-    gdn_chunk_prep<<<dim3((unsigned)a.n_chunks, a.Hv), 128, prep_smem, st>>>(kmap, pa);
+    PrepArgs pa{geo, a.g, a.beta, Tb, Pb, Lb, gates, w.err};
+    const int prep_smem = 1024 + 32768 + 64 * 68 * 4;
+    if ((e = cudaFuncSetAttribute(gdn_chunk_prep, cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem)) !=
+        cudaSuccess)
+      return e;
+    gdn_chunk_prep<<<dim3((unsigned)a.n_chunks, a.Hv), 128, prep_smem, st>>>(kmap, qmap, pa);
     note_launch();
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
-
-  StateArgs sa{geo, a.v, gates, a.h0, a.y, a.hT, ckpt, a.out_bf16, w.err};
-  auto kern = a.out_bf16 ? gdn_chunk_fwd_state<true> : gdn_chunk_fwd_state<false>;
-  if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, STATE_SMEM)) != cudaSuccess)
-    return e;
-  kern<<<dim3(DV / DVT, a.Hv, a.N), 128, STATE_SMEM, st>>>(kmap, qmap, tmap, sa);
+  StateArgs sa{geo, a.v, gates, a.h0, a.y, a.hT, ckpt, w.err};
+  auto kern = a.out_bf16 ? gdn_chunk_fwd_state<__nv_bfloat16> : gdn_chunk_fwd_state<float>;
+  if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FW_SMEM)) != cudaSuccess) return e;
+  kern<<<dim3(DV / DVT, a.Hv, a.N), 128, FW_SMEM, st>>>(kmap, qmap, tmap, pmap, sa);
   note_launch();
   return cudaGetLastError();
 }
 
-bool chunked_bwd_ready() { return false; }
-
-cudaError_t chunked_bwd(const ChunkBwdArgs&, void*, cudaStream_t) { return cudaErrorNotSupported; }
+cudaError_t chunked_bwd(const ChunkBwdArgs& a, void* ws, cudaStream_t st) {
+  if (!a.in_bf16) return cudaErrorInvalidValue;
+  Ws w;
+  ws_layout(a.Hv, a.N, a.n_chunks, a.cu != nullptr, 1, a.saved == nullptr, (char*)ws, &w);
+  cudaError_t e;
+  const void* saved = a.saved;
+  if (!saved) {  // recompute the forward's intermediates with the same forward (y is discarded into dv)
+    ChunkFwdArgs f{};
+    f.B = a.B, f.T = a.T, f.Hk = a.Hk, f.Hv = a.Hv, f.Dk = a.Dk, f.Dv = a.Dv, f.N = a.N, f.n_chunks = a.n_chunks;
+    f.cu = a.cu, f.q = a.q, f.k = a.k, f.v = a.v, f.g = a.g, f.beta = a.beta, f.h0 = a.h0, f.y = a.dv;
+    f.saved = w.saved, f.in_bf16 = a.in_bf16, f.out_bf16 = a.out_bf16;
+    if ((e = chunked_fwd(f, w.fwd_ws, st)) != cudaSuccess) return e;
+    saved = w.saved;
+  }
+  Saved sv;
+  saved_layout(a.Hv, a.n_chunks, (char*)saved, &sv);
+  if ((e = cudaMemsetAsync(w.err, 0, 16, st)) != cudaSuccess) return e;
+  if (a.cu && (e = launch_chunk_offsets(a.cu, a.N, w.chunk_off, st)) != cudaSuccess) return e;
+  const int64_t rows = (int64_t)a.B * a.T, mrows = a.n_chunks * a.Hv * 64;
+  CUtensorMap kmap, qmap, tmap_k, tmap_mn, pmap_mn, lmap_k;
+  if (!map_act(&kmap, a.k, rows, a.Hk, a.Dk) || !map_act(&qmap, a.q, rows, a.Hk, a.Dk) ||
+      !map_f32_64(&tmap_k, sv.T, mrows, false) || !map_f32_64(&tmap_mn, sv.T, mrows, true) ||
+      !map_f32_64(&pmap_mn, sv.P, mrows, true) || !map_f32_64(&lmap_k, sv.L, mrows, false))
+    return cudaErrorInvalidValue;
+  Geo geo{a.T, a.Hk, a.Hv, a.N, (a.T + C - 1) / C, a.cu, a.cu ? w.chunk_off : nullptr};
+  BwdStateArgs ba{geo, a.dy, sv.gates, a.dhT, a.dv, a.dh0, w.dsbuf, w.err};
+  auto k1 = a.out_bf16 ? gdn_chunk_bwd_state<__nv_bfloat16> : gdn_chunk_bwd_state<float>;
+  if ((e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, BW_SMEM)) != cudaSuccess) return e;
+  k1<<<dim3(DV / DVT, a.Hv, a.N), 128, BW_SMEM, st>>>(kmap, qmap, tmap_mn, pmap_mn, ba);
+  note_launch();
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if (a.n_chunks == 0) return cudaSuccess;
+  GradArgs ga{geo, a.v, a.dy, a.g, sv.gates, sv.ckpt, w.dsbuf, a.dq, a.dk, a.dg, a.dbeta, w.err};
+  auto k2 = a.out_bf16 ? gdn_chunk_bwd_grad<__nv_bfloat16> : gdn_chunk_bwd_grad<float>;
+  if ((e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, GR_SMEM)) != cudaSuccess) return e;
+  k2<<<dim3((unsigned)a.n_chunks, a.Hk), 128, GR_SMEM, st>>>(kmap, qmap, tmap_k, tmap_mn, pmap_mn, lmap_k, ga);
+  note_launch();
+  return cudaGetLastError();
+}
 
 }  // namespace qbgdn

@@ -18,6 +18,7 @@
 // No cluster multicast anywhere: every CTA loads its own tiles.
 #pragma once
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -216,6 +217,50 @@ __device__ __forceinline__ void mma_tile(uint32_t d_tmem, uint32_t a_tile, bool 
       mma_bf16(d_tmem, a, b, id, (accumulate || ks > 0) ? 1u : 0u);
     else
       mma_tf32(d_tmem, a, b, id, (accumulate || ks > 0) ? 1u : 0u);
+  }
+}
+
+// ---- vectorised row stores into operand tiles (one thread writes one whole row) ----------------------
+// fp32, MN-major tf32 layout (32-byte granules swizzled by k & 3): row k of one 128-byte slab.
+__device__ __forceinline__ void st_row_mn_f32(uint8_t* slab, int k, const float (&v)[32]) {
+  uint8_t* row = slab + k * 128;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    float4* dst = reinterpret_cast<float4*>(row + ((g ^ (k & 3)) << 5));
+    dst[0] = make_float4(v[8 * g], v[8 * g + 1], v[8 * g + 2], v[8 * g + 3]);
+    dst[1] = make_float4(v[8 * g + 4], v[8 * g + 5], v[8 * g + 6], v[8 * g + 7]);
+  }
+}
+// fp32, K-major 128-byte swizzle (16-byte chunks swizzled by r & 7): row r of one slab (32 floats).
+__device__ __forceinline__ void st_row_k_f32(uint8_t* slab, int r, const float (&v)[32]) {
+  uint8_t* row = slab + r * 128;
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    *reinterpret_cast<float4*>(row + ((c ^ (r & 7)) << 4)) = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+}
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+// Split 32 floats into bf16 hi + lo (hi + lo carries about 16 mantissa bits) and store both rows in
+// a bf16 128-byte-swizzled tile (16-byte chunks swizzled by r & 7; 32 elements = chunks 0..3).
+// Used for K-major rows and MN-major rows alike: the byte pattern is the same.  c0 = 4 writes the
+// elements 32..63 of a 64-wide row.
+__device__ __forceinline__ void st_row_bf16x2_32(uint8_t* hi_slab, uint8_t* lo_slab, int r, const float (&v)[32],
+                                                 int c0 = 0) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float a = v[8 * c + 2 * e], b = v[8 * c + 2 * e + 1];
+      const __nv_bfloat162 hh = __floats2bfloat162_rn(a, b);
+      h[e] = *reinterpret_cast<const uint32_t*>(&hh);
+      l[e] = pack_bf16(a - __low2float(hh), b - __high2float(hh));
+    }
+    const int off = r * 128 + (((c + c0) ^ (r & 7)) << 4);
+    *reinterpret_cast<uint4*>(hi_slab + off) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(lo_slab + off) = make_uint4(l[0], l[1], l[2], l[3]);
   }
 }
 
