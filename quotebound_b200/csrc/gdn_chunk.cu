@@ -127,6 +127,28 @@ __device__ __forceinline__ void load_row32(const __nv_bfloat16* p, bool valid, f
   }
 }
 
+// The same row issued early as raw 16-byte loads and converted when it is needed, so the load's
+// latency overlaps the work in between.
+struct Row32 {
+  uint4 w[4];
+};
+__device__ __forceinline__ void ldg_row32(const __nv_bfloat16* p, bool valid, Row32& r) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) r.w[q] = valid ? __ldg(reinterpret_cast<const uint4*>(p) + q) : make_uint4(0, 0, 0, 0);
+}
+__device__ __forceinline__ void cvt_row32(const Row32& r, float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t w[4] = {r.w[q].x, r.w[q].y, r.w[q].z, r.w[q].w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[e]);
+      v[8 * q + 2 * e] = __low2float(h);
+      v[8 * q + 2 * e + 1] = __high2float(h);
+    }
+  }
+}
+
 template <typename Tout>
 __device__ __forceinline__ void store_row32(Tout* p, const float (&v)[32]);
 template <>
@@ -357,20 +379,33 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_fwd_state(const __grid_const
     tc::tma_load_2d(smem + FW_P + buf * 16384 + 8192, &pmap, &bar_tma[buf], 32, mrow);
   };
 
+  const int i_row = 16 * warp + (lane & 15);  // row of the M = 64 accumulators this thread reads
+  const bool row_owner = lane < 16;
+  const __nv_bfloat16* vbase = static_cast<const __nv_bfloat16*>(a.v) + (size_t)hv * DV + dv0;
+  Row32 vraw;  // this thread's value row of the current chunk, loaded one chunk ahead
   if (nchunks > 0) {
     if (tid == 0) issue_loads(0, 0);
     sg[0][tid] = a.gates[(c_first * Hv + hv) * 128 + tid];
+    ldg_row32(vbase + (seq0 + i_row) * Hv * (size_t)DV, row_owner && i_row < min((int64_t)C, seq1 - seq0), vraw);
   }
   uint32_t ph = 0;
   bool ok = true;
-  const int i_row = 16 * warp + (lane & 15);  // row of the M = 64 accumulators this thread reads
-  const bool row_owner = lane < 16;
 
   for (int64_t jc = 0; jc < nchunks && ok; ++jc) {
     const int buf = (int)(jc & 1);
     const int64_t cg = c_first + jc;
     const int64_t tok0 = seq0 + jc * C;
     const int L = (int)min((int64_t)C, seq1 - tok0);
+    // the next chunk's value row and gates, consumed next iteration
+    Row32 vnext;
+    float gnext = 0.f;
+    {
+      const bool more = jc + 1 < nchunks;
+      const int64_t tn = tok0 + C;
+      ldg_row32(vbase + (tn + i_row) * Hv * (size_t)DV, more && row_owner && i_row < min((int64_t)C, seq1 - tn),
+                vnext);
+      if (more) gnext = __ldg(a.gates + ((cg + 1) * Hv + hv) * 128 + tid);
+    }
 
     // 1. the chunk-start state: saved for the backward, split into the bf16 hi/lo operand (row tid)
     if (a.ckpt) {
@@ -381,18 +416,14 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_fwd_state(const __grid_const
     tc::st_row_bf16x2_32(smem + FW_SHI, smem + FW_SLO, tid, s);
     // 2. this thread's value row (rows past the end read as zero)
     float vr[DVT];
-    load_row32(static_cast<const __nv_bfloat16*>(a.v) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0,
-               row_owner && i_row < L, vr);
+    cvt_row32(vraw, vr);
     // 3. tiles of this chunk
     tc::fence_async_smem();
     tc::fence_before_sync();
     ok = wait_all(&bar_tma[buf], (uint32_t)((jc >> 1) & 1), a.err, 10);
     tc::fence_after_sync();
     if (!ok) break;
-    if (jc + 1 < nchunks) {  // prefetch the next chunk (its buffer's last readers finished)
-      if (tid == 0) issue_loads(jc + 1, buf ^ 1);
-      sg[buf ^ 1][tid] = a.gates[((cg + 1) * Hv + hv) * 128 + tid];
-    }
+    if (jc + 1 < nchunks && tid == 0) issue_loads(jc + 1, buf ^ 1);  // the next chunk's tiles
     const uint32_t kt = tc::smem_u32(smem + FW_K + buf * 16384);
     const uint32_t qt = tc::smem_u32(smem + FW_Q + buf * 16384);
     // 4. R = K S^T, Y = Q S^T (S split hi + lo, MN-major: dk rows)
@@ -479,6 +510,10 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_fwd_state(const __grid_const
         store_row32<Tout>(static_cast<Tout*>(a.y) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0, u);
       }
     }
+    // the other gate buffer was last read before this chunk's first barrier; the next reads follow
+    // the next chunk's first barrier
+    sg[buf ^ 1][tid] = gnext;
+    vraw = vnext;
     tc::fence_before_sync();
   }
   if (ok && a.hT) {
@@ -574,14 +609,18 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_bwd_state(const __grid_const
     tc::tma_load_2d(smem + BW_P + buf * 16384 + 8192, &pmap_mn, &bar_tma[buf], 32, mrow);
   };
 
+  const int i_row = 16 * warp + (lane & 15);
+  const bool row_owner = lane < 16;
+  const __nv_bfloat16* dbase = static_cast<const __nv_bfloat16*>(a.dy) + (size_t)hv * DV + dv0;
+  Row32 draw;  // this thread's dO row of the current chunk, loaded one chunk ahead
   if (nchunks > 0) {
     if (tid == 0) issue_loads(nchunks - 1, 0);
     sg[0][tid] = a.gates[((c_first + nchunks - 1) * Hv + hv) * 128 + tid];
+    const int64_t tl = seq0 + (nchunks - 1) * C;
+    ldg_row32(dbase + (tl + i_row) * Hv * (size_t)DV, row_owner && i_row < min((int64_t)C, seq1 - tl), draw);
   }
   uint32_t ph = 0;
   bool ok = true;
-  const int i_row = 16 * warp + (lane & 15);
-  const bool row_owner = lane < 16;
 
   for (int64_t it = 0; it < nchunks && ok; ++it) {
     const int64_t jc = nchunks - 1 - it;
@@ -589,6 +628,14 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_bwd_state(const __grid_const
     const int64_t cg = c_first + jc;
     const int64_t tok0 = seq0 + jc * C;
     const int L = (int)min((int64_t)C, seq1 - tok0);
+    Row32 dnext;  // the previous chunk's dO row and gates, consumed next iteration
+    float gnext = 0.f;
+    {
+      const bool more = jc > 0;
+      const int64_t tp = tok0 - C;
+      ldg_row32(dbase + (tp + i_row) * Hv * (size_t)DV, more && row_owner, dnext);
+      if (more) gnext = __ldg(a.gates + ((cg - 1) * Hv + hv) * 128 + tid);
+    }
 
     // 1. dS of this chunk's end: saved for the gradient kernel, split into the hi/lo operand (row tid)
     {
@@ -602,8 +649,7 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_bwd_state(const __grid_const
     const float bi = gb[i_row], be = gb[64 + i_row], gi = __expf(bi), bC = gb[63];
     if (row_owner) {
       float d[32];
-      load_row32(static_cast<const __nv_bfloat16*>(a.dy) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0,
-                 i_row < L, d);
+      cvt_row32(draw, d);
       tc::st_row_mn_f32(smem + BW_DO, i_row, d);
 #pragma unroll
       for (int j = 0; j < DVT; ++j) d[j] *= gi;
@@ -614,10 +660,7 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_bwd_state(const __grid_const
     ok = wait_all(&bar_tma[buf], (uint32_t)((it >> 1) & 1), a.err, 20);
     tc::fence_after_sync();
     if (!ok) break;
-    if (jc > 0) {  // prefetch the previous chunk
-      if (tid == 0) issue_loads(jc - 1, buf ^ 1);
-      sg[buf ^ 1][tid] = a.gates[((cg - 1) * Hv + hv) * 128 + tid];
-    }
+    if (jc > 0 && tid == 0) issue_loads(jc - 1, buf ^ 1);  // the previous chunk's tiles
     const uint32_t kt = tc::smem_u32(smem + BW_K + buf * 16384);
     const uint32_t qt = tc::smem_u32(smem + BW_Q + buf * 16384);
     // 3. X1 = K dS^T (dS split hi + lo), G = P^T dO
@@ -694,6 +737,8 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_bwd_state(const __grid_const
 #pragma unroll
       for (int j = 0; j < DVT; ++j) ds[j] = fmaf(gC, ds[j], u[j]);
     }
+    sg[buf ^ 1][tid] = gnext;
+    draw = dnext;
     tc::fence_before_sync();
   }
   if (ok && a.dh0) {
@@ -748,11 +793,13 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_bwd_grad(const __grid_consta
                                                              const __grid_constant__ CUtensorMap tmap_k,
                                                              const __grid_constant__ CUtensorMap tmap_mn,
                                                              const __grid_constant__ CUtensorMap pmap_mn,
-                                                             const __grid_constant__ CUtensorMap lmap_k, GradArgs a) {
+                                                             const __grid_constant__ CUtensorMap lmap_k,
+                                                             const __grid_constant__ CUtensorMap smap_mn,
+                                                             const __grid_constant__ CUtensorMap dmap_mn, GradArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ float sb[64], sbeta[64], sdb[64], scol[64], sred[8];
-  __shared__ uint64_t bar_kq, bar_h, bar_l, bar_mma;
+  __shared__ uint64_t bar_kq, bar_h, bar_l, bar_s, bar_mma;
   __shared__ uint32_t tmem_slot;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -772,6 +819,7 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_bwd_grad(const __grid_consta
     tc::mbar_init(&bar_kq, 1);
     tc::mbar_init(&bar_h, 1);
     tc::mbar_init(&bar_l, 1);
+    tc::mbar_init(&bar_s, 1);
     tc::mbar_init(&bar_mma, 1);
     tc::fence_mbar_init();
   }
@@ -812,17 +860,32 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_bwd_grad(const __grid_consta
 
     for (int sl = 0; sl < DV / DVT && ok; ++sl) {
       const int dv0 = sl * DVT;
-      // a. S and dS slices: bf16 hi/lo K-major [dv][dk] and fp32 MN-major [dv rows][dk]
+      // a. S and dS slices by TMA straight into the fp32 MN-major operand layout [dv rows][dk]; the
+      //    value and dO rows issued meanwhile
+      if (tid == 0) {
+        const int srow = (int)((c * Hv + hv) * DV + dv0);
+        tc::mbar_arrive_expect_tx(&bar_s, 32768);
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          tc::tma_load_2d(smem + GR_SM + 4096 * b, &smap_mn, &bar_s, 32 * b, srow);
+          tc::tma_load_2d(smem + GR_DM + 4096 * b, &dmap_mn, &bar_s, 32 * b, srow);
+        }
+      }
+      Row32 vraw, draw;
+      ldg_row32(static_cast<const __nv_bfloat16*>(a.v) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0, valid, vraw);
+      ldg_row32(static_cast<const __nv_bfloat16*>(a.dy) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0, valid, draw);
+      ok = wait_all(&bar_s, (uint32_t)((r * (DV / DVT) + sl) & 1), a.err, 37);
+      if (!ok) break;
+      // the bf16 hi/lo K-major copies [dv][dk] for the products with K and Q; the fp32 tiles rounded
+      // to tf32 in place
       {
-        const float* sp = a.ckpt + ((c * Hv + hv) * DV + dv0) * (size_t)DK;
-        const float* dp = a.dsbuf + ((c * Hv + hv) * DV + dv0) * (size_t)DK;
-#pragma unroll 2
+#pragma unroll 4
         for (int u = 0; u < 8; ++u) {
           const int idx = tid + 128 * u, row = idx >> 5, c4 = idx & 31, dk = 4 * c4;
-          const float4 sv = *reinterpret_cast<const float4*>(sp + row * DK + dk);
-          const float4 dvv = *reinterpret_cast<const float4*>(dp + row * DK + dk);
-          t5 += sv.x * dvv.x + sv.y * dvv.y + sv.z * dvv.z + sv.w * dvv.w;
           const uint32_t ok_ = tc::off_kmajor(row, dk, DVT, 2), om = tc::off_mnmajor(row, dk, DVT, 4);
+          const float4 sv = *reinterpret_cast<const float4*>(smem + GR_SM + om);
+          const float4 dvv = *reinterpret_cast<const float4*>(smem + GR_DM + om);
+          t5 += sv.x * dvv.x + sv.y * dvv.y + sv.z * dvv.z + sv.w * dvv.w;
           const __nv_bfloat162 s01 = __floats2bfloat162_rn(sv.x, sv.y), s23 = __floats2bfloat162_rn(sv.z, sv.w);
           const __nv_bfloat162 d01 = __floats2bfloat162_rn(dvv.x, dvv.y), d23 = __floats2bfloat162_rn(dvv.z, dvv.w);
           *reinterpret_cast<uint2*>(smem + GR_SHI + ok_) =
@@ -842,8 +905,8 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_bwd_grad(const __grid_consta
         }
       }
       float vr[32], dor[32];
-      load_row32(static_cast<const __nv_bfloat16*>(a.v) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0, valid, vr);
-      load_row32(static_cast<const __nv_bfloat16*>(a.dy) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0, valid, dor);
+      cvt_row32(vraw, vr);
+      cvt_row32(draw, dor);
       if (row_owner) {
         tc::st_row_mn_f32(smem + GR_DOM, i_row, dor);
         tc::st_row_k_f32(smem + GR_DOK, i_row, dor);
@@ -1113,6 +1176,20 @@ bool map_f32_64(CUtensorMap* m, const void* base, int64_t rows, bool mn) {
            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// State rows [rows, 128] fp32 (a chunk-state buffer); box = 32 columns x 32 rows in the 32-byte-atom
+// swizzle: four boxes make the MN-major tf32 operand of a 32-row slice.
+bool map_state_mn(CUtensorMap* m, const void* base, int64_t rows) {
+  EncodeTiled f = encode_fn();
+  if (!f) return false;
+  cuuint64_t dims[2] = {128, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {128 * 4};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t es[2] = {1, 1};
+  return f(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, es,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int64_t a256(int64_t x) { return (x + 255) & ~int64_t(255); }
 
 // The chunk intermediates: [ckpt][T][P][Gamma*KK][gates], fp32.
@@ -1256,10 +1333,15 @@ cudaError_t chunked_bwd(const ChunkBwdArgs& a, void* ws, cudaStream_t st) {
   note_launch();
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   if (a.n_chunks == 0) return cudaSuccess;
+  CUtensorMap smap_mn, dmap_mn;
+  if (!map_state_mn(&smap_mn, sv.ckpt, a.n_chunks * a.Hv * (int64_t)DV) ||
+      !map_state_mn(&dmap_mn, w.dsbuf, a.n_chunks * a.Hv * (int64_t)DV))
+    return cudaErrorInvalidValue;
   GradArgs ga{geo, a.v, a.dy, a.g, sv.gates, sv.ckpt, w.dsbuf, a.dq, a.dk, a.dg, a.dbeta, w.err};
   auto k2 = a.out_bf16 ? gdn_chunk_bwd_grad<__nv_bfloat16> : gdn_chunk_bwd_grad<float>;
   if ((e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, GR_SMEM)) != cudaSuccess) return e;
-  k2<<<dim3((unsigned)a.n_chunks, a.Hk), 128, GR_SMEM, st>>>(kmap, qmap, tmap_k, tmap_mn, pmap_mn, lmap_k, ga);
+  k2<<<dim3((unsigned)a.n_chunks, a.Hk), 128, GR_SMEM, st>>>(kmap, qmap, tmap_k, tmap_mn, pmap_mn, lmap_k, smap_mn,
+                                                             dmap_mn, ga);
   note_launch();
   return cudaGetLastError();
 }

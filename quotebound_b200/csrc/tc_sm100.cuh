@@ -15,7 +15,7 @@
 //    or 8 (tf32) rows.
 //
 // Every slab starts on a 1024-byte boundary, so the hardware's address-based swizzle matches.
-// No cluster multicast anywhere: every CTA loads its own tiles.
+// Every CTA loads its own tiles from its own GPU's memory; no load is shared across a cluster.
 #pragma once
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -67,7 +67,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 }
 
 // ---- TMA ----------------------------------------------------------------------------------------
-// 3-D tiled load (no multicast) into shared memory, completing `bytes` on the mbarrier.
+// 3-D tiled load into this CTA's shared memory, completing `bytes` on the mbarrier.
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
                                             int c2) {
   asm volatile(
