@@ -44,7 +44,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c1", choices=["c1", "c2"])
+    ap.add_argument("--workload", default="c1", choices=["c1", "c2", "c3", "c4"],
+                    help="c1 4B layer (default), c2 batched split over GPUs, c3 varlen (one GPU), c4 verify (one GPU)")
     ap.add_argument("--algo", type=int, default=0, help="0 auto, 1 row-parallel, 2 chunked")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -127,9 +128,10 @@ class ClockSampler:
 class Work:
     """One rank's share of the workload, resident in HBM."""
 
-    def __init__(self, B, T, Hk, Hv, Dk, Dv, seed, device, algo):
+    def __init__(self, B, T, Hk, Hv, Dk, Dv, seed, device, algo, cu_seqlens=None):
         from quotebound_b200 import synthetic
         p = synthetic.make(B, T, Hk, Hv, Dk, Dv, seed=seed, device=device)
+        self.cu = cu_seqlens
         gen = torch.Generator(device=device).manual_seed(seed + 7)
         # raw (pre-norm) q, k: any positive rescale of the normalised vectors gives the same qn, kn
         self.q = (p.q * math.sqrt(Dk) * torch.rand(B, T, Hk, 1, generator=gen, device=device).add_(0.5)).to(torch.bfloat16)
@@ -158,10 +160,11 @@ class Work:
 
         qn, kn, g, beta = op("gate_fwd", lambda: gate.gate_fwd(self.q, self.k, self.a, self.b, self.A_log,
                                                                  self.dt_bias))
+        cu = getattr(self, "cu", None)
         y, hT, saved = op("gdn_fwd", lambda: deltanet.gated_delta_fwd(qn, kn, self.v, g, beta, None, save=True,
-                                                                       algo=self.algo))
+                                                                       algo=self.algo, cu_seqlens=cu))
         dqn, dkn, dv, dg, dbeta, _ = op("gdn_bwd", lambda: deltanet.gated_delta_bwd(
-            qn, kn, self.v, g, beta, None, self.dy, None, saved=saved, algo=self.algo))
+            qn, kn, self.v, g, beta, None, self.dy, None, saved=saved, algo=self.algo, cu_seqlens=cu))
         dq, dk, da, db, dA, ddt = op("gate_bwd", lambda: gate.gate_bwd(self.q, self.k, self.a, self.b, self.A_log,
                                                                         self.dt_bias, dqn, dkn, dg, dbeta))
         return dq, dk, dv, da, db, dA, ddt
@@ -437,9 +440,107 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ---- one-GPU workloads: config 3 (varlen training pass) and config 4 (exact speculative verify) ----
+def _timed(step, steps, warmup, dev):
+    """Mean device ms of `step(events)` over `steps` (L2 flushed before each, outside the events)."""
+    from quotebound_b200 import _lib
+    flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    for _ in range(warmup):
+        step(None)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(dev.index)
+    sampler.start()
+    time.sleep(0.3)
+    n0 = _lib.launches()
+    evs, ops = [], []
+    for _ in range(steps):
+        flush.zero_()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        step(ops)
+        e1.record()
+        evs.append((e0, e1))
+    torch.cuda.synchronize()
+    launches = _lib.launches() - n0
+    clocks = sampler.stop()
+    ms = sum(a.elapsed_time(b) for a, b in evs) / steps
+    per_op = {}
+    for name, a, b in ops:
+        per_op.setdefault(name, []).append(a.elapsed_time(b))
+    return ms, {k: sum(v) / len(v) for k, v in per_op.items()}, launches, clocks
+
+
+def run_single(args):
+    world, rank, local = rank_info()
+    if world > 1:
+        raise SystemExit("workloads c3 and c4 run on one GPU")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from quotebound_b200 import _lib, build, exact, synthetic
+    build.ensure()
+    _lib.load()
+    hbm, tf, src = load_peaks()
+    if args.workload == "c3":
+        lengths = synthetic.varlen_lengths(16, 128, 4096, seed=0)
+        cu = synthetic.cu_from_lengths(lengths)
+        T = cu[-1]
+        W = Work(1, T, 16, 32, 128, 128, 0, dev, args.algo, cu_seqlens=cu)
+        ms, per_op, launches, clocks = _timed(W.step, args.steps, args.warmup, dev)
+        fpt = fwd_flops_per_token_head(128, 128)
+        dom_ms = per_op["gdn_bwd"]
+        ach = 2 * fpt * T * 32 / (dom_ms / 1e3) / 1e12
+        line = {"metric": "GDN fwd+bwd tokens/s, varlen packed batch", "value": round(T / (ms / 1e3), 1),
+                "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic (seeded)",
+                "config": {"workload": f"config3: 16 sequences, lengths U[128,4096] (seed 0), {T} tokens, "
+                                       "Hk=16 Hv=32 Dk=Dv=128, cu_seqlens",
+                           "l2": "flushed before every step", "step": "gate_fwd + gdn_fwd(save) + gdn_bwd + gate_bwd"},
+                "per_op_ms": {k: round(v, 4) for k, v in per_op.items()}, "gpu_launches": int(launches),
+                "clocks": clocks,
+                "roofline": {"kernel": "gdn_bwd", "bound": "tensor", "achieved": round(ach, 3), "peak": tf,
+                             "unit": "TFLOP/s", "frac": round(ach / tf, 5), "peak_source": src, "traffic": None}}
+    else:
+        N, V, Hk, Hv, D = 32, 8, 16, 32, 128
+        p = synthetic.make(N, V, Hk, Hv, D, D, seed=0, device=dev, with_dy=False)
+        q, k, v = p.q.to(torch.bfloat16), p.k.to(torch.bfloat16), p.v.to(torch.bfloat16)
+        g, beta = p.g, p.beta
+        gen = torch.Generator(device=dev).manual_seed(1)
+        state = torch.randn(N, Hv, D, D, generator=gen, device=dev) * 0.05
+
+        def step(events):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            exact.verify(q, k, v, g, beta, state)
+            e1.record()
+            if events is not None:
+                events.append(("verify", e0, e1))
+
+        ms, per_op, launches, clocks = _timed(step, args.steps, args.warmup, dev)
+        nbytes = (N * Hv * D * D * 4 + N * V * Hv * D * D * 4 + N * V * Hk * D * 2 * 2 + N * V * Hv * D * 2 * 2
+                  + N * V * Hv * 4 * 2)
+        ach = nbytes / (per_op["verify"] / 1e3) / 1e9
+        line = {"metric": "exact speculative verify tokens/s", "value": round(N * V / (ms / 1e3), 1),
+                "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic (seeded)",
+                "config": {"workload": "config4: 32 sequences x 8 drafted tokens, Hk=16 Hv=32 Dk=Dv=128, "
+                                       "every token's state kept", "l2": "flushed before every step"},
+                "per_op_ms": {k: round(v, 4) for k, v in per_op.items()}, "gpu_launches": int(launches),
+                "clocks": clocks,
+                "roofline": {"kernel": "gdn_verify", "bound": "hbm", "achieved": round(ach, 1), "peak": hbm,
+                             "unit": "GB/s", "frac": round(ach / hbm, 5), "peak_source": src, "traffic": None,
+                             "bytes_per_launch": nbytes}}
+    print(json.dumps(line), flush=True)
+
+
 if __name__ == "__main__":
     a = parse()
     if a.impl == "reference":
         run_reference(a)
+    elif a.workload in ("c3", "c4"):
+        run_single(a)
     else:
         run_ours(a)
