@@ -63,6 +63,11 @@ def bytes_per_token(Hk, Hv, Dk, Dv, act=2):
     return fwd, bwd
 
 
+# DRAM bytes (read + write) per launch of the dominant op, from one ncu capture of this bench's workload
+# (profiles/gdn_chunk_config1.md, profiles/gdn_verify_config4.md); None where no capture was made.
+TRAFFIC = {("c1", "gdn_bwd"): 354.1e6, ("c4", "verify"): 550.8e6}
+
+
 def load_peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -291,13 +296,15 @@ def run_ours(args):
         if dom in flops:
             ach = flops[dom] / (dom_ms / 1e3) / 1e12
             roof = {"kernel": dom, "bound": "tensor", "achieved": round(ach, 3), "peak": tf, "unit": "TFLOP/s",
-                    "frac": round(ach / tf, 5), "peak_source": src, "traffic": None, "ms_per_launch": round(dom_ms, 4),
+                    "frac": round(ach / tf, 5), "peak_source": src, "traffic": TRAFFIC.get((args.workload, dom)),
+                    "ms_per_launch": round(dom_ms, 4),
                     "hbm_achieved_gbs": round(bytes_[dom] / (dom_ms / 1e3) / 1e9, 1),
                     "hbm_frac": round(bytes_[dom] / (dom_ms / 1e3) / 1e9 / hbm, 5)}
         else:
             ach = bytes_[dom] / (dom_ms / 1e3) / 1e9
             roof = {"kernel": dom, "bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
-                    "frac": round(ach / hbm, 5), "peak_source": src, "traffic": None, "ms_per_launch": round(dom_ms, 4)}
+                    "frac": round(ach / hbm, 5), "peak_source": src, "traffic": TRAFFIC.get((args.workload, dom)),
+                    "ms_per_launch": round(dom_ms, 4)}
         line = {
             "metric": "GDN fwd+bwd tokens/s at 4B layer shape" if args.workload == "c1"
             else "GDN fwd+bwd tokens/s, B=8 T=4096 Hv=64 split over GPUs",
@@ -531,7 +538,8 @@ def run_single(args):
                 "per_op_ms": {k: round(v, 4) for k, v in per_op.items()}, "gpu_launches": int(launches),
                 "clocks": clocks,
                 "roofline": {"kernel": "gdn_verify", "bound": "hbm", "achieved": round(ach, 1), "peak": hbm,
-                             "unit": "GB/s", "frac": round(ach / hbm, 5), "peak_source": src, "traffic": None,
+                             "unit": "GB/s", "frac": round(ach / hbm, 5), "peak_source": src,
+                             "traffic": TRAFFIC.get(("c4", "verify")),
                              "bytes_per_launch": nbytes}}
     print(json.dumps(line), flush=True)
 

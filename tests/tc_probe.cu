@@ -21,7 +21,8 @@ __host__ __device__ inline int tile_bytes(int R, int K, int eb, int mn_major) {
 
 // A logical [M][K], B logical [N][K], D [M][N]; fp32 in global.
 __global__ void __launch_bounds__(128) tc_probe_kernel(int M, int N, int K, int kind, int a_mn, int b_mn,
-                                                       const float* A, const float* B, float* D, int* err) {
+                                                       const float* A, const float* B, float* D, int* err,
+                                                       int lane_off) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_slot;
@@ -58,12 +59,14 @@ __global__ void __launch_bounds__(128) tc_probe_kernel(int M, int N, int K, int 
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = tmem_slot;
+  // M = 64 only: lane_off = 16 puts the accumulator in the upper half of each 32-lane subpartition
+  const uint32_t dst = tmem + ((uint32_t)lane_off << 16);
   if (tid == 0) {
     if (kind == tc::kBF16)
-      tc::mma_tile<tc::kBF16>(tmem, tc::smem_u32(a_tile), a_mn, a_mn ? K : M, tc::smem_u32(b_tile), b_mn,
+      tc::mma_tile<tc::kBF16>(dst, tc::smem_u32(a_tile), a_mn, a_mn ? K : M, tc::smem_u32(b_tile), b_mn,
                               b_mn ? K : N, M, N, K, false);
     else
-      tc::mma_tile<tc::kTF32>(tmem, tc::smem_u32(a_tile), a_mn, a_mn ? K : M, tc::smem_u32(b_tile), b_mn,
+      tc::mma_tile<tc::kTF32>(dst, tc::smem_u32(a_tile), a_mn, a_mn ? K : M, tc::smem_u32(b_tile), b_mn,
                               b_mn ? K : N, M, N, K, false);
     tc::mma_commit(&bar);
   }
@@ -71,8 +74,8 @@ __global__ void __launch_bounds__(128) tc_probe_kernel(int M, int N, int K, int 
   tc::fence_after_sync();
   if (ok) {
     // M = 128: row m in lane m.  M = 64: rows 16w..16w+15 in lanes 32w..32w+15.
-    const int row = M == 128 ? 32 * warp + lane : 16 * warp + lane;
-    const bool mine = M == 128 || lane < 16;
+    const int row = M == 128 ? 32 * warp + lane : 16 * warp + (lane - lane_off);
+    const bool mine = M == 128 || (lane >= lane_off && lane < lane_off + 16);
     for (int c = 0; c < N; c += 16) {
       float v[16];
       tc::tmem_ld16(tc::taddr(tmem, 32 * warp, c), v);
@@ -86,12 +89,13 @@ __global__ void __launch_bounds__(128) tc_probe_kernel(int M, int N, int K, int 
 }
 
 extern "C" int tc_probe_gemm(int M, int N, int K, int kind, int a_mn, int b_mn, const float* A, const float* B,
-                             float* D, int* err) {
+                             float* D, int* err, int lane_off) {
   if ((M != 64 && M != 128) || N < 16 || N > 256 || N % 16 || K < 16 || K > 128 || K % 16) return -1;
+  if (lane_off != 0 && (M != 64 || lane_off != 16)) return -1;
   const int eb = kind == tc::kBF16 ? 2 : 4;
   const int smem = 1024 + tile_bytes(M, K, eb, a_mn) + tile_bytes(N, K, eb, b_mn);
   cudaFuncSetAttribute(tc_probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  tc_probe_kernel<<<1, 128, smem>>>(M, N, K, kind, a_mn, b_mn, A, B, D, err);
+  tc_probe_kernel<<<1, 128, smem>>>(M, N, K, kind, a_mn, b_mn, A, B, D, err, lane_off);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 

@@ -24,7 +24,7 @@ def build_probe():
                         "-Xcompiler", "-fPIC", "-I" + os.path.join(ROOT, "quotebound_b200", "csrc"),
                         os.path.join(HERE, "tc_probe.cu"), "-o", SO], check=True)
     L = ctypes.CDLL(SO)
-    L.tc_probe_gemm.argtypes = [ctypes.c_int] * 6 + [ctypes.c_void_p] * 4
+    L.tc_probe_gemm.argtypes = [ctypes.c_int] * 6 + [ctypes.c_void_p] * 4 + [ctypes.c_int]
     return L
 
 
@@ -41,15 +41,14 @@ def L():
     return build_probe()
 
 
-@pytest.mark.parametrize("kind,M,N,K,a_mn,b_mn", CASES,
-                         ids=lambda v: str(v))
-def test_mma_tile(L, kind, M, N, K, a_mn, b_mn):
+def _tile(L, kind, M, N, K, a_mn, b_mn, lane_off=0):
     gen = torch.Generator(device="cuda").manual_seed(M * 1000 + N * 10 + K + a_mn + 2 * b_mn + kind)
     A = torch.randn(M, K, device="cuda", generator=gen)
     B = torch.randn(N, K, device="cuda", generator=gen)
     D = torch.full((M, N), float("nan"), device="cuda")
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
-    rc = L.tc_probe_gemm(M, N, K, kind, a_mn, b_mn, A.data_ptr(), B.data_ptr(), D.data_ptr(), err.data_ptr())
+    rc = L.tc_probe_gemm(M, N, K, kind, a_mn, b_mn, A.data_ptr(), B.data_ptr(), D.data_ptr(), err.data_ptr(),
+                         lane_off)
     assert rc == 0
     torch.cuda.synchronize()
     assert int(err.item()) == 0, "mbarrier wait timed out"
@@ -60,6 +59,19 @@ def test_mma_tile(L, kind, M, N, K, a_mn, b_mn):
     want = Ar @ Br.T
     rel = ((D.double() - want).norm() / want.norm()).item()
     assert rel < 1e-5, rel
+
+
+@pytest.mark.parametrize("kind,M,N,K,a_mn,b_mn", CASES,
+                         ids=lambda v: str(v))
+def test_mma_tile(L, kind, M, N, K, a_mn, b_mn):
+    _tile(L, kind, M, N, K, a_mn, b_mn)
+
+
+@pytest.mark.parametrize("kind,N,a_mn,b_mn", [(1, 32, 0, 1), (1, 64, 1, 1), (2, 32, 0, 1), (2, 64, 1, 0)])
+def test_mma_m64_upper_half_lanes(L, kind, N, a_mn, b_mn):
+    """An M = 64 accumulator addressed at lane 16: rows 16w..16w+15 land in lanes 32w+16..32w+31, so two
+    M = 64 accumulators can share TMEM columns (lower and upper half of every subpartition)."""
+    _tile(L, kind, 64, N, 64, a_mn, b_mn, lane_off=16)
 
 
 def _expect_offsets(kind):
