@@ -1,18 +1,20 @@
 """Gated DeltaNet forward + backward tokens/s on B200 (one process per GPU).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c1|c2]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c1|c2|c3|c4]
 
-One step is the whole training pass of the recurrence's layer slice over one batch:
-    gate/norm forward (qn, kn, g, beta from q, k, a, b, A_log, dt_bias)
-    -> recurrence forward (y, final state, chunk states saved)
-    -> recurrence backward (dq, dk, dv, dg, dbeta, dh0 given dy)
-    -> gate/norm backward (dq, dk through the norms; da, db; per-head dA_log, ddt_bias)
-    -> when the batch is split over GPUs, one all-reduce of [dA_log | ddt_bias] (NCCL).
+One step is the whole training pass of the recurrence's layer slice over one batch, through the fused
+layer entry points (the norm and gate graph inside the chunked kernels):
+    layer forward (raw q, k normalised; log g, beta from a, b, A_log, dt_bias; y, final state, chunk
+    intermediates saved) -> layer backward (dq, dk through the norms, dv, da, db, per-head dA_log,
+    ddt_bias given dy) -> when the batch is split over GPUs, one all-reduce of [dA_log | ddt_bias] (NCCL).
+With --algo 1 the row-parallel kernels run instead, with the gate graph as separate kernels.
 
 Workloads (synthetic, seeded; shapes and value distributions of the measured configurations):
   c1  Qwen3.5-4B layer: B=1 per GPU, T=2048, Hk=16, Hv=32, Dk=Dv=128, bf16 activations, fp32 g/beta/state.
       Weak scaling: GPU r runs batch row r (global batch = N).
   c2  B=8, T=4096, Hk=16, Hv=64 split over the GPUs by (batch x value-head group); strong scaling.
+  c3  16 sequences of U[128, 4096] tokens packed with cu_seqlens (one GPU).
+  c4  exact speculative verify of 8 drafted tokens for 32 sequences, every state kept (one GPU).
 
 `value` is tokens/s of the whole job (tokens of all ranks / max over ranks of the device time);
 `e2e` is the same metric through the public API with host buffers: every step copies its inputs
@@ -65,7 +67,7 @@ def bytes_per_token(Hk, Hv, Dk, Dv, act=2):
 
 # DRAM bytes (read + write) per launch of the dominant op, from one ncu capture of this bench's workload
 # (profiles/gdn_chunk_config1.md, profiles/gdn_verify_config4.md); None where no capture was made.
-TRAFFIC = {("c1", "gdn_bwd"): 354.1e6, ("c4", "verify"): 550.8e6}
+TRAFFIC = {("c4", "verify"): 550.8e6}
 
 
 def load_peaks():
@@ -163,9 +165,17 @@ class Work:
             events.append((name, e0, e1))
             return out
 
+        cu = getattr(self, "cu", None)
+        if self.algo != 1:  # the fused layer path: norm, gates and recurrence in the chunked kernels
+            from quotebound_b200 import layer
+            y, hT, saved = op("layer_fwd", lambda: layer.gated_delta_layer_fwd(
+                self.q, self.k, self.v, self.a, self.b, self.A_log, self.dt_bias, None, save=True, cu_seqlens=cu))
+            dq, dk, dv, da, db, dA, ddt, _ = op("layer_bwd", lambda: layer.gated_delta_layer_bwd(
+                self.q, self.k, self.v, self.a, self.b, self.A_log, self.dt_bias, None, self.dy, None, saved=saved,
+                cu_seqlens=cu))
+            return dq, dk, dv, da, db, dA, ddt
         qn, kn, g, beta = op("gate_fwd", lambda: gate.gate_fwd(self.q, self.k, self.a, self.b, self.A_log,
                                                                  self.dt_bias))
-        cu = getattr(self, "cu", None)
         y, hT, saved = op("gdn_fwd", lambda: deltanet.gated_delta_fwd(qn, kn, self.v, g, beta, None, save=True,
                                                                        algo=self.algo, cu_seqlens=cu))
         dqn, dkn, dv, dg, dbeta, _ = op("gdn_bwd", lambda: deltanet.gated_delta_bwd(
@@ -287,9 +297,11 @@ def run_ours(args):
         dom = max(per_op, key=per_op.get)
         launch_tokens = B * T if args.workload == "c1" else B * T
         heads = Hv
-        flops = {"gdn_fwd": fpt * launch_tokens * heads, "gdn_bwd": 2 * fpt * launch_tokens * heads}
+        flops = {"gdn_fwd": fpt * launch_tokens * heads, "gdn_bwd": 2 * fpt * launch_tokens * heads,
+                 "layer_fwd": fpt * launch_tokens * heads, "layer_bwd": 2 * fpt * launch_tokens * heads}
         fb, bb = bytes_per_token(Hk, Hv, Dk, Dv)
-        bytes_ = {"gdn_fwd": fb * launch_tokens, "gdn_bwd": bb * launch_tokens,
+        bytes_ = {"gdn_fwd": fb * launch_tokens, "gdn_bwd": bb * launch_tokens, "layer_fwd": fb * launch_tokens,
+                  "layer_bwd": bb * launch_tokens,
                   "gate_fwd": launch_tokens * (2 * Hk * Dk * 2 * 2 + Hv * 4 * 4),
                   "gate_bwd": launch_tokens * (4 * Hk * Dk * 2 + 2 * Hk * Dk * 2 + Hv * 4 * 6)}
         dom_ms = per_op[dom]
@@ -318,7 +330,8 @@ def run_ours(args):
                        "parallelism": f"dp{world}" if args.workload == "c1" else f"bh{world}",
                        "l2": "flushed before every step (512 MiB write, outside the step events)",
                        "algo": {0: "auto", 1: "rows", 2: "chunked"}[args.algo],
-                       "step": "gate_fwd + gdn_fwd(save) + gdn_bwd + gate_bwd" + (" + allreduce" if dist else "")},
+                       "step": ("layer_fwd(save) + layer_bwd" if args.algo != 1 else
+                                "gate_fwd + gdn_fwd(save) + gdn_bwd + gate_bwd") + (" + allreduce" if dist else "")},
             "per_op_ms": {k: round(v, 4) for k, v in per_op.items()},
             "gpu_launches": int(launches),
             "clocks": clocks,
@@ -495,7 +508,8 @@ def run_single(args):
         W = Work(1, T, 16, 32, 128, 128, 0, dev, args.algo, cu_seqlens=cu)
         ms, per_op, launches, clocks = _timed(W.step, args.steps, args.warmup, dev)
         fpt = fwd_flops_per_token_head(128, 128)
-        dom_ms = per_op["gdn_bwd"]
+        dom = "layer_bwd" if "layer_bwd" in per_op else "gdn_bwd"
+        dom_ms = per_op[dom]
         ach = 2 * fpt * T * 32 / (dom_ms / 1e3) / 1e12
         line = {"metric": "GDN fwd+bwd tokens/s, varlen packed batch", "value": round(T / (ms / 1e3), 1),
                 "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
@@ -503,10 +517,10 @@ def run_single(args):
                 "dtype": "bf16", "data": "synthetic (seeded)",
                 "config": {"workload": f"config3: 16 sequences, lengths U[128,4096] (seed 0), {T} tokens, "
                                        "Hk=16 Hv=32 Dk=Dv=128, cu_seqlens",
-                           "l2": "flushed before every step", "step": "gate_fwd + gdn_fwd(save) + gdn_bwd + gate_bwd"},
+                           "l2": "flushed before every step", "step": "layer_fwd(save) + layer_bwd"},
                 "per_op_ms": {k: round(v, 4) for k, v in per_op.items()}, "gpu_launches": int(launches),
                 "clocks": clocks,
-                "roofline": {"kernel": "gdn_bwd", "bound": "tensor", "achieved": round(ach, 3), "peak": tf,
+                "roofline": {"kernel": dom, "bound": "tensor", "achieved": round(ach, 3), "peak": tf,
                              "unit": "TFLOP/s", "frac": round(ach / tf, 5), "peak_source": src, "traffic": None}}
     else:
         N, V, Hk, Hv, D = 32, 8, 16, 32, 128

@@ -40,7 +40,7 @@ extern "C" {
 enum { QB_DTYPE_F32 = 0, QB_DTYPE_BF16 = 1 };
 
 /* Which calls a workspace / saved-state size is asked for. */
-enum { QB_OP_FWD = 0, QB_OP_BWD = 1 };
+enum { QB_OP_FWD = 0, QB_OP_BWD = 1, QB_OP_LAYER_FWD = 2, QB_OP_LAYER_BWD = 3 };
 
 /* Which kernels run the recurrence.  AUTO takes the tensor-core chunked path where the shape has
  * one (Dk = Dv = 128) and the row-parallel path elsewhere; the other two force one path (CHUNKED
@@ -91,6 +91,26 @@ int qb_gdn_bwd(const qb_gdn_desc* d, const void* q, const void* k, const void* v
                const float* beta, const float* h0, const void* dy, const float* dhT, const void* saved,
                void* dq, void* dk, void* dv, float* dg, float* dbeta, float* dh0, void* ws,
                int64_t ws_bytes, void* stream, char* err, int errlen);
+
+/* The recurrence with the norm and gate graph around it fused in (deltanet()'s middle,
+ * src/deltanet.cpp:113-119, compute_g :41-52): q, k are the raw conv outputs [B, T, Hk, Dk] (bf16),
+ * normalised inside as the model does (rms_norm rounded to bf16, times the bf16 scalar 1/Dk for q and
+ * 1/sqrt(Dk) for k); a, b [B, T, Hv] float32 give log g = -exp(A_log) softplus(a + dt_bias) and
+ * beta = sigmoid(b); A_log, dt_bias [Hv] float32.  Needs the chunked path (bf16, Dk = Dv = 128).
+ * saved (training) must hold qb_gdn_layer_saved_bytes(d); the workspace is
+ * qb_gdn_workspace_bytes(d, QB_OP_LAYER_FWD / QB_OP_LAYER_BWD).  The backward returns dq, dk for the
+ * raw rows, da, db [B, T, Hv], and this call's per-head sums dA_log, ddt_bias [Hv] (fixed-order,
+ * overwritten; across GPUs that split the batch, sum them with one all-reduce). */
+int64_t qb_gdn_layer_saved_bytes(const qb_gdn_desc* d, char* err, int errlen);
+int qb_gdn_layer_fwd(const qb_gdn_desc* d, const void* q, const void* k, const void* v, const float* a,
+                     const float* b, const float* A_log, const float* dt_bias, const float* h0, void* y,
+                     float* hT, void* saved, void* ws, int64_t ws_bytes, void* stream, char* err,
+                     int errlen);
+int qb_gdn_layer_bwd(const qb_gdn_desc* d, const void* q, const void* k, const void* v, const float* a,
+                     const float* b, const float* A_log, const float* dt_bias, const float* h0,
+                     const void* dy, const float* dhT, const void* saved, void* dq, void* dk, void* dv,
+                     float* da, float* db, float* dA_log, float* ddt_bias, float* dh0, void* ws,
+                     int64_t ws_bytes, void* stream, char* err, int errlen);
 
 /* One decode step for N independent sequences (gated_delta with T = 1, src/deltanet.cpp:68-80 as
  * the decode path calls it, src/generate.cpp forward(..., cache)):

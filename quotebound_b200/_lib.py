@@ -15,6 +15,8 @@ QB_DTYPE_F32 = 0
 QB_DTYPE_BF16 = 1
 QB_OP_FWD = 0
 QB_OP_BWD = 1
+QB_OP_LAYER_FWD = 2
+QB_OP_LAYER_BWD = 3
 QB_ALGO_AUTO = 0
 QB_ALGO_ROWS = 1
 QB_ALGO_CHUNKED = 2
@@ -23,7 +25,8 @@ QB_ALGO_CHUNKED = 2
 SYMBOLS = (
     "qb_gdn_version", "qb_gdn_launches", "qb_gdn_workspace_bytes", "qb_gdn_saved_bytes", "qb_gdn_fwd", "qb_gdn_bwd",
     "qb_gdn_step", "qb_gdn_verify", "qb_gdn_keep_rows", "qb_gdn_gate_fwd", "qb_gdn_gate_bwd",
-    "qb_gdn_gate_workspace_bytes", "qb_gdn_gate_bwd_noalloc",
+    "qb_gdn_gate_workspace_bytes", "qb_gdn_gate_bwd_noalloc", "qb_gdn_layer_saved_bytes", "qb_gdn_layer_fwd",
+    "qb_gdn_layer_bwd",
 )
 
 
@@ -75,6 +78,12 @@ def load():
     L.qb_gdn_gate_fwd.argtypes = [i64] + [i32] * 5 + [vp] * 10 + [vp, cp, ctypes.c_int]
     L.qb_gdn_gate_bwd.restype = ctypes.c_int
     L.qb_gdn_gate_bwd.argtypes = [i64] + [i32] * 5 + [vp] * 16 + [vp, i64, vp, cp, ctypes.c_int]
+    L.qb_gdn_layer_saved_bytes.restype = i64
+    L.qb_gdn_layer_saved_bytes.argtypes = [dp, cp, ctypes.c_int]
+    L.qb_gdn_layer_fwd.restype = ctypes.c_int
+    L.qb_gdn_layer_fwd.argtypes = [dp] + [vp] * 12 + [i64, vp, cp, ctypes.c_int]
+    L.qb_gdn_layer_bwd.restype = ctypes.c_int
+    L.qb_gdn_layer_bwd.argtypes = [dp] + [vp] * 20 + [i64, vp, cp, ctypes.c_int]
     L.qb_gdn_gate_bwd_noalloc.restype = ctypes.c_int
     L.qb_gdn_gate_bwd_noalloc.argtypes = [i64] + [i32] * 5 + [vp] * 16 + [vp, cp, ctypes.c_int]
     L.qb_gdn_gate_workspace_bytes.restype = i64

@@ -165,6 +165,9 @@ __device__ __forceinline__ void store_row32<float>(float* p, const float (&v)[32
   for (int q = 0; q < 8; ++q) *reinterpret_cast<float4*>(p + 4 * q) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
 }
 
+__device__ __forceinline__ float softplus_f(float x) { return fmaxf(x, 0.f) + log1pf(expf(-fabsf(x))); }
+__device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
+
 __device__ __forceinline__ bool wait_all(uint64_t* bar, uint32_t parity, int* err, int code) {
   return __syncthreads_and(tc::mbar_wait(bar, parity, err, code)) != 0;
 }
@@ -176,6 +179,9 @@ __device__ __forceinline__ bool wait_all(uint64_t* bar, uint32_t parity, int* er
 struct PrepArgs {
   Geo geo;
   const float *g, *beta;
+  // layer mode (g, beta null): the raw gate inputs and the raw q, k rows normalised here
+  const float *a_raw, *b_raw, *A_log, *dt_bias;
+  __nv_bfloat16 *qn, *kn;   // normalised q, k written here [B*T, Hk, Dk] (layer mode)
   float* Tbuf;      // [chunks, Hv, 64, 64]  T = (I + L)^-1, tf32-rounded
   float* Pbuf;      // [chunks, Hv, 64, 64]  P, tf32-rounded
   float* Lbuf;      // [chunks, Hv, 64, 64]  strict-lower Gamma * K K^T (training only), or null
@@ -219,16 +225,70 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CU
     tc::tma_load_3d(qtile, &qmap, &bar_tma, 0, hk, (int)tok0);
     tc::tma_load_3d(qtile + 8192, &qmap, &bar_tma, 64, hk, (int)tok0);
   }
+  const bool layer = a.g == nullptr;
   float lg = 0.f, bt = 0.f;
   if (tid < 64 && tid < L) {
     const int64_t gi = (tok0 + tid) * a.geo.Hv + hv;
-    lg = fmaxf(logf(a.g[gi]), -88.f);
-    bt = a.beta[gi];
+    if (layer) {  // log g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b) (src/deltanet.cpp:41-52, :118)
+      lg = -expf(a.A_log[hv]) * softplus_f(a.a_raw[gi] + a.dt_bias[hv]);
+      bt = sigmoid_f(a.b_raw[gi]);
+    } else {
+      lg = fmaxf(logf(a.g[gi]), -88.f);
+      bt = a.beta[gi];
+    }
   }
   if (tid < 64) sbeta[tid] = bt;
   scan64(lg, sb, stmp);
 
   bool ok = wait_all(&bar_tma, 0, a.err, 1);
+  if (ok && layer) {
+    // q and k rows normalised in place as the model does (src/deltanet.cpp:113-116): rms_norm in fp32,
+    // rounded to bf16, times the bf16 scalar 1/Dk (q) or 1/sqrt(Dk) (k), rounded again.  Thread t
+    // owns half a row (one 128-byte slab row of 64 elements); the order inside a row does not matter.
+    const int row = tid >> 1, half = tid & 1;
+    const bool store = hv % (a.geo.Hv / a.geo.Hk) == 0 && row < L;
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+      uint8_t* tile = m == 0 ? ktile : qtile;
+      uint4* r16 = reinterpret_cast<uint4*>(tile + half * 8192 + row * 128);
+      uint4 w[8];
+      float ss = 0.f;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        w[c] = r16[c];
+        const uint32_t u[4] = {w[c].x, w[c].y, w[c].z, w[c].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&u[e]);
+          ss = fmaf(__low2float(h), __low2float(h), ss);
+          ss = fmaf(__high2float(h), __high2float(h), ss);
+        }
+      }
+      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+      const float r = rsqrtf(ss / DK + 1e-6f);
+      const float sc = m == 0 ? __bfloat162float(__float2bfloat16_rn(rsqrtf((float)DK))) : 1.f / DK;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint32_t u[4] = {w[c].x, w[c].y, w[c].z, w[c].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&u[e]);
+          const float x0 = __bfloat162float(__float2bfloat16_rn(__low2float(h) * r)) * sc;
+          const float x1 = __bfloat162float(__float2bfloat16_rn(__high2float(h) * r)) * sc;
+          u[e] = tc::pack_bf16(x0, x1);
+        }
+        w[c] = make_uint4(u[0], u[1], u[2], u[3]);
+        r16[c] = w[c];
+      }
+      if (store) {  // the normalised row in logical order for the walks and the gradient kernel
+        __nv_bfloat16* dst = (m == 0 ? a.kn : a.qn) + ((tok0 + row) * a.geo.Hk + hk) * (size_t)DK + 64 * half;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) reinterpret_cast<uint4*>(dst)[c] = w[c ^ (row & 7)];
+      }
+    }
+    tc::fence_async_smem();
+    __syncthreads();
+  }
   if (ok && tid == 0) {
     tc::fence_after_sync();
     const uint32_t kt = tc::smem_u32(ktile), qt = tc::smem_u32(qtile);
@@ -644,7 +704,9 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_bwd_state(const __grid_const
       for (int j = 0; j < DVT; ++j) dst[(size_t)j * DK] = ds[j];
     }
     tc::st_row_bf16x2_32(smem + BW_SHI, smem + BW_SLO, tid, ds);
-    // 2. dO row (zero past the end) as the fp32 operand of P^T dO, and gamma dO as bf16 hi/lo
+    // 2. dO row (zero past the end) as the fp32 operand of P^T dO, and gamma dO as bf16 hi/lo; the
+    // gates in sg[buf] were stored by other threads (before the loop, or at the end of the last chunk)
+    __syncthreads();
     const float* gb = sg[buf];
     const float bi = gb[i_row], be = gb[64 + i_row], gi = __expf(bi), bC = gb[63];
     if (row_owner) {
@@ -756,13 +818,17 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_bwd_state(const __grid_const
 struct GradArgs {
   Geo geo;
   const void *v, *dy;       // bf16
-  const float* g;           // [B*T, Hv] (dg = d log g / g)
+  const float* g;           // [B*T, Hv] (dg = d log g / g); null in layer mode
   const float* gates;
   const float* ckpt;        // chunk-start states
   const float* dsbuf;       // chunk-end state cotangents
   void *dq, *dk;            // [B*T, Hk, Dk]
-  float *dg, *dbeta;        // [B*T, Hv]
+  float *dg, *dbeta;        // [B*T, Hv]; layer mode: da, db
   int* err;
+  // layer mode: raw inputs for the norm and gate chain rule, per-chunk head sums of dA_log, ddt_bias
+  const __nv_bfloat16 *q_raw, *k_raw;
+  const float *a_raw, *b_raw, *A_log, *dt_bias;
+  float* head_part;         // [chunks, Hv, 2]
 };
 
 constexpr int GR_K = 0;         // 16 KB bf16 K (TMA)
@@ -1099,33 +1165,109 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_bwd_grad(const __grid_consta
     __syncthreads();
     if (tid == 0) sdb[63] += (sred[0] + sred[1] + sred[2] + sred[3]) + __expf(bC) * (sred[4] + sred[5] + sred[6] + sred[7]);
     __syncthreads();
+    float pa = 0.f, pd = 0.f;  // layer mode: this row's share of the head's dA_log, ddt_bias
     if (valid) {
       float dl = 0.f;  // d log g_i = sum over rows i' >= i of d b_i'
       for (int i2 = 63; i2 >= i_row; --i2) dl += sdb[i2];
       const int64_t gi_idx = (tok0 + i_row) * Hv + hv;
-      // dg = d log g / g; a gate of exactly 0 (log g clamped) gets 0, which keeps g * dg = 0 exact
-      const float gv = a.g[gi_idx];
-      a.dg[gi_idx] = gv > 0.f ? dl / gv : 0.f;
-      a.dbeta[gi_idx] = t1 + dbl;
+      const float dbe = t1 + dbl;
+      if (a.g) {
+        // dg = d log g / g; a gate of exactly 0 (log g clamped) gets 0, which keeps g * dg = 0 exact
+        const float gv = a.g[gi_idx];
+        a.dg[gi_idx] = gv > 0.f ? dl / gv : 0.f;
+        a.dbeta[gi_idx] = dbe;
+      } else {
+        // log g = -e^A softplus(x), x = a + dt_bias: da = d log g * (-e^A sigmoid(x)); beta = sigmoid(b)
+        const float eA = expf(a.A_log[hv]), x = a.a_raw[gi_idx] + a.dt_bias[hv];
+        const float da = dl * (-eA * sigmoid_f(x));
+        const float sb_ = sigmoid_f(a.b_raw[gi_idx]);
+        a.dg[gi_idx] = da;
+        a.dbeta[gi_idx] = dbe * sb_ * (1.f - sb_);
+        pa = dl * (-eA * softplus_f(x));
+        pd = da;
+      }
+    }
+    if (!a.g) {  // fixed-order block sums of the head parameters' gradients for this chunk
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        pa += __shfl_xor_sync(0xffffffffu, pa, o);
+        pd += __shfl_xor_sync(0xffffffffu, pd, o);
+      }
+      __syncthreads();
+      if (lane == 0) {
+        sred[warp] = pa;
+        sred[4 + warp] = pd;
+      }
+      __syncthreads();
+      if (tid == 0) {
+        a.head_part[(c * Hv + hv) * 2] = sred[0] + sred[1] + sred[2] + sred[3];
+        a.head_part[(c * Hv + hv) * 2 + 1] = sred[4] + sred[5] + sred[6] + sred[7];
+      }
     }
     ok = wait_all(&bar_mma, ph_mma, a.err, 36);
     ph_mma ^= 1;
     tc::fence_after_sync();
   }
-  // f. dq, dk rows of this key head
+  // f. dq, dk rows of this key head (layer mode: through the norms to the raw q, k)
   if (ok) {
+    const size_t rowoff = ((tok0 + i_row) * a.geo.Hk + hk) * (size_t)DK;
 #pragma unroll 1
-    for (int h = 0; h < 4; ++h) {
-      float v[32];
-      tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cDQ + 32 * h), v);
-      if (valid) store_row32<Tout>(static_cast<Tout*>(a.dq) + ((tok0 + i_row) * a.geo.Hk + hk) * (size_t)DK + 32 * h, v);
-      tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cDK + 32 * h), v);
-      if (valid) store_row32<Tout>(static_cast<Tout*>(a.dk) + ((tok0 + i_row) * a.geo.Hk + hk) * (size_t)DK + 32 * h, v);
+    for (int m = 0; m < 2; ++m) {
+      const uint32_t col = m == 0 ? cDQ : cDK;
+      Tout* out = static_cast<Tout*>(m == 0 ? a.dq : a.dk) + rowoff;
+      if (!a.g) {
+        // x^ = s bf16(x r), r = rsqrt(mean(x^2) + eps):  dx = s r (dx^ - r^2 (x . dx^) x / Dk)
+        const __nv_bfloat16* xr = (m == 0 ? a.q_raw : a.k_raw) + rowoff;
+        float ss = 0.f, dot = 0.f;
+#pragma unroll 1
+        for (int h = 0; h < 4; ++h) {
+          float v[32], x[32];
+          tc::tmem_ld32(tc::taddr(tmem, 32 * warp, col + 32 * h), v);
+          load_row32(xr + 32 * h, valid, x);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            ss = fmaf(x[j], x[j], ss);
+            dot = fmaf(x[j], v[j], dot);
+          }
+        }
+        const float r = rsqrtf(ss / DK + 1e-6f);
+        const float sc = m == 0 ? 1.f / DK : __bfloat162float(__float2bfloat16_rn(rsqrtf((float)DK)));
+        const float c2 = r * r * dot / DK;
+#pragma unroll 1
+        for (int h = 0; h < 4; ++h) {
+          float v[32], x[32];
+          tc::tmem_ld32(tc::taddr(tmem, 32 * warp, col + 32 * h), v);
+          load_row32(xr + 32 * h, valid, x);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = sc * r * (v[j] - c2 * x[j]);
+          if (valid) store_row32<Tout>(out + 32 * h, v);
+        }
+      } else {
+#pragma unroll 1
+        for (int h = 0; h < 4; ++h) {
+          float v[32];
+          tc::tmem_ld32(tc::taddr(tmem, 32 * warp, col + 32 * h), v);
+          if (valid) store_row32<Tout>(out + 32 * h, v);
+        }
+      }
     }
   }
   tc::fence_before_sync();
   __syncthreads();
   if (warp == 0) tc::tmem_dealloc(tmem, 512);
+}
+
+// dA_log[h], ddt_bias[h] = the per-chunk sums over all chunks, in chunk order (deterministic).
+__global__ void gdn_chunk_head_finish(int64_t n_chunks, int Hv, const float* part, float* dA_log, float* ddt_bias) {
+  for (int h = threadIdx.x; h < Hv; h += blockDim.x) {
+    float sa = 0.f, sd = 0.f;
+    for (int64_t c = 0; c < n_chunks; ++c) {
+      sa += part[(c * Hv + h) * 2];
+      sd += part[(c * Hv + h) * 2 + 1];
+    }
+    dA_log[h] = sa;
+    ddt_bias[h] = sd;
+  }
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -1192,12 +1334,14 @@ bool map_state_mn(CUtensorMap* m, const void* base, int64_t rows) {
 
 int64_t a256(int64_t x) { return (x + 255) & ~int64_t(255); }
 
-// The chunk intermediates: [ckpt][T][P][Gamma*KK][gates], fp32.
+// The chunk intermediates: [ckpt][T][P][Gamma*KK][gates] fp32, and in layer mode the normalised
+// [kn][qn] bf16 rows.
 struct Saved {
   float *ckpt, *T, *P, *L, *gates;
+  __nv_bfloat16 *kn, *qn;
 };
 
-int64_t saved_layout(int Hv, int64_t n_chunks, char* base, Saved* s) {
+int64_t saved_layout(int Hv, int64_t n_chunks, int64_t qk_elems, char* base, Saved* s) {
   int64_t off = 0;
   auto take = [&](int64_t bytes) {
     char* at = base ? base + off : nullptr;
@@ -1210,22 +1354,28 @@ int64_t saved_layout(int Hv, int64_t n_chunks, char* base, Saved* s) {
   x.P = (float*)take(n_chunks * Hv * 4096 * 4);
   x.L = (float*)take(n_chunks * Hv * 4096 * 4);
   x.gates = (float*)take(n_chunks * Hv * 128 * 4);
+  x.kn = (__nv_bfloat16*)take(qk_elems * 2);
+  x.qn = (__nv_bfloat16*)take(qk_elems * 2);
   if (s) *s = x;
   return off;
 }
 
-// Workspace: [chunk_off][err][fwd: T, P, gates when nothing is saved | bwd: dS per chunk, and a saved
-// buffer plus forward workspace when the backward recomputes].
+// Workspace: [chunk_off][err][fwd: T, P, gates (and kn, qn in layer mode) when nothing is saved |
+// bwd: dS per chunk, per-chunk head sums (layer mode), and a saved buffer plus forward workspace when
+// the backward recomputes].
 struct Ws {
   int64_t* chunk_off;
   int* err;
   float *T, *P, *gates;
+  __nv_bfloat16 *kn, *qn;
   float* dsbuf;
+  float* head_part;
   char* saved;
   char* fwd_ws;
 };
 
-int64_t ws_layout(int Hv, int N, int64_t n_chunks, bool varlen, int op, bool with_saved, char* base, Ws* w) {
+int64_t ws_layout(int Hv, int N, int64_t n_chunks, int64_t qk_elems, bool varlen, int op, bool with_saved, char* base,
+                  Ws* w) {
   int64_t off = 0;
   auto take = [&](int64_t bytes) {
     char* at = base ? base + off : nullptr;
@@ -1239,11 +1389,14 @@ int64_t ws_layout(int Hv, int N, int64_t n_chunks, bool varlen, int op, bool wit
     x.T = (float*)take(n_chunks * Hv * 4096 * 4);
     x.P = (float*)take(n_chunks * Hv * 4096 * 4);
     x.gates = (float*)take(n_chunks * Hv * 128 * 4);
+    x.kn = (__nv_bfloat16*)take(qk_elems * 2);
+    x.qn = (__nv_bfloat16*)take(qk_elems * 2);
   } else {
     x.dsbuf = (float*)take(n_chunks * Hv * (int64_t)DV * DK * 4);
+    x.head_part = (float*)take(qk_elems ? n_chunks * Hv * 2 * 4 : 0);
     if (with_saved) {
-      x.saved = take(saved_layout(Hv, n_chunks, nullptr, nullptr));
-      x.fwd_ws = take(ws_layout(Hv, N, n_chunks, varlen, 0, false, nullptr, nullptr));
+      x.saved = take(saved_layout(Hv, n_chunks, qk_elems, nullptr, nullptr));
+      x.fwd_ws = take(ws_layout(Hv, N, n_chunks, qk_elems, varlen, 0, false, nullptr, nullptr));
     }
   }
   if (w) *w = x;
@@ -1255,36 +1408,39 @@ int64_t ws_layout(int Hv, int N, int64_t n_chunks, bool varlen, int op, bool wit
 bool chunked_supported(int Dk, int Dv) { return Dk == DK && Dv == DV && encode_fn() != nullptr; }
 bool chunked_bwd_ready() { return true; }
 
-int64_t chunked_saved_bytes(int Hv, int, int, int64_t n_chunks, int64_t) {
-  return saved_layout(Hv, n_chunks, nullptr, nullptr);
+int64_t chunked_saved_bytes(int Hv, int Hk, int64_t n_chunks, int64_t tokens, bool layer) {
+  return saved_layout(Hv, n_chunks, layer ? tokens * Hk * DK : 0, nullptr, nullptr);
 }
 
-int64_t chunked_ws_bytes(int Hv, int, int, int, int N, int64_t n_chunks, int64_t, bool varlen, int op,
-                         bool with_saved) {
-  return ws_layout(Hv, N, n_chunks, varlen, op, with_saved, nullptr, nullptr);
+int64_t chunked_ws_bytes(int Hv, int Hk, int N, int64_t n_chunks, int64_t tokens, bool varlen, int op, bool with_saved,
+                         bool layer) {
+  return ws_layout(Hv, N, n_chunks, layer ? tokens * Hk * DK : 0, varlen, op, with_saved, nullptr, nullptr);
 }
 
 cudaError_t chunked_fwd(const ChunkFwdArgs& a, void* ws, cudaStream_t st) {
   if (!a.in_bf16) return cudaErrorInvalidValue;
+  const bool layer = a.g == nullptr;
+  const int64_t rows = (int64_t)a.B * a.T, qk = layer ? rows * a.Hk * DK : 0;
   Ws w;
-  ws_layout(a.Hv, a.N, a.n_chunks, a.cu != nullptr, 0, false, (char*)ws, &w);
+  ws_layout(a.Hv, a.N, a.n_chunks, qk, a.cu != nullptr, 0, false, (char*)ws, &w);
   Saved sv{};
   float *Tb = w.T, *Pb = w.P, *gates = w.gates, *ckpt = nullptr, *Lb = nullptr;
+  __nv_bfloat16 *kn = w.kn, *qn = w.qn;
   if (a.saved) {
-    saved_layout(a.Hv, a.n_chunks, (char*)a.saved, &sv);
-    Tb = sv.T, Pb = sv.P, gates = sv.gates, ckpt = sv.ckpt, Lb = sv.L;
+    saved_layout(a.Hv, a.n_chunks, qk, (char*)a.saved, &sv);
+    Tb = sv.T, Pb = sv.P, gates = sv.gates, ckpt = sv.ckpt, Lb = sv.L, kn = sv.kn, qn = sv.qn;
   }
   cudaError_t e;
   if ((e = cudaMemsetAsync(w.err, 0, 16, st)) != cudaSuccess) return e;
   if (a.cu && (e = launch_chunk_offsets(a.cu, a.N, w.chunk_off, st)) != cudaSuccess) return e;
-  const int64_t rows = (int64_t)a.B * a.T, mrows = a.n_chunks * a.Hv * 64;
+  const int64_t mrows = a.n_chunks * a.Hv * 64;
   CUtensorMap kmap, qmap, tmap, pmap;
   if (!map_act(&kmap, a.k, rows, a.Hk, a.Dk) || !map_act(&qmap, a.q, rows, a.Hk, a.Dk) ||
       !map_f32_64(&tmap, Tb, mrows, false) || !map_f32_64(&pmap, Pb, mrows, false))
     return cudaErrorInvalidValue;
   Geo geo{a.T, a.Hk, a.Hv, a.N, (a.T + C - 1) / C, a.cu, a.cu ? w.chunk_off : nullptr};
   if (a.n_chunks > 0) {
-    PrepArgs pa{geo, a.g, a.beta, Tb, Pb, Lb, gates, w.err};
+    PrepArgs pa{geo, a.g, a.beta, a.a_raw, a.b_raw, a.A_log, a.dt_bias, qn, kn, Tb, Pb, Lb, gates, w.err};
     const int prep_smem = 1024 + 32768 + 64 * 68 * 4;
     if ((e = cudaFuncSetAttribute(gdn_chunk_prep, cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem)) !=
         cudaSuccess)
@@ -1293,6 +1449,8 @@ cudaError_t chunked_fwd(const ChunkFwdArgs& a, void* ws, cudaStream_t st) {
     note_launch();
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
+  if (layer && (!map_act(&kmap, kn, rows, a.Hk, a.Dk) || !map_act(&qmap, qn, rows, a.Hk, a.Dk)))
+    return cudaErrorInvalidValue;  // the walk reads the normalised rows
   StateArgs sa{geo, a.v, gates, a.h0, a.y, a.hT, ckpt, w.err};
   auto kern = a.out_bf16 ? gdn_chunk_fwd_state<__nv_bfloat16> : gdn_chunk_fwd_state<float>;
   if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FW_SMEM)) != cudaSuccess) return e;
@@ -1303,8 +1461,10 @@ cudaError_t chunked_fwd(const ChunkFwdArgs& a, void* ws, cudaStream_t st) {
 
 cudaError_t chunked_bwd(const ChunkBwdArgs& a, void* ws, cudaStream_t st) {
   if (!a.in_bf16) return cudaErrorInvalidValue;
+  const bool layer = a.g == nullptr;
+  const int64_t rows = (int64_t)a.B * a.T, qk = layer ? rows * a.Hk * DK : 0;
   Ws w;
-  ws_layout(a.Hv, a.N, a.n_chunks, a.cu != nullptr, 1, a.saved == nullptr, (char*)ws, &w);
+  ws_layout(a.Hv, a.N, a.n_chunks, qk, a.cu != nullptr, 1, a.saved == nullptr, (char*)ws, &w);
   cudaError_t e;
   const void* saved = a.saved;
   if (!saved) {  // recompute the forward's intermediates with the same forward (y is discarded into dv)
@@ -1312,16 +1472,19 @@ cudaError_t chunked_bwd(const ChunkBwdArgs& a, void* ws, cudaStream_t st) {
     f.B = a.B, f.T = a.T, f.Hk = a.Hk, f.Hv = a.Hv, f.Dk = a.Dk, f.Dv = a.Dv, f.N = a.N, f.n_chunks = a.n_chunks;
     f.cu = a.cu, f.q = a.q, f.k = a.k, f.v = a.v, f.g = a.g, f.beta = a.beta, f.h0 = a.h0, f.y = a.dv;
     f.saved = w.saved, f.in_bf16 = a.in_bf16, f.out_bf16 = a.out_bf16;
+    f.a_raw = a.a_raw, f.b_raw = a.b_raw, f.A_log = a.A_log, f.dt_bias = a.dt_bias;
     if ((e = chunked_fwd(f, w.fwd_ws, st)) != cudaSuccess) return e;
     saved = w.saved;
   }
   Saved sv;
-  saved_layout(a.Hv, a.n_chunks, (char*)saved, &sv);
+  saved_layout(a.Hv, a.n_chunks, qk, (char*)saved, &sv);
   if ((e = cudaMemsetAsync(w.err, 0, 16, st)) != cudaSuccess) return e;
   if (a.cu && (e = launch_chunk_offsets(a.cu, a.N, w.chunk_off, st)) != cudaSuccess) return e;
-  const int64_t rows = (int64_t)a.B * a.T, mrows = a.n_chunks * a.Hv * 64;
+  const int64_t mrows = a.n_chunks * a.Hv * 64;
+  const void* kx = layer ? (const void*)sv.kn : a.k;
+  const void* qx = layer ? (const void*)sv.qn : a.q;
   CUtensorMap kmap, qmap, tmap_k, tmap_mn, pmap_mn, lmap_k;
-  if (!map_act(&kmap, a.k, rows, a.Hk, a.Dk) || !map_act(&qmap, a.q, rows, a.Hk, a.Dk) ||
+  if (!map_act(&kmap, kx, rows, a.Hk, a.Dk) || !map_act(&qmap, qx, rows, a.Hk, a.Dk) ||
       !map_f32_64(&tmap_k, sv.T, mrows, false) || !map_f32_64(&tmap_mn, sv.T, mrows, true) ||
       !map_f32_64(&pmap_mn, sv.P, mrows, true) || !map_f32_64(&lmap_k, sv.L, mrows, false))
     return cudaErrorInvalidValue;
@@ -1332,18 +1495,32 @@ cudaError_t chunked_bwd(const ChunkBwdArgs& a, void* ws, cudaStream_t st) {
   k1<<<dim3(DV / DVT, a.Hv, a.N), 128, BW_SMEM, st>>>(kmap, qmap, tmap_mn, pmap_mn, ba);
   note_launch();
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  if (a.n_chunks == 0) return cudaSuccess;
+  if (a.n_chunks == 0) {
+    if (layer) {
+      if ((e = cudaMemsetAsync(a.dA_log, 0, a.Hv * 4, st)) != cudaSuccess) return e;
+      if ((e = cudaMemsetAsync(a.ddt_bias, 0, a.Hv * 4, st)) != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+  }
   CUtensorMap smap_mn, dmap_mn;
   if (!map_state_mn(&smap_mn, sv.ckpt, a.n_chunks * a.Hv * (int64_t)DV) ||
       !map_state_mn(&dmap_mn, w.dsbuf, a.n_chunks * a.Hv * (int64_t)DV))
     return cudaErrorInvalidValue;
-  GradArgs ga{geo, a.v, a.dy, a.g, sv.gates, sv.ckpt, w.dsbuf, a.dq, a.dk, a.dg, a.dbeta, w.err};
+  GradArgs ga{geo, a.v, a.dy, a.g, sv.gates, sv.ckpt, w.dsbuf, a.dq, a.dk, a.dg, a.dbeta, w.err,
+              static_cast<const __nv_bfloat16*>(a.q), static_cast<const __nv_bfloat16*>(a.k),
+              a.a_raw, a.b_raw, a.A_log, a.dt_bias, w.head_part};
   auto k2 = a.out_bf16 ? gdn_chunk_bwd_grad<__nv_bfloat16> : gdn_chunk_bwd_grad<float>;
   if ((e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, GR_SMEM)) != cudaSuccess) return e;
   k2<<<dim3((unsigned)a.n_chunks, a.Hk), 128, GR_SMEM, st>>>(kmap, qmap, tmap_k, tmap_mn, pmap_mn, lmap_k, smap_mn,
                                                              dmap_mn, ga);
   note_launch();
-  return cudaGetLastError();
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if (layer) {
+    gdn_chunk_head_finish<<<1, 128, 0, st>>>(a.n_chunks, a.Hv, w.head_part, a.dA_log, a.ddt_bias);
+    note_launch();
+    e = cudaGetLastError();
+  }
+  return e;
 }
 
 }  // namespace qbgdn

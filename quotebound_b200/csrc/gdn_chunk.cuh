@@ -5,6 +5,8 @@
 
 namespace qbgdn {
 
+// g == nullptr selects layer mode: q, k are the raw (pre-norm) rows and the gates come from
+// a, b, A_log, dt_bias (the norm and gate graph of src/deltanet.cpp:113-119 fused into the kernels).
 struct ChunkFwdArgs {
   int B, T, Hk, Hv, Dk, Dv, N;
   int64_t n_chunks;
@@ -15,8 +17,10 @@ struct ChunkFwdArgs {
   float* hT;
   void* saved;
   int in_bf16, out_bf16;
+  const float *a_raw, *b_raw, *A_log, *dt_bias;
 };
 
+// Layer mode as above: dg, dbeta then receive da, db, and dA_log, ddt_bias the head sums.
 struct ChunkBwdArgs {
   int B, T, Hk, Hv, Dk, Dv, N;
   int64_t n_chunks;
@@ -27,15 +31,18 @@ struct ChunkBwdArgs {
   void *dq, *dk, *dv;
   float *dg, *dbeta, *dh0;
   int in_bf16, out_bf16;
+  const float *a_raw, *b_raw, *A_log, *dt_bias;
+  float *dA_log, *ddt_bias;
 };
 
 bool chunked_supported(int Dk, int Dv);
 // Whether the backward has its own chunked kernels; until then a chunked forward's saved buffer starts
 // with the row-parallel backward's chunk-start states and that backward runs.
 bool chunked_bwd_ready();
-int64_t chunked_saved_bytes(int Hv, int Dk, int Dv, int64_t n_chunks, int64_t tokens);
-int64_t chunked_ws_bytes(int Hv, int Hk, int Dk, int Dv, int N, int64_t n_chunks, int64_t tokens, bool varlen, int op,
-                         bool with_saved);
+// layer: the saved buffer / workspace of the layer-mode path (adds the normalised q, k rows)
+int64_t chunked_saved_bytes(int Hv, int Hk, int64_t n_chunks, int64_t tokens, bool layer);
+int64_t chunked_ws_bytes(int Hv, int Hk, int N, int64_t n_chunks, int64_t tokens, bool varlen, int op, bool with_saved,
+                         bool layer);
 cudaError_t chunked_fwd(const ChunkFwdArgs& a, void* ws, cudaStream_t st);
 cudaError_t chunked_bwd(const ChunkBwdArgs& a, void* ws, cudaStream_t st);
 

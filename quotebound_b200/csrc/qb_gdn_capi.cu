@@ -108,7 +108,7 @@ int check_desc(const qb_gdn_desc* d, Plan* p, char* err, int errlen) {
 }
 
 int64_t saved_bytes_of(const qb_gdn_desc* d, const Plan& p) {
-  if (p.chunked) return chunked_saved_bytes(d->Hv, d->Dk, d->Dv, p.n_chunks, p.tokens);
+  if (p.chunked) return chunked_saved_bytes(d->Hv, d->Hk, p.n_chunks, p.tokens, false);
   return p.n_chunks * d->Hv * (int64_t)d->Dv * d->Dk * 4;
 }
 
@@ -141,8 +141,7 @@ int64_t simt_ws_bytes(const qb_gdn_desc* d, const Plan& p, int op, bool with_sav
       w.saved = (float*)take(saved_bytes_of(d, p));
       // recomputing with the chunked forward needs that forward's own workspace too
       if (p.chunked)
-        w.fwd_ws = take(chunked_ws_bytes(d->Hv, d->Hk, d->Dk, d->Dv, p.N, p.n_chunks, p.tokens, p.varlen, QB_OP_FWD,
-                                         false));
+        w.fwd_ws = take(chunked_ws_bytes(d->Hv, d->Hk, p.N, p.n_chunks, p.tokens, p.varlen, QB_OP_FWD, false, false));
     }
   }
   if (out) *out = w;
@@ -154,7 +153,7 @@ bool chunked_bwd_of(const Plan& p) { return p.chunked && chunked_bwd_ready(); }
 
 int64_t ws_bytes_of(const qb_gdn_desc* d, const Plan& p, int op, bool with_saved) {
   if (op == QB_OP_FWD ? p.chunked : chunked_bwd_of(p))
-    return chunked_ws_bytes(d->Hv, d->Hk, d->Dk, d->Dv, p.N, p.n_chunks, p.tokens, p.varlen, op, with_saved);
+    return chunked_ws_bytes(d->Hv, d->Hk, p.N, p.n_chunks, p.tokens, p.varlen, op, with_saved, false);
   return simt_ws_bytes(d, p, op, with_saved, nullptr, nullptr);
 }
 
@@ -166,12 +165,94 @@ const char* qb_gdn_version(void) { return "qb_gdn 0.1 (sm_100a)"; }
 
 int64_t qb_gdn_launches(void) { return launches(); }
 
+static int check_layer(const qb_gdn_desc* d, Plan* p, char* err, int errlen) {
+  if (check_desc(d, p, err, errlen)) return -1;
+  if (!p->chunked)
+    return fail(err, errlen,
+                "gated delta layer: the fused norm/gate path runs on the chunked kernels: needs Dk = Dv = 128, bf16 "
+                "activations and algo AUTO or CHUNKED (Dk %d, Dv %d, in_dtype %d, algo %d)",
+                d->Dk, d->Dv, d->in_dtype, d->algo);
+  if (d->Hv > 4096) return fail(err, errlen, "gated delta layer: too many value heads (%d)", d->Hv);
+  return 0;
+}
+
 int64_t qb_gdn_workspace_bytes(const qb_gdn_desc* d, int32_t op, char* err, int errlen) {
   Plan p;
+  if (op == QB_OP_LAYER_FWD || op == QB_OP_LAYER_BWD) {
+    if (check_layer(d, &p, err, errlen)) return -1;
+    return chunked_ws_bytes(d->Hv, d->Hk, p.N, p.n_chunks, p.tokens, p.varlen, op == QB_OP_LAYER_FWD ? 0 : 1,
+                            op == QB_OP_LAYER_BWD, true);
+  }
   if (check_desc(d, &p, err, errlen)) return -1;
   if (op != QB_OP_FWD && op != QB_OP_BWD) return fail(err, errlen, "gated delta: unknown op %d", op);
   // the backward's figure covers recomputing the saved states (saved == NULL)
   return ws_bytes_of(d, p, op, op == QB_OP_BWD);
+}
+
+int64_t qb_gdn_layer_saved_bytes(const qb_gdn_desc* d, char* err, int errlen) {
+  Plan p;
+  if (check_layer(d, &p, err, errlen)) return -1;
+  return chunked_saved_bytes(d->Hv, d->Hk, p.n_chunks, p.tokens, true);
+}
+
+int qb_gdn_layer_fwd(const qb_gdn_desc* d, const void* q, const void* k, const void* v, const float* a, const float* b,
+                     const float* A_log, const float* dt_bias, const float* h0, void* y, float* hT, void* saved,
+                     void* ws, int64_t ws_bytes, void* stream, char* err, int errlen) {
+  Plan p;
+  if (check_layer(d, &p, err, errlen)) return -1;
+  if (!q || !k || !v || !a || !b || !A_log || !dt_bias || !y)
+    return fail(err, errlen, "gated delta layer forward: q, k, v, a, b, A_log, dt_bias and y must be non-null");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(y, 16) || (h0 && !aligned(h0, 16)) ||
+      (hT && !aligned(hT, 16)) || (saved && !aligned(saved, 256)))
+    return fail(err, errlen, "gated delta layer forward: q, k, v, y, h0, hT need 16-byte alignment and saved 256-byte");
+  const int64_t need = chunked_ws_bytes(d->Hv, d->Hk, p.N, p.n_chunks, p.tokens, p.varlen, 0, false, true);
+  if (!ws || ws_bytes < need || !aligned(ws, 256))
+    return fail(err, errlen, "gated delta layer forward: a 256-byte aligned workspace of %lld bytes is needed (got %lld)",
+                (long long)need, (long long)ws_bytes);
+  if (p.tokens == 0) return 0;
+  ChunkFwdArgs f{};
+  f.B = d->B, f.T = d->T, f.Hk = d->Hk, f.Hv = d->Hv, f.Dk = d->Dk, f.Dv = d->Dv, f.N = p.N, f.n_chunks = p.n_chunks;
+  f.cu = d->cu_seqlens, f.q = q, f.k = k, f.v = v, f.h0 = h0, f.y = y, f.hT = hT, f.saved = saved;
+  f.in_bf16 = 1, f.out_bf16 = d->out_dtype == QB_DTYPE_BF16;
+  f.a_raw = a, f.b_raw = b, f.A_log = A_log, f.dt_bias = dt_bias;
+  cudaError_t e = chunked_fwd(f, ws, (cudaStream_t)stream);
+  return e == cudaSuccess ? 0 : cuda_fail(e, "gated delta layer forward", err, errlen);
+}
+
+int qb_gdn_layer_bwd(const qb_gdn_desc* d, const void* q, const void* k, const void* v, const float* a, const float* b,
+                     const float* A_log, const float* dt_bias, const float* h0, const void* dy, const float* dhT,
+                     const void* saved, void* dq, void* dk, void* dv, float* da, float* db, float* dA_log,
+                     float* ddt_bias, float* dh0, void* ws, int64_t ws_bytes, void* stream, char* err, int errlen) {
+  Plan p;
+  if (check_layer(d, &p, err, errlen)) return -1;
+  if (!q || !k || !v || !a || !b || !A_log || !dt_bias || !dy || !dq || !dk || !dv || !da || !db || !dA_log ||
+      !ddt_bias)
+    return fail(err, errlen, "gated delta layer backward: inputs and every gradient except dh0 must be non-null");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(dy, 16) || !aligned(dq, 16) ||
+      !aligned(dk, 16) || !aligned(dv, 16) || (h0 && !aligned(h0, 16)) || (dhT && !aligned(dhT, 16)) ||
+      (dh0 && !aligned(dh0, 16)) || (saved && !aligned(saved, 256)))
+    return fail(err, errlen, "gated delta layer backward: tensors need 16-byte alignment and saved 256-byte");
+  const int64_t need = chunked_ws_bytes(d->Hv, d->Hk, p.N, p.n_chunks, p.tokens, p.varlen, 1, saved == nullptr, true);
+  if (!ws || ws_bytes < need || !aligned(ws, 256))
+    return fail(err, errlen, "gated delta layer backward: a 256-byte aligned workspace of %lld bytes is needed (got %lld)",
+                (long long)need, (long long)ws_bytes);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (p.tokens == 0) {
+    cudaError_t e = cudaMemsetAsync(dA_log, 0, d->Hv * 4, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(ddt_bias, 0, d->Hv * 4, st);
+    if (e == cudaSuccess && dh0)
+      e = dhT ? cudaMemcpyAsync(dh0, dhT, (size_t)p.N * d->Hv * d->Dv * d->Dk * 4, cudaMemcpyDeviceToDevice, st)
+              : cudaMemsetAsync(dh0, 0, (size_t)p.N * d->Hv * d->Dv * d->Dk * 4, st);
+    return e == cudaSuccess ? 0 : cuda_fail(e, "gated delta layer backward", err, errlen);
+  }
+  ChunkBwdArgs x{};
+  x.B = d->B, x.T = d->T, x.Hk = d->Hk, x.Hv = d->Hv, x.Dk = d->Dk, x.Dv = d->Dv, x.N = p.N, x.n_chunks = p.n_chunks;
+  x.cu = d->cu_seqlens, x.q = q, x.k = k, x.v = v, x.dy = dy, x.h0 = h0, x.dhT = dhT, x.saved = saved;
+  x.dq = dq, x.dk = dk, x.dv = dv, x.dg = da, x.dbeta = db, x.dh0 = dh0;
+  x.in_bf16 = 1, x.out_bf16 = d->out_dtype == QB_DTYPE_BF16;
+  x.a_raw = a, x.b_raw = b, x.A_log = A_log, x.dt_bias = dt_bias, x.dA_log = dA_log, x.ddt_bias = ddt_bias;
+  cudaError_t e = chunked_bwd(x, ws, st);
+  return e == cudaSuccess ? 0 : cuda_fail(e, "gated delta layer backward", err, errlen);
 }
 
 int64_t qb_gdn_saved_bytes(const qb_gdn_desc* d, char* err, int errlen) {
