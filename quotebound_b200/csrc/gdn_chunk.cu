@@ -165,8 +165,45 @@ __device__ __forceinline__ void store_row32<float>(float* p, const float (&v)[32
   for (int q = 0; q < 8; ++q) *reinterpret_cast<float4*>(p + 4 * q) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
 }
 
+// 16-wide versions (half of a 32-column slice).
+struct Row16 {
+  uint4 w[2];
+};
+__device__ __forceinline__ void cvt_row16(const Row16& r, float (&v)[16]) {
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const uint32_t w[4] = {r.w[q].x, r.w[q].y, r.w[q].z, r.w[q].w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[e]);
+      v[8 * q + 2 * e] = __low2float(h);
+      v[8 * q + 2 * e + 1] = __high2float(h);
+    }
+  }
+}
+template <typename Tout>
+__device__ __forceinline__ void store_row16(Tout* p, const float (&v)[16]);
+template <>
+__device__ __forceinline__ void store_row16<__nv_bfloat16>(__nv_bfloat16* p, const float (&v)[16]) {
+#pragma unroll
+  for (int q = 0; q < 2; ++q)
+    *reinterpret_cast<uint4*>(p + 8 * q) =
+        make_uint4(tc::pack_bf16(v[8 * q], v[8 * q + 1]), tc::pack_bf16(v[8 * q + 2], v[8 * q + 3]),
+                   tc::pack_bf16(v[8 * q + 4], v[8 * q + 5]), tc::pack_bf16(v[8 * q + 6], v[8 * q + 7]));
+}
+template <>
+__device__ __forceinline__ void store_row16<float>(float* p, const float (&v)[16]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) *reinterpret_cast<float4*>(p + 4 * q) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+}
+
 __device__ __forceinline__ float softplus_f(float x) { return fmaxf(x, 0.f) + log1pf(expf(-fabsf(x))); }
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
+
+// Row of chunk row i (0..63) in a stacked [hi; lo] operand image of 128 rows: groups of 16 rows
+// alternate hi, lo, so that an M = 128 accumulator holds row i's hi product in lane 32w + l and its lo
+// product in lane 32w + 16 + l (i = 16w + l), the lanes of one warp.
+__device__ __forceinline__ int img_row(int i) { return 32 * (i >> 4) + (i & 15); }
 
 __device__ __forceinline__ bool wait_all(uint64_t* bar, uint32_t parity, int* err, int code) {
   return __syncthreads_and(tc::mbar_wait(bar, parity, err, code)) != 0;
@@ -182,8 +219,11 @@ struct PrepArgs {
   // layer mode (g, beta null): the raw gate inputs and the raw q, k rows normalised here
   const float *a_raw, *b_raw, *A_log, *dt_bias;
   __nv_bfloat16 *qn, *kn;   // normalised q, k written here [B*T, Hk, Dk] (layer mode)
-  float* Tbuf;      // [chunks, Hv, 64, 64]  T = (I + L)^-1, tf32-rounded
-  float* Pbuf;      // [chunks, Hv, 64, 64]  P, tf32-rounded
+  float* Tbuf;      // [chunks, Hv, 64, 64]  T = (I + L)^-1, tf32-rounded (training only), or null
+  float* Pbuf;      // [chunks, Hv, 64, 64]  P, tf32-rounded (training only), or null
+  uint8_t* Timg;    // [chunks, Hv] x 16 KB: T as the stacked bf16 [T_hi; T_lo] operand image
+  uint8_t* Pimg;    // [chunks, Hv] x 16 KB: P likewise
+  uint8_t* KQimg;   // [chunks, Hk] x 32 KB: the walk's [K; Q] operand (16-row groups interleaved)
   float* Lbuf;      // [chunks, Hv, 64, 64]  strict-lower Gamma * K K^T (training only), or null
   float* gates;     // [chunks, Hv, 2, 64]:  b then beta
   int* err;
@@ -283,7 +323,7 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CU
       if (store) {  // the normalised row in logical order for the walks and the gradient kernel
         __nv_bfloat16* dst = (m == 0 ? a.kn : a.qn) + ((tok0 + row) * a.geo.Hk + hk) * (size_t)DK + 64 * half;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) reinterpret_cast<uint4*>(dst)[c] = w[c ^ (row & 7)];
+        for (int c = 0; c < 8; ++c) reinterpret_cast<uint4*>(dst)[c ^ (row & 7)] = w[c];
       }
     }
     tc::fence_async_smem();
@@ -296,12 +336,27 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CU
     tc::mma_tile<tc::kBF16>(tmem + 64, qt, false, 64, kt, false, 64, 64, 64, DK, false);   // Q K^T
     tc::mma_commit(&bar_mma);
   }
+  if (ok && hv % (a.geo.Hv / a.geo.Hk) == 0) {
+    // the [K; Q] image of this chunk and key head: per 64-column slab, 2 KB row groups K 0-15, Q 0-15,
+    // K 16-31, ... (the swizzle is address-relative within 1 KB, so whole groups move unchanged)
+    uint4* dst = reinterpret_cast<uint4*>(a.KQimg + (size_t)(c * a.geo.Hk + hk) * 32768);
+#pragma unroll 4
+    for (int u = 0; u < 16; ++u) {
+      const int idx = tid + 128 * u, o = idx * 16;
+      const int sl = o >> 14, g = (o >> 12) & 3, part = (o >> 11) & 1, rem = o & 2047;
+      dst[idx] = *reinterpret_cast<const uint4*>((part ? qtile : ktile) + sl * 8192 + g * 2048 + rem);
+    }
+  }
   ok = __syncthreads_and(ok && tc::mbar_wait(&bar_mma, 0, a.err, 2)) != 0;
   tc::fence_after_sync();
   const size_t mat = (size_t)(c * a.geo.Hv + hv) * 4096;
+  // The K and Q tiles are free once the products above completed: they stage the T and P images.
+  uint8_t* timg = ktile;
+  uint8_t* pimg = qtile;
   if (ok) {
     const int i = 16 * warp + (lane & 15);
     const bool owner = lane < 16;
+    const int rh = img_row(i);
     const float bi = sb[i], be = sbeta[i];
     float v[32];
 #pragma unroll
@@ -323,9 +378,14 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CU
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) {
           const int j = 32 * h + jj;
-          v[jj] = tf32_rna(j <= i ? __expf(bi - sb[j]) * v[jj] : 0.f);
+          v[jj] = j <= i ? __expf(bi - sb[j]) * v[jj] : 0.f;
         }
-        store_row32<float>(a.Pbuf + mat + i * 64 + 32 * h, v);
+        tc::st_row_bf16x2_32(pimg, pimg + 2048, rh, v, 4 * h);
+        if (a.Pbuf) {
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) v[jj] = tf32_rna(v[jj]);
+          store_row32<float>(a.Pbuf + mat + i * 64 + 32 * h, v);
+        }
       }
     }
   }
@@ -343,13 +403,35 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CU
       for (int j = 0; j < i; ++j) s = fmaf(-Li[j], t[j], s);
       t[i] = s;
     }
-    // T feeds tf32 MMAs: round to nearest here rather than let the operand read drop bits
-    float* dst = a.Tbuf + mat;
+    // the image: hi and lo halves of column col
 #pragma unroll
-    for (int i = 0; i < 64; ++i) dst[i * 64 + col] = tf32_rna(t[i]);
+    for (int i = 0; i < 64; ++i) {
+      const int r = img_row(i);
+      const uint32_t off = r * 128 + ((((col >> 3) ^ (r & 7))) << 4) + (col & 7) * 2;
+      const __nv_bfloat16 hi = __float2bfloat16_rn(t[i]);
+      *reinterpret_cast<__nv_bfloat16*>(timg + off) = hi;
+      *reinterpret_cast<__nv_bfloat16*>(timg + off + 2048) = __float2bfloat16_rn(t[i] - __bfloat162float(hi));
+    }
+    // T feeds tf32 MMAs in the backward: round to nearest here rather than let the operand read drop bits
+    if (a.Tbuf) {
+      float* dst = a.Tbuf + mat;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) dst[i * 64 + col] = tf32_rna(t[i]);
+    }
     float* gd = a.gates + (c * a.geo.Hv + hv) * 128;
     gd[tid] = sb[tid];
     gd[64 + tid] = sbeta[tid];
+  }
+  __syncthreads();
+  if (ok) {  // both images out, 16-byte stores
+    uint4* td = reinterpret_cast<uint4*>(a.Timg + mat * 4);
+    uint4* pd = reinterpret_cast<uint4*>(a.Pimg + mat * 4);
+#pragma unroll 4
+    for (int u = 0; u < 8; ++u) {
+      const int idx = tid + 128 * u;
+      td[idx] = reinterpret_cast<const uint4*>(timg)[idx];
+      pd[idx] = reinterpret_cast<const uint4*>(pimg)[idx];
+    }
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -367,159 +449,192 @@ struct StateArgs {
   void* y;                // [B*T, Hv, Dv]
   float* hT;              // or null
   float* ckpt;            // [chunks, Hv, Dv, Dk] chunk-start states, or null
+  const uint8_t* Timg;    // [chunks, Hv] x 16 KB operand images from the prep
+  const uint8_t* Pimg;
+  const uint8_t* KQimg;   // [chunks, Hk] x 32 KB
   int* err;
 };
 
 // Shared memory of the forward walk (bytes from a 1024-aligned base).
-constexpr int FW_K = 0;            // 2 x 16 KB bf16 K (TMA)
-constexpr int FW_Q = 32768;        // 2 x 16 KB bf16 Q (TMA)
-constexpr int FW_T = 65536;        // 2 x 16 KB fp32 T, K-major (TMA)
-constexpr int FW_P = 98304;        // 2 x 16 KB fp32 P, K-major (TMA)
-constexpr int FW_SHI = 131072;     // 16 KB bf16 state hi, MN-major [128 dk][32 dv]
-constexpr int FW_SLO = 147456;     // 16 KB bf16 state lo
-constexpr int FW_E = 163840;       // 8 KB fp32 E, MN-major [64][32]
-constexpr int FW_D = 172032;       // 8 KB fp32 D, MN-major [64][32]
-constexpr int FW_DHI = 180224;     // 8 KB bf16 D~ hi, MN-major [64][32]
-constexpr int FW_DLO = 188416;     // 8 KB bf16 D~ lo
+constexpr int FW_KQ = 0;           // 2 x 32 KB bf16 [K; Q] tile, 16-row groups interleaved (TMA)
+constexpr int FW_T = 65536;        // 2 x 16 KB bf16 [T_hi; T_lo] image (bulk copy)
+constexpr int FW_P = 98304;        // 2 x 16 KB bf16 [P_hi; P_lo] image (bulk copy)
+constexpr int FW_S = 131072;       // 16 KB bf16 state [hi | lo], MN-major [128 dk][64]
+constexpr int FW_E = 147456;       // 8 KB bf16 E [hi | lo], MN-major [64][64]
+constexpr int FW_D = 155648;       // 8 KB bf16 D [hi | lo]
+constexpr int FW_DT = 163840;      // 8 KB bf16 D~ = diag(lambda) D [hi | lo]
+constexpr int FW_CK = 172032;      // 16 KB fp32 chunk-start state staging [32 dv][128 dk] (bulk store)
+constexpr int FW_V = 188416;       // 2 x 4 KB bf16 value rows [64][32] (TMA)
 constexpr int FW_SMEM = 196608 + 1024;
 
+// Descriptors of the stacked operands.  The [K; Q] tile holds, per 64-column slab (16 KB), the row
+// groups K 0-15, Q 0-15, K 16-31, Q 16-31, ... (2 KB each).
+// K-step ks of K^T (or Q^T with part = 1) as the M = 128 (dk) MN-major A operand; chunk rows are K.
+__device__ __forceinline__ uint64_t desc_kq_t(uint32_t kq, int part, int ks) {
+  return tc::sdesc(kq + part * 2048 + ks * 4096, 16384, 1024, 2);
+}
+// K-step ks of an N = 64 MN-major [hi | lo] operand (128-byte rows, one per K index).
+__device__ __forceinline__ uint64_t desc_hl(uint32_t tile, int ks) { return tc::sdesc(tile + ks * 2048, 8192, 1024, 2); }
+
+// A operand forms of mma_run: the M = 128 K-major tiles ([K; Q] and the [hi; lo] images), K^T, Q^T.
+enum AForm { kKmaj128 = 0, kKT = 1, kQT = 2 };
+// D (+)= A B over KSTEPS bf16 K-steps of 16, B an N = 64 [hi | lo] MN-major tile.
+template <int KSTEPS, int AFORM>
+__device__ __forceinline__ void mma_run(uint32_t d, uint32_t id, uint32_t a, uint32_t b, bool accumulate) {
+#pragma unroll
+  for (int ks = 0; ks < KSTEPS; ++ks) {
+    const uint64_t ad = AFORM == kKmaj128 ? tc::desc_kmajor(a, 128, ks) : desc_kq_t(a, AFORM == kQT ? 1 : 0, ks);
+    tc::mma_bf16(d, ad, desc_hl(b, ks), id, (accumulate || ks > 0) ? 1u : 0u);
+  }
+}
+
+// This thread's 16 columns (16 half ..) of both N halves of a [hi | lo] accumulator, summed.
+__device__ __forceinline__ void tmem_ld_hl16(uint32_t taddr, int half, float (&x)[16]) {
+  float u[16];
+  tc::tmem_ld16(taddr + 16 * half, x);
+  tc::tmem_ld16(taddr + 32 + 16 * half, u);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) x[j] += u[j];
+}
+// The same, then the hi-row and lo-row products of lanes l and l + 16 summed (both lanes get the sum).
+__device__ __forceinline__ void tmem_ld_hl16_pair(uint32_t taddr, int half, float (&x)[16]) {
+  tmem_ld_hl16(taddr, half, x);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) x[j] += __shfl_xor_sync(0xffffffffu, x[j], 16);
+}
+
+// 256 threads: warp w reads TMEM lanes 32 (w & 3) .. + 31 and handles the value columns
+// 16 (w >> 2) .. + 15 of the CTA's 32; thread t holds S[dv0 + 16 (w >> 2) + j][t & 127].
 template <typename Tout>
-__global__ void __launch_bounds__(128, 1) gdn_chunk_fwd_state(const __grid_constant__ CUtensorMap kmap,
-                                                              const __grid_constant__ CUtensorMap qmap,
-                                                              const __grid_constant__ CUtensorMap tmap,
-                                                              const __grid_constant__ CUtensorMap pmap,
-                                                              StateArgs a) {
+__global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_constant__ CUtensorMap vmap, StateArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ float sg[2][128];
+  __shared__ __align__(16) float sg[2][128];
   __shared__ uint64_t bar_tma[2], bar_mma;
   __shared__ uint32_t tmem_slot;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, half = warp >> 2, dk = tid & 127;
   const int dv0 = blockIdx.x * DVT, hv = blockIdx.y, n = blockIdx.z;
   const int Hv = a.geo.Hv, hk = hv / (Hv / a.geo.Hk);
   int64_t c_first, nchunks, seq0, seq1;
   seq_chunks(a.geo, n, c_first, nchunks, seq0, seq1);
 
-  const uint32_t cR = 0, cY = 32, cD = 64, cO = 96, cS = 128;
+  // TMEM: [K; Q] S^T 0, D 64, S update 128, P D 192 (64 columns each: hi and lo halves)
+  const uint32_t cA = 0, cD = 64, cS = 128, cO = 192;
   if (warp == 0) tc::tmem_alloc(&tmem_slot, 256);
   if (tid == 0) {
     tc::mbar_init(&bar_tma[0], 1);
     tc::mbar_init(&bar_tma[1], 1);
     tc::mbar_init(&bar_mma, 1);
     tc::fence_mbar_init();
-    tc::prefetch_tmap(&kmap);
-    tc::prefetch_tmap(&qmap);
-    tc::prefetch_tmap(&tmap);
-    tc::prefetch_tmap(&pmap);
   }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = tmem_slot;
+  const uint32_t tl = tc::taddr(tmem, 32 * quad, 0);  // this warp's lanes
 
-  float s[DVT];  // s[j] = S[dv0 + j][tid]
+  float s[16];  // s[j] = S[dv0 + 16 half + j][dk]
   {
-    const size_t base = ((size_t)n * Hv + hv) * DV * DK;
+    const size_t base = (((size_t)n * Hv + hv) * DV + dv0 + 16 * half) * DK + dk;
 #pragma unroll
-    for (int j = 0; j < DVT; ++j) s[j] = a.h0 ? a.h0[base + (size_t)(dv0 + j) * DK + tid] : 0.f;
+    for (int j = 0; j < 16; ++j) s[j] = a.h0 ? a.h0[base + (size_t)j * DK] : 0.f;
   }
 
+  // One thread of warp 1 moves everything a chunk reads (the [K; Q], T and P images, the gates and the
+  // value rows) and the checkpoint, so that warp 0's thread issues the MMAs meanwhile and no thread
+  // waits on a global load inside the walk.
   auto issue_loads = [&](int64_t jc, int buf) {
-    const int64_t tok = seq0 + jc * C;
-    const int mrow = (int)(((c_first + jc) * Hv + hv) * 64);
-    tc::mbar_arrive_expect_tx(&bar_tma[buf], 16384 * 4);
-    tc::tma_load_3d(smem + FW_K + buf * 16384, &kmap, &bar_tma[buf], 0, hk, (int)tok);
-    tc::tma_load_3d(smem + FW_K + buf * 16384 + 8192, &kmap, &bar_tma[buf], 64, hk, (int)tok);
-    tc::tma_load_3d(smem + FW_Q + buf * 16384, &qmap, &bar_tma[buf], 0, hk, (int)tok);
-    tc::tma_load_3d(smem + FW_Q + buf * 16384 + 8192, &qmap, &bar_tma[buf], 64, hk, (int)tok);
-    tc::tma_load_2d(smem + FW_T + buf * 16384, &tmap, &bar_tma[buf], 0, mrow);
-    tc::tma_load_2d(smem + FW_T + buf * 16384 + 8192, &tmap, &bar_tma[buf], 32, mrow);
-    tc::tma_load_2d(smem + FW_P + buf * 16384, &pmap, &bar_tma[buf], 0, mrow);
-    tc::tma_load_2d(smem + FW_P + buf * 16384 + 8192, &pmap, &bar_tma[buf], 32, mrow);
+    const int64_t cg = c_first + jc;
+    tc::mbar_arrive_expect_tx(&bar_tma[buf], 32768 + 2 * 16384 + 512 + 4096);
+    tc::bulk_load(smem + FW_KQ + buf * 32768, a.KQimg + (size_t)(cg * a.geo.Hk + hk) * 32768, 32768, &bar_tma[buf]);
+    tc::bulk_load(smem + FW_T + buf * 16384, a.Timg + (size_t)(cg * Hv + hv) * 16384, 16384, &bar_tma[buf]);
+    tc::bulk_load(smem + FW_P + buf * 16384, a.Pimg + (size_t)(cg * Hv + hv) * 16384, 16384, &bar_tma[buf]);
+    tc::bulk_load(sg[buf], a.gates + (cg * Hv + hv) * 128, 512, &bar_tma[buf]);
+    tc::tma_load_3d(smem + FW_V + buf * 4096, &vmap, &bar_tma[buf], dv0, hv, (int)(seq0 + jc * C));
   };
 
-  const int i_row = 16 * warp + (lane & 15);  // row of the M = 64 accumulators this thread reads
-  const bool row_owner = lane < 16;
-  const __nv_bfloat16* vbase = static_cast<const __nv_bfloat16*>(a.v) + (size_t)hv * DV + dv0;
-  Row32 vraw;  // this thread's value row of the current chunk, loaded one chunk ahead
-  if (nchunks > 0) {
-    if (tid == 0) issue_loads(0, 0);
-    sg[0][tid] = a.gates[(c_first * Hv + hv) * 128 + tid];
-    ldg_row32(vbase + (seq0 + i_row) * Hv * (size_t)DV, row_owner && i_row < min((int64_t)C, seq1 - seq0), vraw);
+  // Lane l < 16 owns chunk row i = 16 quad + l for the K-side products (E, D) and lane l + 16 the same
+  // row for the Q-side ones (Y, D~, y).
+  const int i_row = 16 * quad + (lane & 15);
+  const bool kside = lane < 16;
+  if (nchunks > 0 && tid == 32) {
+    tc::prefetch_tmap(&vmap);
+    issue_loads(0, 0);
   }
   uint32_t ph = 0;
   bool ok = true;
+  const uint32_t idA = tc::idesc(tc::kBF16, 128, 64, false, true);
+  const uint32_t idT = tc::idesc(tc::kBF16, 128, 64, true, true);
 
   for (int64_t jc = 0; jc < nchunks && ok; ++jc) {
     const int buf = (int)(jc & 1);
     const int64_t cg = c_first + jc;
     const int64_t tok0 = seq0 + jc * C;
     const int L = (int)min((int64_t)C, seq1 - tok0);
-    // the next chunk's value row and gates, consumed next iteration
-    Row32 vnext;
-    float gnext = 0.f;
-    {
-      const bool more = jc + 1 < nchunks;
-      const int64_t tn = tok0 + C;
-      ldg_row32(vbase + (tn + i_row) * Hv * (size_t)DV, more && row_owner && i_row < min((int64_t)C, seq1 - tn),
-                vnext);
-      if (more) gnext = __ldg(a.gates + ((cg + 1) * Hv + hv) * 128 + tid);
-    }
 
-    // 1. the chunk-start state: saved for the backward, split into the bf16 hi/lo operand (row tid)
+    // 1. the chunk-start state: staged for the bulk store of the checkpoint, and as the [hi | lo]
+    //    operand row dk
     if (a.ckpt) {
-      float* dst = a.ckpt + ((cg * Hv + hv) * DV + dv0) * (size_t)DK + tid;
+      float* ck = reinterpret_cast<float*>(smem + FW_CK) + 16 * half * DK + dk;
 #pragma unroll
-      for (int j = 0; j < DVT; ++j) dst[(size_t)j * DK] = s[j];
+      for (int j = 0; j < 16; ++j) ck[j * DK] = s[j];
     }
-    tc::st_row_bf16x2_32(smem + FW_SHI, smem + FW_SLO, tid, s);
-    // 2. this thread's value row (rows past the end read as zero)
-    float vr[DVT];
-    cvt_row32(vraw, vr);
-    // 3. tiles of this chunk
+    tc::st_row_hilo16(smem + FW_S, dk, s, half);
     tc::fence_async_smem();
     tc::fence_before_sync();
     ok = wait_all(&bar_tma[buf], (uint32_t)((jc >> 1) & 1), a.err, 10);
     tc::fence_after_sync();
     if (!ok) break;
-    if (jc + 1 < nchunks && tid == 0) issue_loads(jc + 1, buf ^ 1);  // the next chunk's tiles
-    const uint32_t kt = tc::smem_u32(smem + FW_K + buf * 16384);
-    const uint32_t qt = tc::smem_u32(smem + FW_Q + buf * 16384);
-    // 4. R = K S^T, Y = Q S^T (S split hi + lo, MN-major: dk rows)
+    const uint32_t kq = tc::smem_u32(smem + FW_KQ + buf * 32768);
+    // 2. [K; Q] S^T in one pass (M = 128, N = 64: the state's hi and lo halves)
     if (tid == 0) {
-      const uint32_t shi = tc::smem_u32(smem + FW_SHI), slo = tc::smem_u32(smem + FW_SLO);
-      tc::mma_tile<tc::kBF16>(tmem + cR, kt, false, 64, shi, true, DK, 64, DVT, DK, false);
-      tc::mma_tile<tc::kBF16>(tmem + cR, kt, false, 64, slo, true, DK, 64, DVT, DK, true);
-      tc::mma_tile<tc::kBF16>(tmem + cY, qt, false, 64, shi, true, DK, 64, DVT, DK, false);
-      tc::mma_tile<tc::kBF16>(tmem + cY, qt, false, 64, slo, true, DK, 64, DVT, DK, true);
+      mma_run<8, kKmaj128>(tmem + cA, idA, kq, tc::smem_u32(smem + FW_S), false);
       tc::mma_commit(&bar_mma);
+    }
+    if (tid == 32) {
+      if (a.ckpt) {
+        tc::bulk_store(a.ckpt + ((cg * Hv + hv) * DV + dv0) * (size_t)DK, smem + FW_CK, DVT * DK * 4);
+        tc::bulk_commit();
+      }
+      if (jc + 1 < nchunks) issue_loads(jc + 1, buf ^ 1);  // the next chunk's tiles
+    }
+    const float* gb = sg[buf];
+    const float bi = gb[i_row], be = gb[64 + i_row], gi = __expf(bi), bC = gb[63];
+    float vr[16];  // this row's values (rows past the sequence's end read as zero)
+    {
+      Row16 raw;
+      const uint4* vp = reinterpret_cast<const uint4*>(smem + FW_V + buf * 4096 + i_row * 64 + 32 * half);
+      raw.w[0] = i_row < L ? vp[0] : make_uint4(0, 0, 0, 0);
+      raw.w[1] = i_row < L ? vp[1] : make_uint4(0, 0, 0, 0);
+      cvt_row16(raw, vr);
     }
     ok = wait_all(&bar_mma, ph, a.err, 11);
     ph ^= 1;
     tc::fence_after_sync();
     if (!ok) break;
-    const float* gb = sg[buf];
-    const float bi = gb[i_row], be = gb[64 + i_row], gi = __expf(bi), bC = gb[63];
-    float yp[DVT];
+    // 3. K side: E = diag(beta) (V - diag(gamma) K S^T) as the [hi | lo] operand; Q side: gamma Q S^T
+    float yp[16];
     {
-      float r[32];
-      tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cR), r);
+      tmem_ld_hl16(tl + cA, half, yp);
+      if (kside) {
+        float e[16];
 #pragma unroll
-      for (int j = 0; j < DVT; ++j) r[j] = tf32_rna(be * (vr[j] - gi * r[j]));
-      if (row_owner) tc::st_row_mn_f32(smem + FW_E, i_row, r);
-      tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cY), yp);
+        for (int j = 0; j < 16; ++j) e[j] = be * (vr[j] - gi * yp[j]);
+        tc::st_row_hilo16(smem + FW_E, i_row, e, half);
+      } else {
 #pragma unroll
-      for (int j = 0; j < DVT; ++j) yp[j] *= gi;
+        for (int j = 0; j < 16; ++j) yp[j] *= gi;
+      }
     }
     tc::fence_async_smem();
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
-    // 5. D = T E
+    // 4. D = T E  ([T_hi; T_lo] stacked: row i's two products in lanes l and l + 16)
     if (tid == 0) {
-      tc::mma_tile<tc::kTF32>(tmem + cD, tc::smem_u32(smem + FW_T + buf * 16384), false, 64,
-                              tc::smem_u32(smem + FW_E), true, 64, 64, DVT, C, false);
+      mma_run<4, kKmaj128>(tmem + cD, idA, tc::smem_u32(smem + FW_T + buf * 16384), tc::smem_u32(smem + FW_E), false);
       tc::mma_commit(&bar_mma);
     }
     ok = wait_all(&bar_mma, ph, a.err, 12);
@@ -527,30 +642,26 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_fwd_state(const __grid_const
     tc::fence_after_sync();
     if (!ok) break;
     {
-      float d[32];
-      tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cD), d);
-      if (row_owner) {
-        const float sc = __expf(bC - bi);
-        float dd[32];
+      float d[16];
+      tmem_ld_hl16_pair(tl + cD, half, d);
+      if (kside) {
+        tc::st_row_hilo16(smem + FW_D, i_row, d, half);
+      } else {
+        const float lam = __expf(bC - bi);
 #pragma unroll
-        for (int j = 0; j < DVT; ++j) {
-          dd[j] = sc * d[j];
-          d[j] = tf32_rna(d[j]);
-        }
-        tc::st_row_mn_f32(smem + FW_D, i_row, d);
-        tc::st_row_bf16x2_32(smem + FW_DHI, smem + FW_DLO, i_row, dd);
+        for (int j = 0; j < 16; ++j) d[j] *= lam;
+        tc::st_row_hilo16(smem + FW_DT, i_row, d, half);
       }
     }
+    if (tid == 32 && a.ckpt) tc::bulk_wait_read();  // the staging buffer is rewritten next chunk
     tc::fence_async_smem();
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
-    // 6. O2 = P D;  S_upd^T = K^T D~ (K as the MN-major A operand: Dk rows, chunk steps as K)
+    // 5. S update^T = K^T D~ (M = 128 dk rows);  O2 = P D ([P_hi; P_lo] stacked)
     if (tid == 0) {
-      tc::mma_tile<tc::kTF32>(tmem + cO, tc::smem_u32(smem + FW_P + buf * 16384), false, 64,
-                              tc::smem_u32(smem + FW_D), true, 64, 64, DVT, C, false);
-      tc::mma_tile<tc::kBF16>(tmem + cS, kt, true, 64, tc::smem_u32(smem + FW_DHI), true, 64, 128, DVT, C, false);
-      tc::mma_tile<tc::kBF16>(tmem + cS, kt, true, 64, tc::smem_u32(smem + FW_DLO), true, 64, 128, DVT, C, true);
+      mma_run<4, kKT>(tmem + cS, idT, kq, tc::smem_u32(smem + FW_DT), false);
+      mma_run<4, kKmaj128>(tmem + cO, idA, tc::smem_u32(smem + FW_P + buf * 16384), tc::smem_u32(smem + FW_D), false);
       tc::mma_commit(&bar_mma);
     }
     ok = wait_all(&bar_mma, ph, a.err, 13);
@@ -558,28 +669,25 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_fwd_state(const __grid_const
     tc::fence_after_sync();
     if (!ok) break;
     {
-      float u[32];
-      tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cS), u);
+      float u[16];
+      tmem_ld_hl16(tl + cS, half, u);
       const float gC = __expf(bC);
 #pragma unroll
-      for (int j = 0; j < DVT; ++j) s[j] = fmaf(gC, s[j], u[j]);
-      tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cO), u);
-      if (row_owner && i_row < L) {
+      for (int j = 0; j < 16; ++j) s[j] = fmaf(gC, s[j], u[j]);
+      tmem_ld_hl16_pair(tl + cO, half, u);
+      if (!kside && i_row < L) {
 #pragma unroll
-        for (int j = 0; j < DVT; ++j) u[j] += yp[j];
-        store_row32<Tout>(static_cast<Tout*>(a.y) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0, u);
+        for (int j = 0; j < 16; ++j) u[j] += yp[j];
+        store_row16<Tout>(static_cast<Tout*>(a.y) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0 + 16 * half, u);
       }
     }
-    // the other gate buffer was last read before this chunk's first barrier; the next reads follow
-    // the next chunk's first barrier
-    sg[buf ^ 1][tid] = gnext;
-    vraw = vnext;
     tc::fence_before_sync();
   }
+  if (tid == 32) tc::bulk_wait();
   if (ok && a.hT) {
-    float* dst = a.hT + (((size_t)n * Hv + hv) * DV + dv0) * DK + tid;
+    float* dst = a.hT + (((size_t)n * Hv + hv) * DV + dv0 + 16 * half) * DK + dk;
 #pragma unroll
-    for (int j = 0; j < DVT; ++j) dst[(size_t)j * DK] = s[j];
+    for (int j = 0; j < 16; ++j) dst[(size_t)j * DK] = s[j];
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -1291,15 +1399,29 @@ EncodeTiled encode_fn() {
 }
 
 // [rows, heads, dim] bf16 activations; box = 64 columns x 1 head x 64 rows, 128-byte swizzle.
-bool map_act(CUtensorMap* m, const void* base, int64_t rows, int heads, int dim) {
+bool map_act(CUtensorMap* m, const void* base, int64_t rows, int heads, int dim, int box_rows = 64) {
   EncodeTiled f = encode_fn();
   if (!f) return false;
   cuuint64_t dims[3] = {(cuuint64_t)dim, (cuuint64_t)heads, (cuuint64_t)rows};
   cuuint64_t strides[2] = {(cuuint64_t)dim * 2, (cuuint64_t)heads * dim * 2};
-  cuuint32_t box[3] = {64, 1, 64};
+  cuuint32_t box[3] = {64, 1, (cuuint32_t)box_rows};
   cuuint32_t es[3] = {1, 1, 1};
   return f(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// bf16 rows [rows, heads, dim] read as unswizzled boxes of box_cols x box_rows of one head (the
+// value or output-gradient rows of a chunk); rows past the end read as zero.
+bool map_rows(CUtensorMap* m, const void* base, int64_t rows, int heads, int dim, int box_cols, int box_rows) {
+  EncodeTiled f = encode_fn();
+  if (!f) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)dim, (cuuint64_t)heads, (cuuint64_t)rows};
+  cuuint64_t strides[2] = {(cuuint64_t)dim * 2, (cuuint64_t)heads * dim * 2};
+  cuuint32_t box[3] = {(cuuint32_t)box_cols, 1, (cuuint32_t)box_rows};
+  cuuint32_t es[3] = {1, 1, 1};
+  return f(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -1334,14 +1456,15 @@ bool map_state_mn(CUtensorMap* m, const void* base, int64_t rows) {
 
 int64_t a256(int64_t x) { return (x + 255) & ~int64_t(255); }
 
-// The chunk intermediates: [ckpt][T][P][Gamma*KK][gates] fp32, and in layer mode the normalised
-// [kn][qn] bf16 rows.
+// The chunk intermediates: [ckpt][T][P][Gamma*KK][gates] fp32, the forward's T and P operand images,
+// and in layer mode the normalised [kn][qn] bf16 rows.
 struct Saved {
   float *ckpt, *T, *P, *L, *gates;
+  uint8_t *Timg, *Pimg, *KQimg;
   __nv_bfloat16 *kn, *qn;
 };
 
-int64_t saved_layout(int Hv, int64_t n_chunks, int64_t qk_elems, char* base, Saved* s) {
+int64_t saved_layout(int Hv, int Hk, int64_t n_chunks, int64_t qk_elems, char* base, Saved* s) {
   int64_t off = 0;
   auto take = [&](int64_t bytes) {
     char* at = base ? base + off : nullptr;
@@ -1354,19 +1477,23 @@ int64_t saved_layout(int Hv, int64_t n_chunks, int64_t qk_elems, char* base, Sav
   x.P = (float*)take(n_chunks * Hv * 4096 * 4);
   x.L = (float*)take(n_chunks * Hv * 4096 * 4);
   x.gates = (float*)take(n_chunks * Hv * 128 * 4);
+  x.Timg = (uint8_t*)take(n_chunks * Hv * 16384);
+  x.Pimg = (uint8_t*)take(n_chunks * Hv * 16384);
+  x.KQimg = (uint8_t*)take(n_chunks * Hk * 32768);
   x.kn = (__nv_bfloat16*)take(qk_elems * 2);
   x.qn = (__nv_bfloat16*)take(qk_elems * 2);
   if (s) *s = x;
   return off;
 }
 
-// Workspace: [chunk_off][err][fwd: T, P, gates (and kn, qn in layer mode) when nothing is saved |
-// bwd: dS per chunk, per-chunk head sums (layer mode), and a saved buffer plus forward workspace when
-// the backward recomputes].
+// Workspace: [chunk_off][err][fwd: T and P images, gates (and kn, qn in layer mode) when nothing is
+// saved | bwd: dS per chunk, per-chunk head sums (layer mode), and a saved buffer plus forward
+// workspace when the backward recomputes].
 struct Ws {
   int64_t* chunk_off;
   int* err;
-  float *T, *P, *gates;
+  uint8_t *Timg, *Pimg, *KQimg;
+  float* gates;
   __nv_bfloat16 *kn, *qn;
   float* dsbuf;
   float* head_part;
@@ -1374,8 +1501,8 @@ struct Ws {
   char* fwd_ws;
 };
 
-int64_t ws_layout(int Hv, int N, int64_t n_chunks, int64_t qk_elems, bool varlen, int op, bool with_saved, char* base,
-                  Ws* w) {
+int64_t ws_layout(int Hv, int Hk, int N, int64_t n_chunks, int64_t qk_elems, bool varlen, int op, bool with_saved,
+                  char* base, Ws* w) {
   int64_t off = 0;
   auto take = [&](int64_t bytes) {
     char* at = base ? base + off : nullptr;
@@ -1386,8 +1513,9 @@ int64_t ws_layout(int Hv, int N, int64_t n_chunks, int64_t qk_elems, bool varlen
   x.chunk_off = (int64_t*)take(varlen ? (int64_t)(N + 1) * 8 : 0);
   x.err = (int*)take(16);
   if (op == 0) {
-    x.T = (float*)take(n_chunks * Hv * 4096 * 4);
-    x.P = (float*)take(n_chunks * Hv * 4096 * 4);
+    x.Timg = (uint8_t*)take(n_chunks * Hv * 16384);
+    x.Pimg = (uint8_t*)take(n_chunks * Hv * 16384);
+    x.KQimg = (uint8_t*)take(n_chunks * Hk * 32768);
     x.gates = (float*)take(n_chunks * Hv * 128 * 4);
     x.kn = (__nv_bfloat16*)take(qk_elems * 2);
     x.qn = (__nv_bfloat16*)take(qk_elems * 2);
@@ -1395,8 +1523,8 @@ int64_t ws_layout(int Hv, int N, int64_t n_chunks, int64_t qk_elems, bool varlen
     x.dsbuf = (float*)take(n_chunks * Hv * (int64_t)DV * DK * 4);
     x.head_part = (float*)take(qk_elems ? n_chunks * Hv * 2 * 4 : 0);
     if (with_saved) {
-      x.saved = take(saved_layout(Hv, n_chunks, qk_elems, nullptr, nullptr));
-      x.fwd_ws = take(ws_layout(Hv, N, n_chunks, qk_elems, varlen, 0, false, nullptr, nullptr));
+      x.saved = take(saved_layout(Hv, Hk, n_chunks, qk_elems, nullptr, nullptr));
+      x.fwd_ws = take(ws_layout(Hv, Hk, N, n_chunks, qk_elems, varlen, 0, false, nullptr, nullptr));
     }
   }
   if (w) *w = x;
@@ -1409,12 +1537,12 @@ bool chunked_supported(int Dk, int Dv) { return Dk == DK && Dv == DV && encode_f
 bool chunked_bwd_ready() { return true; }
 
 int64_t chunked_saved_bytes(int Hv, int Hk, int64_t n_chunks, int64_t tokens, bool layer) {
-  return saved_layout(Hv, n_chunks, layer ? tokens * Hk * DK : 0, nullptr, nullptr);
+  return saved_layout(Hv, Hk, n_chunks, layer ? tokens * Hk * DK : 0, nullptr, nullptr);
 }
 
 int64_t chunked_ws_bytes(int Hv, int Hk, int N, int64_t n_chunks, int64_t tokens, bool varlen, int op, bool with_saved,
                          bool layer) {
-  return ws_layout(Hv, N, n_chunks, layer ? tokens * Hk * DK : 0, varlen, op, with_saved, nullptr, nullptr);
+  return ws_layout(Hv, Hk, N, n_chunks, layer ? tokens * Hk * DK : 0, varlen, op, with_saved, nullptr, nullptr);
 }
 
 cudaError_t chunked_fwd(const ChunkFwdArgs& a, void* ws, cudaStream_t st) {
@@ -1422,25 +1550,24 @@ cudaError_t chunked_fwd(const ChunkFwdArgs& a, void* ws, cudaStream_t st) {
   const bool layer = a.g == nullptr;
   const int64_t rows = (int64_t)a.B * a.T, qk = layer ? rows * a.Hk * DK : 0;
   Ws w;
-  ws_layout(a.Hv, a.N, a.n_chunks, qk, a.cu != nullptr, 0, false, (char*)ws, &w);
+  ws_layout(a.Hv, a.Hk, a.N, a.n_chunks, qk, a.cu != nullptr, 0, false, (char*)ws, &w);
   Saved sv{};
-  float *Tb = w.T, *Pb = w.P, *gates = w.gates, *ckpt = nullptr, *Lb = nullptr;
+  float *Tb = nullptr, *Pb = nullptr, *gates = w.gates, *ckpt = nullptr, *Lb = nullptr;
+  uint8_t *Ti = w.Timg, *Pi = w.Pimg, *KQi = w.KQimg;
   __nv_bfloat16 *kn = w.kn, *qn = w.qn;
   if (a.saved) {
-    saved_layout(a.Hv, a.n_chunks, qk, (char*)a.saved, &sv);
+    saved_layout(a.Hv, a.Hk, a.n_chunks, qk, (char*)a.saved, &sv);
     Tb = sv.T, Pb = sv.P, gates = sv.gates, ckpt = sv.ckpt, Lb = sv.L, kn = sv.kn, qn = sv.qn;
+    Ti = sv.Timg, Pi = sv.Pimg, KQi = sv.KQimg;
   }
   cudaError_t e;
   if ((e = cudaMemsetAsync(w.err, 0, 16, st)) != cudaSuccess) return e;
   if (a.cu && (e = launch_chunk_offsets(a.cu, a.N, w.chunk_off, st)) != cudaSuccess) return e;
-  const int64_t mrows = a.n_chunks * a.Hv * 64;
-  CUtensorMap kmap, qmap, tmap, pmap;
-  if (!map_act(&kmap, a.k, rows, a.Hk, a.Dk) || !map_act(&qmap, a.q, rows, a.Hk, a.Dk) ||
-      !map_f32_64(&tmap, Tb, mrows, false) || !map_f32_64(&pmap, Pb, mrows, false))
-    return cudaErrorInvalidValue;
+  CUtensorMap kmap, qmap;
+  if (!map_act(&kmap, a.k, rows, a.Hk, a.Dk) || !map_act(&qmap, a.q, rows, a.Hk, a.Dk)) return cudaErrorInvalidValue;
   Geo geo{a.T, a.Hk, a.Hv, a.N, (a.T + C - 1) / C, a.cu, a.cu ? w.chunk_off : nullptr};
   if (a.n_chunks > 0) {
-    PrepArgs pa{geo, a.g, a.beta, a.a_raw, a.b_raw, a.A_log, a.dt_bias, qn, kn, Tb, Pb, Lb, gates, w.err};
+    PrepArgs pa{geo, a.g, a.beta, a.a_raw, a.b_raw, a.A_log, a.dt_bias, qn, kn, Tb, Pb, Ti, Pi, KQi, Lb, gates, w.err};
     const int prep_smem = 1024 + 32768 + 64 * 68 * 4;
     if ((e = cudaFuncSetAttribute(gdn_chunk_prep, cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem)) !=
         cudaSuccess)
@@ -1449,12 +1576,12 @@ cudaError_t chunked_fwd(const ChunkFwdArgs& a, void* ws, cudaStream_t st) {
     note_launch();
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
-  if (layer && (!map_act(&kmap, kn, rows, a.Hk, a.Dk) || !map_act(&qmap, qn, rows, a.Hk, a.Dk)))
-    return cudaErrorInvalidValue;  // the walk reads the normalised rows
-  StateArgs sa{geo, a.v, gates, a.h0, a.y, a.hT, ckpt, w.err};
+  CUtensorMap vmap;
+  if (!map_rows(&vmap, a.v, rows, a.Hv, a.Dv, DVT, C)) return cudaErrorInvalidValue;
+  StateArgs sa{geo, a.v, gates, a.h0, a.y, a.hT, ckpt, Ti, Pi, KQi, w.err};
   auto kern = a.out_bf16 ? gdn_chunk_fwd_state<__nv_bfloat16> : gdn_chunk_fwd_state<float>;
   if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FW_SMEM)) != cudaSuccess) return e;
-  kern<<<dim3(DV / DVT, a.Hv, a.N), 128, FW_SMEM, st>>>(kmap, qmap, tmap, pmap, sa);
+  kern<<<dim3(DV / DVT, a.Hv, a.N), 256, FW_SMEM, st>>>(vmap, sa);
   note_launch();
   return cudaGetLastError();
 }
@@ -1464,7 +1591,7 @@ cudaError_t chunked_bwd(const ChunkBwdArgs& a, void* ws, cudaStream_t st) {
   const bool layer = a.g == nullptr;
   const int64_t rows = (int64_t)a.B * a.T, qk = layer ? rows * a.Hk * DK : 0;
   Ws w;
-  ws_layout(a.Hv, a.N, a.n_chunks, qk, a.cu != nullptr, 1, a.saved == nullptr, (char*)ws, &w);
+  ws_layout(a.Hv, a.Hk, a.N, a.n_chunks, qk, a.cu != nullptr, 1, a.saved == nullptr, (char*)ws, &w);
   cudaError_t e;
   const void* saved = a.saved;
   if (!saved) {  // recompute the forward's intermediates with the same forward (y is discarded into dv)
@@ -1477,7 +1604,7 @@ cudaError_t chunked_bwd(const ChunkBwdArgs& a, void* ws, cudaStream_t st) {
     saved = w.saved;
   }
   Saved sv;
-  saved_layout(a.Hv, a.n_chunks, qk, (char*)saved, &sv);
+  saved_layout(a.Hv, a.Hk, a.n_chunks, qk, (char*)saved, &sv);
   if ((e = cudaMemsetAsync(w.err, 0, 16, st)) != cudaSuccess) return e;
   if (a.cu && (e = launch_chunk_offsets(a.cu, a.N, w.chunk_off, st)) != cudaSuccess) return e;
   const int64_t mrows = a.n_chunks * a.Hv * 64;

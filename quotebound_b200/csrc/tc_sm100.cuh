@@ -247,7 +247,8 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 // Used for K-major rows and MN-major rows alike: the byte pattern is the same.  c0 = 4 writes the
 // elements 32..63 of a 64-wide row.
 __device__ __forceinline__ void st_row_bf16x2_32(uint8_t* hi_slab, uint8_t* lo_slab, int r, const float (&v)[32],
-                                                 int c0 = 0) {
+                                                 int c0 = 0, int lo_c0 = -1) {
+  const int lc0 = lo_c0 < 0 ? c0 : lo_c0;
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     uint32_t h[4], l[4];
@@ -258,11 +259,53 @@ __device__ __forceinline__ void st_row_bf16x2_32(uint8_t* hi_slab, uint8_t* lo_s
       h[e] = *reinterpret_cast<const uint32_t*>(&hh);
       l[e] = pack_bf16(a - __low2float(hh), b - __high2float(hh));
     }
-    const int off = r * 128 + (((c + c0) ^ (r & 7)) << 4);
-    *reinterpret_cast<uint4*>(hi_slab + off) = make_uint4(h[0], h[1], h[2], h[3]);
-    *reinterpret_cast<uint4*>(lo_slab + off) = make_uint4(l[0], l[1], l[2], l[3]);
+    *reinterpret_cast<uint4*>(hi_slab + r * 128 + (((c + c0) ^ (r & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(lo_slab + r * 128 + (((c + lc0) ^ (r & 7)) << 4)) = make_uint4(l[0], l[1], l[2], l[3]);
   }
 }
+
+// One 128-byte row [hi of 32 | lo of 32]: the N = 64 operand row whose two halves the MMA multiplies
+// in one instruction (the halves' products are summed by the reader of the accumulator).
+__device__ __forceinline__ void st_row_hilo(uint8_t* tile, int r, const float (&v)[32]) {
+  st_row_bf16x2_32(tile, tile, r, v, 0, 4);
+}
+
+// Half of such a row: 16 floats (columns 16 half .. 16 half + 15 of each 32-wide half) as hi chunks
+// 2 half, 2 half + 1 and lo chunks 4 + 2 half, 5 + 2 half.
+__device__ __forceinline__ void st_row_hilo16(uint8_t* tile, int r, const float (&v)[16], int half) {
+  uint8_t* row = tile + r * 128;
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float a = v[8 * c + 2 * e], b = v[8 * c + 2 * e + 1];
+      const __nv_bfloat162 hh = __floats2bfloat162_rn(a, b);
+      h[e] = *reinterpret_cast<const uint32_t*>(&hh);
+      l[e] = pack_bf16(a - __low2float(hh), b - __high2float(hh));
+    }
+    *reinterpret_cast<uint4*>(row + (((2 * half + c) ^ (r & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(row + (((4 + 2 * half + c) ^ (r & 7)) << 4)) = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+}
+
+// ---- bulk (non-tensor) copies: contiguous bytes, 16-byte aligned addresses and sizes ---------------
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(dst)),
+               "r"(smem_u32(src)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// the shared-memory sources of every committed bulk store have been read
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// every committed bulk store has completed
+__device__ __forceinline__ void bulk_wait() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 }  // namespace tc
 }  // namespace qbgdn
