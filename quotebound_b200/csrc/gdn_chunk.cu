@@ -704,91 +704,92 @@ struct BwdStateArgs {
   void* dv;               // [B*T, Hv, Dv]
   float* dh0;             // or null
   float* dsbuf;           // [chunks, Hv, Dv, Dk]: cotangent of each chunk's end state
+  const uint8_t* Timg;    // the forward's operand images
+  const uint8_t* Pimg;
+  const uint8_t* KQimg;
   int* err;
 };
 
-constexpr int BW_K = 0;            // 2 x 16 KB bf16 K
-constexpr int BW_Q = 32768;        // 2 x 16 KB bf16 Q
-constexpr int BW_T = 65536;        // 2 x 16 KB fp32 T, MN-major tf32 layout (as T^T)
-constexpr int BW_P = 98304;        // 2 x 16 KB fp32 P, MN-major tf32 layout (as P^T)
-constexpr int BW_SHI = 131072;     // 16 KB bf16 dS hi, MN-major [128 dk][32 dv]
-constexpr int BW_SLO = 147456;     // 16 KB bf16 dS lo
-constexpr int BW_DO = 163840;      // 8 KB fp32 dO, MN-major [64][32]
-constexpr int BW_GHI = 172032;     // 8 KB bf16 gamma dO hi, MN-major
-constexpr int BW_GLO = 180224;     // 8 KB bf16 gamma dO lo
-constexpr int BW_DD = 188416;      // 8 KB fp32 dD, MN-major
-constexpr int BW_HHI = 196608;     // 8 KB bf16 H = -beta gamma F hi, MN-major
-constexpr int BW_HLO = 204800;     // 8 KB bf16 H lo
-constexpr int BW_SMEM = 212992 + 1024;
+constexpr int BW_KQ = 0;           // 2 x 32 KB bf16 [K; Q] image
+constexpr int BW_T = 65536;        // 2 x 16 KB bf16 [T_hi; T_lo] image
+constexpr int BW_P = 98304;        // 2 x 16 KB bf16 [P_hi; P_lo] image
+constexpr int BW_S = 131072;       // 16 KB bf16 dS [hi | lo], MN-major [128 dk][64]
+constexpr int BW_DO = 147456;      // 8 KB bf16 dO, MN-major [64][32] (128-byte rows, half used)
+constexpr int BW_GD = 155648;      // 8 KB bf16 gamma dO [hi | lo]
+constexpr int BW_DD = 163840;      // 8 KB bf16 dD [hi | lo]
+constexpr int BW_H = 172032;       // 8 KB bf16 H = -beta gamma F [hi | lo]
+constexpr int BW_CK = 180224;      // 16 KB fp32 dS staging [32 dv][128 dk] (bulk store)
+constexpr int BW_V = 196608;       // 2 x 4 KB bf16 dO rows [64][32] (TMA)
+constexpr int BW_SMEM = 204800 + 1024;
 
+// K-step ks of the transpose of one half (part 0 = hi, 1 = lo) of a [hi; lo] image as the M = 64
+// MN-major A operand: the image's rows (chunk steps) are K.
+__device__ __forceinline__ uint64_t desc_img_t(uint32_t img, int part, int ks) {
+  return tc::sdesc(img + part * 2048 + ks * 4096, 8192, 1024, 2);
+}
+
+// The backward state walk: chunks in reverse, 32 rows of dS per CTA, 256 threads as in the forward walk
+// (thread t holds dS[dv0 + 16 (w >> 2) + j][t & 127]).
 template <typename Tout>
-__global__ void __launch_bounds__(128, 1) gdn_chunk_bwd_state(const __grid_constant__ CUtensorMap kmap,
-                                                              const __grid_constant__ CUtensorMap qmap,
-                                                              const __grid_constant__ CUtensorMap tmap_mn,
-                                                              const __grid_constant__ CUtensorMap pmap_mn,
+__global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_constant__ CUtensorMap dmap,
                                                               BwdStateArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ float sg[2][128];
+  __shared__ __align__(16) float sg[2][128];
   __shared__ uint64_t bar_tma[2], bar_mma;
   __shared__ uint32_t tmem_slot;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, half = warp >> 2, dk = tid & 127;
   const int dv0 = blockIdx.x * DVT, hv = blockIdx.y, n = blockIdx.z;
   const int Hv = a.geo.Hv, hk = hv / (Hv / a.geo.Hk);
   int64_t c_first, nchunks, seq0, seq1;
   seq_chunks(a.geo, n, c_first, nchunks, seq0, seq1);
 
-  const uint32_t cX = 0, cG = 32, cF = 64, cU = 96;
-  if (warp == 0) tc::tmem_alloc(&tmem_slot, 128);
+  // TMEM: [K; Q] dS^T 0 (64), P^T dO 64 (32), F 128 (64), U 192 (64)
+  const uint32_t cX = 0, cG = 64, cF = 128, cU = 192;
+  if (warp == 0) tc::tmem_alloc(&tmem_slot, 256);
   if (tid == 0) {
     tc::mbar_init(&bar_tma[0], 1);
     tc::mbar_init(&bar_tma[1], 1);
     tc::mbar_init(&bar_mma, 1);
     tc::fence_mbar_init();
-    tc::prefetch_tmap(&kmap);
-    tc::prefetch_tmap(&qmap);
-    tc::prefetch_tmap(&tmap_mn);
-    tc::prefetch_tmap(&pmap_mn);
   }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = tmem_slot;
+  const uint32_t tl = tc::taddr(tmem, 32 * quad, 0);
 
-  float ds[DVT];  // ds[j] = dS[dv0 + j][tid]
+  float ds[16];  // ds[j] = dS[dv0 + 16 half + j][dk]
   {
-    const size_t base = ((size_t)n * Hv + hv) * DV * DK;
+    const size_t base = (((size_t)n * Hv + hv) * DV + dv0 + 16 * half) * DK + dk;
 #pragma unroll
-    for (int j = 0; j < DVT; ++j) ds[j] = a.dhT ? a.dhT[base + (size_t)(dv0 + j) * DK + tid] : 0.f;
+    for (int j = 0; j < 16; ++j) ds[j] = a.dhT ? a.dhT[base + (size_t)j * DK] : 0.f;
   }
 
   auto issue_loads = [&](int64_t jc, int buf) {
-    const int64_t tok = seq0 + jc * C;
-    const int mrow = (int)(((c_first + jc) * Hv + hv) * 64);
-    tc::mbar_arrive_expect_tx(&bar_tma[buf], 16384 * 4);
-    tc::tma_load_3d(smem + BW_K + buf * 16384, &kmap, &bar_tma[buf], 0, hk, (int)tok);
-    tc::tma_load_3d(smem + BW_K + buf * 16384 + 8192, &kmap, &bar_tma[buf], 64, hk, (int)tok);
-    tc::tma_load_3d(smem + BW_Q + buf * 16384, &qmap, &bar_tma[buf], 0, hk, (int)tok);
-    tc::tma_load_3d(smem + BW_Q + buf * 16384 + 8192, &qmap, &bar_tma[buf], 64, hk, (int)tok);
-    tc::tma_load_2d(smem + BW_T + buf * 16384, &tmap_mn, &bar_tma[buf], 0, mrow);
-    tc::tma_load_2d(smem + BW_T + buf * 16384 + 8192, &tmap_mn, &bar_tma[buf], 32, mrow);
-    tc::tma_load_2d(smem + BW_P + buf * 16384, &pmap_mn, &bar_tma[buf], 0, mrow);
-    tc::tma_load_2d(smem + BW_P + buf * 16384 + 8192, &pmap_mn, &bar_tma[buf], 32, mrow);
+    const int64_t cg = c_first + jc;
+    tc::mbar_arrive_expect_tx(&bar_tma[buf], 32768 + 2 * 16384 + 512 + 4096);
+    tc::bulk_load(smem + BW_KQ + buf * 32768, a.KQimg + (size_t)(cg * a.geo.Hk + hk) * 32768, 32768, &bar_tma[buf]);
+    tc::bulk_load(smem + BW_T + buf * 16384, a.Timg + (size_t)(cg * Hv + hv) * 16384, 16384, &bar_tma[buf]);
+    tc::bulk_load(smem + BW_P + buf * 16384, a.Pimg + (size_t)(cg * Hv + hv) * 16384, 16384, &bar_tma[buf]);
+    tc::bulk_load(sg[buf], a.gates + (cg * Hv + hv) * 128, 512, &bar_tma[buf]);
+    tc::tma_load_3d(smem + BW_V + buf * 4096, &dmap, &bar_tma[buf], dv0, hv, (int)(seq0 + jc * C));
   };
 
-  const int i_row = 16 * warp + (lane & 15);
-  const bool row_owner = lane < 16;
-  const __nv_bfloat16* dbase = static_cast<const __nv_bfloat16*>(a.dy) + (size_t)hv * DV + dv0;
-  Row32 draw;  // this thread's dO row of the current chunk, loaded one chunk ahead
-  if (nchunks > 0) {
-    if (tid == 0) issue_loads(nchunks - 1, 0);
-    sg[0][tid] = a.gates[((c_first + nchunks - 1) * Hv + hv) * 128 + tid];
-    const int64_t tl = seq0 + (nchunks - 1) * C;
-    ldg_row32(dbase + (tl + i_row) * Hv * (size_t)DV, row_owner && i_row < min((int64_t)C, seq1 - tl), draw);
+  const int i_row = 16 * quad + (lane & 15);
+  const bool kside = lane < 16;
+  if (nchunks > 0 && tid == 32) {
+    tc::prefetch_tmap(&dmap);
+    issue_loads(nchunks - 1, 0);
   }
   uint32_t ph = 0;
   bool ok = true;
+  const uint32_t idX = tc::idesc(tc::kBF16, 128, 64, false, true);  // [K; Q] x [hi | lo]
+  const uint32_t idG = tc::idesc(tc::kBF16, 64, 32, true, true);    // P^T x dO
+  const uint32_t idF = tc::idesc(tc::kBF16, 64, 64, true, true);    // T^T x [hi | lo]
+  const uint32_t idU = tc::idesc(tc::kBF16, 128, 64, true, true);   // Q^T, K^T x [hi | lo]
 
   for (int64_t it = 0; it < nchunks && ok; ++it) {
     const int64_t jc = nchunks - 1 - it;
@@ -796,72 +797,96 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_bwd_state(const __grid_const
     const int64_t cg = c_first + jc;
     const int64_t tok0 = seq0 + jc * C;
     const int L = (int)min((int64_t)C, seq1 - tok0);
-    Row32 dnext;  // the previous chunk's dO row and gates, consumed next iteration
-    float gnext = 0.f;
-    {
-      const bool more = jc > 0;
-      const int64_t tp = tok0 - C;
-      ldg_row32(dbase + (tp + i_row) * Hv * (size_t)DV, more && row_owner, dnext);
-      if (more) gnext = __ldg(a.gates + ((cg - 1) * Hv + hv) * 128 + tid);
-    }
 
-    // 1. dS of this chunk's end: saved for the gradient kernel, split into the hi/lo operand (row tid)
+    // 1. dS of this chunk's end: staged for the gradient kernel, and as the [hi | lo] operand row dk
     {
-      float* dst = a.dsbuf + ((cg * Hv + hv) * DV + dv0) * (size_t)DK + tid;
+      float* ck = reinterpret_cast<float*>(smem + BW_CK) + 16 * half * DK + dk;
 #pragma unroll
-      for (int j = 0; j < DVT; ++j) dst[(size_t)j * DK] = ds[j];
+      for (int j = 0; j < 16; ++j) ck[j * DK] = ds[j];
     }
-    tc::st_row_bf16x2_32(smem + BW_SHI, smem + BW_SLO, tid, ds);
-    // 2. dO row (zero past the end) as the fp32 operand of P^T dO, and gamma dO as bf16 hi/lo; the
-    // gates in sg[buf] were stored by other threads (before the loop, or at the end of the last chunk)
-    __syncthreads();
-    const float* gb = sg[buf];
-    const float bi = gb[i_row], be = gb[64 + i_row], gi = __expf(bi), bC = gb[63];
-    if (row_owner) {
-      float d[32];
-      cvt_row32(draw, d);
-      tc::st_row_mn_f32(smem + BW_DO, i_row, d);
-#pragma unroll
-      for (int j = 0; j < DVT; ++j) d[j] *= gi;
-      tc::st_row_bf16x2_32(smem + BW_GHI, smem + BW_GLO, i_row, d);
-    }
+    tc::st_row_hilo16(smem + BW_S, dk, ds, half);
     tc::fence_async_smem();
     tc::fence_before_sync();
     ok = wait_all(&bar_tma[buf], (uint32_t)((it >> 1) & 1), a.err, 20);
     tc::fence_after_sync();
     if (!ok) break;
-    if (jc > 0 && tid == 0) issue_loads(jc - 1, buf ^ 1);  // the previous chunk's tiles
-    const uint32_t kt = tc::smem_u32(smem + BW_K + buf * 16384);
-    const uint32_t qt = tc::smem_u32(smem + BW_Q + buf * 16384);
-    // 3. X1 = K dS^T (dS split hi + lo), G = P^T dO
-    if (tid == 0) {
-      tc::mma_tile<tc::kBF16>(tmem + cX, kt, false, 64, tc::smem_u32(smem + BW_SHI), true, DK, 64, DVT, DK, false);
-      tc::mma_tile<tc::kBF16>(tmem + cX, kt, false, 64, tc::smem_u32(smem + BW_SLO), true, DK, 64, DVT, DK, true);
-      tc::mma_tile<tc::kTF32>(tmem + cG, tc::smem_u32(smem + BW_P + buf * 16384), true, 64,
-                              tc::smem_u32(smem + BW_DO), true, 64, 64, DVT, C, false);
-      tc::mma_commit(&bar_mma);
+    if (tid == 32) {
+      tc::bulk_store(a.dsbuf + ((cg * Hv + hv) * DV + dv0) * (size_t)DK, smem + BW_CK, DVT * DK * 4);
+      tc::bulk_commit();
     }
-    ok = wait_all(&bar_mma, ph, a.err, 21);
-    ph ^= 1;
-    tc::fence_after_sync();
-    if (!ok) break;
+    const float* gb = sg[buf];
+    const float bi = gb[i_row], be = gb[64 + i_row], gi = __expf(bi), bC = gb[63];
+    // 2. dO row i (zero past the end): as the plain bf16 operand of P^T dO (K side) and as gamma dO
+    //    [hi | lo] (Q side)
     {
-      float x[32], g[32];
-      tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cX), x);
-      tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cG), g);
-      const float lam = __expf(bC - bi);
+      const uint4* vp = reinterpret_cast<const uint4*>(smem + BW_V + buf * 4096 + i_row * 64 + 32 * half);
+      const uint4 w0 = i_row < L ? vp[0] : make_uint4(0, 0, 0, 0);
+      const uint4 w1 = i_row < L ? vp[1] : make_uint4(0, 0, 0, 0);
+      if (kside) {
+        uint8_t* row = smem + BW_DO + i_row * 128;
+        *reinterpret_cast<uint4*>(row + (((2 * half) ^ (i_row & 7)) << 4)) = w0;
+        *reinterpret_cast<uint4*>(row + (((2 * half + 1) ^ (i_row & 7)) << 4)) = w1;
+      } else {
+        Row16 raw;
+        raw.w[0] = w0;
+        raw.w[1] = w1;
+        float d[16];
+        cvt_row16(raw, d);
 #pragma unroll
-      for (int j = 0; j < DVT; ++j) g[j] = tf32_rna(fmaf(lam, x[j], g[j]));
-      if (row_owner) tc::st_row_mn_f32(smem + BW_DD, i_row, g);
+        for (int j = 0; j < 16; ++j) d[j] *= gi;
+        tc::st_row_hilo16(smem + BW_GD, i_row, d, half);
+      }
     }
     tc::fence_async_smem();
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
-    // 4. F = T^T dD
+    const uint32_t kq = tc::smem_u32(smem + BW_KQ + buf * 32768);
+    const uint32_t pimg = tc::smem_u32(smem + BW_P + buf * 16384), timg = tc::smem_u32(smem + BW_T + buf * 16384);
+    // 3. [K; Q] dS^T (the K rows are X1 = K dS^T) and G = P^T dO (P_hi^T and P_lo^T accumulated)
     if (tid == 0) {
-      tc::mma_tile<tc::kTF32>(tmem + cF, tc::smem_u32(smem + BW_T + buf * 16384), true, 64,
-                              tc::smem_u32(smem + BW_DD), true, 64, 64, DVT, C, false);
+      mma_run<8, kKmaj128>(tmem + cX, idX, kq, tc::smem_u32(smem + BW_S), false);
+      const uint32_t dO = tc::smem_u32(smem + BW_DO);
+#pragma unroll
+      for (int part = 0; part < 2; ++part)
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          tc::mma_bf16(tmem + cG, desc_img_t(pimg, part, ks), desc_hl(dO, ks), idG, (part | ks) ? 1u : 0u);
+      tc::mma_commit(&bar_mma);
+    }
+    if (tid == 32) {
+      if (jc > 0) issue_loads(jc - 1, buf ^ 1);  // the previous chunk's tiles
+    }
+    ok = wait_all(&bar_mma, ph, a.err, 21);
+    ph ^= 1;
+    tc::fence_after_sync();
+    if (!ok) break;
+    // 4. dD = diag(lambda) K dS^T + P^T dO (K side), as the [hi | lo] operand.  tcgen05.ld is a
+    //    warp-wide aligned instruction: every lane executes the same loads, outside the branch.
+    {
+      float x[16], g[16];
+      tmem_ld_hl16(tl + cX, half, x);
+      tc::tmem_ld16(tl + cG + 16 * half, g);
+      if (kside) {
+        const float lam = __expf(bC - bi);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) x[j] = fmaf(lam, x[j], g[j]);
+        tc::st_row_hilo16(smem + BW_DD, i_row, x, half);
+      }
+    }
+    if (tid == 32) tc::bulk_wait_read();  // the staging buffer is rewritten next chunk
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    // 5. F = T^T dD (T_hi^T and T_lo^T accumulated; M = 64: row j in the K-side lanes)
+    if (tid == 0) {
+      const uint32_t dd = tc::smem_u32(smem + BW_DD);
+#pragma unroll
+      for (int part = 0; part < 2; ++part)
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          tc::mma_bf16(tmem + cF, desc_img_t(timg, part, ks), desc_hl(dd, ks), idF, (part | ks) ? 1u : 0u);
       tc::mma_commit(&bar_mma);
     }
     ok = wait_all(&bar_mma, ph, a.err, 22);
@@ -869,31 +894,29 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_bwd_state(const __grid_const
     tc::fence_after_sync();
     if (!ok) break;
     {
-      float f[32];
-      tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cF), f);
-      if (row_owner) {
-        float o[32];
+      float f[16];
+      tmem_ld_hl16(tl + cF, half, f);
+      if (kside) {
+        float o[16];
         if (i_row < L) {
 #pragma unroll
-          for (int j = 0; j < DVT; ++j) o[j] = be * f[j];
-          store_row32<Tout>(static_cast<Tout*>(a.dv) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0, o);
+          for (int j = 0; j < 16; ++j) o[j] = be * f[j];
+          store_row16<Tout>(static_cast<Tout*>(a.dv) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0 + 16 * half, o);
         }
         const float h = -be * gi;
 #pragma unroll
-        for (int j = 0; j < DVT; ++j) o[j] = h * f[j];
-        tc::st_row_bf16x2_32(smem + BW_HHI, smem + BW_HLO, i_row, o);
+        for (int j = 0; j < 16; ++j) o[j] = h * f[j];
+        tc::st_row_hilo16(smem + BW_H, i_row, o, half);
       }
     }
     tc::fence_async_smem();
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
-    // 5. U = Q^T (gamma dO) + K^T H (Q, K as MN-major A: Dk rows, chunk steps as K)
+    // 6. U = Q^T (gamma dO) + K^T H (M = 128 dk rows)
     if (tid == 0) {
-      tc::mma_tile<tc::kBF16>(tmem + cU, qt, true, 64, tc::smem_u32(smem + BW_GHI), true, 64, 128, DVT, C, false);
-      tc::mma_tile<tc::kBF16>(tmem + cU, qt, true, 64, tc::smem_u32(smem + BW_GLO), true, 64, 128, DVT, C, true);
-      tc::mma_tile<tc::kBF16>(tmem + cU, kt, true, 64, tc::smem_u32(smem + BW_HHI), true, 64, 128, DVT, C, true);
-      tc::mma_tile<tc::kBF16>(tmem + cU, kt, true, 64, tc::smem_u32(smem + BW_HLO), true, 64, 128, DVT, C, true);
+      mma_run<4, kQT>(tmem + cU, idU, kq, tc::smem_u32(smem + BW_GD), false);
+      mma_run<4, kKT>(tmem + cU, idU, kq, tc::smem_u32(smem + BW_H), true);
       tc::mma_commit(&bar_mma);
     }
     ok = wait_all(&bar_mma, ph, a.err, 23);
@@ -901,24 +924,23 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_bwd_state(const __grid_const
     tc::fence_after_sync();
     if (!ok) break;
     {
-      float u[32];
-      tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cU), u);
+      float u[16];
+      tmem_ld_hl16(tl + cU, half, u);
       const float gC = __expf(bC);
 #pragma unroll
-      for (int j = 0; j < DVT; ++j) ds[j] = fmaf(gC, ds[j], u[j]);
+      for (int j = 0; j < 16; ++j) ds[j] = fmaf(gC, ds[j], u[j]);
     }
-    sg[buf ^ 1][tid] = gnext;
-    draw = dnext;
     tc::fence_before_sync();
   }
+  if (tid == 32) tc::bulk_wait();
   if (ok && a.dh0) {
-    float* dst = a.dh0 + (((size_t)n * Hv + hv) * DV + dv0) * DK + tid;
+    float* dst = a.dh0 + (((size_t)n * Hv + hv) * DV + dv0 + 16 * half) * DK + dk;
 #pragma unroll
-    for (int j = 0; j < DVT; ++j) dst[(size_t)j * DK] = ds[j];
+    for (int j = 0; j < 16; ++j) dst[(size_t)j * DK] = ds[j];
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tmem, 128);
+  if (warp == 0) tc::tmem_dealloc(tmem, 256);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -1616,10 +1638,12 @@ cudaError_t chunked_bwd(const ChunkBwdArgs& a, void* ws, cudaStream_t st) {
       !map_f32_64(&pmap_mn, sv.P, mrows, true) || !map_f32_64(&lmap_k, sv.L, mrows, false))
     return cudaErrorInvalidValue;
   Geo geo{a.T, a.Hk, a.Hv, a.N, (a.T + C - 1) / C, a.cu, a.cu ? w.chunk_off : nullptr};
-  BwdStateArgs ba{geo, a.dy, sv.gates, a.dhT, a.dv, a.dh0, w.dsbuf, w.err};
+  CUtensorMap dmap;
+  if (!map_rows(&dmap, a.dy, rows, a.Hv, a.Dv, DVT, C)) return cudaErrorInvalidValue;
+  BwdStateArgs ba{geo, a.dy, sv.gates, a.dhT, a.dv, a.dh0, w.dsbuf, sv.Timg, sv.Pimg, sv.KQimg, w.err};
   auto k1 = a.out_bf16 ? gdn_chunk_bwd_state<__nv_bfloat16> : gdn_chunk_bwd_state<float>;
   if ((e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, BW_SMEM)) != cudaSuccess) return e;
-  k1<<<dim3(DV / DVT, a.Hv, a.N), 128, BW_SMEM, st>>>(kmap, qmap, tmap_mn, pmap_mn, ba);
+  k1<<<dim3(DV / DVT, a.Hv, a.N), 256, BW_SMEM, st>>>(dmap, ba);
   note_launch();
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   if (a.n_chunks == 0) {

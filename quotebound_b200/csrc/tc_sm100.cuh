@@ -55,13 +55,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait for the phase with the given parity to complete.  Gives up after ~2^22 polls (each
-// poll may itself suspend briefly), writes `code` into *err and returns false; the caller then
-// skips its remaining work, frees its TMEM and returns.  Never spins forever, never traps.
-constexpr uint32_t kMaxPolls = 1u << 22;
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait for the phase with the given parity to complete.  Gives up after about one second of
+// wall time (checked every 256 polls; each poll may itself suspend briefly) or 2^24 polls, writes
+// `code` into *err and returns false; the caller then skips its remaining work, frees its TMEM and
+// returns.  Never spins forever, never traps.
+constexpr uint32_t kMaxPolls = 1u << 24;
+constexpr uint64_t kMaxWaitNs = 1000000000ull;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
-  for (uint32_t i = 0; i < kMaxPolls; ++i)
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1; i < kMaxPolls; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255) == 0 && globaltimer_ns() - t0 > kMaxWaitNs) break;
+  }
   if (err) atomicExch(err, code);
   return false;
 }
