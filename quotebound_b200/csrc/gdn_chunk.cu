@@ -127,28 +127,6 @@ __device__ __forceinline__ void load_row32(const __nv_bfloat16* p, bool valid, f
   }
 }
 
-// The same row issued early as raw 16-byte loads and converted when it is needed, so the load's
-// latency overlaps the work in between.
-struct Row32 {
-  uint4 w[4];
-};
-__device__ __forceinline__ void ldg_row32(const __nv_bfloat16* p, bool valid, Row32& r) {
-#pragma unroll
-  for (int q = 0; q < 4; ++q) r.w[q] = valid ? __ldg(reinterpret_cast<const uint4*>(p) + q) : make_uint4(0, 0, 0, 0);
-}
-__device__ __forceinline__ void cvt_row32(const Row32& r, float (&v)[32]) {
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const uint32_t w[4] = {r.w[q].x, r.w[q].y, r.w[q].z, r.w[q].w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[e]);
-      v[8 * q + 2 * e] = __low2float(h);
-      v[8 * q + 2 * e + 1] = __high2float(h);
-    }
-  }
-}
-
 template <typename Tout>
 __device__ __forceinline__ void store_row32(Tout* p, const float (&v)[32]);
 template <>
@@ -218,9 +196,6 @@ struct PrepArgs {
   const float *g, *beta;
   // layer mode (g, beta null): the raw gate inputs and the raw q, k rows normalised here
   const float *a_raw, *b_raw, *A_log, *dt_bias;
-  __nv_bfloat16 *qn, *kn;   // normalised q, k written here [B*T, Hk, Dk] (layer mode)
-  float* Tbuf;      // [chunks, Hv, 64, 64]  T = (I + L)^-1, tf32-rounded (training only), or null
-  float* Pbuf;      // [chunks, Hv, 64, 64]  P, tf32-rounded (training only), or null
   uint8_t* Timg;    // [chunks, Hv] x 16 KB: T as the stacked bf16 [T_hi; T_lo] operand image
   uint8_t* Pimg;    // [chunks, Hv] x 16 KB: P likewise
   uint8_t* KQimg;   // [chunks, Hk] x 32 KB: the walk's [K; Q] operand (16-row groups interleaved)
@@ -286,7 +261,6 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CU
     // rounded to bf16, times the bf16 scalar 1/Dk (q) or 1/sqrt(Dk) (k), rounded again.  Thread t
     // owns half a row (one 128-byte slab row of 64 elements); the order inside a row does not matter.
     const int row = tid >> 1, half = tid & 1;
-    const bool store = hv % (a.geo.Hv / a.geo.Hk) == 0 && row < L;
 #pragma unroll
     for (int m = 0; m < 2; ++m) {
       uint8_t* tile = m == 0 ? ktile : qtile;
@@ -317,13 +291,7 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CU
           const float x1 = __bfloat162float(__float2bfloat16_rn(__high2float(h) * r)) * sc;
           u[e] = tc::pack_bf16(x0, x1);
         }
-        w[c] = make_uint4(u[0], u[1], u[2], u[3]);
-        r16[c] = w[c];
-      }
-      if (store) {  // the normalised row in logical order for the walks and the gradient kernel
-        __nv_bfloat16* dst = (m == 0 ? a.kn : a.qn) + ((tok0 + row) * a.geo.Hk + hk) * (size_t)DK + 64 * half;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) reinterpret_cast<uint4*>(dst)[c ^ (row & 7)] = w[c];
+        r16[c] = make_uint4(u[0], u[1], u[2], u[3]);
       }
     }
     tc::fence_async_smem();
@@ -381,11 +349,6 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CU
           v[jj] = j <= i ? __expf(bi - sb[j]) * v[jj] : 0.f;
         }
         tc::st_row_bf16x2_32(pimg, pimg + 2048, rh, v, 4 * h);
-        if (a.Pbuf) {
-#pragma unroll
-          for (int jj = 0; jj < 32; ++jj) v[jj] = tf32_rna(v[jj]);
-          store_row32<float>(a.Pbuf + mat + i * 64 + 32 * h, v);
-        }
       }
     }
   }
@@ -411,12 +374,6 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CU
       const __nv_bfloat16 hi = __float2bfloat16_rn(t[i]);
       *reinterpret_cast<__nv_bfloat16*>(timg + off) = hi;
       *reinterpret_cast<__nv_bfloat16*>(timg + off + 2048) = __float2bfloat16_rn(t[i] - __bfloat162float(hi));
-    }
-    // T feeds tf32 MMAs in the backward: round to nearest here rather than let the operand read drop bits
-    if (a.Tbuf) {
-      float* dst = a.Tbuf + mat;
-#pragma unroll
-      for (int i = 0; i < 64; ++i) dst[i * 64 + col] = tf32_rna(t[i]);
     }
     float* gd = a.gates + (c * a.geo.Hv + hv) * 128;
     gd[tid] = sb[tid];
@@ -947,11 +904,10 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
 // Per-chunk gradients: one CTA per (chunk, key head); its value heads in turn, Dv in four slices of 32.
 struct GradArgs {
   Geo geo;
-  const void *v, *dy;       // bf16
   const float* g;           // [B*T, Hv] (dg = d log g / g); null in layer mode
-  const float* gates;
-  const float* ckpt;        // chunk-start states
-  const float* dsbuf;       // chunk-end state cotangents
+  const float* gates;       // [chunks, Hv, 2, 64]
+  const uint8_t *Timg, *Pimg, *KQimg;  // the forward's operand images
+  const float* Lbuf;        // [chunks, Hv, 64, 64] strict-lower Gamma * K K^T
   void *dq, *dk;            // [B*T, Hk, Dk]
   float *dg, *dbeta;        // [B*T, Hv]; layer mode: da, db
   int* err;
@@ -961,61 +917,76 @@ struct GradArgs {
   float* head_part;         // [chunks, Hv, 2]
 };
 
-constexpr int GR_K = 0;         // 16 KB bf16 K (TMA)
-constexpr int GR_Q = 16384;     // 16 KB bf16 Q
-constexpr int GR_TK = 32768;    // 16 KB fp32 T, K-major
-constexpr int GR_TM = 49152;    // 16 KB fp32 T, MN-major (as T^T)
-constexpr int GR_PM = 65536;    // 16 KB fp32 P, MN-major (as P^T)
-constexpr int GR_SHI = 81920;   // 8 KB bf16 S hi, K-major [32 dv][128 dk]      | finalize: Gamma*KK (16 KB)
-constexpr int GR_SLO = 90112;   // 8 KB bf16 S lo
-constexpr int GR_DHI = 98304;   // 8 KB bf16 dS hi                              | finalize: dP^ hi, lo
-constexpr int GR_DLO = 106496;  // 8 KB bf16 dS lo
-constexpr int GR_SM = 114688;   // 16 KB fp32 S, MN-major [32 dv rows][128 dk]   | finalize: dKK hi, lo
-constexpr int GR_DM = 131072;   // 16 KB fp32 dS, MN-major                       | finalize: column-sum scratch
-constexpr int GR_DOM = 147456;  // 8 KB fp32 dO, MN-major [64][32]
-constexpr int GR_DOK = 155648;  // 8 KB fp32 dO, K-major [64][32]
-constexpr int GR_GDO = 163840;  // 8 KB fp32 gamma dO, K-major
-constexpr int GR_E = 172032;    // 8 KB fp32 E, MN-major
-constexpr int GR_DD = 180224;   // 8 KB fp32 dD, MN-major
-constexpr int GR_D = 188416;    // 8 KB fp32 D, K-major
-constexpr int GR_LD = 196608;   // 8 KB fp32 lambda D, K-major
-constexpr int GR_F = 204800;    // 8 KB fp32 F, K-major
-constexpr int GR_NF = 212992;   // 8 KB fp32 -beta gamma F, K-major
-constexpr int GR_SMEM = 221184 + 1024;
+// Shared memory of the gradient kernel.
+constexpr int GR_KQ = 0;           // 32 KB bf16 [K; Q] image
+constexpr int GR_T = 32768;        // 16 KB bf16 [T_hi; T_lo] image of the value head
+constexpr int GR_P = 49152;        // 16 KB bf16 [P_hi; P_lo] image
+constexpr int GR_BUF = 65536;      // 2 x 40 KB slice buffers: S, dS (fp32, MN-major tf32 [32 dv][128 dk]), V, dO rows
+constexpr int GR_BS = 40960;       //   buffer stride; S at +0, dS at +16384, V at +32768, dO at +36864
+constexpr int GR_SHL = 147456;     // 16 KB bf16 [S_hi; S_lo] K-major [64 rows][128 dk]   | A1 [gamma dO; -beta gamma F]
+constexpr int GR_DHL = 163840;     // 16 KB bf16 [dS_hi; dS_lo]                           | A3 [dO; F]
+constexpr int GR_DOT = 180224;     // 8 KB bf16 dO, MN-major [64][32] (operand of P^T dO)
+constexpr int GR_EHL = 188416;     // 8 KB bf16 E [hi | lo]                                | A2 lambda D (tf32)
+constexpr int GR_DDH = 196608;     // 8 KB bf16 dD [hi | lo]                               | B3 D (tf32, K-major)
+constexpr int GR_SMEM = 204800 + 1024;
+// the value head's finalize reuses the slice buffers: L (fp32 [64][64]), the [dP^; dKK] images, a
+// column-sum scratch
+constexpr int GR_L = GR_BUF, GR_FHI = GR_BUF + 16384, GR_FLO = GR_BUF + 32768, GR_SCR = GR_BUF + 49152;
 
+// 16 floats into chunks 4 half .. 4 half + 3 of row r of a K-major fp32 128-byte-swizzled slab.
+__device__ __forceinline__ void st_row_k_f32_16(uint8_t* slab, int r, const float (&v)[16], int half) {
+  uint8_t* row = slab + r * 128;
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+    *reinterpret_cast<float4*>(row + (((4 * half + c) ^ (r & 7)) << 4)) =
+        make_float4(tf32_rna(v[4 * c]), tf32_rna(v[4 * c + 1]), tf32_rna(v[4 * c + 2]), tf32_rna(v[4 * c + 3]));
+}
+// Element j of row r of a bf16 [hi; lo] image (64 columns).
+__device__ __forceinline__ float img_elem(const uint8_t* img, int r, int j) {
+  const uint32_t off = r * 128 + ((((j >> 3) ^ (r & 7))) << 4) + (j & 7) * 2;
+  return __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(img + off)) +
+         __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(img + off + 2048));
+}
+
+// 256 threads.  Warp w reads TMEM lanes 32 (w & 3) .. + 31 and handles columns 16 (w >> 2) .. + 15 of a
+// 32-wide slice (32 (w >> 2) .. of the 64-wide finalize, 64 (w >> 2) .. of the 128-wide output).  The
+// stacked accumulators hold chunk row i = 16 (w & 3) + l in lane l ("lower": R, X1, G, D, F, dQ, dP)
+// and in lane l + 16 ("upper": Y, dK, F D^T).
 template <typename Tout>
-__global__ void __launch_bounds__(128, 1) gdn_chunk_bwd_grad(const __grid_constant__ CUtensorMap kmap,
-                                                             const __grid_constant__ CUtensorMap qmap,
-                                                             const __grid_constant__ CUtensorMap tmap_k,
-                                                             const __grid_constant__ CUtensorMap tmap_mn,
-                                                             const __grid_constant__ CUtensorMap pmap_mn,
-                                                             const __grid_constant__ CUtensorMap lmap_k,
-                                                             const __grid_constant__ CUtensorMap smap_mn,
-                                                             const __grid_constant__ CUtensorMap dmap_mn, GradArgs a) {
+__global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_constant__ CUtensorMap smap_mn,
+                                                             const __grid_constant__ CUtensorMap dmap_mn,
+                                                             const __grid_constant__ CUtensorMap vmap,
+                                                             const __grid_constant__ CUtensorMap omap, GradArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ float sb[64], sbeta[64], sdb[64], scol[64], sred[8];
-  __shared__ uint64_t bar_kq, bar_h, bar_l, bar_s, bar_mma;
+  __shared__ __align__(16) float sgt[128];   // the value head's gates: b[64], beta[64]
+  __shared__ float srow[7][2][64];           // per-row partial sums from both column halves
+  __shared__ float sdb[64], scol[64], sred[16];
+  __shared__ float snorm[2][2][128];
+  __shared__ uint64_t bar_kq, bar_h, bar_l, bar_s[2], bar_mma;
   __shared__ uint32_t tmem_slot;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, half = warp >> 2;
   const int64_t c = blockIdx.x;
   const int hk = blockIdx.y, Hv = a.geo.Hv, ratio = Hv / a.geo.Hk;
   int n, L;
   int64_t tok0;
   chunk_info(a.geo, c, n, tok0, L);
-  const int i_row = 16 * warp + (lane & 15);
-  const bool row_owner = lane < 16;
-  const bool valid = row_owner && i_row < L;
+  const int i_row = 16 * quad + (lane & 15);
+  const bool lower = lane < 16;
+  const bool rvalid = i_row < L;
 
-  // TMEM: R (then D) 0, Y 32, X1 (then F) 64, G 96, dQ 128..255, dK 256..383, dP 384..447, F D^T 448..511
-  const uint32_t cR = 0, cY = 32, cX = 64, cG = 96, cDQ = 128, cDK = 256, cDP = 384, cFD = 448;
+  // TMEM: dQ | dK 0 (128), dP | F D^T 128 (64), [K; Q] S^T 192 (64, then D), [K; Q] dS^T 256 (64,
+  // then F), P^T dO 320 (32)
+  const uint32_t cQK = 0, cPF = 128, cRY = 192, cX = 256, cG = 320;
   if (warp == 0) tc::tmem_alloc(&tmem_slot, 512);
   if (tid == 0) {
     tc::mbar_init(&bar_kq, 1);
     tc::mbar_init(&bar_h, 1);
     tc::mbar_init(&bar_l, 1);
-    tc::mbar_init(&bar_s, 1);
+    tc::mbar_init(&bar_s[0], 1);
+    tc::mbar_init(&bar_s[1], 1);
     tc::mbar_init(&bar_mma, 1);
     tc::fence_mbar_init();
   }
@@ -1023,145 +994,181 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_bwd_grad(const __grid_consta
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = tmem_slot;
-  if (tid == 0) {
+  const uint32_t tl = tc::taddr(tmem, 32 * quad, 0);
+  constexpr int NSL = DV / DVT;
+
+  // slice q = r * NSL + sl of this CTA: S, dS slices and the value and dO rows, into buffer q & 1
+  auto issue_slice = [&](int q) {
+    const int r = q / NSL, sl = q - r * NSL, hv = hk * ratio + r, bs = q & 1;
+    uint8_t* buf = smem + GR_BUF + bs * GR_BS;
+    const int srow = (int)((c * Hv + hv) * DV + sl * DVT);
+    tc::mbar_arrive_expect_tx(&bar_s[bs], 2 * 16384 + 2 * 4096);
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      tc::tma_load_2d(buf + 4096 * b, &smap_mn, &bar_s[bs], 32 * b, srow);
+      tc::tma_load_2d(buf + 16384 + 4096 * b, &dmap_mn, &bar_s[bs], 32 * b, srow);
+    }
+    tc::tma_load_3d(buf + 32768, &vmap, &bar_s[bs], sl * DVT, hv, (int)tok0);
+    tc::tma_load_3d(buf + 36864, &omap, &bar_s[bs], sl * DVT, hv, (int)tok0);
+  };
+  auto issue_head = [&](int r) {
+    const int hv = hk * ratio + r;
+    tc::mbar_arrive_expect_tx(&bar_h, 2 * 16384 + 512);
+    tc::bulk_load(smem + GR_T, a.Timg + (size_t)(c * Hv + hv) * 16384, 16384, &bar_h);
+    tc::bulk_load(smem + GR_P, a.Pimg + (size_t)(c * Hv + hv) * 16384, 16384, &bar_h);
+    tc::bulk_load(sgt, a.gates + (c * Hv + hv) * 128, 512, &bar_h);
+  };
+  if (tid == 32) {
+    tc::prefetch_tmap(&smap_mn);
+    tc::prefetch_tmap(&dmap_mn);
+    tc::prefetch_tmap(&vmap);
+    tc::prefetch_tmap(&omap);
     tc::mbar_arrive_expect_tx(&bar_kq, 32768);
-    tc::tma_load_3d(smem + GR_K, &kmap, &bar_kq, 0, hk, (int)tok0);
-    tc::tma_load_3d(smem + GR_K + 8192, &kmap, &bar_kq, 64, hk, (int)tok0);
-    tc::tma_load_3d(smem + GR_Q, &qmap, &bar_kq, 0, hk, (int)tok0);
-    tc::tma_load_3d(smem + GR_Q + 8192, &qmap, &bar_kq, 64, hk, (int)tok0);
+    tc::bulk_load(smem + GR_KQ, a.KQimg + (size_t)(c * a.geo.Hk + hk) * 32768, 32768, &bar_kq);
+    issue_head(0);
+    issue_slice(0);
   }
   uint32_t ph_mma = 0;
   bool ok = wait_all(&bar_kq, 0, a.err, 30);
-  const uint32_t kt = tc::smem_u32(smem + GR_K), qt = tc::smem_u32(smem + GR_Q);
+  const uint32_t kq = tc::smem_u32(smem + GR_KQ);
+  const uint32_t idRY = tc::idesc(tc::kBF16, 128, 64, false, false);
+  const uint32_t idG = tc::idesc(tc::kBF16, 64, 32, true, true);
+  const uint32_t idD = tc::idesc(tc::kBF16, 128, 64, false, true);
+  const uint32_t idF = tc::idesc(tc::kBF16, 64, 64, true, true);
+  const uint32_t idC1 = tc::idesc(tc::kTF32, 128, 128, false, true);
+  const uint32_t idC2 = tc::idesc(tc::kTF32, 64, 128, false, true);
+  const uint32_t idC3 = tc::idesc(tc::kTF32, 128, 64, false, false);
+  const uint32_t idF1 = tc::idesc(tc::kBF16, 128, 128, false, true);
+  const uint32_t idF2 = tc::idesc(tc::kBF16, 64, 128, true, true);
+  float t5 = 0.f;  // sum of S (.) dS over this thread's elements (block-summed per value head)
 
   for (int r = 0; r < ratio && ok; ++r) {
     const int hv = hk * ratio + r;
-    const int mrow = (int)((c * Hv + hv) * 64);
-    if (tid == 0) {
-      tc::mbar_arrive_expect_tx(&bar_h, 16384 * 3);
-      tc::tma_load_2d(smem + GR_TK, &tmap_k, &bar_h, 0, mrow);
-      tc::tma_load_2d(smem + GR_TK + 8192, &tmap_k, &bar_h, 32, mrow);
-      tc::tma_load_2d(smem + GR_TM, &tmap_mn, &bar_h, 0, mrow);
-      tc::tma_load_2d(smem + GR_TM + 8192, &tmap_mn, &bar_h, 32, mrow);
-      tc::tma_load_2d(smem + GR_PM, &pmap_mn, &bar_h, 0, mrow);
-      tc::tma_load_2d(smem + GR_PM + 8192, &pmap_mn, &bar_h, 32, mrow);
-    }
-    sb[tid & 63] = a.gates[(c * Hv + hv) * 128 + (tid & 63)];
-    if (tid < 64) sbeta[tid] = a.gates[(c * Hv + hv) * 128 + 64 + tid];
-    __syncthreads();
-    const float bi = sb[i_row], be = sbeta[i_row], gi = __expf(bi), bC = sb[63], lam = __expf(bC - bi);
-    float t1 = 0.f, t2 = 0.f, t3 = 0.f, t4 = 0.f, t5 = 0.f;
     ok = wait_all(&bar_h, (uint32_t)(r & 1), a.err, 31);
     if (!ok) break;
+    const float bi = sgt[i_row], be = sgt[64 + i_row], gi = __expf(bi), bC = sgt[63], lam = __expf(bC - bi);
+    const uint32_t timg = tc::smem_u32(smem + GR_T), pimg = tc::smem_u32(smem + GR_P);
+    float t1 = 0.f, t2 = 0.f, t3 = 0.f, t4 = 0.f;
+    t5 = 0.f;
 
-    for (int sl = 0; sl < DV / DVT && ok; ++sl) {
-      const int dv0 = sl * DVT;
-      // a. S and dS slices by TMA straight into the fp32 MN-major operand layout [dv rows][dk]; the
-      //    value and dO rows issued meanwhile
-      if (tid == 0) {
-        const int srow = (int)((c * Hv + hv) * DV + dv0);
-        tc::mbar_arrive_expect_tx(&bar_s, 32768);
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          tc::tma_load_2d(smem + GR_SM + 4096 * b, &smap_mn, &bar_s, 32 * b, srow);
-          tc::tma_load_2d(smem + GR_DM + 4096 * b, &dmap_mn, &bar_s, 32 * b, srow);
-        }
-      }
-      Row32 vraw, draw;
-      ldg_row32(static_cast<const __nv_bfloat16*>(a.v) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0, valid, vraw);
-      ldg_row32(static_cast<const __nv_bfloat16*>(a.dy) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0, valid, draw);
-      ok = wait_all(&bar_s, (uint32_t)((r * (DV / DVT) + sl) & 1), a.err, 37);
+    for (int sl = 0; sl < NSL && ok; ++sl) {
+      const int q = r * NSL + sl, bs = q & 1;
+      uint8_t* buf = smem + GR_BUF + bs * GR_BS;
+      ok = wait_all(&bar_s[bs], (uint32_t)((q >> 1) & 1), a.err, 37);
       if (!ok) break;
-      // the bf16 hi/lo K-major copies [dv][dk] for the products with K and Q; the fp32 tiles rounded
-      // to tf32 in place
-      {
-#pragma unroll 4
-        for (int u = 0; u < 8; ++u) {
-          const int idx = tid + 128 * u, row = idx >> 5, c4 = idx & 31, dk = 4 * c4;
-          const uint32_t ok_ = tc::off_kmajor(row, dk, DVT, 2), om = tc::off_mnmajor(row, dk, DVT, 4);
-          const float4 sv = *reinterpret_cast<const float4*>(smem + GR_SM + om);
-          const float4 dvv = *reinterpret_cast<const float4*>(smem + GR_DM + om);
-          t5 += sv.x * dvv.x + sv.y * dvv.y + sv.z * dvv.z + sv.w * dvv.w;
-          const __nv_bfloat162 s01 = __floats2bfloat162_rn(sv.x, sv.y), s23 = __floats2bfloat162_rn(sv.z, sv.w);
-          const __nv_bfloat162 d01 = __floats2bfloat162_rn(dvv.x, dvv.y), d23 = __floats2bfloat162_rn(dvv.z, dvv.w);
-          *reinterpret_cast<uint2*>(smem + GR_SHI + ok_) =
-              make_uint2(*reinterpret_cast<const uint32_t*>(&s01), *reinterpret_cast<const uint32_t*>(&s23));
-          *reinterpret_cast<uint2*>(smem + GR_SLO + ok_) =
-              make_uint2(tc::pack_bf16(sv.x - __low2float(s01), sv.y - __high2float(s01)),
-                         tc::pack_bf16(sv.z - __low2float(s23), sv.w - __high2float(s23)));
-          *reinterpret_cast<uint2*>(smem + GR_DHI + ok_) =
-              make_uint2(*reinterpret_cast<const uint32_t*>(&d01), *reinterpret_cast<const uint32_t*>(&d23));
-          *reinterpret_cast<uint2*>(smem + GR_DLO + ok_) =
-              make_uint2(tc::pack_bf16(dvv.x - __low2float(d01), dvv.y - __high2float(d01)),
-                         tc::pack_bf16(dvv.z - __low2float(d23), dvv.w - __high2float(d23)));
-          *reinterpret_cast<float4*>(smem + GR_SM + om) =
-              make_float4(tf32_rna(sv.x), tf32_rna(sv.y), tf32_rna(sv.z), tf32_rna(sv.w));
-          *reinterpret_cast<float4*>(smem + GR_DM + om) =
-              make_float4(tf32_rna(dvv.x), tf32_rna(dvv.y), tf32_rna(dvv.z), tf32_rna(dvv.w));
-        }
-      }
-      float vr[32], dor[32];
-      cvt_row32(vraw, vr);
-      cvt_row32(draw, dor);
-      if (row_owner) {
-        tc::st_row_mn_f32(smem + GR_DOM, i_row, dor);
-        tc::st_row_k_f32(smem + GR_DOK, i_row, dor);
-        float gd[32];
+      if (tid == 32 && sl + 1 < NSL) issue_slice(q + 1);  // the other buffer's last reader has finished
+      // a. S and dS as bf16 [hi; lo] K-major copies (rows dv, then dv + 32) for the products with K
+      //    and Q; the fp32 tiles rounded to tf32 in place for the products over dv
 #pragma unroll
-        for (int j = 0; j < 32; ++j) gd[j] = tf32_rna(gi * dor[j]);
-        tc::st_row_k_f32(smem + GR_GDO, i_row, gd);
+      for (int u = 0; u < 4; ++u) {
+        const int idx = tid + 256 * u, row = idx >> 5, dk = 4 * (idx & 31);
+        const uint32_t om = tc::off_mnmajor(row, dk, DVT, 4);
+        const uint32_t oh = tc::off_kmajor(row, dk, 64, 2), ol = tc::off_kmajor(row + 32, dk, 64, 2);
+        const float4 sv = *reinterpret_cast<const float4*>(buf + om);
+        const float4 dvv = *reinterpret_cast<const float4*>(buf + 16384 + om);
+        t5 += sv.x * dvv.x + sv.y * dvv.y + sv.z * dvv.z + sv.w * dvv.w;
+        const __nv_bfloat162 s01 = __floats2bfloat162_rn(sv.x, sv.y), s23 = __floats2bfloat162_rn(sv.z, sv.w);
+        const __nv_bfloat162 d01 = __floats2bfloat162_rn(dvv.x, dvv.y), d23 = __floats2bfloat162_rn(dvv.z, dvv.w);
+        *reinterpret_cast<uint2*>(smem + GR_SHL + oh) =
+            make_uint2(*reinterpret_cast<const uint32_t*>(&s01), *reinterpret_cast<const uint32_t*>(&s23));
+        *reinterpret_cast<uint2*>(smem + GR_SHL + ol) =
+            make_uint2(tc::pack_bf16(sv.x - __low2float(s01), sv.y - __high2float(s01)),
+                       tc::pack_bf16(sv.z - __low2float(s23), sv.w - __high2float(s23)));
+        *reinterpret_cast<uint2*>(smem + GR_DHL + oh) =
+            make_uint2(*reinterpret_cast<const uint32_t*>(&d01), *reinterpret_cast<const uint32_t*>(&d23));
+        *reinterpret_cast<uint2*>(smem + GR_DHL + ol) =
+            make_uint2(tc::pack_bf16(dvv.x - __low2float(d01), dvv.y - __high2float(d01)),
+                       tc::pack_bf16(dvv.z - __low2float(d23), dvv.w - __high2float(d23)));
+        *reinterpret_cast<float4*>(buf + om) = make_float4(tf32_rna(sv.x), tf32_rna(sv.y), tf32_rna(sv.z), tf32_rna(sv.w));
+        *reinterpret_cast<float4*>(buf + 16384 + om) =
+            make_float4(tf32_rna(dvv.x), tf32_rna(dvv.y), tf32_rna(dvv.z), tf32_rna(dvv.w));
+      }
+      // this row's values and output gradients (zero past the end)
+      float vr[16], dor[16];
+      {
+        Row16 rv, rd;
+        const uint4* vp = reinterpret_cast<const uint4*>(buf + 32768 + i_row * 64 + 32 * half);
+        const uint4* dp = reinterpret_cast<const uint4*>(buf + 36864 + i_row * 64 + 32 * half);
+        const uint4 z = make_uint4(0, 0, 0, 0);
+        rv.w[0] = rvalid ? vp[0] : z;
+        rv.w[1] = rvalid ? vp[1] : z;
+        rd.w[0] = rvalid ? dp[0] : z;
+        rd.w[1] = rvalid ? dp[1] : z;
+        cvt_row16(rv, vr);
+        cvt_row16(rd, dor);
+        if (lower) {  // dO as the plain bf16 operand of P^T dO
+          uint8_t* row = smem + GR_DOT + i_row * 128;
+          *reinterpret_cast<uint4*>(row + (((2 * half) ^ (i_row & 7)) << 4)) = rd.w[0];
+          *reinterpret_cast<uint4*>(row + (((2 * half + 1) ^ (i_row & 7)) << 4)) = rd.w[1];
+        }
       }
       tc::fence_async_smem();
       tc::fence_before_sync();
       __syncthreads();
       tc::fence_after_sync();
-      // b. R = K S^T, Y = Q S^T, X1 = K dS^T (bf16, split), G = P^T dO (tf32)
+      // b. [K; Q] S^T, [K; Q] dS^T (the K rows: X1), P^T dO
       if (tid == 0) {
-        const uint32_t shi = tc::smem_u32(smem + GR_SHI), slo = tc::smem_u32(smem + GR_SLO);
-        const uint32_t dhi = tc::smem_u32(smem + GR_DHI), dlo = tc::smem_u32(smem + GR_DLO);
-        tc::mma_tile<tc::kBF16>(tmem + cR, kt, false, 64, shi, false, DVT, 64, DVT, DK, false);
-        tc::mma_tile<tc::kBF16>(tmem + cR, kt, false, 64, slo, false, DVT, 64, DVT, DK, true);
-        tc::mma_tile<tc::kBF16>(tmem + cY, qt, false, 64, shi, false, DVT, 64, DVT, DK, false);
-        tc::mma_tile<tc::kBF16>(tmem + cY, qt, false, 64, slo, false, DVT, 64, DVT, DK, true);
-        tc::mma_tile<tc::kBF16>(tmem + cX, kt, false, 64, dhi, false, DVT, 64, DVT, DK, false);
-        tc::mma_tile<tc::kBF16>(tmem + cX, kt, false, 64, dlo, false, DVT, 64, DVT, DK, true);
-        tc::mma_tile<tc::kTF32>(tmem + cG, tc::smem_u32(smem + GR_PM), true, 64, tc::smem_u32(smem + GR_DOM), true,
-                                64, 64, DVT, C, false);
+        const uint32_t shl = tc::smem_u32(smem + GR_SHL), dhl = tc::smem_u32(smem + GR_DHL);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          tc::mma_bf16(tmem + cRY, tc::desc_kmajor(kq, 128, ks), tc::desc_kmajor(shl, 64, ks), idRY, ks > 0);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          tc::mma_bf16(tmem + cX, tc::desc_kmajor(kq, 128, ks), tc::desc_kmajor(dhl, 64, ks), idRY, ks > 0);
+        const uint32_t dot = tc::smem_u32(smem + GR_DOT);
+#pragma unroll
+        for (int part = 0; part < 2; ++part)
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            tc::mma_bf16(tmem + cG, desc_img_t(pimg, part, ks), desc_hl(dot, ks), idG, (part | ks) ? 1u : 0u);
         tc::mma_commit(&bar_mma);
       }
       ok = wait_all(&bar_mma, ph_mma, a.err, 32);
       ph_mma ^= 1;
       tc::fence_after_sync();
       if (!ok) break;
-      float rr[32], xx[32];
+      float rr[16], xx[16];
       {
-        float y[32], g[32];
-        tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cR), rr);
-        tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cY), y);
-        tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cX), xx);
-        tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cG), g);
-        float e[32];
+        float g[16];
+        tmem_ld_hl16(tl + cRY, half, rr);  // lower: R, upper: Y
+        tmem_ld_hl16(tl + cX, half, xx);   // lower: X1
+        tc::tmem_ld16(tl + cG + 16 * half, g);
+        if (lower) {
+          float e[16];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          t3 = fmaf(dor[j], y[j], t3);
-          e[j] = tf32_rna(be * (vr[j] - gi * rr[j]));
-          g[j] = tf32_rna(fmaf(lam, xx[j], g[j]));
-        }
-        if (row_owner) {
-          tc::st_row_mn_f32(smem + GR_E, i_row, e);
-          tc::st_row_mn_f32(smem + GR_DD, i_row, g);
+          for (int j = 0; j < 16; ++j) {
+            e[j] = be * (vr[j] - gi * rr[j]);
+            g[j] = fmaf(lam, xx[j], g[j]);
+          }
+          tc::st_row_hilo16(smem + GR_EHL, i_row, e, half);
+          tc::st_row_hilo16(smem + GR_DDH, i_row, g, half);
+        } else {
+          float gd[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            t3 = fmaf(dor[j], rr[j], t3);
+            gd[j] = gi * dor[j];
+          }
+          // the lower rows of A1 and A3 (the [hi; lo] tiles of S and dS are no longer read)
+          st_row_k_f32_16(smem + GR_SHL, img_row(i_row), gd, half);
+          st_row_k_f32_16(smem + GR_DHL, img_row(i_row), dor, half);
         }
       }
       tc::fence_async_smem();
       tc::fence_before_sync();
       __syncthreads();
       tc::fence_after_sync();
-      // c. D = T E, F = T^T dD (tf32); D reuses R's columns, F those of X1
+      // c. D = T E ([T_hi; T_lo] stacked), F = T^T dD (T_hi^T and T_lo^T accumulated)
       if (tid == 0) {
-        tc::mma_tile<tc::kTF32>(tmem + cR, tc::smem_u32(smem + GR_TK), false, 64, tc::smem_u32(smem + GR_E), true, 64,
-                                64, DVT, C, false);
-        tc::mma_tile<tc::kTF32>(tmem + cX, tc::smem_u32(smem + GR_TM), true, 64, tc::smem_u32(smem + GR_DD), true, 64,
-                                64, DVT, C, false);
+        const uint32_t ehl = tc::smem_u32(smem + GR_EHL), ddh = tc::smem_u32(smem + GR_DDH);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          tc::mma_bf16(tmem + cRY, tc::desc_kmajor(timg, 128, ks), desc_hl(ehl, ks), idD, ks > 0);
+#pragma unroll
+        for (int part = 0; part < 2; ++part)
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            tc::mma_bf16(tmem + cX, desc_img_t(timg, part, ks), desc_hl(ddh, ks), idF, (part | ks) ? 1u : 0u);
         tc::mma_commit(&bar_mma);
       }
       ok = wait_all(&bar_mma, ph_mma, a.err, 33);
@@ -1169,48 +1176,50 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_bwd_grad(const __grid_consta
       tc::fence_after_sync();
       if (!ok) break;
       {
-        float d[32], f[32];
-        tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cR), d);
-        tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cX), f);
-        float w[32];
+        float d[16], f[16];
+        tmem_ld_hl16_pair(tl + cRY, half, d);  // D, both lanes of the pair
+        tmem_ld_hl16(tl + cX, half, f);        // lower: F
+        if (lower) {
+          float w[16];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          t1 = fmaf(f[j], vr[j] - gi * rr[j], t1);
-          t2 = fmaf(f[j], rr[j], t2);
-          t4 = fmaf(d[j], xx[j], t4);
-        }
-        if (row_owner) {
+          for (int j = 0; j < 16; ++j) {
+            t1 = fmaf(f[j], vr[j] - gi * rr[j], t1);
+            t2 = fmaf(f[j], rr[j], t2);
+            t4 = fmaf(d[j], xx[j], t4);
+            w[j] = -be * gi * f[j];
+          }
+          st_row_k_f32_16(smem + GR_SHL, img_row(i_row) + 16, w, half);   // A1 upper: -beta gamma F
+          st_row_k_f32_16(smem + GR_DHL, img_row(i_row) + 16, f, half);   // A3 upper: F
 #pragma unroll
-          for (int j = 0; j < 32; ++j) w[j] = tf32_rna(d[j]);
-          tc::st_row_k_f32(smem + GR_D, i_row, w);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) w[j] = tf32_rna(lam * d[j]);
-          tc::st_row_k_f32(smem + GR_LD, i_row, w);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) w[j] = tf32_rna(f[j]);
-          tc::st_row_k_f32(smem + GR_F, i_row, w);
-          const float h = -be * gi;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) w[j] = tf32_rna(h * f[j]);
-          tc::st_row_k_f32(smem + GR_NF, i_row, w);
+          for (int j = 0; j < 16; ++j) w[j] = lam * d[j];
+          st_row_k_f32_16(smem + GR_EHL, i_row, w, half);                 // A2: lambda D
+        } else {
+          st_row_k_f32_16(smem + GR_DDH, i_row, d, half);                 // B3: D (as D^T, K-major)
         }
       }
       tc::fence_async_smem();
       tc::fence_before_sync();
       __syncthreads();
       tc::fence_after_sync();
-      // d. accumulate over the slice's value rows: dQ += (gamma dO) S, dK += (lambda D) dS - (beta gamma F) S,
-      //    dP += dO D^T, FD += F D^T   (all tf32, K = 32 value rows)
+      // d. over the slice's value rows (tf32, K = 32): dQ | dK += [gamma dO; -beta gamma F] S,
+      //    dK += (lambda D) dS (M = 64 in the upper lanes), dP | F D^T += [dO; F] D^T
       if (tid == 0) {
         const bool first = r == 0 && sl == 0;
-        const uint32_t sm = tc::smem_u32(smem + GR_SM), dm = tc::smem_u32(smem + GR_DM);
-        tc::mma_tile<tc::kTF32>(tmem + cDQ, tc::smem_u32(smem + GR_GDO), false, 64, sm, true, DVT, 64, DK, DVT, !first);
-        tc::mma_tile<tc::kTF32>(tmem + cDK, tc::smem_u32(smem + GR_LD), false, 64, dm, true, DVT, 64, DK, DVT, !first);
-        tc::mma_tile<tc::kTF32>(tmem + cDK, tc::smem_u32(smem + GR_NF), false, 64, sm, true, DVT, 64, DK, DVT, true);
-        tc::mma_tile<tc::kTF32>(tmem + cDP, tc::smem_u32(smem + GR_DOK), false, 64, tc::smem_u32(smem + GR_D), false,
-                                64, 64, 64, DVT, sl > 0);
-        tc::mma_tile<tc::kTF32>(tmem + cFD, tc::smem_u32(smem + GR_F), false, 64, tc::smem_u32(smem + GR_D), false, 64,
-                                64, 64, DVT, sl > 0);
+        const uint32_t s32 = tc::smem_u32(buf), d32 = tc::smem_u32(buf + 16384);
+        const uint32_t a1 = tc::smem_u32(smem + GR_SHL), a3 = tc::smem_u32(smem + GR_DHL);
+        const uint32_t a2 = tc::smem_u32(smem + GR_EHL), b3 = tc::smem_u32(smem + GR_DDH);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          tc::mma_tf32(tmem + cQK, tc::desc_kmajor(a1, 128, ks), tc::desc_mnmajor(s32, DVT, ks, 8), idC1,
+                       (!first || ks > 0) ? 1u : 0u);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          tc::mma_tf32(tmem + cQK + (16u << 16), tc::desc_kmajor(a2, 64, ks), tc::desc_mnmajor(d32, DVT, ks, 8), idC2,
+                       1u);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          tc::mma_tf32(tmem + cPF, tc::desc_kmajor(a3, 128, ks), tc::desc_kmajor(b3, 64, ks), idC3,
+                       (sl > 0 || ks > 0) ? 1u : 0u);
         tc::mma_commit(&bar_mma);
       }
       ok = wait_all(&bar_mma, ph_mma, a.err, 34);
@@ -1220,87 +1229,118 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_bwd_grad(const __grid_consta
     if (!ok) break;
 
     // e. finalize this value head: dP^ and dKK, the Gamma terms of d b, and their MMAs into dQ, dK
-    if (tid == 0) {
+    if (tid == 32) {
       tc::mbar_arrive_expect_tx(&bar_l, 16384);
-      tc::tma_load_2d(smem + GR_SHI, &lmap_k, &bar_l, 0, mrow);
-      tc::tma_load_2d(smem + GR_SHI + 8192, &lmap_k, &bar_l, 32, mrow);
+      tc::bulk_load(smem + GR_L, a.Lbuf + (size_t)(c * Hv + hv) * 4096, 16384, &bar_l);
     }
     ok = wait_all(&bar_l, (uint32_t)(r & 1), a.err, 35);
     if (!ok) break;
-    float* scratch = reinterpret_cast<float*>(smem + GR_DM);  // [64][65]
-    float rowsum = 0.f, dbl = 0.f;
+    float* scratch = reinterpret_cast<float*>(smem + GR_SCR);  // [64][65]
+    const float* Lm = reinterpret_cast<const float*>(smem + GR_L);
+    float rsum = 0.f, dbl = 0.f, xl[32];
     {
+      float v[32], o[32];
+      tc::tmem_ld32(tl + cPF + 32 * half, v);  // lower: dP, upper: F D^T
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        float dp[32], fd[32], ph[32], kh[32];
-        tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cDP + 32 * h), dp);
-        tc::tmem_ld32(tc::taddr(tmem, 32 * warp, cFD + 32 * h), fd);
-        if (row_owner) {
-#pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            const int j = 32 * h + jj;
-            const float gam = j <= i_row ? __expf(bi - sb[j]) : 0.f;
-            const float pij = *reinterpret_cast<const float*>(smem + GR_PM + tc::off_mnmajor(i_row, j, 64, 4));
-            const float lh = *reinterpret_cast<const float*>(smem + GR_SHI + tc::off_kmajor(i_row, j, 64, 4));
-            const float xp = j <= i_row ? dp[jj] * pij : 0.f;
-            const float dl = j < i_row ? -fd[jj] : 0.f;
-            const float xl = dl * be * lh;
-            dbl = fmaf(dl, lh, dbl);
-            rowsum += xp + xl;
-            scratch[i_row * 65 + j] = xp + xl;
-            ph[jj] = dp[jj] * gam;          // dP^
-            kh[jj] = dl * be * gam;         // dKK
-          }
-          tc::st_row_bf16x2_32(smem + GR_DHI, smem + GR_DLO, i_row, ph, 4 * h);
-          tc::st_row_bf16x2_32(smem + GR_SM, smem + GR_SM + 8192, i_row, kh, 4 * h);
+      for (int jj = 0; jj < 32; ++jj) {
+        const int j = 32 * half + jj;
+        const float gam = j <= i_row ? __expf(bi - sgt[j]) : 0.f;
+        if (lower) {
+          const float xp = j <= i_row ? v[jj] * img_elem(smem + GR_P, img_row(i_row), j) : 0.f;
+          rsum += xp;
+          scratch[i_row * 65 + j] = xp;
+          o[jj] = v[jj] * gam;                 // dP^
+        } else {
+          const float dl = j < i_row ? -v[jj] : 0.f;
+          const float lh = Lm[i_row * 64 + j];
+          xl[jj] = dl * be * lh;
+          rsum += xl[jj];
+          dbl = fmaf(dl, lh, dbl);
+          o[jj] = dl * be * gam;               // dKK
         }
       }
+      const int ri = img_row(i_row) + (lower ? 0 : 16);
+      tc::st_row_bf16x2_32(smem + GR_FHI, smem + GR_FLO, ri, o, 4 * half);
+    }
+    __syncthreads();
+    if (!lower) {
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) scratch[i_row * 65 + 32 * half + jj] += xl[jj];
+    }
+    // per-row partials from both column halves: 0 t1, 1 t2, 2 t4 (lower), 3 t3 (upper), 4 row sum of
+    // the P terms (lower), 5 that of the L terms (upper), 6 the d beta part of the L terms (upper)
+    if (lower) {
+      srow[0][half][i_row] = t1;
+      srow[1][half][i_row] = t2;
+      srow[2][half][i_row] = t4;
+      srow[4][half][i_row] = rsum;
+    } else {
+      srow[3][half][i_row] = t3;
+      srow[5][half][i_row] = rsum;
+      srow[6][half][i_row] = dbl;
+    }
+    {
+      float t5w = t5;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) t5w += __shfl_xor_sync(0xffffffffu, t5w, o);
+      if (lane == 0) sred[warp] = t5w;
     }
     tc::fence_async_smem();
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
     if (tid == 0) {
-      const uint32_t phi = tc::smem_u32(smem + GR_DHI), plo = tc::smem_u32(smem + GR_DLO);
-      const uint32_t khi = tc::smem_u32(smem + GR_SM), klo = tc::smem_u32(smem + GR_SM + 8192);
-      // dQ += dP^ K;  dK += dP^^T Q + dKK K + dKK^T K   (K, Q as MN-major B: chunk rows, Dk contiguous)
-      tc::mma_tile<tc::kBF16>(tmem + cDQ, phi, false, 64, kt, true, 64, 64, DK, C, true);
-      tc::mma_tile<tc::kBF16>(tmem + cDQ, plo, false, 64, kt, true, 64, 64, DK, C, true);
-      tc::mma_tile<tc::kBF16>(tmem + cDK, phi, true, 64, qt, true, 64, 64, DK, C, true);
-      tc::mma_tile<tc::kBF16>(tmem + cDK, plo, true, 64, qt, true, 64, 64, DK, C, true);
-      tc::mma_tile<tc::kBF16>(tmem + cDK, khi, false, 64, kt, true, 64, 64, DK, C, true);
-      tc::mma_tile<tc::kBF16>(tmem + cDK, klo, false, 64, kt, true, 64, 64, DK, C, true);
-      tc::mma_tile<tc::kBF16>(tmem + cDK, khi, true, 64, kt, true, 64, 64, DK, C, true);
-      tc::mma_tile<tc::kBF16>(tmem + cDK, klo, true, 64, kt, true, 64, 64, DK, C, true);
+      // dQ | dK += [dP^; dKK] K (hi then lo);  dK += dP^^T Q + dKK^T K  (M = 64, upper lanes)
+      const uint32_t fhi = tc::smem_u32(smem + GR_FHI), flo = tc::smem_u32(smem + GR_FLO);
+#pragma unroll
+      for (int m = 0; m < 2; ++m) {
+        const uint32_t f = m ? flo : fhi;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          tc::mma_bf16(tmem + cQK, tc::desc_kmajor(f, 128, ks), desc_kq_t(kq, 0, ks), idF1, 1u);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          tc::mma_bf16(tmem + cQK + (16u << 16), desc_img_t(f, 0, ks), desc_kq_t(kq, 1, ks), idF2, 1u);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          tc::mma_bf16(tmem + cQK + (16u << 16), desc_img_t(f, 1, ks), desc_kq_t(kq, 0, ks), idF2, 1u);
+      }
       tc::mma_commit(&bar_mma);
     }
-    // column sums of the Gamma terms (fixed order) and the block sums of lambda t4 and t5
+    // column sums of the Gamma terms (fixed order); row totals; d b
     if (tid < 64) {
       float cs = 0.f;
       for (int i = 0; i < 64; ++i) cs += scratch[i * 65 + tid];
       scol[tid] = cs;
     }
-    float lt4 = row_owner ? lam * t4 : 0.f;
+    __syncthreads();
+    float lt4 = 0.f;
+    if (tid < 64) {
+      const int i = tid;
+      const float bi_ = sgt[i], be_ = sgt[64 + i], gi_ = __expf(bi_), lam_ = __expf(bC - bi_);
+      const float t2_ = srow[1][0][i] + srow[1][1][i], t3_ = srow[3][0][i] + srow[3][1][i];
+      const float t4_ = srow[2][0][i] + srow[2][1][i];
+      const float rs = srow[4][0][i] + srow[4][1][i] + srow[5][0][i] + srow[5][1][i];
+      sdb[i] = rs - scol[i] + gi_ * t3_ - be_ * gi_ * t2_ - lam_ * t4_;
+      lt4 = lam_ * t4_;
+    }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      lt4 += __shfl_xor_sync(0xffffffffu, lt4, o);
-      t5 += __shfl_xor_sync(0xffffffffu, t5, o);
-    }
-    if (lane == 0) {
-      sred[warp] = lt4;
-      sred[4 + warp] = t5;
-    }
+    for (int o = 16; o > 0; o >>= 1) lt4 += __shfl_xor_sync(0xffffffffu, lt4, o);
+    if (lane == 0 && warp < 2) sred[8 + warp] = lt4;
     __syncthreads();
-    if (row_owner) sdb[i_row] = rowsum - scol[i_row] + gi * t3 - be * gi * t2 - lam * t4;
-    __syncthreads();
-    if (tid == 0) sdb[63] += (sred[0] + sred[1] + sred[2] + sred[3]) + __expf(bC) * (sred[4] + sred[5] + sred[6] + sred[7]);
+    if (tid == 0) {
+      float st5 = 0.f;
+      for (int w = 0; w < 8; ++w) st5 += sred[w];
+      sdb[63] += (sred[8] + sred[9]) + __expf(bC) * st5;
+    }
     __syncthreads();
     float pa = 0.f, pd = 0.f;  // layer mode: this row's share of the head's dA_log, ddt_bias
-    if (valid) {
+    if (tid < 64 && tid < L) {
+      const int i = tid;
       float dl = 0.f;  // d log g_i = sum over rows i' >= i of d b_i'
-      for (int i2 = 63; i2 >= i_row; --i2) dl += sdb[i2];
-      const int64_t gi_idx = (tok0 + i_row) * Hv + hv;
-      const float dbe = t1 + dbl;
+      for (int i2 = 63; i2 >= i; --i2) dl += sdb[i2];
+      const int64_t gi_idx = (tok0 + i) * Hv + hv;
+      const float dbe = srow[0][0][i] + srow[0][1][i] + srow[6][0][i] + srow[6][1][i];
       if (a.g) {
         // dg = d log g / g; a gate of exactly 0 (log g clamped) gets 0, which keeps g * dg = 0 exact
         const float gv = a.g[gi_idx];
@@ -1323,63 +1363,63 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_bwd_grad(const __grid_consta
         pa += __shfl_xor_sync(0xffffffffu, pa, o);
         pd += __shfl_xor_sync(0xffffffffu, pd, o);
       }
-      __syncthreads();
-      if (lane == 0) {
-        sred[warp] = pa;
-        sred[4 + warp] = pd;
+      if (lane == 0 && warp < 2) {
+        sred[12 + warp] = pa;
+        sred[14 + warp] = pd;
       }
       __syncthreads();
       if (tid == 0) {
-        a.head_part[(c * Hv + hv) * 2] = sred[0] + sred[1] + sred[2] + sred[3];
-        a.head_part[(c * Hv + hv) * 2 + 1] = sred[4] + sred[5] + sred[6] + sred[7];
+        a.head_part[(c * Hv + hv) * 2] = sred[12] + sred[13];
+        a.head_part[(c * Hv + hv) * 2 + 1] = sred[14] + sred[15];
       }
     }
     ok = wait_all(&bar_mma, ph_mma, a.err, 36);
     ph_mma ^= 1;
     tc::fence_after_sync();
+    // the next value head's tiles (the finalize's buffers and the images are free now)
+    if (ok && r + 1 < ratio && tid == 32) {
+      issue_head(r + 1);
+      issue_slice((r + 1) * NSL);
+    }
   }
-  // f. dq, dk rows of this key head (layer mode: through the norms to the raw q, k)
+  // f. dq (lower lanes) and dk (upper lanes) rows of this key head, 64 columns per thread (layer mode:
+  //    through the norms to the raw q, k)
   if (ok) {
-    const size_t rowoff = ((tok0 + i_row) * a.geo.Hk + hk) * (size_t)DK;
-#pragma unroll 1
-    for (int m = 0; m < 2; ++m) {
-      const uint32_t col = m == 0 ? cDQ : cDK;
-      Tout* out = static_cast<Tout*>(m == 0 ? a.dq : a.dk) + rowoff;
-      if (!a.g) {
-        // x^ = s bf16(x r), r = rsqrt(mean(x^2) + eps):  dx = s r (dx^ - r^2 (x . dx^) x / Dk)
-        const __nv_bfloat16* xr = (m == 0 ? a.q_raw : a.k_raw) + rowoff;
-        float ss = 0.f, dot = 0.f;
-#pragma unroll 1
-        for (int h = 0; h < 4; ++h) {
-          float v[32], x[32];
-          tc::tmem_ld32(tc::taddr(tmem, 32 * warp, col + 32 * h), v);
-          load_row32(xr + 32 * h, valid, x);
+    const size_t rowoff = ((tok0 + i_row) * a.geo.Hk + hk) * (size_t)DK + 64 * half;
+    Tout* out = static_cast<Tout*>(lower ? a.dq : a.dk) + rowoff;
+    float v0[32], v1[32];
+    tc::tmem_ld32(tl + cQK + 64 * half, v0);
+    tc::tmem_ld32(tl + cQK + 64 * half + 32, v1);
+    if (!a.g) {
+      // x^ = s bf16(x r), r = rsqrt(mean(x^2) + eps):  dx = s r (dx^ - r^2 (x . dx^) x / Dk)
+      const __nv_bfloat16* xr = (lower ? a.q_raw : a.k_raw) + rowoff;
+      float x0[32], x1[32];
+      load_row32(xr, rvalid, x0);
+      load_row32(xr + 32, rvalid, x1);
+      float ss = 0.f, dot = 0.f;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            ss = fmaf(x[j], x[j], ss);
-            dot = fmaf(x[j], v[j], dot);
-          }
-        }
-        const float r = rsqrtf(ss / DK + 1e-6f);
-        const float sc = m == 0 ? 1.f / DK : __bfloat162float(__float2bfloat16_rn(rsqrtf((float)DK)));
-        const float c2 = r * r * dot / DK;
-#pragma unroll 1
-        for (int h = 0; h < 4; ++h) {
-          float v[32], x[32];
-          tc::tmem_ld32(tc::taddr(tmem, 32 * warp, col + 32 * h), v);
-          load_row32(xr + 32 * h, valid, x);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = sc * r * (v[j] - c2 * x[j]);
-          if (valid) store_row32<Tout>(out + 32 * h, v);
-        }
-      } else {
-#pragma unroll 1
-        for (int h = 0; h < 4; ++h) {
-          float v[32];
-          tc::tmem_ld32(tc::taddr(tmem, 32 * warp, col + 32 * h), v);
-          if (valid) store_row32<Tout>(out + 32 * h, v);
-        }
+      for (int j = 0; j < 32; ++j) {
+        ss = fmaf(x0[j], x0[j], fmaf(x1[j], x1[j], ss));
+        dot = fmaf(x0[j], v0[j], fmaf(x1[j], v1[j], dot));
       }
+      const int ln = 32 * quad + lane;
+      snorm[0][half][ln] = ss;
+      snorm[1][half][ln] = dot;
+      __syncthreads();
+      ss += snorm[0][half ^ 1][ln];
+      dot += snorm[1][half ^ 1][ln];
+      const float rn = rsqrtf(ss / DK + 1e-6f);
+      const float sc = lower ? 1.f / DK : __bfloat162float(__float2bfloat16_rn(rsqrtf((float)DK)));
+      const float c2 = rn * rn * dot / DK;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        v0[j] = sc * rn * (v0[j] - c2 * x0[j]);
+        v1[j] = sc * rn * (v1[j] - c2 * x1[j]);
+      }
+    }
+    if (rvalid) {
+      store_row32<Tout>(out, v0);
+      store_row32<Tout>(out + 32, v1);
     }
   }
   tc::fence_before_sync();
@@ -1447,21 +1487,6 @@ bool map_rows(CUtensorMap* m, const void* base, int64_t rows, int heads, int dim
            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Stacked [rows, 64] fp32 matrices; box = 32 columns x 64 rows.  mn = the 32-byte-atom swizzle, which
-// lands the box as the MN-major tf32 operand (the matrix used transposed); otherwise the 128-byte
-// swizzle, the K-major operand.
-bool map_f32_64(CUtensorMap* m, const void* base, int64_t rows, bool mn) {
-  EncodeTiled f = encode_fn();
-  if (!f) return false;
-  cuuint64_t dims[2] = {64, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {64 * 4};
-  cuuint32_t box[2] = {32, 64};
-  cuuint32_t es[2] = {1, 1};
-  return f(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, es,
-           CU_TENSOR_MAP_INTERLEAVE_NONE, mn ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
-           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 // State rows [rows, 128] fp32 (a chunk-state buffer); box = 32 columns x 32 rows in the 32-byte-atom
 // swizzle: four boxes make the MN-major tf32 operand of a 32-row slice.
 bool map_state_mn(CUtensorMap* m, const void* base, int64_t rows) {
@@ -1478,15 +1503,14 @@ bool map_state_mn(CUtensorMap* m, const void* base, int64_t rows) {
 
 int64_t a256(int64_t x) { return (x + 255) & ~int64_t(255); }
 
-// The chunk intermediates: [ckpt][T][P][Gamma*KK][gates] fp32, the forward's T and P operand images,
-// and in layer mode the normalised [kn][qn] bf16 rows.
+// The chunk intermediates: [ckpt][Gamma*KK][gates] fp32 and the forward's T, P and [K; Q] operand
+// images.
 struct Saved {
-  float *ckpt, *T, *P, *L, *gates;
+  float *ckpt, *L, *gates;
   uint8_t *Timg, *Pimg, *KQimg;
-  __nv_bfloat16 *kn, *qn;
 };
 
-int64_t saved_layout(int Hv, int Hk, int64_t n_chunks, int64_t qk_elems, char* base, Saved* s) {
+int64_t saved_layout(int Hv, int Hk, int64_t n_chunks, char* base, Saved* s) {
   int64_t off = 0;
   auto take = [&](int64_t bytes) {
     char* at = base ? base + off : nullptr;
@@ -1495,35 +1519,30 @@ int64_t saved_layout(int Hv, int Hk, int64_t n_chunks, int64_t qk_elems, char* b
   };
   Saved x;
   x.ckpt = (float*)take(n_chunks * Hv * (int64_t)DV * DK * 4);
-  x.T = (float*)take(n_chunks * Hv * 4096 * 4);
-  x.P = (float*)take(n_chunks * Hv * 4096 * 4);
   x.L = (float*)take(n_chunks * Hv * 4096 * 4);
   x.gates = (float*)take(n_chunks * Hv * 128 * 4);
   x.Timg = (uint8_t*)take(n_chunks * Hv * 16384);
   x.Pimg = (uint8_t*)take(n_chunks * Hv * 16384);
   x.KQimg = (uint8_t*)take(n_chunks * Hk * 32768);
-  x.kn = (__nv_bfloat16*)take(qk_elems * 2);
-  x.qn = (__nv_bfloat16*)take(qk_elems * 2);
   if (s) *s = x;
   return off;
 }
 
-// Workspace: [chunk_off][err][fwd: T and P images, gates (and kn, qn in layer mode) when nothing is
-// saved | bwd: dS per chunk, per-chunk head sums (layer mode), and a saved buffer plus forward
-// workspace when the backward recomputes].
+// Workspace: [chunk_off][err][fwd: T, P and [K; Q] images, gates when nothing is saved | bwd: dS per
+// chunk, per-chunk head sums (layer mode), and a saved buffer plus forward workspace when the backward
+// recomputes].
 struct Ws {
   int64_t* chunk_off;
   int* err;
   uint8_t *Timg, *Pimg, *KQimg;
   float* gates;
-  __nv_bfloat16 *kn, *qn;
   float* dsbuf;
   float* head_part;
   char* saved;
   char* fwd_ws;
 };
 
-int64_t ws_layout(int Hv, int Hk, int N, int64_t n_chunks, int64_t qk_elems, bool varlen, int op, bool with_saved,
+int64_t ws_layout(int Hv, int Hk, int N, int64_t n_chunks, bool layer, bool varlen, int op, bool with_saved,
                   char* base, Ws* w) {
   int64_t off = 0;
   auto take = [&](int64_t bytes) {
@@ -1539,14 +1558,12 @@ int64_t ws_layout(int Hv, int Hk, int N, int64_t n_chunks, int64_t qk_elems, boo
     x.Pimg = (uint8_t*)take(n_chunks * Hv * 16384);
     x.KQimg = (uint8_t*)take(n_chunks * Hk * 32768);
     x.gates = (float*)take(n_chunks * Hv * 128 * 4);
-    x.kn = (__nv_bfloat16*)take(qk_elems * 2);
-    x.qn = (__nv_bfloat16*)take(qk_elems * 2);
   } else {
     x.dsbuf = (float*)take(n_chunks * Hv * (int64_t)DV * DK * 4);
-    x.head_part = (float*)take(qk_elems ? n_chunks * Hv * 2 * 4 : 0);
+    x.head_part = (float*)take(layer ? n_chunks * Hv * 2 * 4 : 0);
     if (with_saved) {
-      x.saved = take(saved_layout(Hv, Hk, n_chunks, qk_elems, nullptr, nullptr));
-      x.fwd_ws = take(ws_layout(Hv, Hk, N, n_chunks, qk_elems, varlen, 0, false, nullptr, nullptr));
+      x.saved = take(saved_layout(Hv, Hk, n_chunks, nullptr, nullptr));
+      x.fwd_ws = take(ws_layout(Hv, Hk, N, n_chunks, layer, varlen, 0, false, nullptr, nullptr));
     }
   }
   if (w) *w = x;
@@ -1559,27 +1576,26 @@ bool chunked_supported(int Dk, int Dv) { return Dk == DK && Dv == DV && encode_f
 bool chunked_bwd_ready() { return true; }
 
 int64_t chunked_saved_bytes(int Hv, int Hk, int64_t n_chunks, int64_t tokens, bool layer) {
-  return saved_layout(Hv, Hk, n_chunks, layer ? tokens * Hk * DK : 0, nullptr, nullptr);
+  return saved_layout(Hv, Hk, n_chunks, nullptr, nullptr);
 }
 
 int64_t chunked_ws_bytes(int Hv, int Hk, int N, int64_t n_chunks, int64_t tokens, bool varlen, int op, bool with_saved,
                          bool layer) {
-  return ws_layout(Hv, Hk, N, n_chunks, layer ? tokens * Hk * DK : 0, varlen, op, with_saved, nullptr, nullptr);
+  return ws_layout(Hv, Hk, N, n_chunks, layer, varlen, op, with_saved, nullptr, nullptr);
 }
 
 cudaError_t chunked_fwd(const ChunkFwdArgs& a, void* ws, cudaStream_t st) {
   if (!a.in_bf16) return cudaErrorInvalidValue;
   const bool layer = a.g == nullptr;
-  const int64_t rows = (int64_t)a.B * a.T, qk = layer ? rows * a.Hk * DK : 0;
+  const int64_t rows = (int64_t)a.B * a.T;
   Ws w;
-  ws_layout(a.Hv, a.Hk, a.N, a.n_chunks, qk, a.cu != nullptr, 0, false, (char*)ws, &w);
+  ws_layout(a.Hv, a.Hk, a.N, a.n_chunks, layer, a.cu != nullptr, 0, false, (char*)ws, &w);
   Saved sv{};
-  float *Tb = nullptr, *Pb = nullptr, *gates = w.gates, *ckpt = nullptr, *Lb = nullptr;
+  float *gates = w.gates, *ckpt = nullptr, *Lb = nullptr;
   uint8_t *Ti = w.Timg, *Pi = w.Pimg, *KQi = w.KQimg;
-  __nv_bfloat16 *kn = w.kn, *qn = w.qn;
   if (a.saved) {
-    saved_layout(a.Hv, a.Hk, a.n_chunks, qk, (char*)a.saved, &sv);
-    Tb = sv.T, Pb = sv.P, gates = sv.gates, ckpt = sv.ckpt, Lb = sv.L, kn = sv.kn, qn = sv.qn;
+    saved_layout(a.Hv, a.Hk, a.n_chunks, (char*)a.saved, &sv);
+    gates = sv.gates, ckpt = sv.ckpt, Lb = sv.L;
     Ti = sv.Timg, Pi = sv.Pimg, KQi = sv.KQimg;
   }
   cudaError_t e;
@@ -1589,7 +1605,7 @@ cudaError_t chunked_fwd(const ChunkFwdArgs& a, void* ws, cudaStream_t st) {
   if (!map_act(&kmap, a.k, rows, a.Hk, a.Dk) || !map_act(&qmap, a.q, rows, a.Hk, a.Dk)) return cudaErrorInvalidValue;
   Geo geo{a.T, a.Hk, a.Hv, a.N, (a.T + C - 1) / C, a.cu, a.cu ? w.chunk_off : nullptr};
   if (a.n_chunks > 0) {
-    PrepArgs pa{geo, a.g, a.beta, a.a_raw, a.b_raw, a.A_log, a.dt_bias, qn, kn, Tb, Pb, Ti, Pi, KQi, Lb, gates, w.err};
+    PrepArgs pa{geo, a.g, a.beta, a.a_raw, a.b_raw, a.A_log, a.dt_bias, Ti, Pi, KQi, Lb, gates, w.err};
     const int prep_smem = 1024 + 32768 + 64 * 68 * 4;
     if ((e = cudaFuncSetAttribute(gdn_chunk_prep, cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem)) !=
         cudaSuccess)
@@ -1611,9 +1627,9 @@ cudaError_t chunked_fwd(const ChunkFwdArgs& a, void* ws, cudaStream_t st) {
 cudaError_t chunked_bwd(const ChunkBwdArgs& a, void* ws, cudaStream_t st) {
   if (!a.in_bf16) return cudaErrorInvalidValue;
   const bool layer = a.g == nullptr;
-  const int64_t rows = (int64_t)a.B * a.T, qk = layer ? rows * a.Hk * DK : 0;
+  const int64_t rows = (int64_t)a.B * a.T;
   Ws w;
-  ws_layout(a.Hv, a.Hk, a.N, a.n_chunks, qk, a.cu != nullptr, 1, a.saved == nullptr, (char*)ws, &w);
+  ws_layout(a.Hv, a.Hk, a.N, a.n_chunks, layer, a.cu != nullptr, 1, a.saved == nullptr, (char*)ws, &w);
   cudaError_t e;
   const void* saved = a.saved;
   if (!saved) {  // recompute the forward's intermediates with the same forward (y is discarded into dv)
@@ -1626,17 +1642,9 @@ cudaError_t chunked_bwd(const ChunkBwdArgs& a, void* ws, cudaStream_t st) {
     saved = w.saved;
   }
   Saved sv;
-  saved_layout(a.Hv, a.Hk, a.n_chunks, qk, (char*)saved, &sv);
+  saved_layout(a.Hv, a.Hk, a.n_chunks, (char*)saved, &sv);
   if ((e = cudaMemsetAsync(w.err, 0, 16, st)) != cudaSuccess) return e;
   if (a.cu && (e = launch_chunk_offsets(a.cu, a.N, w.chunk_off, st)) != cudaSuccess) return e;
-  const int64_t mrows = a.n_chunks * a.Hv * 64;
-  const void* kx = layer ? (const void*)sv.kn : a.k;
-  const void* qx = layer ? (const void*)sv.qn : a.q;
-  CUtensorMap kmap, qmap, tmap_k, tmap_mn, pmap_mn, lmap_k;
-  if (!map_act(&kmap, kx, rows, a.Hk, a.Dk) || !map_act(&qmap, qx, rows, a.Hk, a.Dk) ||
-      !map_f32_64(&tmap_k, sv.T, mrows, false) || !map_f32_64(&tmap_mn, sv.T, mrows, true) ||
-      !map_f32_64(&pmap_mn, sv.P, mrows, true) || !map_f32_64(&lmap_k, sv.L, mrows, false))
-    return cudaErrorInvalidValue;
   Geo geo{a.T, a.Hk, a.Hv, a.N, (a.T + C - 1) / C, a.cu, a.cu ? w.chunk_off : nullptr};
   CUtensorMap dmap;
   if (!map_rows(&dmap, a.dy, rows, a.Hv, a.Dv, DVT, C)) return cudaErrorInvalidValue;
@@ -1657,13 +1665,14 @@ cudaError_t chunked_bwd(const ChunkBwdArgs& a, void* ws, cudaStream_t st) {
   if (!map_state_mn(&smap_mn, sv.ckpt, a.n_chunks * a.Hv * (int64_t)DV) ||
       !map_state_mn(&dmap_mn, w.dsbuf, a.n_chunks * a.Hv * (int64_t)DV))
     return cudaErrorInvalidValue;
-  GradArgs ga{geo, a.v, a.dy, a.g, sv.gates, sv.ckpt, w.dsbuf, a.dq, a.dk, a.dg, a.dbeta, w.err,
+  CUtensorMap vmap;
+  if (!map_rows(&vmap, a.v, rows, a.Hv, a.Dv, DVT, C)) return cudaErrorInvalidValue;
+  GradArgs ga{geo, a.g, sv.gates, sv.Timg, sv.Pimg, sv.KQimg, sv.L, a.dq, a.dk, a.dg, a.dbeta, w.err,
               static_cast<const __nv_bfloat16*>(a.q), static_cast<const __nv_bfloat16*>(a.k),
               a.a_raw, a.b_raw, a.A_log, a.dt_bias, w.head_part};
   auto k2 = a.out_bf16 ? gdn_chunk_bwd_grad<__nv_bfloat16> : gdn_chunk_bwd_grad<float>;
   if ((e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, GR_SMEM)) != cudaSuccess) return e;
-  k2<<<dim3((unsigned)a.n_chunks, a.Hk), 128, GR_SMEM, st>>>(kmap, qmap, tmap_k, tmap_mn, pmap_mn, lmap_k, smap_mn,
-                                                             dmap_mn, ga);
+  k2<<<dim3((unsigned)a.n_chunks, a.Hk), 256, GR_SMEM, st>>>(smap_mn, dmap_mn, vmap, dmap, ga);
   note_launch();
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   if (layer) {
