@@ -941,6 +941,24 @@ __device__ __forceinline__ void st_row_k_f32_16(uint8_t* slab, int r, const floa
     *reinterpret_cast<float4*>(row + (((4 * half + c) ^ (r & 7)) << 4)) =
         make_float4(tf32_rna(v[4 * c]), tf32_rna(v[4 * c + 1]), tf32_rna(v[4 * c + 2]), tf32_rna(v[4 * c + 3]));
 }
+// 16 floats as bf16 hi (into hi_img) and lo (into lo_img), row r, 16-byte chunks c0 and c0 + 1 of a
+// 128-byte-swizzled tile.
+__device__ __forceinline__ void st_hilo16_chunks(uint8_t* hi_img, uint8_t* lo_img, int r, const float (&v)[16], int c0) {
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float x = v[8 * c + 2 * e], y = v[8 * c + 2 * e + 1];
+      const __nv_bfloat162 hh = __floats2bfloat162_rn(x, y);
+      h[e] = *reinterpret_cast<const uint32_t*>(&hh);
+      l[e] = tc::pack_bf16(x - __low2float(hh), y - __high2float(hh));
+    }
+    const int off = r * 128 + (((c0 + c) ^ (r & 7)) << 4);
+    *reinterpret_cast<uint4*>(hi_img + off) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(lo_img + off) = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+}
 // Element j of row r of a bf16 [hi; lo] image (64 columns).
 __device__ __forceinline__ float img_elem(const uint8_t* img, int r, int j) {
   const uint32_t off = r * 128 + ((((j >> 3) ^ (r & 7))) << 4) + (j & 7) * 2;
@@ -961,7 +979,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(16) float sgt[128];   // the value head's gates: b[64], beta[64]
   __shared__ float srow[7][2][64];           // per-row partial sums from both column halves
-  __shared__ float sdb[64], scol[64], sred[16];
+  __shared__ float sdb[65], sred[16];
   __shared__ float snorm[2][2][128];
   __shared__ uint64_t bar_kq, bar_h, bar_l, bar_s[2], bar_mma;
   __shared__ uint32_t tmem_slot;
@@ -1059,13 +1077,20 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
       if (tid == 32 && sl + 1 < NSL) issue_slice(q + 1);  // the other buffer's last reader has finished
       // a. S and dS as bf16 [hi; lo] K-major copies (rows dv, then dv + 32) for the products with K
       //    and Q; the fp32 tiles rounded to tf32 in place for the products over dv
+      float4 s_in[4], d_in[4];  // all loads first: the stores below may not be reordered across them
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int idx = tid + 256 * u, row = idx >> 5, dk = 4 * (idx & 31);
+        const uint32_t om = tc::off_mnmajor(row, dk, DVT, 4);
+        s_in[u] = *reinterpret_cast<const float4*>(buf + om);
+        d_in[u] = *reinterpret_cast<const float4*>(buf + 16384 + om);
+      }
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int idx = tid + 256 * u, row = idx >> 5, dk = 4 * (idx & 31);
         const uint32_t om = tc::off_mnmajor(row, dk, DVT, 4);
         const uint32_t oh = tc::off_kmajor(row, dk, 64, 2), ol = tc::off_kmajor(row + 32, dk, 64, 2);
-        const float4 sv = *reinterpret_cast<const float4*>(buf + om);
-        const float4 dvv = *reinterpret_cast<const float4*>(buf + 16384 + om);
+        const float4 sv = s_in[u], dvv = d_in[u];
         t5 += sv.x * dvv.x + sv.y * dvv.y + sv.z * dvv.z + sv.w * dvv.w;
         const __nv_bfloat162 s01 = __floats2bfloat162_rn(sv.x, sv.y), s23 = __floats2bfloat162_rn(sv.z, sv.w);
         const __nv_bfloat162 d01 = __floats2bfloat162_rn(dvv.x, dvv.y), d23 = __floats2bfloat162_rn(dvv.z, dvv.w);
@@ -1237,47 +1262,81 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
     if (!ok) break;
     float* scratch = reinterpret_cast<float*>(smem + GR_SCR);  // [64][65]
     const float* Lm = reinterpret_cast<const float*>(smem + GR_L);
-    float rsum = 0.f, dbl = 0.f, xl[32];
+    float rsum = 0.f, dbl = 0.f;
     {
-      float v[32], o[32];
-      tc::tmem_ld32(tl + cPF + 32 * half, v);  // lower: dP, upper: F D^T
+      // Lane l holds dP[i][32 half + 0..31], lane l + 16 holds F D^T there; one exchange leaves each
+      // lane both for 16 columns: j0 = 32 half (lower lane), 32 half + 16 (upper lane).
+      float v[32], dp[16], fd[16];
+      tc::tmem_ld32(tl + cPF + 32 * half, v);
 #pragma unroll
-      for (int jj = 0; jj < 32; ++jj) {
-        const int j = 32 * half + jj;
-        const float gam = j <= i_row ? __expf(bi - sgt[j]) : 0.f;
-        if (lower) {
-          const float xp = j <= i_row ? v[jj] * img_elem(smem + GR_P, img_row(i_row), j) : 0.f;
-          rsum += xp;
-          scratch[i_row * 65 + j] = xp;
-          o[jj] = v[jj] * gam;                 // dP^
-        } else {
-          const float dl = j < i_row ? -v[jj] : 0.f;
-          const float lh = Lm[i_row * 64 + j];
-          xl[jj] = dl * be * lh;
-          rsum += xl[jj];
-          dbl = fmaf(dl, lh, dbl);
-          o[jj] = dl * be * gam;               // dKK
+      for (int k = 0; k < 16; ++k) {
+        const float x = __shfl_xor_sync(0xffffffffu, lower ? v[16 + k] : v[k], 16);
+        dp[k] = lower ? v[k] : x;
+        fd[k] = lower ? x : v[16 + k];
+      }
+      const int j0 = 32 * half + (lower ? 0 : 16);
+      // this row's P (hi + lo from the image) and Gamma * KK for the 16 columns, loaded up front
+      float pv[16], lv[16];
+      {
+        const int r = img_row(i_row);
+        const uint8_t* prow = smem + GR_P + r * 128;
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          const int ch = (j0 >> 3) + cc;
+          const uint4 hi = *reinterpret_cast<const uint4*>(prow + ((ch ^ (r & 7)) << 4));
+          const uint4 lo = *reinterpret_cast<const uint4*>(prow + 2048 + ((ch ^ (r & 7)) << 4));
+          const uint32_t hw[4] = {hi.x, hi.y, hi.z, hi.w}, lw[4] = {lo.x, lo.y, lo.z, lo.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&hw[e]);
+            const __nv_bfloat162 l2 = *reinterpret_cast<const __nv_bfloat162*>(&lw[e]);
+            pv[8 * cc + 2 * e] = __low2float(h2) + __low2float(l2);
+            pv[8 * cc + 2 * e + 1] = __high2float(h2) + __high2float(l2);
+          }
+        }
+        const float4* lrow = reinterpret_cast<const float4*>(Lm + i_row * 64 + j0);
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          const float4 x = lrow[c4];
+          lv[4 * c4] = x.x, lv[4 * c4 + 1] = x.y, lv[4 * c4 + 2] = x.z, lv[4 * c4 + 3] = x.w;
         }
       }
-      const int ri = img_row(i_row) + (lower ? 0 : 16);
-      tc::st_row_bf16x2_32(smem + GR_FHI, smem + GR_FLO, ri, o, 4 * half);
-    }
-    __syncthreads();
-    if (!lower) {
+      float ph[16], kh[16], xs[16];
 #pragma unroll
-      for (int jj = 0; jj < 32; ++jj) scratch[i_row * 65 + 32 * half + jj] += xl[jj];
+      for (int k = 0; k < 16; ++k) {
+        const int j = j0 + k;
+        const float gam = j <= i_row ? __expf(bi - sgt[j]) : 0.f;
+        const float xp = j <= i_row ? dp[k] * pv[k] : 0.f;
+        const float dl = j < i_row ? -fd[k] : 0.f;
+        const float xl = dl * be * lv[k];
+        dbl = fmaf(dl, lv[k], dbl);
+        xs[k] = xp + xl;
+        rsum += xs[k];
+        ph[k] = dp[k] * gam;        // dP^
+        kh[k] = dl * be * gam;      // dKK
+      }
+#pragma unroll
+      for (int k = 0; k < 16; ++k) scratch[i_row * 65 + j0 + k] = xs[k];
+      const int r = img_row(i_row), c0 = j0 >> 3;
+      st_hilo16_chunks(smem + GR_FHI, smem + GR_FLO, r, ph, c0);
+      st_hilo16_chunks(smem + GR_FHI, smem + GR_FLO, r + 16, kh, c0);
     }
-    // per-row partials from both column halves: 0 t1, 1 t2, 2 t4 (lower), 3 t3 (upper), 4 row sum of
-    // the P terms (lower), 5 that of the L terms (upper), 6 the d beta part of the L terms (upper)
+    // per-row partials from both column halves: 0 t1, 1 t2, 2 t4 (lower lanes), 3 t3 (upper lanes),
+    // 4 the Gamma-term row sum and 6 the d beta part of the L terms (both lanes of the pair summed)
     if (lower) {
       srow[0][half][i_row] = t1;
       srow[1][half][i_row] = t2;
       srow[2][half][i_row] = t4;
-      srow[4][half][i_row] = rsum;
     } else {
       srow[3][half][i_row] = t3;
-      srow[5][half][i_row] = rsum;
-      srow[6][half][i_row] = dbl;
+    }
+    {
+      float rs = rsum + __shfl_xor_sync(0xffffffffu, rsum, 16);
+      float db2 = dbl + __shfl_xor_sync(0xffffffffu, dbl, 16);
+      if (lower) {
+        srow[4][half][i_row] = rs;
+        srow[6][half][i_row] = db2;
+      }
     }
     {
       float t5w = t5;
@@ -1307,38 +1366,52 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
       }
       tc::mma_commit(&bar_mma);
     }
-    // column sums of the Gamma terms (fixed order); row totals; d b
-    if (tid < 64) {
+    // column sums of the Gamma terms (fixed order: four 16-row partials, then their sum); row totals; d b
+    {
+      const int col = tid & 63, part = tid >> 6;
       float cs = 0.f;
-      for (int i = 0; i < 64; ++i) cs += scratch[i * 65 + tid];
-      scol[tid] = cs;
+#pragma unroll 4
+      for (int i = 16 * part; i < 16 * part + 16; ++i) cs += scratch[i * 65 + col];
+      scratch[64 * 65 + part * 64 + col] = cs;
     }
     __syncthreads();
-    float lt4 = 0.f;
+    float lt4 = 0.f, dbv = 0.f;
     if (tid < 64) {
       const int i = tid;
+      const float* cp = reinterpret_cast<const float*>(smem + GR_SCR) + 64 * 65;
+      const float csum = (cp[i] + cp[64 + i]) + (cp[128 + i] + cp[192 + i]);
       const float bi_ = sgt[i], be_ = sgt[64 + i], gi_ = __expf(bi_), lam_ = __expf(bC - bi_);
       const float t2_ = srow[1][0][i] + srow[1][1][i], t3_ = srow[3][0][i] + srow[3][1][i];
       const float t4_ = srow[2][0][i] + srow[2][1][i];
-      const float rs = srow[4][0][i] + srow[4][1][i] + srow[5][0][i] + srow[5][1][i];
-      sdb[i] = rs - scol[i] + gi_ * t3_ - be_ * gi_ * t2_ - lam_ * t4_;
+      const float rs = srow[4][0][i] + srow[4][1][i];
+      dbv = rs - csum + gi_ * t3_ - be_ * gi_ * t2_ - lam_ * t4_;
       lt4 = lam_ * t4_;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) lt4 += __shfl_xor_sync(0xffffffffu, lt4, o);
     if (lane == 0 && warp < 2) sred[8 + warp] = lt4;
     __syncthreads();
-    if (tid == 0) {
+    if (tid == 63) {
       float st5 = 0.f;
       for (int w = 0; w < 8; ++w) st5 += sred[w];
-      sdb[63] += (sred[8] + sred[9]) + __expf(bC) * st5;
+      dbv += (sred[8] + sred[9]) + __expf(bC) * st5;
+    }
+    // d log g_i = sum over rows i' >= i of d b_i': a suffix scan over the 64 rows (two warps)
+    if (tid < 64) {
+      float x = dbv;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_down_sync(0xffffffffu, x, o);
+        if (lane + o < 32) x += y;
+      }
+      if (tid == 32) sdb[0] = x;  // the upper warp's total (rows 32..63)
+      sdb[1 + tid] = x;
     }
     __syncthreads();
     float pa = 0.f, pd = 0.f;  // layer mode: this row's share of the head's dA_log, ddt_bias
     if (tid < 64 && tid < L) {
       const int i = tid;
-      float dl = 0.f;  // d log g_i = sum over rows i' >= i of d b_i'
-      for (int i2 = 63; i2 >= i; --i2) dl += sdb[i2];
+      const float dl = sdb[1 + i] + (i < 32 ? sdb[0] : 0.f);  // d log g_i
       const int64_t gi_idx = (tok0 + i) * Hv + hv;
       const float dbe = srow[0][0][i] + srow[0][1][i] + srow[6][0][i] + srow[6][1][i];
       if (a.g) {
