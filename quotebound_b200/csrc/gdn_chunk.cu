@@ -300,8 +300,10 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CU
   if (ok && tid == 0) {
     tc::fence_after_sync();
     const uint32_t kt = tc::smem_u32(ktile), qt = tc::smem_u32(qtile);
-    tc::mma_tile<tc::kBF16>(tmem, kt, false, 64, kt, false, 64, 64, 64, DK, false);        // K K^T
-    tc::mma_tile<tc::kBF16>(tmem + 64, qt, false, 64, kt, false, 64, 64, 64, DK, false);   // Q K^T
+    // K K^T into the lower half-lanes and Q K^T into the upper half-lanes of the same 64 columns, so
+    // that all 128 threads own one row of one product
+    tc::mma_tile<tc::kBF16>(tmem, kt, false, 64, kt, false, 64, 64, 64, DK, false);
+    tc::mma_tile<tc::kBF16>(tmem + (16u << 16), qt, false, 64, kt, false, 64, 64, 64, DK, false);
     tc::mma_commit(&bar_mma);
   }
   if (ok && hv % (a.geo.Hv / a.geo.Hk) == 0) {
@@ -318,66 +320,125 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CU
   ok = __syncthreads_and(ok && tc::mbar_wait(&bar_mma, 0, a.err, 2)) != 0;
   tc::fence_after_sync();
   const size_t mat = (size_t)(c * a.geo.Hv + hv) * 4096;
-  // The K and Q tiles are free once the products above completed: they stage the T and P images.
-  uint8_t* timg = ktile;
+  // The Q tile is free once the products above completed: it stages the P image.
   uint8_t* pimg = qtile;
+  float* Lt = Lm;  // transposed: Lt[j * LS + i] = beta_i Gamma_ij (K K^T)_ij for j < i
   if (ok) {
     const int i = 16 * warp + (lane & 15);
-    const bool owner = lane < 16;
-    const int rh = img_row(i);
+    const bool kkside = lane < 16;  // lower lanes: K K^T row i; upper lanes: Q K^T row i
     const float bi = sb[i], be = sbeta[i];
     float v[32];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      tc::tmem_ld32(tc::taddr(tmem, 32 * warp, 32 * h), v);  // K K^T
-      if (owner) {
-        float lrow[32];
+      tc::tmem_ld32(tc::taddr(tmem, 32 * warp, 32 * h), v);
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          const int j = 32 * h + jj;
-          const float gk = j < i ? __expf(bi - sb[j]) * v[jj] : 0.f;
-          Lm[i * LS + j] = be * gk;
-          lrow[jj] = gk;
-        }
-        if (a.Lbuf) store_row32<float>(a.Lbuf + mat + i * 64 + 32 * h, lrow);
+      for (int jj = 0; jj < 32; ++jj) {
+        const int j = 32 * h + jj;
+        const float gam = __expf(bi - sb[j]);  // Gamma_ij (only j <= i is used)
+        v[jj] = (kkside ? j < i : j <= i) ? gam * v[jj] : 0.f;
       }
-      tc::tmem_ld32(tc::taddr(tmem, 32 * warp, 64 + 32 * h), v);  // Q K^T
-      if (owner) {
+      if (kkside) {
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          const int j = 32 * h + jj;
-          v[jj] = j <= i ? __expf(bi - sb[j]) * v[jj] : 0.f;
-        }
-        tc::st_row_bf16x2_32(pimg, pimg + 2048, rh, v, 4 * h);
+        for (int jj = 0; jj < 32; ++jj) Lt[(32 * h + jj) * LS + i] = be * v[jj];
+        if (a.Lbuf) store_row32<float>(a.Lbuf + mat + i * 64 + 32 * h, v);
+      } else {
+        tc::st_row_bf16x2_32(pimg, pimg + 2048, img_row(i), v, 4 * h);
       }
     }
   }
   tc::fence_before_sync();
   __syncthreads();
+  // T = (I + L)^-1 in 2 x 2 blocks of 32: T00 = (I + L00)^-1 and T11 = (I + L11)^-1 by column sweep
+  // (thread (b, c) < 64 owns column c of block b in registers: t_j is final once the columns before it
+  // have been swept, and sweeping column j updates the rows below it independently), then
+  // T10 = -T11 (L10 T00) as two 32 x 32 products over all 128 threads.  Tt[col * 64 + row] holds T
+  // transposed (in the K tile, free now).
+  float* Tt = reinterpret_cast<float*>(ktile);
   if (ok && tid < 64) {
-    // column `col` of T = (I + L)^-1 by forward substitution, kept in registers
-    const int col = tid;
-    float t[64];
+    const int b = tid >> 5, cc = tid & 31;
+    float t[32];
 #pragma unroll
-    for (int i = 0; i < 64; ++i) {
-      float s = (i == col) ? 1.f : 0.f;
-      const float* Li = Lm + i * LS;
+    for (int i = 0; i < 32; ++i) t[i] = i == cc ? 1.f : 0.f;
 #pragma unroll
-      for (int j = 0; j < i; ++j) s = fmaf(-Li[j], t[j], s);
-      t[i] = s;
+    for (int j = 0; j < 31; ++j) {
+      const float tj = t[j];
+      const float* Lj = Lt + (32 * b + j) * LS + 32 * b;
+#pragma unroll
+      for (int i4 = (j + 1) & ~3; i4 < 32; i4 += 4) {
+        const float4 l4 = *reinterpret_cast<const float4*>(Lj + i4);
+        if (i4 + 0 > j) t[i4 + 0] = fmaf(-l4.x, tj, t[i4 + 0]);
+        if (i4 + 1 > j) t[i4 + 1] = fmaf(-l4.y, tj, t[i4 + 1]);
+        if (i4 + 2 > j) t[i4 + 2] = fmaf(-l4.z, tj, t[i4 + 2]);
+        t[i4 + 3] = fmaf(-l4.w, tj, t[i4 + 3]);
+      }
     }
-    // the image: hi and lo halves of column col
+    float4* dst = reinterpret_cast<float4*>(Tt + (32 * b + cc) * 64 + 32 * b);
 #pragma unroll
-    for (int i = 0; i < 64; ++i) {
-      const int r = img_row(i);
-      const uint32_t off = r * 128 + ((((col >> 3) ^ (r & 7))) << 4) + (col & 7) * 2;
-      const __nv_bfloat16 hi = __float2bfloat16_rn(t[i]);
-      *reinterpret_cast<__nv_bfloat16*>(timg + off) = hi;
-      *reinterpret_cast<__nv_bfloat16*>(timg + off + 2048) = __float2bfloat16_rn(t[i] - __bfloat162float(hi));
+    for (int q = 0; q < 8; ++q) dst[q] = make_float4(t[4 * q], t[4 * q + 1], t[4 * q + 2], t[4 * q + 3]);
+    if (b == 1) {  // T01 = 0 (the columns of block 1 above the diagonal block)
+      float4* z = reinterpret_cast<float4*>(Tt + (32 + cc) * 64);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) z[q] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     float* gd = a.gates + (c * a.geo.Hv + hv) * 128;
     gd[tid] = sb[tid];
     gd[64 + tid] = sbeta[tid];
+  }
+  __syncthreads();
+  float* Xs = Lm;  // X = L10 T00 [32][32], where L was (after the products read it)
+  {
+    const int r = tid & 31, cg = tid >> 5;  // row r of the block, columns 8 cg .. 8 cg + 7
+    float x[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) x[q] = 0.f;
+    if (ok) {
+#pragma unroll 2
+      for (int k4 = 0; k4 < 8; ++k4) {
+        float l[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) l[e] = Lt[(4 * k4 + e) * LS + 32 + r];  // L[32 + r][k]
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 tq = *reinterpret_cast<const float4*>(Tt + (8 * cg + q) * 64 + 4 * k4);  // T00[k][c]
+          x[q] = fmaf(l[0], tq.x, fmaf(l[1], tq.y, fmaf(l[2], tq.z, fmaf(l[3], tq.w, x[q]))));
+        }
+      }
+    }
+    __syncthreads();
+    reinterpret_cast<float4*>(Xs + r * 32 + 8 * cg)[0] = make_float4(x[0], x[1], x[2], x[3]);
+    reinterpret_cast<float4*>(Xs + r * 32 + 8 * cg)[1] = make_float4(x[4], x[5], x[6], x[7]);
+    __syncthreads();
+    float y[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) y[q] = 0.f;
+    if (ok) {
+#pragma unroll 4
+      for (int k = 0; k < 32; ++k) {
+        const float tk = Tt[(32 + k) * 64 + 32 + r];  // T11[r][k] (zero for k > r)
+        const float4 x0 = reinterpret_cast<const float4*>(Xs + k * 32 + 8 * cg)[0];
+        const float4 x1 = reinterpret_cast<const float4*>(Xs + k * 32 + 8 * cg)[1];
+        y[0] = fmaf(-tk, x0.x, y[0]);
+        y[1] = fmaf(-tk, x0.y, y[1]);
+        y[2] = fmaf(-tk, x0.z, y[2]);
+        y[3] = fmaf(-tk, x0.w, y[3]);
+        y[4] = fmaf(-tk, x1.x, y[4]);
+        y[5] = fmaf(-tk, x1.y, y[5]);
+        y[6] = fmaf(-tk, x1.z, y[6]);
+        y[7] = fmaf(-tk, x1.w, y[7]);
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) Tt[(8 * cg + q) * 64 + 32 + r] = y[q];  // T10[r][c]
+    }
+  }
+  __syncthreads();
+  // the T image (staged where L was): thread (row i, half) converts columns 32 half .. + 31 of row i
+  uint8_t* timg = reinterpret_cast<uint8_t*>(Lm);
+  if (ok) {
+    const int i = tid & 63, h = tid >> 6;
+    float v[32];
+#pragma unroll
+    for (int jj = 0; jj < 32; ++jj) v[jj] = Tt[(32 * h + jj) * 64 + i];
+    tc::st_row_bf16x2_32(timg, timg + 2048, img_row(i), v, 4 * h);
   }
   __syncthreads();
   if (ok) {  // both images out, 16-byte stores
