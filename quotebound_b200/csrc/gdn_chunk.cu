@@ -470,8 +470,16 @@ struct StateArgs {
   const uint8_t* Timg;    // [chunks, Hv] x 16 KB operand images from the prep
   const uint8_t* Pimg;
   const uint8_t* KQimg;   // [chunks, Hk] x 32 KB
+  // training: D = T E for the backward (or null), fp32 tiles [chunks, Hv, Dv / 32 slices][64 rows][32]
+  float* Ds;
   int* err;
 };
+
+// Store 16 floats (4 x 16 bytes).
+__device__ __forceinline__ void st16_f32(float* p, const float (&v)[16]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) reinterpret_cast<float4*>(p)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+}
 
 // Shared memory of the forward walk (bytes from a 1024-aligned base).
 constexpr int FW_KQ = 0;           // 2 x 32 KB bf16 [K; Q] tile, 16-row groups interleaved (TMA)
@@ -483,7 +491,8 @@ constexpr int FW_D = 155648;       // 8 KB bf16 D [hi | lo]
 constexpr int FW_DT = 163840;      // 8 KB bf16 D~ = diag(lambda) D [hi | lo]
 constexpr int FW_CK = 172032;      // 16 KB fp32 chunk-start state staging [32 dv][128 dk] (bulk store)
 constexpr int FW_V = 188416;       // 2 x 4 KB bf16 value rows [64][32] (TMA)
-constexpr int FW_SMEM = 196608 + 1024;
+constexpr int FW_DS = 196608;      // 2 x 8 KB fp32 D rows [64][32] staging (bulk store, training)
+constexpr int FW_SMEM = 212992 + 1024;
 
 // Descriptors of the stacked operands.  The [K; Q] tile holds, per 64-column slab (16 KB), the row
 // groups K 0-15, Q 0-15, K 16-31, Q 16-31, ... (2 KB each).
@@ -634,6 +643,8 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
     if (!ok) break;
     // 3. K side: E = diag(beta) (V - diag(gamma) K S^T) as the [hi | lo] operand; Q side: gamma Q S^T
     float yp[16];
+    const int srow_off = i_row * 128 + 64 * half;  // this thread's 16 floats in a [64][32] fp32 staging tile
+    const size_t ptile = ((size_t)(cg * Hv + hv) * (DV / DVT) + blockIdx.x) * 2048;  // this CTA's tile
     {
       tmem_ld_hl16(tl + cA, half, yp);
       if (kside) {
@@ -655,6 +666,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
       mma_run<4, kKmaj128>(tmem + cD, idA, tc::smem_u32(smem + FW_T + buf * 16384), tc::smem_u32(smem + FW_E), false);
       tc::mma_commit(&bar_mma);
     }
+
     ok = wait_all(&bar_mma, ph, a.err, 12);
     ph ^= 1;
     tc::fence_after_sync();
@@ -665,6 +677,8 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
       if (kside) {
         tc::st_row_hilo16(smem + FW_D, i_row, d, half);
       } else {
+        // (the other staging buffer's store was read before the last chunk's final barrier)
+        if (a.Ds) st16_f32(reinterpret_cast<float*>(smem + FW_DS + buf * 8192 + srow_off), d);
         const float lam = __expf(bC - bi);
 #pragma unroll
         for (int j = 0; j < 16; ++j) d[j] *= lam;
@@ -681,6 +695,10 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
       mma_run<4, kKT>(tmem + cS, idT, kq, tc::smem_u32(smem + FW_DT), false);
       mma_run<4, kKmaj128>(tmem + cO, idA, tc::smem_u32(smem + FW_P + buf * 16384), tc::smem_u32(smem + FW_D), false);
       tc::mma_commit(&bar_mma);
+    }
+    if (tid == 32 && a.Ds) {
+      tc::bulk_store(a.Ds + ptile, smem + FW_DS + buf * 8192, 8192);
+      tc::bulk_commit();
     }
     ok = wait_all(&bar_mma, ph, a.err, 13);
     ph ^= 1;
@@ -725,20 +743,22 @@ struct BwdStateArgs {
   const uint8_t* Timg;    // the forward's operand images
   const uint8_t* Pimg;
   const uint8_t* KQimg;
+  float* Fs;              // F = T^T dD for the gradient kernel, fp32 tiles [chunks, Hv, Dv / 32][64][32]
   int* err;
 };
 
 constexpr int BW_KQ = 0;           // 2 x 32 KB bf16 [K; Q] image
-constexpr int BW_T = 65536;        // 2 x 16 KB bf16 [T_hi; T_lo] image
-constexpr int BW_P = 98304;        // 2 x 16 KB bf16 [P_hi; P_lo] image
-constexpr int BW_S = 131072;       // 16 KB bf16 dS [hi | lo], MN-major [128 dk][64]
-constexpr int BW_DO = 147456;      // 8 KB bf16 dO, MN-major [64][32] (128-byte rows, half used)
-constexpr int BW_GD = 155648;      // 8 KB bf16 gamma dO [hi | lo]
-constexpr int BW_DD = 163840;      // 8 KB bf16 dD [hi | lo]
-constexpr int BW_H = 172032;       // 8 KB bf16 H = -beta gamma F [hi | lo]
-constexpr int BW_CK = 180224;      // 16 KB fp32 dS staging [32 dv][128 dk] (bulk store)
-constexpr int BW_V = 196608;       // 2 x 4 KB bf16 dO rows [64][32] (TMA)
-constexpr int BW_SMEM = 204800 + 1024;
+constexpr int BW_T = 65536;        // 16 KB bf16 [T_hi; T_lo] image (reloaded once the chunk's F is done)
+constexpr int BW_P = 81920;        // 16 KB bf16 [P_hi; P_lo] image (reloaded once P^T dO is done)
+constexpr int BW_S = 98304;        // 16 KB bf16 dS [hi | lo], MN-major [128 dk][64]
+constexpr int BW_DO = 114688;      // 8 KB bf16 dO, MN-major [64][32] (128-byte rows, half used)
+constexpr int BW_GD = 122880;      // 8 KB bf16 gamma dO [hi | lo]
+constexpr int BW_DD = 131072;      // 8 KB bf16 dD [hi | lo]
+constexpr int BW_H = 139264;       // 8 KB bf16 H = -beta gamma F [hi | lo]
+constexpr int BW_CK = 147456;      // 16 KB fp32 dS staging [32 dv][128 dk] (bulk store)
+constexpr int BW_V = 163840;       // 2 x 4 KB bf16 dO rows [64][32] (TMA)
+constexpr int BW_FS = 172032;      // 2 x 8 KB fp32 F rows [64][32] staging (bulk store)
+constexpr int BW_SMEM = 188416 + 1024;
 
 // K-step ks of the transpose of one half (part 0 = hi, 1 = lo) of a [hi; lo] image as the M = 64
 // MN-major A operand: the image's rows (chunk steps) are K.
@@ -746,15 +766,33 @@ __device__ __forceinline__ uint64_t desc_img_t(uint32_t img, int part, int ks) {
   return tc::sdesc(img + part * 2048 + ks * 4096, 8192, 1024, 2);
 }
 
+// Load 16 fp32 of a shared row.
+__device__ __forceinline__ void ld16_f32(const uint8_t* p, float (&v)[16]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float4 x = reinterpret_cast<const float4*>(p)[q];
+    v[4 * q] = x.x, v[4 * q + 1] = x.y, v[4 * q + 2] = x.z, v[4 * q + 3] = x.w;
+  }
+}
+// 16 bf16 of a shared row as floats, zero unless valid.
+__device__ __forceinline__ void ld16_bf16(const uint8_t* p, bool valid, float (&v)[16]) {
+  Row16 r;
+  const uint4 z = make_uint4(0, 0, 0, 0);
+  r.w[0] = valid ? reinterpret_cast<const uint4*>(p)[0] : z;
+  r.w[1] = valid ? reinterpret_cast<const uint4*>(p)[1] : z;
+  cvt_row16(r, v);
+}
+
 // The backward state walk: chunks in reverse, 32 rows of dS per CTA, 256 threads as in the forward walk
-// (thread t holds dS[dv0 + 16 (w >> 2) + j][t & 127]).
+// (thread t holds dS[dv0 + 16 (w >> 2) + j][t & 127]).  Besides dv, the per-chunk dS and dh0 it leaves
+// the gradient kernel F = T^T dD.
 template <typename Tout>
 __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_constant__ CUtensorMap dmap,
                                                               BwdStateArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(16) float sg[2][128];
-  __shared__ uint64_t bar_tma[2], bar_mma;
+  __shared__ uint64_t bar_tma[2], bar_t, bar_p, bar_mma;
   __shared__ uint32_t tmem_slot;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -770,6 +808,8 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
   if (tid == 0) {
     tc::mbar_init(&bar_tma[0], 1);
     tc::mbar_init(&bar_tma[1], 1);
+    tc::mbar_init(&bar_t, 1);
+    tc::mbar_init(&bar_p, 1);
     tc::mbar_init(&bar_mma, 1);
     tc::fence_mbar_init();
   }
@@ -786,21 +826,30 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
     for (int j = 0; j < 16; ++j) ds[j] = a.dhT ? a.dhT[base + (size_t)j * DK] : 0.f;
   }
 
-  auto issue_loads = [&](int64_t jc, int buf) {
+  // one thread of warp 1 issues every copy; the T and P images have one buffer each, refilled as soon
+  // as the chunk's last product with them has completed
+  auto issue_main = [&](int64_t jc, int buf) {
     const int64_t cg = c_first + jc;
-    tc::mbar_arrive_expect_tx(&bar_tma[buf], 32768 + 2 * 16384 + 512 + 4096);
+    tc::mbar_arrive_expect_tx(&bar_tma[buf], 32768 + 512 + 4096);
     tc::bulk_load(smem + BW_KQ + buf * 32768, a.KQimg + (size_t)(cg * a.geo.Hk + hk) * 32768, 32768, &bar_tma[buf]);
-    tc::bulk_load(smem + BW_T + buf * 16384, a.Timg + (size_t)(cg * Hv + hv) * 16384, 16384, &bar_tma[buf]);
-    tc::bulk_load(smem + BW_P + buf * 16384, a.Pimg + (size_t)(cg * Hv + hv) * 16384, 16384, &bar_tma[buf]);
     tc::bulk_load(sg[buf], a.gates + (cg * Hv + hv) * 128, 512, &bar_tma[buf]);
     tc::tma_load_3d(smem + BW_V + buf * 4096, &dmap, &bar_tma[buf], dv0, hv, (int)(seq0 + jc * C));
   };
-
+  auto issue_t = [&](int64_t jc) {
+    tc::mbar_arrive_expect_tx(&bar_t, 16384);
+    tc::bulk_load(smem + BW_T, a.Timg + (size_t)((c_first + jc) * Hv + hv) * 16384, 16384, &bar_t);
+  };
+  auto issue_p = [&](int64_t jc) {
+    tc::mbar_arrive_expect_tx(&bar_p, 16384);
+    tc::bulk_load(smem + BW_P, a.Pimg + (size_t)((c_first + jc) * Hv + hv) * 16384, 16384, &bar_p);
+  };
   const int i_row = 16 * quad + (lane & 15);
   const bool kside = lane < 16;
   if (nchunks > 0 && tid == 32) {
     tc::prefetch_tmap(&dmap);
-    issue_loads(nchunks - 1, 0);
+    issue_main(nchunks - 1, 0);
+    issue_t(nchunks - 1);
+    issue_p(nchunks - 1);
   }
   uint32_t ph = 0;
   bool ok = true;
@@ -815,6 +864,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
     const int64_t cg = c_first + jc;
     const int64_t tok0 = seq0 + jc * C;
     const int L = (int)min((int64_t)C, seq1 - tok0);
+    const int srow_off = i_row * 128 + 64 * half;  // this thread's 16 floats in a [64][32] fp32 tile
 
     // 1. dS of this chunk's end: staged for the gradient kernel, and as the [hi | lo] operand row dk
     {
@@ -825,12 +875,15 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
     tc::st_row_hilo16(smem + BW_S, dk, ds, half);
     tc::fence_async_smem();
     tc::fence_before_sync();
-    ok = wait_all(&bar_tma[buf], (uint32_t)((it >> 1) & 1), a.err, 20);
+    ok = tc::mbar_wait(&bar_tma[buf], (uint32_t)((it >> 1) & 1), a.err, 20) &&
+         tc::mbar_wait(&bar_t, (uint32_t)(it & 1), a.err, 25) && tc::mbar_wait(&bar_p, (uint32_t)(it & 1), a.err, 26);
+    ok = __syncthreads_and(ok) != 0;
     tc::fence_after_sync();
     if (!ok) break;
     if (tid == 32) {
       tc::bulk_store(a.dsbuf + ((cg * Hv + hv) * DV + dv0) * (size_t)DK, smem + BW_CK, DVT * DK * 4);
       tc::bulk_commit();
+      if (jc > 0) issue_main(jc - 1, buf ^ 1);  // the previous chunk's [K; Q], gates and dO rows
     }
     const float* gb = sg[buf];
     const float bi = gb[i_row], be = gb[64 + i_row], gi = __expf(bi), bC = gb[63];
@@ -860,7 +913,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t kq = tc::smem_u32(smem + BW_KQ + buf * 32768);
-    const uint32_t pimg = tc::smem_u32(smem + BW_P + buf * 16384), timg = tc::smem_u32(smem + BW_T + buf * 16384);
+    const uint32_t pimg = tc::smem_u32(smem + BW_P), timg = tc::smem_u32(smem + BW_T);
     // 3. [K; Q] dS^T (the K rows are X1 = K dS^T) and G = P^T dO (P_hi^T and P_lo^T accumulated)
     if (tid == 0) {
       mma_run<8, kKmaj128>(tmem + cX, idX, kq, tc::smem_u32(smem + BW_S), false);
@@ -872,13 +925,11 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
           tc::mma_bf16(tmem + cG, desc_img_t(pimg, part, ks), desc_hl(dO, ks), idG, (part | ks) ? 1u : 0u);
       tc::mma_commit(&bar_mma);
     }
-    if (tid == 32) {
-      if (jc > 0) issue_loads(jc - 1, buf ^ 1);  // the previous chunk's tiles
-    }
     ok = wait_all(&bar_mma, ph, a.err, 21);
     ph ^= 1;
     tc::fence_after_sync();
     if (!ok) break;
+    if (tid == 32 && jc > 0) issue_p(jc - 1);  // P's last reader has completed
     // 4. dD = diag(lambda) K dS^T + P^T dO (K side), as the [hi | lo] operand.  tcgen05.ld is a
     //    warp-wide aligned instruction: every lane executes the same loads, outside the branch.
     {
@@ -911,10 +962,13 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
     ph ^= 1;
     tc::fence_after_sync();
     if (!ok) break;
+    if (tid == 32 && jc > 0) issue_t(jc - 1);  // T's last reader has completed
     {
       float f[16];
       tmem_ld_hl16(tl + cF, half, f);
       if (kside) {
+        // (the other staging buffer's store was read before the last chunk's step-4 barrier)
+        st16_f32(reinterpret_cast<float*>(smem + BW_FS + buf * 8192 + srow_off), f);
         float o[16];
         if (i_row < L) {
 #pragma unroll
@@ -936,6 +990,10 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
       mma_run<4, kQT>(tmem + cU, idU, kq, tc::smem_u32(smem + BW_GD), false);
       mma_run<4, kKT>(tmem + cU, idU, kq, tc::smem_u32(smem + BW_H), true);
       tc::mma_commit(&bar_mma);
+    }
+    if (tid == 32) {
+      tc::bulk_store(a.Fs + ((size_t)(cg * Hv + hv) * (DV / DVT) + blockIdx.x) * 2048, smem + BW_FS + buf * 8192, 8192);
+      tc::bulk_commit();
     }
     ok = wait_all(&bar_mma, ph, a.err, 23);
     ph ^= 1;
@@ -963,12 +1021,18 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
 
 // ------------------------------------------------------------------------------------------------
 // Per-chunk gradients: one CTA per (chunk, key head); its value heads in turn, Dv in four slices of 32.
+// D comes from the forward walk and F from the reverse walk.  Per value head this kernel accumulates
+// over the value rows dO S, F S, D dS (unscaled) and dO D^T, F D^T; the finalize takes the per-row
+// terms of d log g from them -- Q_i . (dO S)_i = dO_i . Y_i, K_i . (F S)_i = F_i . R_i,
+// K_i . (D dS)_i = D_i . (K dS^T)_i -- and adds gamma dO S, -beta gamma F S + lambda D dS and the
+// Gamma-masked products into dQ and dK.
 struct GradArgs {
   Geo geo;
   const float* g;           // [B*T, Hv] (dg = d log g / g); null in layer mode
   const float* gates;       // [chunks, Hv, 2, 64]
-  const uint8_t *Timg, *Pimg, *KQimg;  // the forward's operand images
+  const uint8_t *Pimg, *KQimg;  // the forward's operand images
   const float* Lbuf;        // [chunks, Hv, 64, 64] strict-lower Gamma * K K^T
+  const float *Ds, *Fs;     // D and F, fp32 tiles [chunks, Hv, Dv / 32][64][32]
   void *dq, *dk;            // [B*T, Hk, Dk]
   float *dg, *dbeta;        // [B*T, Hv]; layer mode: da, db
   int* err;
@@ -980,16 +1044,12 @@ struct GradArgs {
 
 // Shared memory of the gradient kernel.
 constexpr int GR_KQ = 0;           // 32 KB bf16 [K; Q] image
-constexpr int GR_T = 32768;        // 16 KB bf16 [T_hi; T_lo] image of the value head
-constexpr int GR_P = 49152;        // 16 KB bf16 [P_hi; P_lo] image
-constexpr int GR_BUF = 65536;      // 2 x 40 KB slice buffers: S, dS (fp32, MN-major tf32 [32 dv][128 dk]), V, dO rows
-constexpr int GR_BS = 40960;       //   buffer stride; S at +0, dS at +16384, V at +32768, dO at +36864
-constexpr int GR_SHL = 147456;     // 16 KB bf16 [S_hi; S_lo] K-major [64 rows][128 dk]   | A1 [gamma dO; -beta gamma F]
-constexpr int GR_DHL = 163840;     // 16 KB bf16 [dS_hi; dS_lo]                           | A3 [dO; F]
-constexpr int GR_DOT = 180224;     // 8 KB bf16 dO, MN-major [64][32] (operand of P^T dO)
-constexpr int GR_EHL = 188416;     // 8 KB bf16 E [hi | lo]                                | A2 lambda D (tf32)
-constexpr int GR_DDH = 196608;     // 8 KB bf16 dD [hi | lo]                               | B3 D (tf32, K-major)
-constexpr int GR_SMEM = 204800 + 1024;
+constexpr int GR_P = 32768;        // 16 KB bf16 [P_hi; P_lo] image of the value head
+constexpr int GR_BUF = 49152;      // 2 x 56 KB slice buffers: S, dS (fp32, MN-major tf32 [32 dv][128 dk]),
+constexpr int GR_BS = 57344;       //   D, F (fp32 [64][32]), dO and V rows (bf16 [64][32])
+constexpr int GR_A = 163840;       // 16 KB tf32 [dO; F], K-major, 16-row groups interleaved
+constexpr int GR_DT = 180224;      // 8 KB tf32 D, K-major [64][32] (A of D dS, B of [dO; F] D^T)
+constexpr int GR_SMEM = 188416 + 1024;
 // the value head's finalize reuses the slice buffers: L (fp32 [64][64]), the [dP^; dKK] images, a
 // column-sum scratch
 constexpr int GR_L = GR_BUF, GR_FHI = GR_BUF + 16384, GR_FLO = GR_BUF + 32768, GR_SCR = GR_BUF + 49152;
@@ -1020,26 +1080,34 @@ __device__ __forceinline__ void st_hilo16_chunks(uint8_t* hi_img, uint8_t* lo_im
     *reinterpret_cast<uint4*>(lo_img + off) = make_uint4(l[0], l[1], l[2], l[3]);
   }
 }
-// Element j of row r of a bf16 [hi; lo] image (64 columns).
-__device__ __forceinline__ float img_elem(const uint8_t* img, int r, int j) {
-  const uint32_t off = r * 128 + ((((j >> 3) ^ (r & 7))) << 4) + (j & 7) * 2;
-  return __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(img + off)) +
-         __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(img + off + 2048));
+// 32 bf16 of row r of a K-major bf16 image slab (128-byte swizzle), columns 32 m .. 32 m + 31.
+__device__ __forceinline__ void ld_img_row32(const uint8_t* slab, int r, int m, float (&v)[32]) {
+#pragma unroll
+  for (int cc = 0; cc < 4; ++cc) {
+    const uint4 w = *reinterpret_cast<const uint4*>(slab + r * 128 + (((4 * m + cc) ^ (r & 7)) << 4));
+    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&u[e]);
+      v[8 * cc + 2 * e] = __low2float(h);
+      v[8 * cc + 2 * e + 1] = __high2float(h);
+    }
+  }
 }
 
 // 256 threads.  Warp w reads TMEM lanes 32 (w & 3) .. + 31 and handles columns 16 (w >> 2) .. + 15 of a
-// 32-wide slice (32 (w >> 2) .. of the 64-wide finalize, 64 (w >> 2) .. of the 128-wide output).  The
-// stacked accumulators hold chunk row i = 16 (w & 3) + l in lane l ("lower": R, X1, G, D, F, dQ, dP)
-// and in lane l + 16 ("upper": Y, dK, F D^T).
+// 32-wide slice (32 (w >> 2) .. of the 64-wide finalize, 64 (w >> 2) .. of the 128-wide dk).  The
+// stacked accumulators hold chunk row i = 16 (w & 3) + l in lane l ("lower": dQ, dO S, dP) and in lane
+// l + 16 ("upper": dK, F S, D dS, F D^T).
 template <typename Tout>
 __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_constant__ CUtensorMap smap_mn,
                                                              const __grid_constant__ CUtensorMap dmap_mn,
-                                                             const __grid_constant__ CUtensorMap vmap,
-                                                             const __grid_constant__ CUtensorMap omap, GradArgs a) {
+                                                             const __grid_constant__ CUtensorMap omap,
+                                                             const __grid_constant__ CUtensorMap vmap, GradArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(16) float sgt[128];   // the value head's gates: b[64], beta[64]
-  __shared__ float srow[7][2][64];           // per-row partial sums from both column halves
+  __shared__ float srow[6][2][64];           // per-row partial sums from both column halves
   __shared__ float sdb[65], sred[16];
   __shared__ float snorm[2][2][128];
   __shared__ uint64_t bar_kq, bar_h, bar_l, bar_s[2], bar_mma;
@@ -1056,9 +1124,8 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
   const bool lower = lane < 16;
   const bool rvalid = i_row < L;
 
-  // TMEM: dQ | dK 0 (128), dP | F D^T 128 (64), [K; Q] S^T 192 (64, then D), [K; Q] dS^T 256 (64,
-  // then F), P^T dO 320 (32)
-  const uint32_t cQK = 0, cPF = 128, cRY = 192, cX = 256, cG = 320;
+  // TMEM: dQ | dK 0 (128), dO S | F S 128 (128), D dS 256 (upper lanes, 128), dP | F D^T 384 (64)
+  const uint32_t cQK = 0, cA1 = 128, cA2 = 256, cPF = 384;
   if (warp == 0) tc::tmem_alloc(&tmem_slot, 512);
   if (tid == 0) {
     tc::mbar_init(&bar_kq, 1);
@@ -1076,32 +1143,34 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
   const uint32_t tl = tc::taddr(tmem, 32 * quad, 0);
   constexpr int NSL = DV / DVT;
 
-  // slice q = r * NSL + sl of this CTA: S, dS slices and the value and dO rows, into buffer q & 1
+  // slice q = r * NSL + sl of this CTA: S, dS slices, D and F tiles, dO and value rows, into buffer q & 1
   auto issue_slice = [&](int q) {
     const int r = q / NSL, sl = q - r * NSL, hv = hk * ratio + r, bs = q & 1;
     uint8_t* buf = smem + GR_BUF + bs * GR_BS;
-    const int srow = (int)((c * Hv + hv) * DV + sl * DVT);
-    tc::mbar_arrive_expect_tx(&bar_s[bs], 2 * 16384 + 2 * 4096);
+    const int srow_ = (int)((c * Hv + hv) * DV + sl * DVT);
+    const size_t tile = ((size_t)(c * Hv + hv) * NSL + sl) * 2048;
+    tc::mbar_arrive_expect_tx(&bar_s[bs], 2 * 16384 + 2 * 8192 + 2 * 4096);
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
-      tc::tma_load_2d(buf + 4096 * b, &smap_mn, &bar_s[bs], 32 * b, srow);
-      tc::tma_load_2d(buf + 16384 + 4096 * b, &dmap_mn, &bar_s[bs], 32 * b, srow);
+      tc::tma_load_2d(buf + 4096 * b, &smap_mn, &bar_s[bs], 32 * b, srow_);
+      tc::tma_load_2d(buf + 16384 + 4096 * b, &dmap_mn, &bar_s[bs], 32 * b, srow_);
     }
-    tc::tma_load_3d(buf + 32768, &vmap, &bar_s[bs], sl * DVT, hv, (int)tok0);
-    tc::tma_load_3d(buf + 36864, &omap, &bar_s[bs], sl * DVT, hv, (int)tok0);
+    tc::bulk_load(buf + 32768, a.Ds + tile, 8192, &bar_s[bs]);
+    tc::bulk_load(buf + 40960, a.Fs + tile, 8192, &bar_s[bs]);
+    tc::tma_load_3d(buf + 49152, &omap, &bar_s[bs], sl * DVT, hv, (int)tok0);
+    tc::tma_load_3d(buf + 53248, &vmap, &bar_s[bs], sl * DVT, hv, (int)tok0);
   };
   auto issue_head = [&](int r) {
     const int hv = hk * ratio + r;
-    tc::mbar_arrive_expect_tx(&bar_h, 2 * 16384 + 512);
-    tc::bulk_load(smem + GR_T, a.Timg + (size_t)(c * Hv + hv) * 16384, 16384, &bar_h);
+    tc::mbar_arrive_expect_tx(&bar_h, 16384 + 512);
     tc::bulk_load(smem + GR_P, a.Pimg + (size_t)(c * Hv + hv) * 16384, 16384, &bar_h);
     tc::bulk_load(sgt, a.gates + (c * Hv + hv) * 128, 512, &bar_h);
   };
   if (tid == 32) {
     tc::prefetch_tmap(&smap_mn);
     tc::prefetch_tmap(&dmap_mn);
-    tc::prefetch_tmap(&vmap);
     tc::prefetch_tmap(&omap);
+    tc::prefetch_tmap(&vmap);
     tc::mbar_arrive_expect_tx(&bar_kq, 32768);
     tc::bulk_load(smem + GR_KQ, a.KQimg + (size_t)(c * a.geo.Hk + hk) * 32768, 32768, &bar_kq);
     issue_head(0);
@@ -1110,25 +1179,19 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
   uint32_t ph_mma = 0;
   bool ok = wait_all(&bar_kq, 0, a.err, 30);
   const uint32_t kq = tc::smem_u32(smem + GR_KQ);
-  const uint32_t idRY = tc::idesc(tc::kBF16, 128, 64, false, false);
-  const uint32_t idG = tc::idesc(tc::kBF16, 64, 32, true, true);
-  const uint32_t idD = tc::idesc(tc::kBF16, 128, 64, false, true);
-  const uint32_t idF = tc::idesc(tc::kBF16, 64, 64, true, true);
   const uint32_t idC1 = tc::idesc(tc::kTF32, 128, 128, false, true);
   const uint32_t idC2 = tc::idesc(tc::kTF32, 64, 128, false, true);
   const uint32_t idC3 = tc::idesc(tc::kTF32, 128, 64, false, false);
   const uint32_t idF1 = tc::idesc(tc::kBF16, 128, 128, false, true);
   const uint32_t idF2 = tc::idesc(tc::kBF16, 64, 128, true, true);
-  float t5 = 0.f;  // sum of S (.) dS over this thread's elements (block-summed per value head)
 
   for (int r = 0; r < ratio && ok; ++r) {
     const int hv = hk * ratio + r;
     ok = wait_all(&bar_h, (uint32_t)(r & 1), a.err, 31);
     if (!ok) break;
     const float bi = sgt[i_row], be = sgt[64 + i_row], gi = __expf(bi), bC = sgt[63], lam = __expf(bC - bi);
-    const uint32_t timg = tc::smem_u32(smem + GR_T), pimg = tc::smem_u32(smem + GR_P);
-    float t1 = 0.f, t2 = 0.f, t3 = 0.f, t4 = 0.f;
-    t5 = 0.f;
+    float t5 = 0.f;   // sum of S (.) dS over this thread's elements
+    float fv = 0.f;   // lower lanes: F_i . V_i over this thread's value rows
 
     for (int sl = 0; sl < NSL && ok; ++sl) {
       const int q = r * NSL + sl, bs = q & 1;
@@ -1136,175 +1199,60 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
       ok = wait_all(&bar_s[bs], (uint32_t)((q >> 1) & 1), a.err, 37);
       if (!ok) break;
       if (tid == 32 && sl + 1 < NSL) issue_slice(q + 1);  // the other buffer's last reader has finished
-      // a. S and dS as bf16 [hi; lo] K-major copies (rows dv, then dv + 32) for the products with K
-      //    and Q; the fp32 tiles rounded to tf32 in place for the products over dv
-      float4 s_in[4], d_in[4];  // all loads first: the stores below may not be reordered across them
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int idx = tid + 256 * u, row = idx >> 5, dk = 4 * (idx & 31);
-        const uint32_t om = tc::off_mnmajor(row, dk, DVT, 4);
-        s_in[u] = *reinterpret_cast<const float4*>(buf + om);
-        d_in[u] = *reinterpret_cast<const float4*>(buf + 16384 + om);
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int idx = tid + 256 * u, row = idx >> 5, dk = 4 * (idx & 31);
-        const uint32_t om = tc::off_mnmajor(row, dk, DVT, 4);
-        const uint32_t oh = tc::off_kmajor(row, dk, 64, 2), ol = tc::off_kmajor(row + 32, dk, 64, 2);
-        const float4 sv = s_in[u], dvv = d_in[u];
-        t5 += sv.x * dvv.x + sv.y * dvv.y + sv.z * dvv.z + sv.w * dvv.w;
-        const __nv_bfloat162 s01 = __floats2bfloat162_rn(sv.x, sv.y), s23 = __floats2bfloat162_rn(sv.z, sv.w);
-        const __nv_bfloat162 d01 = __floats2bfloat162_rn(dvv.x, dvv.y), d23 = __floats2bfloat162_rn(dvv.z, dvv.w);
-        *reinterpret_cast<uint2*>(smem + GR_SHL + oh) =
-            make_uint2(*reinterpret_cast<const uint32_t*>(&s01), *reinterpret_cast<const uint32_t*>(&s23));
-        *reinterpret_cast<uint2*>(smem + GR_SHL + ol) =
-            make_uint2(tc::pack_bf16(sv.x - __low2float(s01), sv.y - __high2float(s01)),
-                       tc::pack_bf16(sv.z - __low2float(s23), sv.w - __high2float(s23)));
-        *reinterpret_cast<uint2*>(smem + GR_DHL + oh) =
-            make_uint2(*reinterpret_cast<const uint32_t*>(&d01), *reinterpret_cast<const uint32_t*>(&d23));
-        *reinterpret_cast<uint2*>(smem + GR_DHL + ol) =
-            make_uint2(tc::pack_bf16(dvv.x - __low2float(d01), dvv.y - __high2float(d01)),
-                       tc::pack_bf16(dvv.z - __low2float(d23), dvv.w - __high2float(d23)));
-        *reinterpret_cast<float4*>(buf + om) = make_float4(tf32_rna(sv.x), tf32_rna(sv.y), tf32_rna(sv.z), tf32_rna(sv.w));
-        *reinterpret_cast<float4*>(buf + 16384 + om) =
-            make_float4(tf32_rna(dvv.x), tf32_rna(dvv.y), tf32_rna(dvv.z), tf32_rna(dvv.w));
-      }
-      // this row's values and output gradients (zero past the end)
-      float vr[16], dor[16];
+      // a. S, dS rounded to tf32 in place (the B operands of the products over the value rows); t5
       {
-        Row16 rv, rd;
-        const uint4* vp = reinterpret_cast<const uint4*>(buf + 32768 + i_row * 64 + 32 * half);
-        const uint4* dp = reinterpret_cast<const uint4*>(buf + 36864 + i_row * 64 + 32 * half);
-        const uint4 z = make_uint4(0, 0, 0, 0);
-        rv.w[0] = rvalid ? vp[0] : z;
-        rv.w[1] = rvalid ? vp[1] : z;
-        rd.w[0] = rvalid ? dp[0] : z;
-        rd.w[1] = rvalid ? dp[1] : z;
-        cvt_row16(rv, vr);
-        cvt_row16(rd, dor);
-        if (lower) {  // dO as the plain bf16 operand of P^T dO
-          uint8_t* row = smem + GR_DOT + i_row * 128;
-          *reinterpret_cast<uint4*>(row + (((2 * half) ^ (i_row & 7)) << 4)) = rd.w[0];
-          *reinterpret_cast<uint4*>(row + (((2 * half + 1) ^ (i_row & 7)) << 4)) = rd.w[1];
+        float4 s_in[4], d_in[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int idx = tid + 256 * u;
+          s_in[u] = reinterpret_cast<const float4*>(buf)[idx];
+          d_in[u] = reinterpret_cast<const float4*>(buf + 16384)[idx];
         }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int idx = tid + 256 * u;
+          const float4 sv = s_in[u], dvv = d_in[u];
+          t5 += sv.x * dvv.x + sv.y * dvv.y + sv.z * dvv.z + sv.w * dvv.w;
+          reinterpret_cast<float4*>(buf)[idx] = make_float4(tf32_rna(sv.x), tf32_rna(sv.y), tf32_rna(sv.z), tf32_rna(sv.w));
+          reinterpret_cast<float4*>(buf + 16384)[idx] =
+              make_float4(tf32_rna(dvv.x), tf32_rna(dvv.y), tf32_rna(dvv.z), tf32_rna(dvv.w));
+        }
+      }
+      // b. the operands of row i: lower lanes F (into [dO; F]) and F . V; upper lanes dO and D
+      if (lower) {
+        float f[16], v[16];
+        ld16_f32(buf + 40960 + i_row * 128 + 64 * half, f);
+        ld16_bf16(buf + 53248 + i_row * 64 + 32 * half, rvalid, v);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) fv = fmaf(f[j], v[j], fv);
+        st_row_k_f32_16(smem + GR_A, img_row(i_row) + 16, f, half);
+      } else {
+        float o[16], d[16];
+        ld16_bf16(buf + 49152 + i_row * 64 + 32 * half, rvalid, o);
+        ld16_f32(buf + 32768 + i_row * 128 + 64 * half, d);
+        st_row_k_f32_16(smem + GR_A, img_row(i_row), o, half);
+        st_row_k_f32_16(smem + GR_DT, i_row, d, half);
       }
       tc::fence_async_smem();
       tc::fence_before_sync();
       __syncthreads();
       tc::fence_after_sync();
-      // b. [K; Q] S^T, [K; Q] dS^T (the K rows: X1), P^T dO
+      // c. over the slice's value rows (tf32, K = 32): [dO; F] S, D dS (M = 64 in the upper lanes),
+      //    [dO; F] D^T
       if (tid == 0) {
-        const uint32_t shl = tc::smem_u32(smem + GR_SHL), dhl = tc::smem_u32(smem + GR_DHL);
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks)
-          tc::mma_bf16(tmem + cRY, tc::desc_kmajor(kq, 128, ks), tc::desc_kmajor(shl, 64, ks), idRY, ks > 0);
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks)
-          tc::mma_bf16(tmem + cX, tc::desc_kmajor(kq, 128, ks), tc::desc_kmajor(dhl, 64, ks), idRY, ks > 0);
-        const uint32_t dot = tc::smem_u32(smem + GR_DOT);
-#pragma unroll
-        for (int part = 0; part < 2; ++part)
-#pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
-            tc::mma_bf16(tmem + cG, desc_img_t(pimg, part, ks), desc_hl(dot, ks), idG, (part | ks) ? 1u : 0u);
-        tc::mma_commit(&bar_mma);
-      }
-      ok = wait_all(&bar_mma, ph_mma, a.err, 32);
-      ph_mma ^= 1;
-      tc::fence_after_sync();
-      if (!ok) break;
-      float rr[16], xx[16];
-      {
-        float g[16];
-        tmem_ld_hl16(tl + cRY, half, rr);  // lower: R, upper: Y
-        tmem_ld_hl16(tl + cX, half, xx);   // lower: X1
-        tc::tmem_ld16(tl + cG + 16 * half, g);
-        if (lower) {
-          float e[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            e[j] = be * (vr[j] - gi * rr[j]);
-            g[j] = fmaf(lam, xx[j], g[j]);
-          }
-          tc::st_row_hilo16(smem + GR_EHL, i_row, e, half);
-          tc::st_row_hilo16(smem + GR_DDH, i_row, g, half);
-        } else {
-          float gd[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            t3 = fmaf(dor[j], rr[j], t3);
-            gd[j] = gi * dor[j];
-          }
-          // the lower rows of A1 and A3 (the [hi; lo] tiles of S and dS are no longer read)
-          st_row_k_f32_16(smem + GR_SHL, img_row(i_row), gd, half);
-          st_row_k_f32_16(smem + GR_DHL, img_row(i_row), dor, half);
-        }
-      }
-      tc::fence_async_smem();
-      tc::fence_before_sync();
-      __syncthreads();
-      tc::fence_after_sync();
-      // c. D = T E ([T_hi; T_lo] stacked), F = T^T dD (T_hi^T and T_lo^T accumulated)
-      if (tid == 0) {
-        const uint32_t ehl = tc::smem_u32(smem + GR_EHL), ddh = tc::smem_u32(smem + GR_DDH);
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks)
-          tc::mma_bf16(tmem + cRY, tc::desc_kmajor(timg, 128, ks), desc_hl(ehl, ks), idD, ks > 0);
-#pragma unroll
-        for (int part = 0; part < 2; ++part)
-#pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
-            tc::mma_bf16(tmem + cX, desc_img_t(timg, part, ks), desc_hl(ddh, ks), idF, (part | ks) ? 1u : 0u);
-        tc::mma_commit(&bar_mma);
-      }
-      ok = wait_all(&bar_mma, ph_mma, a.err, 33);
-      ph_mma ^= 1;
-      tc::fence_after_sync();
-      if (!ok) break;
-      {
-        float d[16], f[16];
-        tmem_ld_hl16_pair(tl + cRY, half, d);  // D, both lanes of the pair
-        tmem_ld_hl16(tl + cX, half, f);        // lower: F
-        if (lower) {
-          float w[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            t1 = fmaf(f[j], vr[j] - gi * rr[j], t1);
-            t2 = fmaf(f[j], rr[j], t2);
-            t4 = fmaf(d[j], xx[j], t4);
-            w[j] = -be * gi * f[j];
-          }
-          st_row_k_f32_16(smem + GR_SHL, img_row(i_row) + 16, w, half);   // A1 upper: -beta gamma F
-          st_row_k_f32_16(smem + GR_DHL, img_row(i_row) + 16, f, half);   // A3 upper: F
-#pragma unroll
-          for (int j = 0; j < 16; ++j) w[j] = lam * d[j];
-          st_row_k_f32_16(smem + GR_EHL, i_row, w, half);                 // A2: lambda D
-        } else {
-          st_row_k_f32_16(smem + GR_DDH, i_row, d, half);                 // B3: D (as D^T, K-major)
-        }
-      }
-      tc::fence_async_smem();
-      tc::fence_before_sync();
-      __syncthreads();
-      tc::fence_after_sync();
-      // d. over the slice's value rows (tf32, K = 32): dQ | dK += [gamma dO; -beta gamma F] S,
-      //    dK += (lambda D) dS (M = 64 in the upper lanes), dP | F D^T += [dO; F] D^T
-      if (tid == 0) {
-        const bool first = r == 0 && sl == 0;
         const uint32_t s32 = tc::smem_u32(buf), d32 = tc::smem_u32(buf + 16384);
-        const uint32_t a1 = tc::smem_u32(smem + GR_SHL), a3 = tc::smem_u32(smem + GR_DHL);
-        const uint32_t a2 = tc::smem_u32(smem + GR_EHL), b3 = tc::smem_u32(smem + GR_DDH);
+        const uint32_t aa = tc::smem_u32(smem + GR_A), dt = tc::smem_u32(smem + GR_DT);
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
-          tc::mma_tf32(tmem + cQK, tc::desc_kmajor(a1, 128, ks), tc::desc_mnmajor(s32, DVT, ks, 8), idC1,
-                       (!first || ks > 0) ? 1u : 0u);
+          tc::mma_tf32(tmem + cA1, tc::desc_kmajor(aa, 128, ks), tc::desc_mnmajor(s32, DVT, ks, 8), idC1,
+                       (sl > 0 || ks > 0) ? 1u : 0u);
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
-          tc::mma_tf32(tmem + cQK + (16u << 16), tc::desc_kmajor(a2, 64, ks), tc::desc_mnmajor(d32, DVT, ks, 8), idC2,
-                       1u);
+          tc::mma_tf32(tmem + cA2 + (16u << 16), tc::desc_kmajor(dt, 64, ks), tc::desc_mnmajor(d32, DVT, ks, 8), idC2,
+                       (sl > 0 || ks > 0) ? 1u : 0u);
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
-          tc::mma_tf32(tmem + cPF, tc::desc_kmajor(a3, 128, ks), tc::desc_kmajor(b3, 64, ks), idC3,
+          tc::mma_tf32(tmem + cPF, tc::desc_kmajor(aa, 128, ks), tc::desc_kmajor(dt, 64, ks), idC3,
                        (sl > 0 || ks > 0) ? 1u : 0u);
         tc::mma_commit(&bar_mma);
       }
@@ -1314,14 +1262,46 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
     }
     if (!ok) break;
 
-    // e. finalize this value head: dP^ and dKK, the Gamma terms of d b, and their MMAs into dQ, dK
+    // e. finalize this value head
     if (tid == 32) {
       tc::mbar_arrive_expect_tx(&bar_l, 16384);
       tc::bulk_load(smem + GR_L, a.Lbuf + (size_t)(c * Hv + hv) * 4096, 16384, &bar_l);
     }
+    // e1. the row terms from the unscaled products, and their scaled sum into dQ (lower lanes) and dK
+    //     (upper lanes), 64 columns per thread in two passes of 32
+    {
+      float ta = 0.f, tb = 0.f;  // lower: Q . dO S; upper: K . F S and K . D dS
+      const float wa = lower ? gi : -be * gi;
+#pragma unroll 1
+      for (int m = 0; m < 2; ++m) {
+        const int col = 64 * half + 32 * m;
+        float x1[32], x2[32], kqr[32];
+        tc::tmem_ld32(tl + cA1 + col, x1);
+        tc::tmem_ld32(tl + cA2 + col, x2);
+        ld_img_row32(smem + GR_KQ + half * 16384, img_row(i_row) + (lower ? 16 : 0), m, kqr);
+        float q0[32];
+        if (r > 0) tc::tmem_ld32(tl + cQK + col, q0);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          ta = fmaf(kqr[j], x1[j], ta);
+          tb = fmaf(kqr[j], x2[j], tb);
+          const float w = wa * x1[j] + (lower ? 0.f : lam * x2[j]);
+          q0[j] = r > 0 ? q0[j] + w : w;
+        }
+        tc::tmem_st32(tl + cQK + col, q0);
+      }
+      tc::tmem_wait_st();
+      if (lower) {
+        srow[0][half][i_row] = ta;   // t3
+        srow[1][half][i_row] = fv;   // F . V
+      } else {
+        srow[2][half][i_row] = ta;   // t2
+        srow[3][half][i_row] = tb;   // t4
+      }
+    }
     ok = wait_all(&bar_l, (uint32_t)(r & 1), a.err, 35);
     if (!ok) break;
-    float* scratch = reinterpret_cast<float*>(smem + GR_SCR);  // [64][65]
+    float* scratch = reinterpret_cast<float*>(smem + GR_SCR);  // [64][65], then 4 x 64 column partials
     const float* Lm = reinterpret_cast<const float*>(smem + GR_L);
     float rsum = 0.f, dbl = 0.f;
     {
@@ -1339,13 +1319,13 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
       // this row's P (hi + lo from the image) and Gamma * KK for the 16 columns, loaded up front
       float pv[16], lv[16];
       {
-        const int r = img_row(i_row);
-        const uint8_t* prow = smem + GR_P + r * 128;
+        const int rr = img_row(i_row);
+        const uint8_t* prow = smem + GR_P + rr * 128;
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
           const int ch = (j0 >> 3) + cc;
-          const uint4 hi = *reinterpret_cast<const uint4*>(prow + ((ch ^ (r & 7)) << 4));
-          const uint4 lo = *reinterpret_cast<const uint4*>(prow + 2048 + ((ch ^ (r & 7)) << 4));
+          const uint4 hi = *reinterpret_cast<const uint4*>(prow + ((ch ^ (rr & 7)) << 4));
+          const uint4 lo = *reinterpret_cast<const uint4*>(prow + 2048 + ((ch ^ (rr & 7)) << 4));
           const uint32_t hw[4] = {hi.x, hi.y, hi.z, hi.w}, lw[4] = {lo.x, lo.y, lo.z, lo.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
@@ -1355,12 +1335,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
             pv[8 * cc + 2 * e + 1] = __high2float(h2) + __high2float(l2);
           }
         }
-        const float4* lrow = reinterpret_cast<const float4*>(Lm + i_row * 64 + j0);
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          const float4 x = lrow[c4];
-          lv[4 * c4] = x.x, lv[4 * c4 + 1] = x.y, lv[4 * c4 + 2] = x.z, lv[4 * c4 + 3] = x.w;
-        }
+        ld16_f32(reinterpret_cast<const uint8_t*>(Lm + i_row * 64 + j0), lv);
       }
       float ph[16], kh[16], xs[16];
 #pragma unroll
@@ -1378,25 +1353,16 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
       }
 #pragma unroll
       for (int k = 0; k < 16; ++k) scratch[i_row * 65 + j0 + k] = xs[k];
-      const int r = img_row(i_row), c0 = j0 >> 3;
-      st_hilo16_chunks(smem + GR_FHI, smem + GR_FLO, r, ph, c0);
-      st_hilo16_chunks(smem + GR_FHI, smem + GR_FLO, r + 16, kh, c0);
+      const int rr = img_row(i_row), c0 = j0 >> 3;
+      st_hilo16_chunks(smem + GR_FHI, smem + GR_FLO, rr, ph, c0);
+      st_hilo16_chunks(smem + GR_FHI, smem + GR_FLO, rr + 16, kh, c0);
     }
-    // per-row partials from both column halves: 0 t1, 1 t2, 2 t4 (lower lanes), 3 t3 (upper lanes),
-    // 4 the Gamma-term row sum and 6 the d beta part of the L terms (both lanes of the pair summed)
-    if (lower) {
-      srow[0][half][i_row] = t1;
-      srow[1][half][i_row] = t2;
-      srow[2][half][i_row] = t4;
-    } else {
-      srow[3][half][i_row] = t3;
-    }
-    {
-      float rs = rsum + __shfl_xor_sync(0xffffffffu, rsum, 16);
-      float db2 = dbl + __shfl_xor_sync(0xffffffffu, dbl, 16);
+    {  // the row sums of both lanes of the pair, per column half
+      const float rs = rsum + __shfl_xor_sync(0xffffffffu, rsum, 16);
+      const float db2 = dbl + __shfl_xor_sync(0xffffffffu, dbl, 16);
       if (lower) {
         srow[4][half][i_row] = rs;
-        srow[6][half][i_row] = db2;
+        srow[5][half][i_row] = db2;
       }
     }
     {
@@ -1439,11 +1405,12 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
     float lt4 = 0.f, dbv = 0.f;
     if (tid < 64) {
       const int i = tid;
-      const float* cp = reinterpret_cast<const float*>(smem + GR_SCR) + 64 * 65;
+      const float* cp = scratch + 64 * 65;
       const float csum = (cp[i] + cp[64 + i]) + (cp[128 + i] + cp[192 + i]);
       const float bi_ = sgt[i], be_ = sgt[64 + i], gi_ = __expf(bi_), lam_ = __expf(bC - bi_);
-      const float t2_ = srow[1][0][i] + srow[1][1][i], t3_ = srow[3][0][i] + srow[3][1][i];
-      const float t4_ = srow[2][0][i] + srow[2][1][i];
+      const float t3_ = srow[0][0][i] + srow[0][1][i];
+      const float t2_ = srow[2][0][i] + srow[2][1][i];
+      const float t4_ = srow[3][0][i] + srow[3][1][i];
       const float rs = srow[4][0][i] + srow[4][1][i];
       dbv = rs - csum + gi_ * t3_ - be_ * gi_ * t2_ - lam_ * t4_;
       lt4 = lam_ * t4_;
@@ -1474,7 +1441,10 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
       const int i = tid;
       const float dl = sdb[1 + i] + (i < 32 ? sdb[0] : 0.f);  // d log g_i
       const int64_t gi_idx = (tok0 + i) * Hv + hv;
-      const float dbe = srow[0][0][i] + srow[0][1][i] + srow[6][0][i] + srow[6][1][i];
+      // d beta = F . (V - gamma R) + the L terms;  F . R = K . (F S) = t2
+      const float gi_ = __expf(sgt[i]);
+      const float t1_ = (srow[1][0][i] + srow[1][1][i]) - gi_ * (srow[2][0][i] + srow[2][1][i]);
+      const float dbe = t1_ + srow[5][0][i] + srow[5][1][i];
       if (a.g) {
         // dg = d log g / g; a gate of exactly 0 (log g clamped) gets 0, which keeps g * dg = 0 exact
         const float gv = a.g[gi_idx];
@@ -1510,7 +1480,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
     ok = wait_all(&bar_mma, ph_mma, a.err, 36);
     ph_mma ^= 1;
     tc::fence_after_sync();
-    // the next value head's tiles (the finalize's buffers and the images are free now)
+    // the next value head's tiles (the finalize's buffers and the P image are free now)
     if (ok && r + 1 < ratio && tid == 32) {
       issue_head(r + 1);
       issue_slice((r + 1) * NSL);
@@ -1642,6 +1612,7 @@ int64_t a256(int64_t x) { return (x + 255) & ~int64_t(255); }
 struct Saved {
   float *ckpt, *L, *gates;
   uint8_t *Timg, *Pimg, *KQimg;
+  float* Ds;
 };
 
 int64_t saved_layout(int Hv, int Hk, int64_t n_chunks, char* base, Saved* s) {
@@ -1658,6 +1629,7 @@ int64_t saved_layout(int Hv, int Hk, int64_t n_chunks, char* base, Saved* s) {
   x.Timg = (uint8_t*)take(n_chunks * Hv * 16384);
   x.Pimg = (uint8_t*)take(n_chunks * Hv * 16384);
   x.KQimg = (uint8_t*)take(n_chunks * Hk * 32768);
+  x.Ds = (float*)take(n_chunks * Hv * 64 * DV * 4);
   if (s) *s = x;
   return off;
 }
@@ -1671,6 +1643,7 @@ struct Ws {
   uint8_t *Timg, *Pimg, *KQimg;
   float* gates;
   float* dsbuf;
+  float* Fs;         // F = T^T dD from the reverse walk, fp32 tiles [chunks, Hv, 4][64][32]
   float* head_part;
   char* saved;
   char* fwd_ws;
@@ -1694,6 +1667,7 @@ int64_t ws_layout(int Hv, int Hk, int N, int64_t n_chunks, bool layer, bool varl
     x.gates = (float*)take(n_chunks * Hv * 128 * 4);
   } else {
     x.dsbuf = (float*)take(n_chunks * Hv * (int64_t)DV * DK * 4);
+    x.Fs = (float*)take(n_chunks * Hv * 64 * DV * 4);
     x.head_part = (float*)take(layer ? n_chunks * Hv * 2 * 4 : 0);
     if (with_saved) {
       x.saved = take(saved_layout(Hv, Hk, n_chunks, nullptr, nullptr));
@@ -1750,7 +1724,7 @@ cudaError_t chunked_fwd(const ChunkFwdArgs& a, void* ws, cudaStream_t st) {
   }
   CUtensorMap vmap;
   if (!map_rows(&vmap, a.v, rows, a.Hv, a.Dv, DVT, C)) return cudaErrorInvalidValue;
-  StateArgs sa{geo, a.v, gates, a.h0, a.y, a.hT, ckpt, Ti, Pi, KQi, w.err};
+  StateArgs sa{geo, a.v, gates, a.h0, a.y, a.hT, ckpt, Ti, Pi, KQi, a.saved ? sv.Ds : nullptr, w.err};
   auto kern = a.out_bf16 ? gdn_chunk_fwd_state<__nv_bfloat16> : gdn_chunk_fwd_state<float>;
   if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FW_SMEM)) != cudaSuccess) return e;
   kern<<<dim3(DV / DVT, a.Hv, a.N), 256, FW_SMEM, st>>>(vmap, sa);
@@ -1780,9 +1754,10 @@ cudaError_t chunked_bwd(const ChunkBwdArgs& a, void* ws, cudaStream_t st) {
   if ((e = cudaMemsetAsync(w.err, 0, 16, st)) != cudaSuccess) return e;
   if (a.cu && (e = launch_chunk_offsets(a.cu, a.N, w.chunk_off, st)) != cudaSuccess) return e;
   Geo geo{a.T, a.Hk, a.Hv, a.N, (a.T + C - 1) / C, a.cu, a.cu ? w.chunk_off : nullptr};
-  CUtensorMap dmap;
-  if (!map_rows(&dmap, a.dy, rows, a.Hv, a.Dv, DVT, C)) return cudaErrorInvalidValue;
-  BwdStateArgs ba{geo, a.dy, sv.gates, a.dhT, a.dv, a.dh0, w.dsbuf, sv.Timg, sv.Pimg, sv.KQimg, w.err};
+  CUtensorMap dmap, vmap;
+  if (!map_rows(&dmap, a.dy, rows, a.Hv, a.Dv, DVT, C) || !map_rows(&vmap, a.v, rows, a.Hv, a.Dv, DVT, C))
+    return cudaErrorInvalidValue;
+  BwdStateArgs ba{geo, a.dy, sv.gates, a.dhT, a.dv, a.dh0, w.dsbuf, sv.Timg, sv.Pimg, sv.KQimg, w.Fs, w.err};
   auto k1 = a.out_bf16 ? gdn_chunk_bwd_state<__nv_bfloat16> : gdn_chunk_bwd_state<float>;
   if ((e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, BW_SMEM)) != cudaSuccess) return e;
   k1<<<dim3(DV / DVT, a.Hv, a.N), 256, BW_SMEM, st>>>(dmap, ba);
@@ -1799,14 +1774,12 @@ cudaError_t chunked_bwd(const ChunkBwdArgs& a, void* ws, cudaStream_t st) {
   if (!map_state_mn(&smap_mn, sv.ckpt, a.n_chunks * a.Hv * (int64_t)DV) ||
       !map_state_mn(&dmap_mn, w.dsbuf, a.n_chunks * a.Hv * (int64_t)DV))
     return cudaErrorInvalidValue;
-  CUtensorMap vmap;
-  if (!map_rows(&vmap, a.v, rows, a.Hv, a.Dv, DVT, C)) return cudaErrorInvalidValue;
-  GradArgs ga{geo, a.g, sv.gates, sv.Timg, sv.Pimg, sv.KQimg, sv.L, a.dq, a.dk, a.dg, a.dbeta, w.err,
+  GradArgs ga{geo, a.g, sv.gates, sv.Pimg, sv.KQimg, sv.L, sv.Ds, w.Fs, a.dq, a.dk, a.dg, a.dbeta, w.err,
               static_cast<const __nv_bfloat16*>(a.q), static_cast<const __nv_bfloat16*>(a.k),
               a.a_raw, a.b_raw, a.A_log, a.dt_bias, w.head_part};
   auto k2 = a.out_bf16 ? gdn_chunk_bwd_grad<__nv_bfloat16> : gdn_chunk_bwd_grad<float>;
   if ((e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, GR_SMEM)) != cudaSuccess) return e;
-  k2<<<dim3((unsigned)a.n_chunks, a.Hk), 256, GR_SMEM, st>>>(smap_mn, dmap_mn, vmap, dmap, ga);
+  k2<<<dim3((unsigned)a.n_chunks, a.Hk), 256, GR_SMEM, st>>>(smap_mn, dmap_mn, dmap, vmap, ga);
   note_launch();
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   if (layer) {
