@@ -340,7 +340,13 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CU
       if (kkside) {
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) Lt[(32 * h + jj) * LS + i] = be * v[jj];
-        if (a.Lbuf) store_row32<float>(a.Lbuf + mat + i * 64 + 32 * h, v);
+        if (a.Lbuf) {  // 16-byte chunk c of row i at position c ^ (i & 15): conflict-free row reads
+          float* lrow = a.Lbuf + mat + i * 64;
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            reinterpret_cast<float4*>(lrow)[(8 * h + q) ^ (i & 15)] =
+                make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        }
       } else {
         tc::st_row_bf16x2_32(pimg, pimg + 2048, img_row(i), v, 4 * h);
       }
@@ -481,6 +487,22 @@ __device__ __forceinline__ void st16_f32(float* p, const float (&v)[16]) {
   for (int q = 0; q < 4; ++q) reinterpret_cast<float4*>(p)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
 }
 
+// 16 floats of row r of a [64][32] fp32 tile whose 16-byte chunks are swizzled by r & 7 (chunks
+// 4 half .. 4 half + 3): conflict-free when the lanes of a warp own consecutive rows.
+__device__ __forceinline__ void st16_f32_sw(uint8_t* tile, int r, int half, const float (&v)[16]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    *reinterpret_cast<float4*>(tile + r * 128 + (((4 * half + q) ^ (r & 7)) << 4)) =
+        make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+}
+__device__ __forceinline__ void ld16_f32_sw(const uint8_t* tile, int r, int half, float (&v)[16]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float4 x = *reinterpret_cast<const float4*>(tile + r * 128 + (((4 * half + q) ^ (r & 7)) << 4));
+    v[4 * q] = x.x, v[4 * q + 1] = x.y, v[4 * q + 2] = x.z, v[4 * q + 3] = x.w;
+  }
+}
+
 // Shared memory of the forward walk (bytes from a 1024-aligned base).
 constexpr int FW_KQ = 0;           // 2 x 32 KB bf16 [K; Q] tile, 16-row groups interleaved (TMA)
 constexpr int FW_T = 65536;        // 2 x 16 KB bf16 [T_hi; T_lo] image (bulk copy)
@@ -603,10 +625,10 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
 
     // 1. the chunk-start state: staged for the bulk store of the checkpoint, and as the [hi | lo]
     //    operand row dk
-    if (a.ckpt) {
+    if (a.ckpt) {  // rounded to tf32: its one reader takes it as a tf32 operand
       float* ck = reinterpret_cast<float*>(smem + FW_CK) + 16 * half * DK + dk;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) ck[j * DK] = s[j];
+      for (int j = 0; j < 16; ++j) ck[j * DK] = tf32_rna(s[j]);
     }
     tc::st_row_hilo16(smem + FW_S, dk, s, half);
     tc::fence_async_smem();
@@ -643,7 +665,6 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
     if (!ok) break;
     // 3. K side: E = diag(beta) (V - diag(gamma) K S^T) as the [hi | lo] operand; Q side: gamma Q S^T
     float yp[16];
-    const int srow_off = i_row * 128 + 64 * half;  // this thread's 16 floats in a [64][32] fp32 staging tile
     const size_t ptile = ((size_t)(cg * Hv + hv) * (DV / DVT) + blockIdx.x) * 2048;  // this CTA's tile
     {
       tmem_ld_hl16(tl + cA, half, yp);
@@ -678,7 +699,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
         tc::st_row_hilo16(smem + FW_D, i_row, d, half);
       } else {
         // (the other staging buffer's store was read before the last chunk's final barrier)
-        if (a.Ds) st16_f32(reinterpret_cast<float*>(smem + FW_DS + buf * 8192 + srow_off), d);
+        if (a.Ds) st16_f32_sw(smem + FW_DS + buf * 8192, i_row, half, d);
         const float lam = __expf(bC - bi);
 #pragma unroll
         for (int j = 0; j < 16; ++j) d[j] *= lam;
@@ -864,13 +885,12 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
     const int64_t cg = c_first + jc;
     const int64_t tok0 = seq0 + jc * C;
     const int L = (int)min((int64_t)C, seq1 - tok0);
-    const int srow_off = i_row * 128 + 64 * half;  // this thread's 16 floats in a [64][32] fp32 tile
 
     // 1. dS of this chunk's end: staged for the gradient kernel, and as the [hi | lo] operand row dk
-    {
+    {  // rounded to tf32: its one reader takes it as a tf32 operand
       float* ck = reinterpret_cast<float*>(smem + BW_CK) + 16 * half * DK + dk;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) ck[j * DK] = ds[j];
+      for (int j = 0; j < 16; ++j) ck[j * DK] = tf32_rna(ds[j]);
     }
     tc::st_row_hilo16(smem + BW_S, dk, ds, half);
     tc::fence_async_smem();
@@ -968,7 +988,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
       tmem_ld_hl16(tl + cF, half, f);
       if (kside) {
         // (the other staging buffer's store was read before the last chunk's step-4 barrier)
-        st16_f32(reinterpret_cast<float*>(smem + BW_FS + buf * 8192 + srow_off), f);
+        st16_f32_sw(smem + BW_FS + buf * 8192, i_row, half, f);
         float o[16];
         if (i_row < L) {
 #pragma unroll
@@ -1192,6 +1212,19 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
     const float bi = sgt[i_row], be = sgt[64 + i_row], gi = __expf(bi), bC = sgt[63], lam = __expf(bC - bi);
     float t5 = 0.f;   // sum of S (.) dS over this thread's elements
     float fv = 0.f;   // lower lanes: F_i . V_i over this thread's value rows
+    // the finalize's per-row inputs of the gate chain rule, loaded now (consumed at the end of the head)
+    float in0 = 0.f, in1 = 0.f, eA = 0.f, dtb = 0.f;
+    if (tid < 64 && tid < L) {
+      const int64_t gi_idx = (tok0 + tid) * Hv + hv;
+      if (a.g) {
+        in0 = __ldg(a.g + gi_idx);
+      } else {
+        in0 = __ldg(a.a_raw + gi_idx);
+        in1 = __ldg(a.b_raw + gi_idx);
+        eA = __ldg(a.A_log + hv);
+        dtb = __ldg(a.dt_bias + hv);
+      }
+    }
 
     for (int sl = 0; sl < NSL && ok; ++sl) {
       const int q = r * NSL + sl, bs = q & 1;
@@ -1199,29 +1232,18 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
       ok = wait_all(&bar_s[bs], (uint32_t)((q >> 1) & 1), a.err, 37);
       if (!ok) break;
       if (tid == 32 && sl + 1 < NSL) issue_slice(q + 1);  // the other buffer's last reader has finished
-      // a. S, dS rounded to tf32 in place (the B operands of the products over the value rows); t5
-      {
-        float4 s_in[4], d_in[4];
+      // a. t5 (S and dS arrive rounded to tf32, the B operands of the products over the value rows)
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int idx = tid + 256 * u;
-          s_in[u] = reinterpret_cast<const float4*>(buf)[idx];
-          d_in[u] = reinterpret_cast<const float4*>(buf + 16384)[idx];
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int idx = tid + 256 * u;
-          const float4 sv = s_in[u], dvv = d_in[u];
-          t5 += sv.x * dvv.x + sv.y * dvv.y + sv.z * dvv.z + sv.w * dvv.w;
-          reinterpret_cast<float4*>(buf)[idx] = make_float4(tf32_rna(sv.x), tf32_rna(sv.y), tf32_rna(sv.z), tf32_rna(sv.w));
-          reinterpret_cast<float4*>(buf + 16384)[idx] =
-              make_float4(tf32_rna(dvv.x), tf32_rna(dvv.y), tf32_rna(dvv.z), tf32_rna(dvv.w));
-        }
+      for (int u = 0; u < 4; ++u) {
+        const int idx = tid + 256 * u;
+        const float4 sv = reinterpret_cast<const float4*>(buf)[idx];
+        const float4 dvv = reinterpret_cast<const float4*>(buf + 16384)[idx];
+        t5 += sv.x * dvv.x + sv.y * dvv.y + sv.z * dvv.z + sv.w * dvv.w;
       }
       // b. the operands of row i: lower lanes F (into [dO; F]) and F . V; upper lanes dO and D
       if (lower) {
         float f[16], v[16];
-        ld16_f32(buf + 40960 + i_row * 128 + 64 * half, f);
+        ld16_f32_sw(buf + 40960, i_row, half, f);
         ld16_bf16(buf + 53248 + i_row * 64 + 32 * half, rvalid, v);
 #pragma unroll
         for (int j = 0; j < 16; ++j) fv = fmaf(f[j], v[j], fv);
@@ -1229,7 +1251,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
       } else {
         float o[16], d[16];
         ld16_bf16(buf + 49152 + i_row * 64 + 32 * half, rvalid, o);
-        ld16_f32(buf + 32768 + i_row * 128 + 64 * half, d);
+        ld16_f32_sw(buf + 32768, i_row, half, d);
         st_row_k_f32_16(smem + GR_A, img_row(i_row), o, half);
         st_row_k_f32_16(smem + GR_DT, i_row, d, half);
       }
@@ -1335,7 +1357,11 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
             pv[8 * cc + 2 * e + 1] = __high2float(h2) + __high2float(l2);
           }
         }
-        ld16_f32(reinterpret_cast<const uint8_t*>(Lm + i_row * 64 + j0), lv);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 x = reinterpret_cast<const float4*>(Lm + i_row * 64)[((j0 >> 2) + q) ^ (i_row & 15)];
+          lv[4 * q] = x.x, lv[4 * q + 1] = x.y, lv[4 * q + 2] = x.z, lv[4 * q + 3] = x.w;
+        }
       }
       float ph[16], kh[16], xs[16];
 #pragma unroll
@@ -1447,17 +1473,16 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
       const float dbe = t1_ + srow[5][0][i] + srow[5][1][i];
       if (a.g) {
         // dg = d log g / g; a gate of exactly 0 (log g clamped) gets 0, which keeps g * dg = 0 exact
-        const float gv = a.g[gi_idx];
-        a.dg[gi_idx] = gv > 0.f ? dl / gv : 0.f;
+        a.dg[gi_idx] = in0 > 0.f ? dl / in0 : 0.f;
         a.dbeta[gi_idx] = dbe;
       } else {
         // log g = -e^A softplus(x), x = a + dt_bias: da = d log g * (-e^A sigmoid(x)); beta = sigmoid(b)
-        const float eA = expf(a.A_log[hv]), x = a.a_raw[gi_idx] + a.dt_bias[hv];
-        const float da = dl * (-eA * sigmoid_f(x));
-        const float sb_ = sigmoid_f(a.b_raw[gi_idx]);
+        const float ea = expf(eA), x = in0 + dtb;
+        const float da = dl * (-ea * sigmoid_f(x));
+        const float sb_ = sigmoid_f(in1);
         a.dg[gi_idx] = da;
         a.dbeta[gi_idx] = dbe * sb_ * (1.f - sb_);
-        pa = dl * (-eA * softplus_f(x));
+        pa = dl * (-ea * softplus_f(x));
         pd = da;
       }
     }
