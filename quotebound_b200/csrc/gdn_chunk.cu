@@ -208,13 +208,14 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CU
                                                       const __grid_constant__ CUtensorMap qmap, PrepArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 32 KB in all, so that several CTAs share an SM: the K and Q tiles, then (once the products have
+  // read them) T transposed in the K tile and L transposed, then L10 T00, in the Q tile
   uint8_t* ktile = smem;                                   // 16 KB bf16
   uint8_t* qtile = smem + 16384;                           // 16 KB bf16
-  float* Lm = reinterpret_cast<float*>(smem + 32768);      // [64][68]
   __shared__ float sb[64], sbeta[64], stmp[2];
   __shared__ uint64_t bar_tma, bar_mma;
   __shared__ uint32_t tmem_slot;
-  constexpr int LS = 68;
+  constexpr int LS = 64;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t c = blockIdx.x;
@@ -223,7 +224,7 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CU
   int64_t tok0;
   chunk_info(a.geo, c, n, tok0, L);
 
-  if (warp == 0) tc::tmem_alloc(&tmem_slot, 128);
+  if (warp == 0) tc::tmem_alloc(&tmem_slot, 64);
   if (tid == 0) {
     tc::mbar_init(&bar_tma, 1);
     tc::mbar_init(&bar_mma, 1);
@@ -320,8 +321,9 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CU
   ok = __syncthreads_and(ok && tc::mbar_wait(&bar_mma, 0, a.err, 2)) != 0;
   tc::fence_after_sync();
   const size_t mat = (size_t)(c * a.geo.Hv + hv) * 4096;
-  // The Q tile is free once the products above completed: it stages the P image.
-  uint8_t* pimg = qtile;
+  // the images go straight to global memory, 16-byte chunks in the tile's swizzled order
+  uint8_t* pimg = a.Pimg + mat * 4;
+  float* Lm = reinterpret_cast<float*>(qtile);  // free once the products above completed
   float* Lt = Lm;  // transposed: Lt[j * LS + i] = beta_i Gamma_ij (K K^T)_ij for j < i
   if (ok) {
     const int i = 16 * warp + (lane & 15);
@@ -391,7 +393,7 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CU
     gd[64 + tid] = sbeta[tid];
   }
   __syncthreads();
-  float* Xs = Lm;  // X = L10 T00 [32][32], where L was (after the products read it)
+  float* Xs = Lm;  // X = L10 T00 [32][32], where L was (once the products have read it)
   {
     const int r = tid & 31, cg = tid >> 5;  // row r of the block, columns 8 cg .. 8 cg + 7
     float x[8];
@@ -437,29 +439,18 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CU
     }
   }
   __syncthreads();
-  // the T image (staged where L was): thread (row i, half) converts columns 32 half .. + 31 of row i
-  uint8_t* timg = reinterpret_cast<uint8_t*>(Lm);
+  // the T image: thread (row i, half) converts columns 32 half .. + 31 of row i
   if (ok) {
     const int i = tid & 63, h = tid >> 6;
     float v[32];
 #pragma unroll
     for (int jj = 0; jj < 32; ++jj) v[jj] = Tt[(32 * h + jj) * 64 + i];
+    uint8_t* timg = a.Timg + mat * 4;
     tc::st_row_bf16x2_32(timg, timg + 2048, img_row(i), v, 4 * h);
-  }
-  __syncthreads();
-  if (ok) {  // both images out, 16-byte stores
-    uint4* td = reinterpret_cast<uint4*>(a.Timg + mat * 4);
-    uint4* pd = reinterpret_cast<uint4*>(a.Pimg + mat * 4);
-#pragma unroll 4
-    for (int u = 0; u < 8; ++u) {
-      const int idx = tid + 128 * u;
-      td[idx] = reinterpret_cast<const uint4*>(timg)[idx];
-      pd[idx] = reinterpret_cast<const uint4*>(pimg)[idx];
-    }
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tmem, 128);
+  if (warp == 0) tc::tmem_dealloc(tmem, 64);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -1739,7 +1730,7 @@ cudaError_t chunked_fwd(const ChunkFwdArgs& a, void* ws, cudaStream_t st) {
   Geo geo{a.T, a.Hk, a.Hv, a.N, (a.T + C - 1) / C, a.cu, a.cu ? w.chunk_off : nullptr};
   if (a.n_chunks > 0) {
     PrepArgs pa{geo, a.g, a.beta, a.a_raw, a.b_raw, a.A_log, a.dt_bias, Ti, Pi, KQi, Lb, gates, w.err};
-    const int prep_smem = 1024 + 32768 + 64 * 68 * 4;
+    const int prep_smem = 1024 + 32768;
     if ((e = cudaFuncSetAttribute(gdn_chunk_prep, cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem)) !=
         cudaSuccess)
       return e;
