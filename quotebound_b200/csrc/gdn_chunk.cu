@@ -505,7 +505,8 @@ constexpr int FW_DT = 163840;      // 8 KB bf16 D~ = diag(lambda) D [hi | lo]
 constexpr int FW_CK = 172032;      // 16 KB fp32 chunk-start state staging [32 dv][128 dk] (bulk store)
 constexpr int FW_V = 188416;       // 2 x 4 KB bf16 value rows [64][32] (TMA)
 constexpr int FW_DS = 196608;      // 2 x 8 KB fp32 D rows [64][32] staging (bulk store, training)
-constexpr int FW_SMEM = 212992 + 1024;
+constexpr int FW_Y = 212992;       // 8 KB output rows [64][32] staging (TMA store of full chunks)
+constexpr int FW_SMEM = 221184 + 1024;
 
 // Descriptors of the stacked operands.  The [K; Q] tile holds, per 64-column slab (16 KB), the row
 // groups K 0-15, Q 0-15, K 16-31, Q 16-31, ... (2 KB each).
@@ -546,7 +547,8 @@ __device__ __forceinline__ void tmem_ld_hl16_pair(uint32_t taddr, int half, floa
 // 256 threads: warp w reads TMEM lanes 32 (w & 3) .. + 31 and handles the value columns
 // 16 (w >> 2) .. + 15 of the CTA's 32; thread t holds S[dv0 + 16 (w >> 2) + j][t & 127].
 template <typename Tout>
-__global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_constant__ CUtensorMap vmap, StateArgs a) {
+__global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_constant__ CUtensorMap vmap,
+                                                              const __grid_constant__ CUtensorMap ymap, StateArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(16) float sg[2][128];
@@ -607,6 +609,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
   bool ok = true;
   const uint32_t idA = tc::idesc(tc::kBF16, 128, 64, false, true);
   const uint32_t idT = tc::idesc(tc::kBF16, 128, 64, true, true);
+  int64_t ystage_tok = -1;  // first token of the full chunk whose output rows wait in the staging tile
 
   for (int64_t jc = 0; jc < nchunks && ok; ++jc) {
     const int buf = (int)(jc & 1);
@@ -634,10 +637,9 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
       tc::mma_commit(&bar_mma);
     }
     if (tid == 32) {
-      if (a.ckpt) {
-        tc::bulk_store(a.ckpt + ((cg * Hv + hv) * DV + dv0) * (size_t)DK, smem + FW_CK, DVT * DK * 4);
-        tc::bulk_commit();
-      }
+      if (a.ckpt) tc::bulk_store(a.ckpt + ((cg * Hv + hv) * DV + dv0) * (size_t)DK, smem + FW_CK, DVT * DK * 4);
+      if (ystage_tok >= 0) tc::tma_store_3d(&ymap, smem + FW_Y, dv0, hv, (int)ystage_tok);  // last chunk's y
+      tc::bulk_commit();
       if (jc + 1 < nchunks) issue_loads(jc + 1, buf ^ 1);  // the next chunk's tiles
     }
     const float* gb = sg[buf];
@@ -697,7 +699,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
         tc::st_row_hilo16(smem + FW_DT, i_row, d, half);
       }
     }
-    if (tid == 32 && a.ckpt) tc::bulk_wait_read();  // the staging buffer is rewritten next chunk
+    if (tid == 32) tc::bulk_wait_read();  // the staging buffers are rewritten below and next chunk
     tc::fence_async_smem();
     tc::fence_before_sync();
     __syncthreads();
@@ -723,13 +725,25 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
 #pragma unroll
       for (int j = 0; j < 16; ++j) s[j] = fmaf(gC, s[j], u[j]);
       tmem_ld_hl16_pair(tl + cO, half, u);
-      if (!kside && i_row < L) {
+      if (!kside) {
 #pragma unroll
         for (int j = 0; j < 16; ++j) u[j] += yp[j];
-        store_row16<Tout>(static_cast<Tout*>(a.y) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0 + 16 * half, u);
+        if (L == C)  // a full chunk goes out by one TMA store after the next barrier
+          store_row16<Tout>(reinterpret_cast<Tout*>(smem + FW_Y) + i_row * DVT + 16 * half, u);
+        else if (i_row < L)  // the rows after a sequence's end belong to the next sequence: not written
+          store_row16<Tout>(static_cast<Tout*>(a.y) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0 + 16 * half, u);
       }
     }
+    ystage_tok = L == C ? tok0 : -1;
+    tc::fence_async_smem();
     tc::fence_before_sync();
+  }
+  if (ok && ystage_tok >= 0) {  // the last chunk's output rows
+    __syncthreads();
+    if (tid == 32) {
+      tc::tma_store_3d(&ymap, smem + FW_Y, dv0, hv, (int)ystage_tok);
+      tc::bulk_commit();
+    }
   }
   if (tid == 32) tc::bulk_wait();
   if (ok && a.hT) {
@@ -770,7 +784,8 @@ constexpr int BW_H = 139264;       // 8 KB bf16 H = -beta gamma F [hi | lo]
 constexpr int BW_CK = 147456;      // 16 KB fp32 dS staging [32 dv][128 dk] (bulk store)
 constexpr int BW_V = 163840;       // 2 x 4 KB bf16 dO rows [64][32] (TMA)
 constexpr int BW_FS = 172032;      // 2 x 8 KB fp32 F rows [64][32] staging (bulk store)
-constexpr int BW_SMEM = 188416 + 1024;
+constexpr int BW_DV = 188416;      // 8 KB dv rows [64][32] staging (TMA store of full chunks)
+constexpr int BW_SMEM = 196608 + 1024;
 
 // K-step ks of the transpose of one half (part 0 = hi, 1 = lo) of a [hi; lo] image as the M = 64
 // MN-major A operand: the image's rows (chunk steps) are K.
@@ -800,6 +815,7 @@ __device__ __forceinline__ void ld16_bf16(const uint8_t* p, bool valid, float (&
 // the gradient kernel F = T^T dD.
 template <typename Tout>
 __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_constant__ CUtensorMap dmap,
+                                                              const __grid_constant__ CUtensorMap dvmap,
                                                               BwdStateArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -891,11 +907,6 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
     ok = __syncthreads_and(ok) != 0;
     tc::fence_after_sync();
     if (!ok) break;
-    if (tid == 32) {
-      tc::bulk_store(a.dsbuf + ((cg * Hv + hv) * DV + dv0) * (size_t)DK, smem + BW_CK, DVT * DK * 4);
-      tc::bulk_commit();
-      if (jc > 0) issue_main(jc - 1, buf ^ 1);  // the previous chunk's [K; Q], gates and dO rows
-    }
     const float* gb = sg[buf];
     const float bi = gb[i_row], be = gb[64 + i_row], gi = __expf(bi), bC = gb[63];
     // 2. dO row i (zero past the end): as the plain bf16 operand of P^T dO (K side) and as gamma dO
@@ -935,6 +946,11 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
         for (int ks = 0; ks < 4; ++ks)
           tc::mma_bf16(tmem + cG, desc_img_t(pimg, part, ks), desc_hl(dO, ks), idG, (part | ks) ? 1u : 0u);
       tc::mma_commit(&bar_mma);
+    }
+    if (tid == 32) {  // while the products run: this chunk's dS out, the previous chunk's tiles in
+      tc::bulk_store(a.dsbuf + ((cg * Hv + hv) * DV + dv0) * (size_t)DK, smem + BW_CK, DVT * DK * 4);
+      tc::bulk_commit();
+      if (jc > 0) issue_main(jc - 1, buf ^ 1);  // the previous chunk's [K; Q], gates and dO rows
     }
     ok = wait_all(&bar_mma, ph, a.err, 21);
     ph ^= 1;
@@ -981,11 +997,12 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
         // (the other staging buffer's store was read before the last chunk's step-4 barrier)
         st16_f32_sw(smem + BW_FS + buf * 8192, i_row, half, f);
         float o[16];
-        if (i_row < L) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) o[j] = be * f[j];
+        for (int j = 0; j < 16; ++j) o[j] = be * f[j];
+        if (L == C)  // a full chunk goes out by one TMA store after the barrier below
+          store_row16<Tout>(reinterpret_cast<Tout*>(smem + BW_DV) + i_row * DVT + 16 * half, o);
+        else if (i_row < L)  // the rows after a sequence's end belong to the next sequence: not written
           store_row16<Tout>(static_cast<Tout*>(a.dv) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0 + 16 * half, o);
-        }
         const float h = -be * gi;
 #pragma unroll
         for (int j = 0; j < 16; ++j) o[j] = h * f[j];
@@ -1004,6 +1021,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
     }
     if (tid == 32) {
       tc::bulk_store(a.Fs + ((size_t)(cg * Hv + hv) * (DV / DVT) + blockIdx.x) * 2048, smem + BW_FS + buf * 8192, 8192);
+      if (L == C) tc::tma_store_3d(&dvmap, smem + BW_DV, dv0, hv, (int)tok0);
       tc::bulk_commit();
     }
     ok = wait_all(&bar_mma, ph, a.err, 23);
@@ -1595,14 +1613,17 @@ bool map_act(CUtensorMap* m, const void* base, int64_t rows, int heads, int dim,
 
 // bf16 rows [rows, heads, dim] read as unswizzled boxes of box_cols x box_rows of one head (the
 // value or output-gradient rows of a chunk); rows past the end read as zero.
-bool map_rows(CUtensorMap* m, const void* base, int64_t rows, int heads, int dim, int box_cols, int box_rows) {
+bool map_rows(CUtensorMap* m, const void* base, int64_t rows, int heads, int dim, int box_cols, int box_rows,
+              bool f32 = false) {
   EncodeTiled f = encode_fn();
   if (!f) return false;
+  const cuuint64_t eb = f32 ? 4 : 2;
   cuuint64_t dims[3] = {(cuuint64_t)dim, (cuuint64_t)heads, (cuuint64_t)rows};
-  cuuint64_t strides[2] = {(cuuint64_t)dim * 2, (cuuint64_t)heads * dim * 2};
+  cuuint64_t strides[2] = {(cuuint64_t)dim * eb, (cuuint64_t)heads * dim * eb};
   cuuint32_t box[3] = {(cuuint32_t)box_cols, 1, (cuuint32_t)box_rows};
   cuuint32_t es[3] = {1, 1, 1};
-  return f(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+  return f(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base),
+           dims, strides, box, es,
            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -1738,12 +1759,13 @@ cudaError_t chunked_fwd(const ChunkFwdArgs& a, void* ws, cudaStream_t st) {
     note_launch();
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
-  CUtensorMap vmap;
-  if (!map_rows(&vmap, a.v, rows, a.Hv, a.Dv, DVT, C)) return cudaErrorInvalidValue;
+  CUtensorMap vmap, ymap;
+  if (!map_rows(&vmap, a.v, rows, a.Hv, a.Dv, DVT, C) || !map_rows(&ymap, a.y, rows, a.Hv, a.Dv, DVT, C, !a.out_bf16))
+    return cudaErrorInvalidValue;
   StateArgs sa{geo, a.v, gates, a.h0, a.y, a.hT, ckpt, Ti, Pi, KQi, a.saved ? sv.Ds : nullptr, w.err};
   auto kern = a.out_bf16 ? gdn_chunk_fwd_state<__nv_bfloat16> : gdn_chunk_fwd_state<float>;
   if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FW_SMEM)) != cudaSuccess) return e;
-  kern<<<dim3(DV / DVT, a.Hv, a.N), 256, FW_SMEM, st>>>(vmap, sa);
+  kern<<<dim3(DV / DVT, a.Hv, a.N), 256, FW_SMEM, st>>>(vmap, ymap, sa);
   note_launch();
   return cudaGetLastError();
 }
@@ -1770,13 +1792,14 @@ cudaError_t chunked_bwd(const ChunkBwdArgs& a, void* ws, cudaStream_t st) {
   if ((e = cudaMemsetAsync(w.err, 0, 16, st)) != cudaSuccess) return e;
   if (a.cu && (e = launch_chunk_offsets(a.cu, a.N, w.chunk_off, st)) != cudaSuccess) return e;
   Geo geo{a.T, a.Hk, a.Hv, a.N, (a.T + C - 1) / C, a.cu, a.cu ? w.chunk_off : nullptr};
-  CUtensorMap dmap, vmap;
-  if (!map_rows(&dmap, a.dy, rows, a.Hv, a.Dv, DVT, C) || !map_rows(&vmap, a.v, rows, a.Hv, a.Dv, DVT, C))
+  CUtensorMap dmap, vmap, dvmap;
+  if (!map_rows(&dmap, a.dy, rows, a.Hv, a.Dv, DVT, C) || !map_rows(&vmap, a.v, rows, a.Hv, a.Dv, DVT, C) ||
+      !map_rows(&dvmap, a.dv, rows, a.Hv, a.Dv, DVT, C, !a.out_bf16))
     return cudaErrorInvalidValue;
   BwdStateArgs ba{geo, a.dy, sv.gates, a.dhT, a.dv, a.dh0, w.dsbuf, sv.Timg, sv.Pimg, sv.KQimg, w.Fs, w.err};
   auto k1 = a.out_bf16 ? gdn_chunk_bwd_state<__nv_bfloat16> : gdn_chunk_bwd_state<float>;
   if ((e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, BW_SMEM)) != cudaSuccess) return e;
-  k1<<<dim3(DV / DVT, a.Hv, a.N), 256, BW_SMEM, st>>>(dmap, ba);
+  k1<<<dim3(DV / DVT, a.Hv, a.N), 256, BW_SMEM, st>>>(dmap, dvmap, ba);
   note_launch();
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   if (a.n_chunks == 0) {
