@@ -204,7 +204,7 @@ struct PrepArgs {
   int* err;
 };
 
-__global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CUtensorMap kmap,
+__global__ void __launch_bounds__(128, 4) gdn_chunk_prep(const __grid_constant__ CUtensorMap kmap,
                                                       const __grid_constant__ CUtensorMap qmap, PrepArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -219,7 +219,7 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CU
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t c = blockIdx.x;
-  const int hv = blockIdx.y, hk = hv / (a.geo.Hv / a.geo.Hk);
+  const int hk = blockIdx.y, ratio = a.geo.Hv / a.geo.Hk;
   int n, L;
   int64_t tok0;
   chunk_info(a.geo, c, n, tok0, L);
@@ -242,19 +242,22 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CU
     tc::tma_load_3d(qtile + 8192, &qmap, &bar_tma, 64, hk, (int)tok0);
   }
   const bool layer = a.g == nullptr;
-  float lg = 0.f, bt = 0.f;
-  if (tid < 64 && tid < L) {
-    const int64_t gi = (tok0 + tid) * a.geo.Hv + hv;
-    if (layer) {  // log g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b) (src/deltanet.cpp:41-52, :118)
-      lg = -expf(a.A_log[hv]) * softplus_f(a.a_raw[gi] + a.dt_bias[hv]);
-      bt = sigmoid_f(a.b_raw[gi]);
-    } else {
-      lg = fmaxf(logf(a.g[gi]), -88.f);
-      bt = a.beta[gi];
+  // the gate inputs of the first value head, loaded while the tiles arrive
+  auto gate_in = [&](int hv, float& lg, float& bt) {
+    lg = 0.f, bt = 0.f;
+    if (tid < 64 && tid < L) {
+      const int64_t gi = (tok0 + tid) * a.geo.Hv + hv;
+      if (layer) {  // log g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b) (src/deltanet.cpp:41-52, :118)
+        lg = -expf(a.A_log[hv]) * softplus_f(a.a_raw[gi] + a.dt_bias[hv]);
+        bt = sigmoid_f(a.b_raw[gi]);
+      } else {
+        lg = fmaxf(logf(a.g[gi]), -88.f);
+        bt = a.beta[gi];
+      }
     }
-  }
-  if (tid < 64) sbeta[tid] = bt;
-  scan64(lg, sb, stmp);
+  };
+  float lg, bt;
+  gate_in(hk * ratio, lg, bt);
 
   bool ok = wait_all(&bar_tma, 0, a.err, 1);
   if (ok && layer) {
@@ -307,7 +310,7 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CU
     tc::mma_tile<tc::kBF16>(tmem + (16u << 16), qt, false, 64, kt, false, 64, 64, 64, DK, false);
     tc::mma_commit(&bar_mma);
   }
-  if (ok && hv % (a.geo.Hv / a.geo.Hk) == 0) {
+  if (ok) {
     // the [K; Q] image of this chunk and key head: per 64-column slab, 2 KB row groups K 0-15, Q 0-15,
     // K 16-31, ... (the swizzle is address-relative within 1 KB, so whole groups move unchanged)
     uint4* dst = reinterpret_cast<uint4*>(a.KQimg + (size_t)(c * a.geo.Hk + hk) * 32768);
@@ -320,6 +323,14 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CU
   }
   ok = __syncthreads_and(ok && tc::mbar_wait(&bar_mma, 0, a.err, 2)) != 0;
   tc::fence_after_sync();
+  // The products are the same for every value head of the key head; the gates are not.  Each value
+  // head in turn: its gated L and P, T, the images.
+  for (int r = 0; r < ratio && ok; ++r) {
+  const int hv = hk * ratio + r;
+  if (r > 0) gate_in(hv, lg, bt);
+  if (tid < 64) sbeta[tid] = bt;
+  scan64(lg, sb, stmp);
+  __syncthreads();
   const size_t mat = (size_t)(c * a.geo.Hv + hv) * 4096;
   // the images go straight to global memory, 16-byte chunks in the tile's swizzled order
   uint8_t* pimg = a.Pimg + mat * 4;
@@ -447,6 +458,8 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep(const __grid_constant__ CU
     for (int jj = 0; jj < 32; ++jj) v[jj] = Tt[(32 * h + jj) * 64 + i];
     uint8_t* timg = a.Timg + mat * 4;
     tc::st_row_bf16x2_32(timg, timg + 2048, img_row(i), v, 4 * h);
+  }
+  __syncthreads();  // the shared buffers and the gate scan are reused by the next value head
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -1755,7 +1768,7 @@ cudaError_t chunked_fwd(const ChunkFwdArgs& a, void* ws, cudaStream_t st) {
     if ((e = cudaFuncSetAttribute(gdn_chunk_prep, cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem)) !=
         cudaSuccess)
       return e;
-    gdn_chunk_prep<<<dim3((unsigned)a.n_chunks, a.Hv), 128, prep_smem, st>>>(kmap, qmap, pa);
+    gdn_chunk_prep<<<dim3((unsigned)a.n_chunks, a.Hk), 128, prep_smem, st>>>(kmap, qmap, pa);
     note_launch();
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
