@@ -959,6 +959,9 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
         for (int ks = 0; ks < 4; ++ks)
           tc::mma_bf16(tmem + cG, desc_img_t(pimg, part, ks), desc_hl(dO, ks), idG, (part | ks) ? 1u : 0u);
       tc::mma_commit(&bar_mma);
+      // U's first half Q^T (gamma dO) needs no result of this chunk: it runs during the next epilogue,
+      // and step 6 adds K^T H to it
+      mma_run<4, kQT>(tmem + cU, idU, kq, tc::smem_u32(smem + BW_GD), false);
     }
     if (tid == 32) {  // while the products run: this chunk's dS out, the previous chunk's tiles in
       tc::bulk_store(a.dsbuf + ((cg * Hv + hv) * DV + dv0) * (size_t)DK, smem + BW_CK, DVT * DK * 4);
@@ -1026,9 +1029,8 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
-    // 6. U = Q^T (gamma dO) + K^T H (M = 128 dk rows)
+    // 6. U = Q^T (gamma dO) (issued in step 3) + K^T H (M = 128 dk rows)
     if (tid == 0) {
-      mma_run<4, kQT>(tmem + cU, idU, kq, tc::smem_u32(smem + BW_GD), false);
       mma_run<4, kKT>(tmem + cU, idU, kq, tc::smem_u32(smem + BW_H), true);
       tc::mma_commit(&bar_mma);
     }
