@@ -542,13 +542,35 @@ __device__ __forceinline__ void mma_run(uint32_t d, uint32_t id, uint32_t a, uin
   }
 }
 
-// This thread's 16 columns (16 half ..) of both N halves of a [hi | lo] accumulator, summed.
+// This thread's 16 columns (16 half ..) of both N halves of a [hi | lo] accumulator, summed (both
+// loads in flight together).
 __device__ __forceinline__ void tmem_ld_hl16(uint32_t taddr, int half, float (&x)[16]) {
-  float u[16];
-  tc::tmem_ld16(taddr + 16 * half, x);
-  tc::tmem_ld16(taddr + 32 + 16 * half, u);
+  uint32_t a[16], b[16];
+  tc::tmem_ld16_nw(taddr + 16 * half, a);
+  tc::tmem_ld16_nw(taddr + 32 + 16 * half, b);
+  tc::tmem_wait_ld();
+  tc::reg_fence(a);
+  tc::reg_fence(b);
 #pragma unroll
-  for (int j = 0; j < 16; ++j) x[j] += u[j];
+  for (int j = 0; j < 16; ++j) x[j] = __uint_as_float(a[j]) + __uint_as_float(b[j]);
+}
+// Two such [hi | lo] sums, four loads in flight together.
+__device__ __forceinline__ void tmem_ld_hl16x2(uint32_t ta, uint32_t tb, int half, float (&x)[16], float (&y)[16]) {
+  uint32_t a0[16], a1[16], b0[16], b1[16];
+  tc::tmem_ld16_nw(ta + 16 * half, a0);
+  tc::tmem_ld16_nw(ta + 32 + 16 * half, a1);
+  tc::tmem_ld16_nw(tb + 16 * half, b0);
+  tc::tmem_ld16_nw(tb + 32 + 16 * half, b1);
+  tc::tmem_wait_ld();
+  tc::reg_fence(a0);
+  tc::reg_fence(a1);
+  tc::reg_fence(b0);
+  tc::reg_fence(b1);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    x[j] = __uint_as_float(a0[j]) + __uint_as_float(a1[j]);
+    y[j] = __uint_as_float(b0[j]) + __uint_as_float(b1[j]);
+  }
 }
 // The same, then the hi-row and lo-row products of lanes l and l + 16 summed (both lanes get the sum).
 __device__ __forceinline__ void tmem_ld_hl16_pair(uint32_t taddr, int half, float (&x)[16]) {
@@ -732,12 +754,13 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
     tc::fence_after_sync();
     if (!ok) break;
     {
-      float u[16];
-      tmem_ld_hl16(tl + cS, half, u);
+      float u[16], o2[16];
+      tmem_ld_hl16x2(tl + cS, tl + cO, half, u, o2);
       const float gC = __expf(bC);
 #pragma unroll
       for (int j = 0; j < 16; ++j) s[j] = fmaf(gC, s[j], u[j]);
-      tmem_ld_hl16_pair(tl + cO, half, u);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) u[j] = o2[j] + __shfl_xor_sync(0xffffffffu, o2[j], 16);
       if (!kside) {
 #pragma unroll
         for (int j = 0; j < 16; ++j) u[j] += yp[j];
@@ -977,8 +1000,21 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
     //    warp-wide aligned instruction: every lane executes the same loads, outside the branch.
     {
       float x[16], g[16];
-      tmem_ld_hl16(tl + cX, half, x);
-      tc::tmem_ld16(tl + cG + 16 * half, g);
+      {
+        uint32_t a0[16], a1[16], b0[16];
+        tc::tmem_ld16_nw(tl + cX + 16 * half, a0);
+        tc::tmem_ld16_nw(tl + cX + 32 + 16 * half, a1);
+        tc::tmem_ld16_nw(tl + cG + 16 * half, b0);
+        tc::tmem_wait_ld();
+        tc::reg_fence(a0);
+        tc::reg_fence(a1);
+        tc::reg_fence(b0);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          x[j] = __uint_as_float(a0[j]) + __uint_as_float(a1[j]);
+          g[j] = __uint_as_float(b0[j]);
+        }
+      }
       if (kside) {
         const float lam = __expf(bC - bi);
 #pragma unroll
