@@ -51,6 +51,7 @@ def parse():
     ap.add_argument("--algo", type=int, default=0, help="0 auto, 1 row-parallel, 2 chunked")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of a CUDA graph of the step")
     return ap.parse_args()
 
 
@@ -243,6 +244,30 @@ def run_ours(args):
         allreduce(out[5], out[6])
     torch.cuda.synchronize()
 
+    # The step's launches captured once in a CUDA graph and replayed (the library's host-side work --
+    # argument checks, tensor maps, workspace allocation -- then costs nothing per step); the gradient
+    # all-reduce runs eagerly after each replay.
+    graph, gout, graph_launches = None, None, 0
+    if not args.no_graph:
+        try:
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                W.step()
+            torch.cuda.current_stream().wait_stream(side)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            n_cap = _lib.launches()
+            with torch.cuda.graph(graph):
+                gout = W.step()
+            graph_launches = _lib.launches() - n_cap
+            graph.replay()
+            torch.cuda.synchronize()
+        except Exception as exc:  # capture unsupported here: time eager launches
+            print(f"bench: CUDA graph capture failed ({exc}); timing eager launches", file=sys.stderr)
+            graph, gout = None, None
+            torch.cuda.synchronize()
+
     sampler = ClockSampler(local)
     if dist:
         torch.distributed.barrier()
@@ -257,16 +282,26 @@ def run_ours(args):
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
-        out = W.step(op_events)
+        if graph is not None:
+            graph.replay()
+            out = gout
+        else:
+            out = W.step(op_events)
         allreduce(out[5], out[6])
         e1.record()
         step_events.append((e0, e1))
     torch.cuda.synchronize()
     if dist:
         torch.distributed.barrier()
-    launches = _lib.launches() - n0
+    launches = (_lib.launches() - n0) + graph_launches * args.steps
     clocks = sampler.stop()
     ms = sum(a.elapsed_time(b) for a, b in step_events) / args.steps
+    if graph is not None:  # the per-op split from eager steps (after eager warm-up: the graph's pool is its own)
+        for k in range(3 + args.steps):
+            flush_l2(flush)
+            out = W.step(op_events if k >= 3 else None)
+            allreduce(out[5], out[6])
+        torch.cuda.synchronize()
     per_op = {}
     for name, a, b in op_events:
         per_op.setdefault(name, []).append(a.elapsed_time(b))
@@ -329,6 +364,7 @@ def run_ours(args):
                        "global_batch": world * B if args.workload == "c1" else 8, "seq_len": T,
                        "parallelism": f"dp{world}" if args.workload == "c1" else f"bh{world}",
                        "l2": "flushed before every step (512 MiB write, outside the step events)",
+                       "launch": "CUDA graph of the step, replayed" if graph is not None else "eager",
                        "algo": {0: "auto", 1: "rows", 2: "chunked"}[args.algo],
                        "step": ("layer_fwd(save) + layer_bwd" if args.algo != 1 else
                                 "gate_fwd + gdn_fwd(save) + gdn_bwd + gate_bwd") + (" + allreduce" if dist else "")},
