@@ -149,6 +149,25 @@ def test_varlen_matches_oracle():
     assert_close(pf, run_gpu(pf, ROWS, cu), oracle_all(pf, cu), 1e-5, ref_worst=True)
 
 
+@pytest.mark.parametrize("lengths", [None, [130, 1, 64, 257, 40]])
+def test_chunked_fp32_outputs(lengths):
+    """bf16 activations with float32 y and gradients on the chunked path (the float32 output tiles and
+    their stores), fixed-length and varlen with partial last chunks.  With no bf16 rounding of the
+    outputs the error budget is the kernels' own: rel-L2 <= 1e-3."""
+    cu = synthetic.cu_from_lengths(lengths) if lengths else None
+    T = cu[-1] if cu else 200
+    p = synthetic.make(1, T, 16, 32, 128, 128, seed=21, dtype=torch.bfloat16, h0_std=0.02, dhT_std=0.02,
+                       cu_seqlens=cu, uniform_gate=0.9)
+    d = p.to("cuda")
+    y, hT, saved = deltanet.gated_delta_fwd(d.q, d.k, d.v, d.g, d.beta, d.h0, cu_seqlens=cu, save=True,
+                                            out_dtype=torch.float32, algo=CHUNKED)
+    grads = deltanet.gated_delta_bwd(d.q, d.k, d.v, d.g, d.beta, d.h0, d.dy, d.dhT, saved=saved, cu_seqlens=cu,
+                                     algo=CHUNKED, grad_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert y.dtype == torch.float32 and grads[0].dtype == torch.float32 and grads[2].dtype == torch.float32
+    assert_close(p, (y, hT, grads), oracle_all(p.to(dtype=torch.float32), cu), 1e-3)
+
+
 def test_golden_fixtures_through_the_abi():
     for f in sorted(os.listdir(GOLDEN)):
         if not f.endswith(".npz"):
