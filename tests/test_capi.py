@@ -140,3 +140,24 @@ def test_step_verify_gate_validation(L):
     assert L.qb_gdn_verify(1, 0, 2, 4, 128, 128, 1, 1, *([None] * 8), None, err, len(err)) == -1
     assert L.qb_gdn_gate_fwd(10, 2, 4, 100, 1, 1, *([None] * 10), None, err, len(err)) == -1
     assert L.qb_gdn_keep_rows(1, 2, 4, 128, 128, None, None, None, None, None, err, len(err)) == -1
+
+
+@pytest.mark.parametrize("bad", [dict(Dk=64, Dv=64), dict(in_dtype=_lib.QB_DTYPE_F32), dict(algo=_lib.QB_ALGO_ROWS)])
+def test_layer_path_refuses_what_the_chunked_kernels_cannot_take(L, bad):
+    """The fused norm/gate path runs on the chunked kernels only: other shapes, float32 activations or
+    the row-parallel algo are refused (workspace, saved-buffer and both calls alike), before any launch."""
+    d = desc(**bad)
+    err = _lib.err_buf()
+    for op in (_lib.QB_OP_LAYER_FWD, _lib.QB_OP_LAYER_BWD):
+        assert L.qb_gdn_workspace_bytes(ctypes.byref(d), op, err, len(err)) == -1
+        assert b"fused norm/gate path" in err.value
+    assert L.qb_gdn_layer_saved_bytes(ctypes.byref(d), err, len(err)) == -1
+    fake = ctypes.c_void_p(0x10000)
+    assert L.qb_gdn_layer_fwd(ctypes.byref(d), *([fake] * 12), 1 << 30, None, err, len(err)) == -1
+    assert L.qb_gdn_layer_bwd(ctypes.byref(d), *([fake] * 20), 1 << 30, None, err, len(err)) == -1
+    assert b"fused norm/gate path" in err.value
+
+
+def test_unknown_op_is_refused(L):
+    n, e = ws_or_err(L, desc(), 9)
+    assert n == -1 and "unknown op" in e

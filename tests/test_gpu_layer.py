@@ -111,3 +111,31 @@ def test_layer_autograd():
     want = dict(zip(NAMES, go))
     for name, x in zip(("dq", "dk", "dv", "da", "db", "dA_log", "ddt_bias", "dh0"), xs):
         assert rel(x.grad, want[name]) <= 2e-3, name
+
+
+def test_layer_argument_checks():
+    """On a GPU (where the chunked path is available) the layer calls refuse null, misaligned and
+    short-workspace arguments with the reason, and enqueue nothing."""
+    import ctypes
+    from quotebound_b200 import deltanet
+    L = _lib.load()
+    q = torch.zeros(1, 128, 2, 128, dtype=torch.bfloat16, device="cuda")
+    v = torch.zeros(1, 128, 4, 128, dtype=torch.bfloat16, device="cuda")
+    d = deltanet.make_desc(q, v)
+    err = _lib.err_buf()
+    need = L.qb_gdn_workspace_bytes(ctypes.byref(d), _lib.QB_OP_LAYER_FWD, err, len(err))
+    assert need > 0, err.value
+    assert L.qb_gdn_layer_saved_bytes(ctypes.byref(d), err, len(err)) > 0
+    fake, odd = ctypes.c_void_p(0x10000), ctypes.c_void_p(0x10002)
+    assert L.qb_gdn_layer_fwd(ctypes.byref(d), *([None] * 12), need, None, err, len(err)) == -1
+    assert b"non-null" in err.value
+    args = [fake] * 7 + [None, fake, None, None]  # q k v a b A_log dt_bias, h0, y, hT, saved
+    assert L.qb_gdn_layer_fwd(ctypes.byref(d), odd, *args[1:], fake, need, None, err, len(err)) == -1
+    assert b"alignment" in err.value
+    assert L.qb_gdn_layer_fwd(ctypes.byref(d), *args, fake, need - 1, None, err, len(err)) == -1
+    assert b"workspace" in err.value
+    need_b = L.qb_gdn_workspace_bytes(ctypes.byref(d), _lib.QB_OP_LAYER_BWD, err, len(err))
+    assert need_b > 0
+    assert L.qb_gdn_layer_bwd(ctypes.byref(d), *([None] * 20), need_b, None, err, len(err)) == -1
+    assert b"non-null" in err.value
+    torch.cuda.synchronize()
