@@ -50,10 +50,11 @@ constexpr int DK = 128;
 constexpr int DV = 128;
 constexpr int DVT = 32;     // value rows of the state per CTA in the walks; the dv slice in the gradient kernel
 
+// fp32 to the nearest tf32 (10 mantissa bits), ties away from zero: add half of the 13 dropped bits'
+// weight to the bit pattern and clear them (a carry into the exponent is the correct rounding up;
+// infinities keep their pattern).
 __device__ __forceinline__ float tf32_rna(float x) {
-  uint32_t u;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u) : "f"(x));
-  return __uint_as_float(u);
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
 }
 
 // Chunk geometry: chunk index -> sequence, first token, valid steps.
@@ -727,7 +728,12 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
         tc::st_row_hilo16(smem + FW_D, i_row, d, half);
       } else {
         // (the other staging buffer's store was read before the last chunk's final barrier)
-        if (a.Ds) st16_f32_sw(smem + FW_DS + buf * 8192, i_row, half, d);
+        if (a.Ds) {  // tf32-rounded: the gradient kernel's tf32 operand, loaded as is
+          float dr[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) dr[j] = tf32_rna(d[j]);
+          st16_f32_sw(smem + FW_DS + buf * 8192, i_row, half, dr);
+        }
         const float lam = __expf(bC - bi);
 #pragma unroll
         for (int j = 0; j < 16; ++j) d[j] *= lam;
@@ -805,7 +811,9 @@ struct BwdStateArgs {
   const uint8_t* Timg;    // the forward's operand images
   const uint8_t* Pimg;
   const uint8_t* KQimg;
-  float* Fs;              // F = T^T dD for the gradient kernel, fp32 tiles [chunks, Hv, Dv / 32][64][32]
+  // the gradient kernel's A operand [dO; F] (F = T^T dD), tf32, as the 128-row K-major image with
+  // 16-row groups interleaved: [chunks, Hv, Dv / 32] x 16 KB
+  uint8_t* Aimg;
   int* err;
 };
 
@@ -819,9 +827,9 @@ constexpr int BW_DD = 131072;      // 8 KB bf16 dD [hi | lo]
 constexpr int BW_H = 139264;       // 8 KB bf16 H = -beta gamma F [hi | lo]
 constexpr int BW_CK = 147456;      // 16 KB fp32 dS staging [32 dv][128 dk] (bulk store)
 constexpr int BW_V = 163840;       // 2 x 4 KB bf16 dO rows [64][32] (TMA)
-constexpr int BW_FS = 172032;      // 2 x 8 KB fp32 F rows [64][32] staging (bulk store)
-constexpr int BW_DV = 188416;      // 8 KB dv rows [64][32] staging (TMA store of full chunks)
-constexpr int BW_SMEM = 196608 + 1024;
+constexpr int BW_FS = 172032;      // 2 x 16 KB [dO; F] operand image staging (bulk store)
+constexpr int BW_DV = 204800;      // 8 KB dv rows [64][32] staging (TMA store of full chunks)
+constexpr int BW_SMEM = 212992 + 1024;
 
 // K-step ks of the transpose of one half (part 0 = hi, 1 = lo) of a [hi; lo] image as the M = 64
 // MN-major A operand: the image's rows (chunk steps) are K.
@@ -961,6 +969,9 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
         raw.w[1] = w1;
         float d[16];
         cvt_row16(raw, d);
+        // dO (exact in tf32) into the gradient kernel's image, lower row of the pair (the other staging
+        // buffer's store was read before the last chunk's step-4 barrier)
+        st16_f32_sw(smem + BW_FS + buf * 16384, img_row(i_row), half, d);
 #pragma unroll
         for (int j = 0; j < 16; ++j) d[j] *= gi;
         tc::st_row_hilo16(smem + BW_GD, i_row, d, half);
@@ -1046,8 +1057,12 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
       float f[16];
       tmem_ld_hl16(tl + cF, half, f);
       if (kside) {
-        // (the other staging buffer's store was read before the last chunk's step-4 barrier)
-        st16_f32_sw(smem + BW_FS + buf * 8192, i_row, half, f);
+        {  // F, tf32-rounded, into the image's upper row of the pair
+          float fr[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) fr[j] = tf32_rna(f[j]);
+          st16_f32_sw(smem + BW_FS + buf * 16384, img_row(i_row) + 16, half, fr);
+        }
         float o[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) o[j] = be * f[j];
@@ -1071,7 +1086,8 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
       tc::mma_commit(&bar_mma);
     }
     if (tid == 32) {
-      tc::bulk_store(a.Fs + ((size_t)(cg * Hv + hv) * (DV / DVT) + blockIdx.x) * 2048, smem + BW_FS + buf * 8192, 8192);
+      tc::bulk_store(a.Aimg + ((size_t)(cg * Hv + hv) * (DV / DVT) + blockIdx.x) * 16384, smem + BW_FS + buf * 16384,
+                     16384);
       if (L == C) tc::tma_store_3d(&dvmap, smem + BW_DV, dv0, hv, (int)tok0);
       tc::bulk_commit();
     }
@@ -1112,7 +1128,8 @@ struct GradArgs {
   const float* gates;       // [chunks, Hv, 2, 64]
   const uint8_t *Pimg, *KQimg;  // the forward's operand images
   const float* Lbuf;        // [chunks, Hv, 64, 64] strict-lower Gamma * K K^T
-  const float *Ds, *Fs;     // D and F, fp32 tiles [chunks, Hv, Dv / 32][64][32]
+  const float* Ds;          // D (tf32-rounded), fp32 tiles [chunks, Hv, Dv / 32][64][32], rows swizzled
+  const uint8_t* Aimg;      // [dO; F] operand images [chunks, Hv, Dv / 32] x 16 KB
   void *dq, *dk;            // [B*T, Hk, Dk]
   float *dg, *dbeta;        // [B*T, Hv]; layer mode: da, db
   int* err;
@@ -1125,11 +1142,9 @@ struct GradArgs {
 // Shared memory of the gradient kernel.
 constexpr int GR_KQ = 0;           // 32 KB bf16 [K; Q] image
 constexpr int GR_P = 32768;        // 16 KB bf16 [P_hi; P_lo] image of the value head
-constexpr int GR_BUF = 49152;      // 2 x 56 KB slice buffers: S, dS (fp32, MN-major tf32 [32 dv][128 dk]),
-constexpr int GR_BS = 57344;       //   D, F (fp32 [64][32]), dO and V rows (bf16 [64][32])
-constexpr int GR_A = 163840;       // 16 KB tf32 [dO; F], K-major, 16-row groups interleaved
-constexpr int GR_DT = 180224;      // 8 KB tf32 D, K-major [64][32] (A of D dS, B of [dO; F] D^T)
-constexpr int GR_SMEM = 188416 + 1024;
+constexpr int GR_BUF = 49152;      // 2 x 60 KB slice buffers: S, dS (tf32, MN-major [32 dv][128 dk], +0, +16 KB),
+constexpr int GR_BS = 61440;       //   the [dO; F] image (+32 KB), D (K-major [64][32], +48 KB), V rows (+56 KB)
+constexpr int GR_SMEM = 172032 + 1024;
 // the value head's finalize reuses the slice buffers: L (fp32 [64][64]), the [dP^; dKK] images, a
 // column-sum scratch
 constexpr int GR_L = GR_BUF, GR_FHI = GR_BUF + 16384, GR_FLO = GR_BUF + 32768, GR_SCR = GR_BUF + 49152;
@@ -1182,7 +1197,6 @@ __device__ __forceinline__ void ld_img_row32(const uint8_t* slab, int r, int m, 
 template <typename Tout>
 __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_constant__ CUtensorMap smap_mn,
                                                              const __grid_constant__ CUtensorMap dmap_mn,
-                                                             const __grid_constant__ CUtensorMap omap,
                                                              const __grid_constant__ CUtensorMap vmap, GradArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -1228,17 +1242,16 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
     const int r = q / NSL, sl = q - r * NSL, hv = hk * ratio + r, bs = q & 1;
     uint8_t* buf = smem + GR_BUF + bs * GR_BS;
     const int srow_ = (int)((c * Hv + hv) * DV + sl * DVT);
-    const size_t tile = ((size_t)(c * Hv + hv) * NSL + sl) * 2048;
-    tc::mbar_arrive_expect_tx(&bar_s[bs], 2 * 16384 + 2 * 8192 + 2 * 4096);
+    const size_t tile = (size_t)(c * Hv + hv) * NSL + sl;
+    tc::mbar_arrive_expect_tx(&bar_s[bs], 3 * 16384 + 8192 + 4096);
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
       tc::tma_load_2d(buf + 4096 * b, &smap_mn, &bar_s[bs], 32 * b, srow_);
       tc::tma_load_2d(buf + 16384 + 4096 * b, &dmap_mn, &bar_s[bs], 32 * b, srow_);
     }
-    tc::bulk_load(buf + 32768, a.Ds + tile, 8192, &bar_s[bs]);
-    tc::bulk_load(buf + 40960, a.Fs + tile, 8192, &bar_s[bs]);
-    tc::tma_load_3d(buf + 49152, &omap, &bar_s[bs], sl * DVT, hv, (int)tok0);
-    tc::tma_load_3d(buf + 53248, &vmap, &bar_s[bs], sl * DVT, hv, (int)tok0);
+    tc::bulk_load(buf + 32768, a.Aimg + tile * 16384, 16384, &bar_s[bs]);
+    tc::bulk_load(buf + 49152, a.Ds + tile * 2048, 8192, &bar_s[bs]);
+    tc::tma_load_3d(buf + 57344, &vmap, &bar_s[bs], sl * DVT, hv, (int)tok0);
   };
   auto issue_head = [&](int r) {
     const int hv = hk * ratio + r;
@@ -1249,7 +1262,6 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
   if (tid == 32) {
     tc::prefetch_tmap(&smap_mn);
     tc::prefetch_tmap(&dmap_mn);
-    tc::prefetch_tmap(&omap);
     tc::prefetch_tmap(&vmap);
     tc::mbar_arrive_expect_tx(&bar_kq, 32768);
     tc::bulk_load(smem + GR_KQ, a.KQimg + (size_t)(c * a.geo.Hk + hk) * 32768, 32768, &bar_kq);
@@ -1292,38 +1304,12 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
       ok = wait_all(&bar_s[bs], (uint32_t)((q >> 1) & 1), a.err, 37);
       if (!ok) break;
       if (tid == 32 && sl + 1 < NSL) issue_slice(q + 1);  // the other buffer's last reader has finished
-      // a. t5 (S and dS arrive rounded to tf32, the B operands of the products over the value rows)
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int idx = tid + 256 * u;
-        const float4 sv = reinterpret_cast<const float4*>(buf)[idx];
-        const float4 dvv = reinterpret_cast<const float4*>(buf + 16384)[idx];
-        t5 += sv.x * dvv.x + sv.y * dvv.y + sv.z * dvv.z + sv.w * dvv.w;
-      }
-      // b. the operands of row i: lower lanes F (into [dO; F]) and F . V; upper lanes dO and D
-      if (lower) {
-        float f[16], v[16];
-        ld16_f32_sw(buf + 40960, i_row, half, f);
-        ld16_bf16(buf + 53248 + i_row * 64 + 32 * half, rvalid, v);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) fv = fmaf(f[j], v[j], fv);
-        st_row_k_f32_16(smem + GR_A, img_row(i_row) + 16, f, half);
-      } else {
-        float o[16], d[16];
-        ld16_bf16(buf + 49152 + i_row * 64 + 32 * half, rvalid, o);
-        ld16_f32_sw(buf + 32768, i_row, half, d);
-        st_row_k_f32_16(smem + GR_A, img_row(i_row), o, half);
-        st_row_k_f32_16(smem + GR_DT, i_row, d, half);
-      }
-      tc::fence_async_smem();
-      tc::fence_before_sync();
-      __syncthreads();
-      tc::fence_after_sync();
-      // c. over the slice's value rows (tf32, K = 32): [dO; F] S, D dS (M = 64 in the upper lanes),
-      //    [dO; F] D^T
+      // a. over the slice's value rows (tf32, K = 32; every operand arrives in its final form): [dO; F] S,
+      //    D dS (M = 64 in the upper lanes), [dO; F] D^T -- issued at once
       if (tid == 0) {
+        tc::fence_after_sync();
         const uint32_t s32 = tc::smem_u32(buf), d32 = tc::smem_u32(buf + 16384);
-        const uint32_t aa = tc::smem_u32(smem + GR_A), dt = tc::smem_u32(smem + GR_DT);
+        const uint32_t aa = tc::smem_u32(buf + 32768), dt = tc::smem_u32(buf + 49152);
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
           tc::mma_tf32(tmem + cA1, tc::desc_kmajor(aa, 128, ks), tc::desc_mnmajor(s32, DVT, ks, 8), idC1,
@@ -1337,6 +1323,21 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
           tc::mma_tf32(tmem + cPF, tc::desc_kmajor(aa, 128, ks), tc::desc_kmajor(dt, 64, ks), idC3,
                        (sl > 0 || ks > 0) ? 1u : 0u);
         tc::mma_commit(&bar_mma);
+      }
+      // b. meanwhile: t5 = S (.) dS, and F_i . V_i (lower lanes)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int idx = tid + 256 * u;
+        const float4 sv = reinterpret_cast<const float4*>(buf)[idx];
+        const float4 dvv = reinterpret_cast<const float4*>(buf + 16384)[idx];
+        t5 += sv.x * dvv.x + sv.y * dvv.y + sv.z * dvv.z + sv.w * dvv.w;
+      }
+      if (lower) {
+        float f[16], v[16];
+        ld16_f32_sw(buf + 32768, img_row(i_row) + 16, half, f);
+        ld16_bf16(buf + 57344 + i_row * 64 + 32 * half, rvalid, v);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) fv = fmaf(f[j], v[j], fv);
       }
       ok = wait_all(&bar_mma, ph_mma, a.err, 34);
       ph_mma ^= 1;
@@ -1731,7 +1732,7 @@ struct Ws {
   uint8_t *Timg, *Pimg, *KQimg;
   float* gates;
   float* dsbuf;
-  float* Fs;         // F = T^T dD from the reverse walk, fp32 tiles [chunks, Hv, 4][64][32]
+  uint8_t* Aimg;     // [dO; F] operand images from the reverse walk, [chunks, Hv, 4] x 16 KB
   float* head_part;
   char* saved;
   char* fwd_ws;
@@ -1755,7 +1756,7 @@ int64_t ws_layout(int Hv, int Hk, int N, int64_t n_chunks, bool layer, bool varl
     x.gates = (float*)take(n_chunks * Hv * 128 * 4);
   } else {
     x.dsbuf = (float*)take(n_chunks * Hv * (int64_t)DV * DK * 4);
-    x.Fs = (float*)take(n_chunks * Hv * 64 * DV * 4);
+    x.Aimg = (uint8_t*)take(n_chunks * Hv * (DV / DVT) * 16384);
     x.head_part = (float*)take(layer ? n_chunks * Hv * 2 * 4 : 0);
     if (with_saved) {
       x.saved = take(saved_layout(Hv, Hk, n_chunks, nullptr, nullptr));
@@ -1847,7 +1848,7 @@ cudaError_t chunked_bwd(const ChunkBwdArgs& a, void* ws, cudaStream_t st) {
   if (!map_rows(&dmap, a.dy, rows, a.Hv, a.Dv, DVT, C) || !map_rows(&vmap, a.v, rows, a.Hv, a.Dv, DVT, C) ||
       !map_rows(&dvmap, a.dv, rows, a.Hv, a.Dv, DVT, C, !a.out_bf16))
     return cudaErrorInvalidValue;
-  BwdStateArgs ba{geo, a.dy, sv.gates, a.dhT, a.dv, a.dh0, w.dsbuf, sv.Timg, sv.Pimg, sv.KQimg, w.Fs, w.err};
+  BwdStateArgs ba{geo, a.dy, sv.gates, a.dhT, a.dv, a.dh0, w.dsbuf, sv.Timg, sv.Pimg, sv.KQimg, w.Aimg, w.err};
   auto k1 = a.out_bf16 ? gdn_chunk_bwd_state<__nv_bfloat16> : gdn_chunk_bwd_state<float>;
   if ((e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, BW_SMEM)) != cudaSuccess) return e;
   k1<<<dim3(DV / DVT, a.Hv, a.N), 256, BW_SMEM, st>>>(dmap, dvmap, ba);
@@ -1864,12 +1865,12 @@ cudaError_t chunked_bwd(const ChunkBwdArgs& a, void* ws, cudaStream_t st) {
   if (!map_state_mn(&smap_mn, sv.ckpt, a.n_chunks * a.Hv * (int64_t)DV) ||
       !map_state_mn(&dmap_mn, w.dsbuf, a.n_chunks * a.Hv * (int64_t)DV))
     return cudaErrorInvalidValue;
-  GradArgs ga{geo, a.g, sv.gates, sv.Pimg, sv.KQimg, sv.L, sv.Ds, w.Fs, a.dq, a.dk, a.dg, a.dbeta, w.err,
+  GradArgs ga{geo, a.g, sv.gates, sv.Pimg, sv.KQimg, sv.L, sv.Ds, w.Aimg, a.dq, a.dk, a.dg, a.dbeta, w.err,
               static_cast<const __nv_bfloat16*>(a.q), static_cast<const __nv_bfloat16*>(a.k),
               a.a_raw, a.b_raw, a.A_log, a.dt_bias, w.head_part};
   auto k2 = a.out_bf16 ? gdn_chunk_bwd_grad<__nv_bfloat16> : gdn_chunk_bwd_grad<float>;
   if ((e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, GR_SMEM)) != cudaSuccess) return e;
-  k2<<<dim3((unsigned)a.n_chunks, a.Hk), 256, GR_SMEM, st>>>(smap_mn, dmap_mn, dmap, vmap, ga);
+  k2<<<dim3((unsigned)a.n_chunks, a.Hk), 256, GR_SMEM, st>>>(smap_mn, dmap_mn, vmap, ga);
   note_launch();
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   if (layer) {
