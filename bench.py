@@ -247,26 +247,33 @@ def run_ours(args):
     # The step's launches captured once in a CUDA graph and replayed (the library's host-side work --
     # argument checks, tensor maps, workspace allocation -- then costs nothing per step); the gradient
     # all-reduce runs eagerly after each replay.
-    graph, gout, graph_launches = None, None, 0
+    # With several ranks the all-reduce is captured too (NCCL supports capture; the communicator was
+    # created by the eager warm-up); if that capture fails, the graph holds the step alone.
+    graph, gout, graph_launches, graph_reduces = None, None, 0, False
     if not args.no_graph:
-        try:
-            side = torch.cuda.Stream()
-            side.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(side):
-                W.step()
-            torch.cuda.current_stream().wait_stream(side)
-            torch.cuda.synchronize()
-            graph = torch.cuda.CUDAGraph()
-            n_cap = _lib.launches()
-            with torch.cuda.graph(graph):
-                gout = W.step()
-            graph_launches = _lib.launches() - n_cap
-            graph.replay()
-            torch.cuda.synchronize()
-        except Exception as exc:  # capture unsupported here: time eager launches
-            print(f"bench: CUDA graph capture failed ({exc}); timing eager launches", file=sys.stderr)
-            graph, gout = None, None
-            torch.cuda.synchronize()
+        for with_reduce in ((True, False) if dist else (False,)):
+            try:
+                side = torch.cuda.Stream()
+                side.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(side):
+                    W.step()
+                torch.cuda.current_stream().wait_stream(side)
+                torch.cuda.synchronize()
+                graph = torch.cuda.CUDAGraph()
+                n_cap = _lib.launches()
+                with torch.cuda.graph(graph):
+                    gout = W.step()
+                    if with_reduce:
+                        allreduce(gout[5], gout[6])
+                graph_launches = _lib.launches() - n_cap
+                graph.replay()
+                torch.cuda.synchronize()
+                graph_reduces = with_reduce
+                break
+            except Exception as exc:  # capture unsupported here: try without the collective, then eager
+                print(f"bench: CUDA graph capture failed ({exc})", file=sys.stderr)
+                graph, gout = None, None
+                torch.cuda.synchronize()
 
     sampler = ClockSampler(local)
     if dist:
@@ -284,10 +291,11 @@ def run_ours(args):
         e0.record()
         if graph is not None:
             graph.replay()
-            out = gout
+            if not graph_reduces:
+                allreduce(gout[5], gout[6])
         else:
             out = W.step(op_events)
-        allreduce(out[5], out[6])
+            allreduce(out[5], out[6])
         e1.record()
         step_events.append((e0, e1))
     torch.cuda.synchronize()
@@ -364,7 +372,8 @@ def run_ours(args):
                        "global_batch": world * B if args.workload == "c1" else 8, "seq_len": T,
                        "parallelism": f"dp{world}" if args.workload == "c1" else f"bh{world}",
                        "l2": "flushed before every step (512 MiB write, outside the step events)",
-                       "launch": "CUDA graph of the step, replayed" if graph is not None else "eager",
+                       "launch": ("CUDA graph of the step" + (" and its all-reduce" if graph_reduces else "") +
+                                  ", replayed") if graph is not None else "eager",
                        "algo": {0: "auto", 1: "rows", 2: "chunked"}[args.algo],
                        "step": ("layer_fwd(save) + layer_bwd" if args.algo != 1 else
                                 "gate_fwd + gdn_fwd(save) + gdn_bwd + gate_bwd") + (" + allreduce" if dist else "")},
@@ -377,6 +386,9 @@ def run_ours(args):
         if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(args.workload)
         print(json.dumps(line), flush=True)
+    # a graph that holds an NCCL call is released before its process group
+    del graph, gout
+    torch.cuda.synchronize()
     if dist:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
