@@ -21,15 +21,17 @@
 //   d b_i (log-gate cumsum) from every Gamma, gamma and lambda above; d log g = reverse cumsum of d b.
 //
 // Kernels:
-//   gdn_chunk_prep       (chunks, Hv): K K^T and Q K^T on the tensor cores, T by forward substitution;
-//                        writes T, P, Gamma*KK (training) and the gates.  Fully parallel.
+//   gdn_chunk_prep       (chunks, Hk): K K^T and Q K^T on the tensor cores, then per value head of the
+//                        key head T by forward substitution; writes the T, P and [K; Q] operand images
+//                        and the gates.  Fully parallel.
 //   gdn_chunk_fwd_state  (Dv/32, Hv, sequences): the chunks of a sequence in order, 32 state rows in
 //                        registers; three tcgen05 rounds per chunk (K S^T, Q S^T | T E | P D, K^T D~).
 //                        Writes y and, for training, the chunk-start states.
 //   gdn_chunk_bwd_state  (Dv/32, Hv, sequences): the chunks in reverse with 32 rows of dS; three rounds
 //                        (K dS^T, P^T dO | T^T dD | Q^T (gamma dO), K^T H).  Writes dv, dS per chunk, dh0.
 //   gdn_chunk_bwd_grad   (chunks, Hk): everything else per chunk, the value heads of a key head in turn
-//                        so dq and dk are summed over the group in TMEM in a fixed order.
+//                        so dq and dk are summed over the group in TMEM in a fixed order; K K^T is
+//                        recomputed there from the [K; Q] image (one MMA per CTA).
 // Operand precision: input x input products in bf16 (exact); input x computed with the computed tile
 // split into bf16 hi + lo (about 16 mantissa bits); computed x computed in tf32 (round to nearest).
 #include <cuda.h>
@@ -191,7 +193,7 @@ __device__ __forceinline__ bool wait_all(uint64_t* bar, uint32_t parity, int* er
 }  // namespace
 
 // ------------------------------------------------------------------------------------------------
-// Per (chunk, value head): T, P, Gamma*KK and the gates of the chunk.
+// Per (chunk, key head): the [K; Q] image; per value head of the group T, P and the gates of the chunk.
 struct PrepArgs {
   Geo geo;
   const float *g, *beta;
@@ -200,7 +202,6 @@ struct PrepArgs {
   uint8_t* Timg;    // [chunks, Hv] x 16 KB: T as the stacked bf16 [T_hi; T_lo] operand image
   uint8_t* Pimg;    // [chunks, Hv] x 16 KB: P likewise
   uint8_t* KQimg;   // [chunks, Hk] x 32 KB: the walk's [K; Q] operand (16-row groups interleaved)
-  float* Lbuf;      // [chunks, Hv, 64, 64]  strict-lower Gamma * K K^T (training only), or null
   float* gates;     // [chunks, Hv, 2, 64]:  b then beta
   int* err;
 };
@@ -243,29 +244,41 @@ __global__ void __launch_bounds__(128, 4) gdn_chunk_prep(const __grid_constant__
     tc::tma_load_3d(qtile + 8192, &qmap, &bar_tma, 64, hk, (int)tok0);
   }
   const bool layer = a.g == nullptr;
-  // the gate inputs of the first value head, loaded while the tiles arrive
-  auto gate_in = [&](int hv, float& lg, float& bt) {
-    lg = 0.f, bt = 0.f;
+  // a value head's raw gate inputs (loaded one head ahead, so that their latency hides behind the
+  // previous head's work), then log g and beta from them
+  auto gate_load = [&](int hv, float (&gr)[4]) {
+    gr[0] = gr[1] = gr[2] = gr[3] = 0.f;
     if (tid < 64 && tid < L) {
       const int64_t gi = (tok0 + tid) * a.geo.Hv + hv;
-      if (layer) {  // log g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b) (src/deltanet.cpp:41-52, :118)
-        lg = -expf(a.A_log[hv]) * softplus_f(a.a_raw[gi] + a.dt_bias[hv]);
-        bt = sigmoid_f(a.b_raw[gi]);
+      if (layer) {
+        gr[0] = a.a_raw[gi], gr[1] = a.b_raw[gi], gr[2] = a.A_log[hv], gr[3] = a.dt_bias[hv];
       } else {
-        lg = fmaxf(logf(a.g[gi]), -88.f);
-        bt = a.beta[gi];
+        gr[0] = a.g[gi], gr[1] = a.beta[gi];
       }
     }
   };
-  float lg, bt;
-  gate_in(hk * ratio, lg, bt);
+  auto gate_eval = [&](const float (&gr)[4], float& lg, float& bt) {
+    lg = 0.f, bt = 0.f;
+    if (tid < 64 && tid < L) {
+      if (layer) {  // log g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b) (src/deltanet.cpp:41-52, :118)
+        lg = -expf(gr[2]) * softplus_f(gr[0] + gr[3]);
+        bt = sigmoid_f(gr[1]);
+      } else {
+        lg = fmaxf(logf(gr[0]), -88.f);
+        bt = gr[1];
+      }
+    }
+  };
+  float gr[4];
+  gate_load(hk * ratio, gr);
 
   bool ok = wait_all(&bar_tma, 0, a.err, 1);
   if (ok && layer) {
     // q and k rows normalised in place as the model does (src/deltanet.cpp:113-116): rms_norm in fp32,
     // rounded to bf16, times the bf16 scalar 1/Dk (q) or 1/sqrt(Dk) (k), rounded again.  Thread t
-    // owns half a row (one 128-byte slab row of 64 elements); the order inside a row does not matter.
-    const int row = tid >> 1, half = tid & 1;
+    // owns half a row (one 128-byte slab row of 64 elements); the order inside a row does not matter,
+    // so step c touches chunk c ^ (row & 7): eight consecutive rows then hit eight different banks.
+    const int row = tid >> 1, half = tid & 1, rx = row & 7;
 #pragma unroll
     for (int m = 0; m < 2; ++m) {
       uint8_t* tile = m == 0 ? ktile : qtile;
@@ -274,7 +287,7 @@ __global__ void __launch_bounds__(128, 4) gdn_chunk_prep(const __grid_constant__
       float ss = 0.f;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
-        w[c] = r16[c];
+        w[c] = r16[c ^ rx];
         const uint32_t u[4] = {w[c].x, w[c].y, w[c].z, w[c].w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -296,7 +309,7 @@ __global__ void __launch_bounds__(128, 4) gdn_chunk_prep(const __grid_constant__
           const float x1 = __bfloat162float(__float2bfloat16_rn(__high2float(h) * r)) * sc;
           u[e] = tc::pack_bf16(x0, x1);
         }
-        r16[c] = make_uint4(u[0], u[1], u[2], u[3]);
+        r16[c ^ rx] = make_uint4(u[0], u[1], u[2], u[3]);
       }
     }
     tc::fence_async_smem();
@@ -328,7 +341,9 @@ __global__ void __launch_bounds__(128, 4) gdn_chunk_prep(const __grid_constant__
   // head in turn: its gated L and P, T, the images.
   for (int r = 0; r < ratio && ok; ++r) {
   const int hv = hk * ratio + r;
-  if (r > 0) gate_in(hv, lg, bt);
+  float lg, bt;
+  gate_eval(gr, lg, bt);
+  if (r + 1 < ratio) gate_load(hv + 1, gr);
   if (tid < 64) sbeta[tid] = bt;
   scan64(lg, sb, stmp);
   __syncthreads();
@@ -354,13 +369,6 @@ __global__ void __launch_bounds__(128, 4) gdn_chunk_prep(const __grid_constant__
       if (kkside) {
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) Lt[(32 * h + jj) * LS + i] = be * v[jj];
-        if (a.Lbuf) {  // 16-byte chunk c of row i at position c ^ (i & 15): conflict-free row reads
-          float* lrow = a.Lbuf + mat + i * 64;
-#pragma unroll
-          for (int q = 0; q < 8; ++q)
-            reinterpret_cast<float4*>(lrow)[(8 * h + q) ^ (i & 15)] =
-                make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-        }
       } else {
         tc::st_row_bf16x2_32(pimg, pimg + 2048, img_row(i), v, 4 * h);
       }
@@ -1127,7 +1135,6 @@ struct GradArgs {
   const float* g;           // [B*T, Hv] (dg = d log g / g); null in layer mode
   const float* gates;       // [chunks, Hv, 2, 64]
   const uint8_t *Pimg, *KQimg;  // the forward's operand images
-  const float* Lbuf;        // [chunks, Hv, 64, 64] strict-lower Gamma * K K^T
   const float* Ds;          // D (tf32-rounded), fp32 tiles [chunks, Hv, Dv / 32][64][32], rows swizzled
   const uint8_t* Aimg;      // [dO; F] operand images [chunks, Hv, Dv / 32] x 16 KB
   void *dq, *dk;            // [B*T, Hk, Dk]
@@ -1144,10 +1151,10 @@ constexpr int GR_KQ = 0;           // 32 KB bf16 [K; Q] image
 constexpr int GR_P = 32768;        // 16 KB bf16 [P_hi; P_lo] image of the value head
 constexpr int GR_BUF = 49152;      // 2 x 60 KB slice buffers: S, dS (tf32, MN-major [32 dv][128 dk], +0, +16 KB),
 constexpr int GR_BS = 61440;       //   the [dO; F] image (+32 KB), D (K-major [64][32], +48 KB), V rows (+56 KB)
-constexpr int GR_SMEM = 172032 + 1024;
-// the value head's finalize reuses the slice buffers: L (fp32 [64][64]), the [dP^; dKK] images, a
-// column-sum scratch
-constexpr int GR_L = GR_BUF, GR_FHI = GR_BUF + 16384, GR_FLO = GR_BUF + 32768, GR_SCR = GR_BUF + 49152;
+constexpr int GR_KO = 172032;      // 16 KB bf16 K rows alone (K-major): the B operand of K K^T
+constexpr int GR_SMEM = 188416 + 1024;
+// the value head's finalize reuses the slice buffers: the [dP^; dKK] images, a column-sum scratch
+constexpr int GR_FHI = GR_BUF + 16384, GR_FLO = GR_BUF + 32768, GR_SCR = GR_BUF + 49152;
 
 // 16 floats into chunks 4 half .. 4 half + 3 of row r of a K-major fp32 128-byte-swizzled slab.
 __device__ __forceinline__ void st_row_k_f32_16(uint8_t* slab, int r, const float (&v)[16], int half) {
@@ -1204,7 +1211,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
   __shared__ float srow[6][2][64];           // per-row partial sums from both column halves
   __shared__ float sdb[65], sred[16];
   __shared__ float snorm[2][2][128];
-  __shared__ uint64_t bar_kq, bar_h, bar_l, bar_s[2], bar_mma;
+  __shared__ uint64_t bar_kq, bar_h, bar_kk, bar_s[2], bar_mma;
   __shared__ uint32_t tmem_slot;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1218,13 +1225,14 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
   const bool lower = lane < 16;
   const bool rvalid = i_row < L;
 
-  // TMEM: dQ | dK 0 (128), dO S | F S 128 (128), D dS 256 (upper lanes, 128), dP | F D^T 384 (64)
-  const uint32_t cQK = 0, cA1 = 128, cA2 = 256, cPF = 384;
+  // TMEM: dQ | dK 0 (128), dO S | F S 128 (128), D dS 256 (upper lanes, 128), dP | F D^T 384 (64),
+  // K K^T 448 (64, lower lanes; the upper lanes get Q K^T, unused)
+  const uint32_t cQK = 0, cA1 = 128, cA2 = 256, cPF = 384, cKK = 448;
   if (warp == 0) tc::tmem_alloc(&tmem_slot, 512);
   if (tid == 0) {
     tc::mbar_init(&bar_kq, 1);
     tc::mbar_init(&bar_h, 1);
-    tc::mbar_init(&bar_l, 1);
+    tc::mbar_init(&bar_kk, 1);
     tc::mbar_init(&bar_s[0], 1);
     tc::mbar_init(&bar_s[1], 1);
     tc::mbar_init(&bar_mma, 1);
@@ -1271,6 +1279,27 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
   uint32_t ph_mma = 0;
   bool ok = wait_all(&bar_kq, 0, a.err, 30);
   const uint32_t kq = tc::smem_u32(smem + GR_KQ);
+  // K K^T (the same for every value head of the group): the image's K row groups (2 KB each) copied
+  // unchanged into a K-only tile (the swizzle is relative to 1 KB, so whole groups keep it), then
+  // [K; Q] K^T in eight MMAs; consumed by the finalizes
+  if (ok) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int o = (tid + 256 * u) * 16, sl = o >> 13, g = (o >> 11) & 3, rem = o & 2047;
+      *reinterpret_cast<uint4*>(smem + GR_KO + o) =
+          *reinterpret_cast<const uint4*>(smem + GR_KQ + sl * 16384 + g * 4096 + rem);
+    }
+  }
+  tc::fence_async_smem();
+  ok = __syncthreads_and(ok) != 0;
+  if (ok && tid == 0) {
+    tc::fence_after_sync();
+    const uint32_t ko = tc::smem_u32(smem + GR_KO), idK = tc::idesc(tc::kBF16, 128, 64, false, false);
+#pragma unroll
+    for (int ks = 0; ks < DK / 16; ++ks)
+      tc::mma_bf16(tmem + cKK, tc::desc_kmajor(kq, 128, ks), tc::desc_kmajor(ko, 64, ks), idK, ks > 0 ? 1u : 0u);
+    tc::mma_commit(&bar_kk);
+  }
   const uint32_t idC1 = tc::idesc(tc::kTF32, 128, 128, false, true);
   const uint32_t idC2 = tc::idesc(tc::kTF32, 64, 128, false, true);
   const uint32_t idC3 = tc::idesc(tc::kTF32, 128, 64, false, false);
@@ -1346,10 +1375,6 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
     if (!ok) break;
 
     // e. finalize this value head
-    if (tid == 32) {
-      tc::mbar_arrive_expect_tx(&bar_l, 16384);
-      tc::bulk_load(smem + GR_L, a.Lbuf + (size_t)(c * Hv + hv) * 4096, 16384, &bar_l);
-    }
     // e1. the row terms from the unscaled products, and their scaled sum into dQ (lower lanes) and dK
     //     (upper lanes), 64 columns per thread in two passes of 32
     {
@@ -1382,25 +1407,29 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
         srow[3][half][i_row] = tb;   // t4
       }
     }
-    ok = wait_all(&bar_l, (uint32_t)(r & 1), a.err, 35);
+    ok = wait_all(&bar_kk, 0u, a.err, 35);
     if (!ok) break;
+    tc::fence_after_sync();
     float* scratch = reinterpret_cast<float*>(smem + GR_SCR);  // [64][65], then 4 x 64 column partials
-    const float* Lm = reinterpret_cast<const float*>(smem + GR_L);
     float rsum = 0.f, dbl = 0.f;
     {
       // Lane l holds dP[i][32 half + 0..31], lane l + 16 holds F D^T there; one exchange leaves each
-      // lane both for 16 columns: j0 = 32 half (lower lane), 32 half + 16 (upper lane).
-      float v[32], dp[16], fd[16];
+      // lane both for 16 columns: j0 = 32 half (lower lane), 32 half + 16 (upper lane).  K K^T row i
+      // is in lane l alone; its second 16 columns go to lane l + 16.
+      float v[32], kk32[32], dp[16], fd[16], kk[16];
       tc::tmem_ld32(tl + cPF + 32 * half, v);
+      tc::tmem_ld32(tl + cKK + 32 * half, kk32);
 #pragma unroll
       for (int k = 0; k < 16; ++k) {
         const float x = __shfl_xor_sync(0xffffffffu, lower ? v[16 + k] : v[k], 16);
+        const float y = __shfl_xor_sync(0xffffffffu, kk32[16 + k], 16);
         dp[k] = lower ? v[k] : x;
         fd[k] = lower ? x : v[16 + k];
+        kk[k] = lower ? kk32[k] : y;
       }
       const int j0 = 32 * half + (lower ? 0 : 16);
-      // this row's P (hi + lo from the image) and Gamma * KK for the 16 columns, loaded up front
-      float pv[16], lv[16];
+      // this row's P (hi + lo from the image) for the 16 columns, loaded up front
+      float pv[16];
       {
         const int rr = img_row(i_row);
         const uint8_t* prow = smem + GR_P + rr * 128;
@@ -1418,11 +1447,6 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
             pv[8 * cc + 2 * e + 1] = __high2float(h2) + __high2float(l2);
           }
         }
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float4 x = reinterpret_cast<const float4*>(Lm + i_row * 64)[((j0 >> 2) + q) ^ (i_row & 15)];
-          lv[4 * q] = x.x, lv[4 * q + 1] = x.y, lv[4 * q + 2] = x.z, lv[4 * q + 3] = x.w;
-        }
       }
       float ph[16], kh[16], xs[16];
 #pragma unroll
@@ -1431,8 +1455,9 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
         const float gam = j <= i_row ? __expf(bi - sgt[j]) : 0.f;
         const float xp = j <= i_row ? dp[k] * pv[k] : 0.f;
         const float dl = j < i_row ? -fd[k] : 0.f;
-        const float xl = dl * be * lv[k];
-        dbl = fmaf(dl, lv[k], dbl);
+        const float lv = gam * kk[k];  // L_ij / beta_i = Gamma_ij (K K^T)_ij
+        const float xl = dl * be * lv;
+        dbl = fmaf(dl, lv, dbl);
         xs[k] = xp + xl;
         rsum += xs[k];
         ph[k] = dp[k] * gam;        // dP^
@@ -1696,10 +1721,10 @@ bool map_state_mn(CUtensorMap* m, const void* base, int64_t rows) {
 
 int64_t a256(int64_t x) { return (x + 255) & ~int64_t(255); }
 
-// The chunk intermediates: [ckpt][Gamma*KK][gates] fp32 and the forward's T, P and [K; Q] operand
-// images.
+// The chunk intermediates: [ckpt][gates] fp32, the forward's T, P and [K; Q] operand images and its
+// tf32-rounded D tiles.
 struct Saved {
-  float *ckpt, *L, *gates;
+  float *ckpt, *gates;
   uint8_t *Timg, *Pimg, *KQimg;
   float* Ds;
 };
@@ -1713,7 +1738,6 @@ int64_t saved_layout(int Hv, int Hk, int64_t n_chunks, char* base, Saved* s) {
   };
   Saved x;
   x.ckpt = (float*)take(n_chunks * Hv * (int64_t)DV * DK * 4);
-  x.L = (float*)take(n_chunks * Hv * 4096 * 4);
   x.gates = (float*)take(n_chunks * Hv * 128 * 4);
   x.Timg = (uint8_t*)take(n_chunks * Hv * 16384);
   x.Pimg = (uint8_t*)take(n_chunks * Hv * 16384);
@@ -1788,11 +1812,11 @@ cudaError_t chunked_fwd(const ChunkFwdArgs& a, void* ws, cudaStream_t st) {
   Ws w;
   ws_layout(a.Hv, a.Hk, a.N, a.n_chunks, layer, a.cu != nullptr, 0, false, (char*)ws, &w);
   Saved sv{};
-  float *gates = w.gates, *ckpt = nullptr, *Lb = nullptr;
+  float *gates = w.gates, *ckpt = nullptr;
   uint8_t *Ti = w.Timg, *Pi = w.Pimg, *KQi = w.KQimg;
   if (a.saved) {
     saved_layout(a.Hv, a.Hk, a.n_chunks, (char*)a.saved, &sv);
-    gates = sv.gates, ckpt = sv.ckpt, Lb = sv.L;
+    gates = sv.gates, ckpt = sv.ckpt;
     Ti = sv.Timg, Pi = sv.Pimg, KQi = sv.KQimg;
   }
   cudaError_t e;
@@ -1802,7 +1826,7 @@ cudaError_t chunked_fwd(const ChunkFwdArgs& a, void* ws, cudaStream_t st) {
   if (!map_act(&kmap, a.k, rows, a.Hk, a.Dk) || !map_act(&qmap, a.q, rows, a.Hk, a.Dk)) return cudaErrorInvalidValue;
   Geo geo{a.T, a.Hk, a.Hv, a.N, (a.T + C - 1) / C, a.cu, a.cu ? w.chunk_off : nullptr};
   if (a.n_chunks > 0) {
-    PrepArgs pa{geo, a.g, a.beta, a.a_raw, a.b_raw, a.A_log, a.dt_bias, Ti, Pi, KQi, Lb, gates, w.err};
+    PrepArgs pa{geo, a.g, a.beta, a.a_raw, a.b_raw, a.A_log, a.dt_bias, Ti, Pi, KQi, gates, w.err};
     const int prep_smem = 1024 + 32768;
     if ((e = cudaFuncSetAttribute(gdn_chunk_prep, cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem)) !=
         cudaSuccess)
@@ -1865,7 +1889,7 @@ cudaError_t chunked_bwd(const ChunkBwdArgs& a, void* ws, cudaStream_t st) {
   if (!map_state_mn(&smap_mn, sv.ckpt, a.n_chunks * a.Hv * (int64_t)DV) ||
       !map_state_mn(&dmap_mn, w.dsbuf, a.n_chunks * a.Hv * (int64_t)DV))
     return cudaErrorInvalidValue;
-  GradArgs ga{geo, a.g, sv.gates, sv.Pimg, sv.KQimg, sv.L, sv.Ds, w.Aimg, a.dq, a.dk, a.dg, a.dbeta, w.err,
+  GradArgs ga{geo, a.g, sv.gates, sv.Pimg, sv.KQimg, sv.Ds, w.Aimg, a.dq, a.dk, a.dg, a.dbeta, w.err,
               static_cast<const __nv_bfloat16*>(a.q), static_cast<const __nv_bfloat16*>(a.k),
               a.a_raw, a.b_raw, a.A_log, a.dt_bias, w.head_part};
   auto k2 = a.out_bf16 ? gdn_chunk_bwd_grad<__nv_bfloat16> : gdn_chunk_bwd_grad<float>;
