@@ -114,22 +114,6 @@ __device__ __forceinline__ void scan64(float x, float* out, float* tmp) {
   if (tid < 64) out[tid] = x;
 }
 
-// 32 bf16 activations of one row (zero if !valid) as floats.
-__device__ __forceinline__ void load_row32(const __nv_bfloat16* p, bool valid, float (&v)[32]) {
-  if (valid) {
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      float t8[8];
-      load_vec<8>(p + 8 * q, t8);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[8 * q + e] = t8[e];
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = 0.f;
-  }
-}
-
 template <typename Tout>
 __device__ __forceinline__ void store_row32(Tout* p, const float (&v)[32]);
 template <>
@@ -1144,6 +1128,8 @@ struct GradArgs {
   const __nv_bfloat16 *q_raw, *k_raw;
   const float *a_raw, *b_raw, *A_log, *dt_bias;
   float* head_part;         // [chunks, Hv, 2]
+  float *dA_log, *ddt_bias; // [Hv]: the sums over all chunks, written by the CTA that finishes last
+  unsigned* done;           // CTAs finished (zero when the kernel starts)
 };
 
 // Shared memory of the gradient kernel.
@@ -1152,9 +1138,20 @@ constexpr int GR_P = 32768;        // 16 KB bf16 [P_hi; P_lo] image of the value
 constexpr int GR_BUF = 49152;      // 2 x 60 KB slice buffers: S, dS (tf32, MN-major [32 dv][128 dk], +0, +16 KB),
 constexpr int GR_BS = 61440;       //   the [dO; F] image (+32 KB), D (K-major [64][32], +48 KB), V rows (+56 KB)
 constexpr int GR_KO = 172032;      // 16 KB bf16 K rows alone (K-major): the B operand of K K^T
-constexpr int GR_SMEM = 188416 + 1024;
-// the value head's finalize reuses the slice buffers: the [dP^; dKK] images, a column-sum scratch
-constexpr int GR_FHI = GR_BUF + 16384, GR_FLO = GR_BUF + 32768, GR_SCR = GR_BUF + 49152;
+constexpr int GR_RAW = 188416;     // 32 KB layer mode: the raw q (rows 0-63) and k (rows 64-127) rows, 256 B each
+constexpr int GR_SMEM = 221184 + 1024;
+// The value head's finalize reuses the second slice buffer (its last slice is an odd one): the
+// [dP^; dKK] images and a column-sum scratch; meanwhile the next value head's first slice arrives in
+// the first buffer.
+constexpr int GR_FHI = GR_BUF + GR_BS, GR_FLO = GR_BUF + GR_BS + 16384, GR_SCR = GR_BUF + GR_BS + 32768;
+static_assert((DV / DVT) % 2 == 0, "a value head's last slice must use the second buffer");
+static_assert(32768 + (64 * 65 + 4 * 64) * 4 <= GR_BS, "finalize scratch exceeds a slice buffer");
+
+// 16 bytes global -> shared by the non-bulk asynchronous copy; the issuing thread waits for its own.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(tc::smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // 16 floats into chunks 4 half .. 4 half + 3 of row r of a K-major fp32 128-byte-swizzled slab.
 __device__ __forceinline__ void st_row_k_f32_16(uint8_t* slab, int r, const float (&v)[16], int half) {
@@ -1207,12 +1204,13 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
                                                              const __grid_constant__ CUtensorMap vmap, GradArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ __align__(16) float sgt[128];   // the value head's gates: b[64], beta[64]
+  __shared__ __align__(16) float sgt[2][128];  // the value heads' gates: b[64], beta[64] (double-buffered)
   __shared__ float srow[6][2][64];           // per-row partial sums from both column halves
   __shared__ float sdb[65], sred[16];
   __shared__ float snorm[2][2][128];
   __shared__ uint64_t bar_kq, bar_h, bar_kk, bar_s[2], bar_mma;
   __shared__ uint32_t tmem_slot;
+  __shared__ int s_last;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quad = warp & 3, half = warp >> 2;
@@ -1244,6 +1242,15 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
   const uint32_t tmem = tmem_slot;
   const uint32_t tl = tc::taddr(tmem, 32 * quad, 0);
   constexpr int NSL = DV / DVT;
+  // layer mode: this thread's half row of raw q (lower lanes) or k (upper lanes) for the norm chain rule
+  // at the end, fetched now; 16-byte chunks swizzled by the row
+  const size_t rowoff = ((tok0 + i_row) * a.geo.Hk + hk) * (size_t)DK + 64 * half;
+  uint8_t* rawrow = smem + GR_RAW + ((lower ? 0 : 64) + i_row) * 256 + 128 * half;
+  if (!a.g && rvalid) {
+    const uint8_t* src = reinterpret_cast<const uint8_t*>((lower ? a.q_raw : a.k_raw) + rowoff);
+#pragma unroll
+    for (int cc = 0; cc < 8; ++cc) cp_async16(rawrow + ((cc ^ (i_row & 7)) << 4), src + 16 * cc);
+  }
 
   // slice q = r * NSL + sl of this CTA: S, dS slices, D and F tiles, dO and value rows, into buffer q & 1
   auto issue_slice = [&](int q) {
@@ -1265,7 +1272,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
     const int hv = hk * ratio + r;
     tc::mbar_arrive_expect_tx(&bar_h, 16384 + 512);
     tc::bulk_load(smem + GR_P, a.Pimg + (size_t)(c * Hv + hv) * 16384, 16384, &bar_h);
-    tc::bulk_load(sgt, a.gates + (c * Hv + hv) * 128, 512, &bar_h);
+    tc::bulk_load(sgt[r & 1], a.gates + (c * Hv + hv) * 128, 512, &bar_h);
   };
   if (tid == 32) {
     tc::prefetch_tmap(&smap_mn);
@@ -1310,7 +1317,8 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
     const int hv = hk * ratio + r;
     ok = wait_all(&bar_h, (uint32_t)(r & 1), a.err, 31);
     if (!ok) break;
-    const float bi = sgt[i_row], be = sgt[64 + i_row], gi = __expf(bi), bC = sgt[63], lam = __expf(bC - bi);
+    const float* sg = sgt[r & 1];
+    const float bi = sg[i_row], be = sg[64 + i_row], gi = __expf(bi), bC = sg[63], lam = __expf(bC - bi);
     float t5 = 0.f;   // sum of S (.) dS over this thread's elements
     float fv = 0.f;   // lower lanes: F_i . V_i over this thread's value rows
     // the finalize's per-row inputs of the gate chain rule, loaded now (consumed at the end of the head)
@@ -1332,7 +1340,9 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
       uint8_t* buf = smem + GR_BUF + bs * GR_BS;
       ok = wait_all(&bar_s[bs], (uint32_t)((q >> 1) & 1), a.err, 37);
       if (!ok) break;
-      if (tid == 32 && sl + 1 < NSL) issue_slice(q + 1);  // the other buffer's last reader has finished
+      // the other buffer's last reader has finished (the finalize uses the second buffer, so the next
+      // value head's first slice goes out during this head's last slice)
+      if (tid == 32 && q + 1 < ratio * NSL) issue_slice(q + 1);
       // a. over the slice's value rows (tf32, K = 32; every operand arrives in its final form): [dO; F] S,
       //    D dS (M = 64 in the upper lanes), [dO; F] D^T -- issued at once
       if (tid == 0) {
@@ -1452,7 +1462,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
 #pragma unroll
       for (int k = 0; k < 16; ++k) {
         const int j = j0 + k;
-        const float gam = j <= i_row ? __expf(bi - sgt[j]) : 0.f;
+        const float gam = j <= i_row ? __expf(bi - sg[j]) : 0.f;
         const float xp = j <= i_row ? dp[k] * pv[k] : 0.f;
         const float dl = j < i_row ? -fd[k] : 0.f;
         const float lv = gam * kk[k];  // L_ij / beta_i = Gamma_ij (K K^T)_ij
@@ -1487,6 +1497,8 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
+    // the P image has been read: the next value head's P and gates (into the other gate buffer)
+    if (tid == 32 && r + 1 < ratio) issue_head(r + 1);
     if (tid == 0) {
       // dQ | dK += [dP^; dKK] K (hi then lo);  dK += dP^^T Q + dKK^T K  (M = 64, upper lanes)
       const uint32_t fhi = tc::smem_u32(smem + GR_FHI), flo = tc::smem_u32(smem + GR_FLO);
@@ -1519,7 +1531,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
       const int i = tid;
       const float* cp = scratch + 64 * 65;
       const float csum = (cp[i] + cp[64 + i]) + (cp[128 + i] + cp[192 + i]);
-      const float bi_ = sgt[i], be_ = sgt[64 + i], gi_ = __expf(bi_), lam_ = __expf(bC - bi_);
+      const float bi_ = sg[i], be_ = sg[64 + i], gi_ = __expf(bi_), lam_ = __expf(bC - bi_);
       const float t3_ = srow[0][0][i] + srow[0][1][i];
       const float t2_ = srow[2][0][i] + srow[2][1][i];
       const float t4_ = srow[3][0][i] + srow[3][1][i];
@@ -1554,7 +1566,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
       const float dl = sdb[1 + i] + (i < 32 ? sdb[0] : 0.f);  // d log g_i
       const int64_t gi_idx = (tok0 + i) * Hv + hv;
       // d beta = F . (V - gamma R) + the L terms;  F . R = K . (F S) = t2
-      const float gi_ = __expf(sgt[i]);
+      const float gi_ = __expf(sg[i]);
       const float t1_ = (srow[1][0][i] + srow[1][1][i]) - gi_ * (srow[2][0][i] + srow[2][1][i]);
       const float dbe = t1_ + srow[5][0][i] + srow[5][1][i];
       if (a.g) {
@@ -1588,29 +1600,35 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
         a.head_part[(c * Hv + hv) * 2 + 1] = sred[14] + sred[15];
       }
     }
+    tc::fence_async_smem();  // the scratch writes before the next TMA into this buffer
     ok = wait_all(&bar_mma, ph_mma, a.err, 36);
     ph_mma ^= 1;
     tc::fence_after_sync();
-    // the next value head's tiles (the finalize's buffers and the P image are free now)
-    if (ok && r + 1 < ratio && tid == 32) {
-      issue_head(r + 1);
-      issue_slice((r + 1) * NSL);
-    }
   }
   // f. dq (lower lanes) and dk (upper lanes) rows of this key head, 64 columns per thread (layer mode:
   //    through the norms to the raw q, k)
+  if (!a.g) cp_async_wait_all();
   if (ok) {
-    const size_t rowoff = ((tok0 + i_row) * a.geo.Hk + hk) * (size_t)DK + 64 * half;
     Tout* out = static_cast<Tout*>(lower ? a.dq : a.dk) + rowoff;
     float v0[32], v1[32];
     tc::tmem_ld32(tl + cQK + 64 * half, v0);
     tc::tmem_ld32(tl + cQK + 64 * half + 32, v1);
     if (!a.g) {
       // x^ = s bf16(x r), r = rsqrt(mean(x^2) + eps):  dx = s r (dx^ - r^2 (x . dx^) x / Dk)
-      const __nv_bfloat16* xr = (lower ? a.q_raw : a.k_raw) + rowoff;
       float x0[32], x1[32];
-      load_row32(xr, rvalid, x0);
-      load_row32(xr + 32, rvalid, x1);
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc) {
+        uint4 w = make_uint4(0, 0, 0, 0);
+        if (rvalid) w = *reinterpret_cast<const uint4*>(rawrow + ((cc ^ (i_row & 7)) << 4));
+        const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+        float* xd = cc < 4 ? x0 + 8 * cc : x1 + 8 * (cc - 4);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&u[e]);
+          xd[2 * e] = __low2float(h);
+          xd[2 * e + 1] = __high2float(h);
+        }
+      }
       float ss = 0.f, dot = 0.f;
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
@@ -1640,18 +1658,32 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
   tc::fence_before_sync();
   __syncthreads();
   if (warp == 0) tc::tmem_dealloc(tmem, 512);
-}
-
-// dA_log[h], ddt_bias[h] = the per-chunk sums over all chunks, in chunk order (deterministic).
-__global__ void gdn_chunk_head_finish(int64_t n_chunks, int Hv, const float* part, float* dA_log, float* ddt_bias) {
-  for (int h = threadIdx.x; h < Hv; h += blockDim.x) {
-    float sa = 0.f, sd = 0.f;
-    for (int64_t c = 0; c < n_chunks; ++c) {
-      sa += part[(c * Hv + h) * 2];
-      sd += part[(c * Hv + h) * 2 + 1];
+  if (!a.g) {
+    // layer mode: the CTA that finishes last sums every chunk's head terms, in chunk order (the same
+    // result whichever CTA it is):  dA_log[h], ddt_bias[h] = sum over chunks of head_part[c][h][0 | 1]
+    if (tid == 0) {
+      __threadfence();
+      s_last = atomicAdd(a.done, 1u) == gridDim.x * gridDim.y - 1;
     }
-    dA_log[h] = sa;
-    ddt_bias[h] = sd;
+    __syncthreads();
+    if (s_last) {
+      __threadfence();
+      const int64_t nc = gridDim.x;
+      for (int j = tid; j < 2 * Hv; j += blockDim.x) {
+        const float* p = a.head_part + j;  // head j >> 1, term j & 1
+        float s = 0.f;
+        int64_t cc = 0;
+        for (; cc + 8 <= nc; cc += 8) {
+          float x[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) x[e] = __ldcg(p + (cc + e) * Hv * 2);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) s += x[e];
+        }
+        for (; cc < nc; ++cc) s += __ldcg(p + cc * Hv * 2);
+        ((j & 1) ? a.ddt_bias : a.dA_log)[j >> 1] = s;
+      }
+    }
   }
 }
 
@@ -1752,7 +1784,7 @@ int64_t saved_layout(int Hv, int Hk, int64_t n_chunks, char* base, Saved* s) {
 // recomputes].
 struct Ws {
   int64_t* chunk_off;
-  int* err;
+  int* err;          // 4 words, zeroed by each call: [0] the error code, [2] the gradient kernel's CTA count
   uint8_t *Timg, *Pimg, *KQimg;
   float* gates;
   float* dsbuf;
@@ -1891,18 +1923,13 @@ cudaError_t chunked_bwd(const ChunkBwdArgs& a, void* ws, cudaStream_t st) {
     return cudaErrorInvalidValue;
   GradArgs ga{geo, a.g, sv.gates, sv.Pimg, sv.KQimg, sv.Ds, w.Aimg, a.dq, a.dk, a.dg, a.dbeta, w.err,
               static_cast<const __nv_bfloat16*>(a.q), static_cast<const __nv_bfloat16*>(a.k),
-              a.a_raw, a.b_raw, a.A_log, a.dt_bias, w.head_part};
+              a.a_raw, a.b_raw, a.A_log, a.dt_bias, w.head_part, a.dA_log, a.ddt_bias,
+              reinterpret_cast<unsigned*>(w.err + 2)};
   auto k2 = a.out_bf16 ? gdn_chunk_bwd_grad<__nv_bfloat16> : gdn_chunk_bwd_grad<float>;
   if ((e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, GR_SMEM)) != cudaSuccess) return e;
   k2<<<dim3((unsigned)a.n_chunks, a.Hk), 256, GR_SMEM, st>>>(smap_mn, dmap_mn, vmap, ga);
   note_launch();
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  if (layer) {
-    gdn_chunk_head_finish<<<1, 128, 0, st>>>(a.n_chunks, a.Hv, w.head_part, a.dA_log, a.ddt_bias);
-    note_launch();
-    e = cudaGetLastError();
-  }
-  return e;
+  return cudaGetLastError();
 }
 
 }  // namespace qbgdn
