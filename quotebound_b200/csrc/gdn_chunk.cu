@@ -199,6 +199,7 @@ __global__ void __launch_bounds__(128, 4) gdn_chunk_prep(const __grid_constant__
   uint8_t* ktile = smem;                                   // 16 KB bf16
   uint8_t* qtile = smem + 16384;                           // 16 KB bf16
   __shared__ float sb[64], sbeta[64], stmp[2];
+  __shared__ __align__(16) float sX[2][16][16];  // the inverse's 16 x 16 intermediate products
   __shared__ uint64_t bar_tma, bar_mma;
   __shared__ uint32_t tmem_slot;
   constexpr int LS = 64;
@@ -360,23 +361,24 @@ __global__ void __launch_bounds__(128, 4) gdn_chunk_prep(const __grid_constant__
   }
   tc::fence_before_sync();
   __syncthreads();
-  // T = (I + L)^-1 in 2 x 2 blocks of 32: T00 = (I + L00)^-1 and T11 = (I + L11)^-1 by column sweep
-  // (thread (b, c) < 64 owns column c of block b in registers: t_j is final once the columns before it
-  // have been swept, and sweeping column j updates the rows below it independently), then
-  // T10 = -T11 (L10 T00) as two 32 x 32 products over all 128 threads.  Tt[col * 64 + row] holds T
-  // transposed (in the K tile, free now).
+  // T = (I + L)^-1 in 2 x 2 blocks of 32, each 32 x 32 diagonal block itself in 2 x 2 blocks of 16:
+  // the four 16 x 16 diagonal blocks A_b = (I + L_bb)^-1 by column sweep (thread (b, c) < 64 owns column
+  // c of A_b in registers: t_j is final once the columns before it have been swept, and sweeping column
+  // j updates the rows below it independently), then C = -A_(2m+1) (L_(2m+1, 2m) A_2m) completes the
+  // 32 x 32 block T_mm, then T10 = -T11 (L10 T00) as two 32 x 32 products over all 128 threads.
+  // Tt[col * 64 + row] holds T transposed (in the K tile, free now).
   float* Tt = reinterpret_cast<float*>(ktile);
   if (ok && tid < 64) {
-    const int b = tid >> 5, cc = tid & 31;
-    float t[32];
+    const int b = tid >> 4, cc = tid & 15;
+    float t[16];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) t[i] = i == cc ? 1.f : 0.f;
+    for (int i = 0; i < 16; ++i) t[i] = i == cc ? 1.f : 0.f;
 #pragma unroll
-    for (int j = 0; j < 31; ++j) {
+    for (int j = 0; j < 15; ++j) {
       const float tj = t[j];
-      const float* Lj = Lt + (32 * b + j) * LS + 32 * b;
+      const float* Lj = Lt + (16 * b + j) * LS + 16 * b;
 #pragma unroll
-      for (int i4 = (j + 1) & ~3; i4 < 32; i4 += 4) {
+      for (int i4 = (j + 1) & ~3; i4 < 16; i4 += 4) {
         const float4 l4 = *reinterpret_cast<const float4*>(Lj + i4);
         if (i4 + 0 > j) t[i4 + 0] = fmaf(-l4.x, tj, t[i4 + 0]);
         if (i4 + 1 > j) t[i4 + 1] = fmaf(-l4.y, tj, t[i4 + 1]);
@@ -384,17 +386,53 @@ __global__ void __launch_bounds__(128, 4) gdn_chunk_prep(const __grid_constant__
         t[i4 + 3] = fmaf(-l4.w, tj, t[i4 + 3]);
       }
     }
-    float4* dst = reinterpret_cast<float4*>(Tt + (32 * b + cc) * 64 + 32 * b);
+    // column 16 b + cc: rows 16 b .. + 15 are A_b's column; for odd b the rows 16 (b - 1) .. + 15 above
+    // it in the same 32 x 32 block are zero, and for b >= 2 so are rows 0 .. 31 (T01 = 0)
+    float* col = Tt + (16 * b + cc) * 64;
 #pragma unroll
-    for (int q = 0; q < 8; ++q) dst[q] = make_float4(t[4 * q], t[4 * q + 1], t[4 * q + 2], t[4 * q + 3]);
-    if (b == 1) {  // T01 = 0 (the columns of block 1 above the diagonal block)
-      float4* z = reinterpret_cast<float4*>(Tt + (32 + cc) * 64);
+    for (int q = 0; q < 4; ++q)
+      reinterpret_cast<float4*>(col + 16 * b)[q] = make_float4(t[4 * q], t[4 * q + 1], t[4 * q + 2], t[4 * q + 3]);
+    if (b & 1) {
 #pragma unroll
-      for (int q = 0; q < 8; ++q) z[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int q = 0; q < 4; ++q) reinterpret_cast<float4*>(col + 16 * (b - 1))[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (b >= 2) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) reinterpret_cast<float4*>(col)[q] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     float* gd = a.gates + (c * a.geo.Hv + hv) * 128;
     gd[tid] = sb[tid];
     gd[64 + tid] = sbeta[tid];
+  }
+  __syncthreads();
+  {
+    // thread (m, r, cg): row r of the 16 x 16 off-diagonal block of T_mm, columns 4 cg .. 4 cg + 3
+    const int m = tid >> 6, r = tid & 15, cg = (tid >> 4) & 3, o = 32 * m;
+    float x[4] = {0.f, 0.f, 0.f, 0.f};
+    if (ok) {  // X' = L_(2m+1, 2m) A_2m  (A_2m[k][c] = 0 for k < c)
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const float l = Lt[(o + k) * LS + o + 16 + r];  // L[o + 16 + r][o + k]
+#pragma unroll
+        for (int e = 0; e < 4; ++e) x[e] = fmaf(l, Tt[(o + 4 * cg + e) * 64 + o + k], x[e]);
+      }
+      reinterpret_cast<float4*>(sX[m][r])[cg] = make_float4(x[0], x[1], x[2], x[3]);
+    }
+    __syncthreads();
+    if (ok) {  // C = -A_(2m+1) X'  (A_(2m+1)[r][k] = 0 for k > r)
+      float y[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const float ak = Tt[(o + 16 + k) * 64 + o + 16 + r];
+        const float4 xk = reinterpret_cast<const float4*>(sX[m][k])[cg];
+        y[0] = fmaf(-ak, xk.x, y[0]);
+        y[1] = fmaf(-ak, xk.y, y[1]);
+        y[2] = fmaf(-ak, xk.z, y[2]);
+        y[3] = fmaf(-ak, xk.w, y[3]);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) Tt[(o + 4 * cg + e) * 64 + o + 16 + r] = y[e];
+    }
   }
   __syncthreads();
   float* Xs = Lm;  // X = L10 T00 [32][32], where L was (once the products have read it)
