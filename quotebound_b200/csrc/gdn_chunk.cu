@@ -752,23 +752,27 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
     tc::fence_after_sync();
     if (!ok) break;
     {
+      // both lanes of the pair hold row i of D; one instruction stream for both: the K-side lane writes
+      // D as the [hi | lo] operand of P D and columns 0-7 of the tf32 copy, the Q-side lane
+      // D~ = diag(lambda) D for the state update and columns 8-15 of the copy
       float d[16];
       tmem_ld_hl16_pair(tl + cD, half, d);
-      if (kside) {
-        tc::st_row_hilo16(smem + FW_D, i_row, d, half);
-      } else {
-        // (the other staging buffer's store was read before the last chunk's final barrier)
-        if (a.Ds) {  // tf32-rounded: the gradient kernel's tf32 operand, loaded as is
-          float dr[16];
+      // (the other staging buffer's store was read before the last chunk's final barrier)
+      if (a.Ds) {  // tf32-rounded: the gradient kernel's tf32 operand, loaded as is
+        uint8_t* row = smem + FW_DS + buf * 8192 + i_row * 128;
+        const int q0 = 4 * half + (kside ? 0 : 2);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) dr[j] = tf32_rna(d[j]);
-          st16_f32_sw(smem + FW_DS + buf * 8192, i_row, half, dr);
+        for (int q = 0; q < 2; ++q) {
+          float x[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) x[e] = tf32_rna(kside ? d[4 * q + e] : d[8 + 4 * q + e]);
+          *reinterpret_cast<float4*>(row + (((q0 + q) ^ (i_row & 7)) << 4)) = make_float4(x[0], x[1], x[2], x[3]);
         }
-        const float lam = __expf(bC - bi);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) d[j] *= lam;
-        tc::st_row_hilo16(smem + FW_DT, i_row, d, half);
       }
+      const float sc = kside ? 1.f : __expf(bC - bi);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) d[j] *= sc;
+      tc::st_row_hilo16(smem + (kside ? FW_D : FW_DT), i_row, d, half);
     }
     if (tid == 32) tc::bulk_wait_read();  // the staging buffers are rewritten below and next chunk
     tc::fence_async_smem();
@@ -884,6 +888,40 @@ __device__ __forceinline__ void ld16_bf16(const uint8_t* p, bool valid, float (&
   cvt_row16(r, v);
 }
 
+// 8 floats as the bf16 [hi | lo] pair of a 128-byte-swizzled operand row r: hi into chunk hc, lo into
+// chunk hc + 4 (columns 8 (hc & 3) .. + 7 of each 32-wide half).
+__device__ __forceinline__ void st_hilo8(uint8_t* tile, int r, const float (&v)[8], int hc) {
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const __nv_bfloat162 hh = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+    h[e] = *reinterpret_cast<const uint32_t*>(&hh);
+    l[e] = tc::pack_bf16(v[2 * e] - __low2float(hh), v[2 * e + 1] - __high2float(hh));
+  }
+  uint8_t* row = tile + r * 128;
+  *reinterpret_cast<uint4*>(row + ((hc ^ (r & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
+  *reinterpret_cast<uint4*>(row + (((hc + 4) ^ (r & 7)) << 4)) = make_uint4(l[0], l[1], l[2], l[3]);
+}
+// 8 floats into 16-byte chunks q0, q0 + 1 of row r of a 128-byte-row fp32 tile swizzled by r & 7.
+__device__ __forceinline__ void st8_f32_sw(uint8_t* tile, int r, int q0, const float (&v)[8]) {
+#pragma unroll
+  for (int q = 0; q < 2; ++q)
+    *reinterpret_cast<float4*>(tile + r * 128 + (((q0 + q) ^ (r & 7)) << 4)) =
+        make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+}
+template <typename Tout>
+__device__ __forceinline__ void store_row8(Tout* p, const float (&v)[8]);
+template <>
+__device__ __forceinline__ void store_row8<__nv_bfloat16>(__nv_bfloat16* p, const float (&v)[8]) {
+  *reinterpret_cast<uint4*>(p) = make_uint4(tc::pack_bf16(v[0], v[1]), tc::pack_bf16(v[2], v[3]),
+                                            tc::pack_bf16(v[4], v[5]), tc::pack_bf16(v[6], v[7]));
+}
+template <>
+__device__ __forceinline__ void store_row8<float>(float* p, const float (&v)[8]) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+
 // The backward state walk: chunks in reverse, 32 rows of dS per CTA, 256 threads as in the forward walk
 // (thread t holds dS[dv0 + 16 (w >> 2) + j][t & 127]).  Besides dv, the per-chunk dS and dh0 it leaves
 // the gradient kernel F = T^T dD.
@@ -983,29 +1021,29 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
     if (!ok) break;
     const float* gb = sg[buf];
     const float bi = gb[i_row], be = gb[64 + i_row], gi = __expf(bi), bC = gb[63];
-    // 2. dO row i (zero past the end): as the plain bf16 operand of P^T dO (K side) and as gamma dO
-    //    [hi | lo] (Q side)
+    // 2. dO row i (zero past the end) as the plain bf16 operand of P^T dO, as gamma dO [hi | lo] and, exact
+    //    in tf32, into the gradient kernel's image (lower row of the pair; the other staging buffer's
+    //    store was read before the last chunk's step-4 barrier).  One instruction stream for the lane
+    //    pair: the K-side lane takes columns 0-7 of the thread's 16, the Q-side lane columns 8-15.
     {
-      const uint4* vp = reinterpret_cast<const uint4*>(smem + BW_V + buf * 4096 + i_row * 64 + 32 * half);
-      const uint4 w0 = i_row < L ? vp[0] : make_uint4(0, 0, 0, 0);
-      const uint4 w1 = i_row < L ? vp[1] : make_uint4(0, 0, 0, 0);
-      if (kside) {
-        uint8_t* row = smem + BW_DO + i_row * 128;
-        *reinterpret_cast<uint4*>(row + (((2 * half) ^ (i_row & 7)) << 4)) = w0;
-        *reinterpret_cast<uint4*>(row + (((2 * half + 1) ^ (i_row & 7)) << 4)) = w1;
-      } else {
-        Row16 raw;
-        raw.w[0] = w0;
-        raw.w[1] = w1;
-        float d[16];
-        cvt_row16(raw, d);
-        // dO (exact in tf32) into the gradient kernel's image, lower row of the pair (the other staging
-        // buffer's store was read before the last chunk's step-4 barrier)
-        st16_f32_sw(smem + BW_FS + buf * 16384, img_row(i_row), half, d);
+      const int hc = kside ? 0 : 1;
+      const uint4 w = i_row < L ? reinterpret_cast<const uint4*>(smem + BW_V + buf * 4096 + i_row * 64 + 32 * half)[hc]
+                                : make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(smem + BW_DO + i_row * 128 + (((2 * half + hc) ^ (i_row & 7)) << 4)) = w;
+      float d[8];
+      {
+        const uint32_t u[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-        for (int j = 0; j < 16; ++j) d[j] *= gi;
-        tc::st_row_hilo16(smem + BW_GD, i_row, d, half);
+        for (int e = 0; e < 4; ++e) {
+          const __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&u[e]);
+          d[2 * e] = __low2float(h2);
+          d[2 * e + 1] = __high2float(h2);
+        }
       }
+      st8_f32_sw(smem + BW_FS + buf * 16384, img_row(i_row), 4 * half + 2 * hc, d);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) d[j] *= gi;
+      st_hilo8(smem + BW_GD, i_row, d, 2 * half + hc);
     }
     tc::fence_async_smem();
     tc::fence_before_sync();
@@ -1056,12 +1094,17 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
           g[j] = __uint_as_float(b0[j]);
         }
       }
-      if (kside) {
-        const float lam = __expf(bC - bi);
+      // the K-side lane forms dD; the Q-side lane takes its columns 8-15 and stores them
+      const float lam = __expf(bC - bi);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) x[j] = fmaf(lam, x[j], g[j]);
-        tc::st_row_hilo16(smem + BW_DD, i_row, x, half);
+      for (int j = 0; j < 16; ++j) x[j] = fmaf(lam, x[j], g[j]);
+      float d8[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float y = __shfl_xor_sync(0xffffffffu, x[8 + j], 16);
+        d8[j] = kside ? x[j] : y;
       }
+      st_hilo8(smem + BW_DD, i_row, d8, 2 * half + (kside ? 0 : 1));
     }
     if (tid == 32) tc::bulk_wait_read();  // the staging buffer is rewritten next chunk
     tc::fence_async_smem();
@@ -1086,25 +1129,32 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
     {
       float f[16];
       tmem_ld_hl16(tl + cF, half, f);
-      if (kside) {
-        {  // F, tf32-rounded, into the image's upper row of the pair
-          float fr[16];
+      // F's row i is in the K-side lane; the Q-side lane takes its columns 8-15, and both lanes write
+      // their 8 columns of the three outputs with one instruction stream
+      const int hc = kside ? 0 : 1;
+      float f8[8];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) fr[j] = tf32_rna(f[j]);
-          st16_f32_sw(smem + BW_FS + buf * 16384, img_row(i_row) + 16, half, fr);
-        }
-        float o[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) o[j] = be * f[j];
-        if (L == C)  // a full chunk goes out by one TMA store after the barrier below
-          store_row16<Tout>(reinterpret_cast<Tout*>(smem + BW_DV) + i_row * DVT + 16 * half, o);
-        else if (i_row < L)  // the rows after a sequence's end belong to the next sequence: not written
-          store_row16<Tout>(static_cast<Tout*>(a.dv) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0 + 16 * half, o);
-        const float h = -be * gi;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) o[j] = h * f[j];
-        tc::st_row_hilo16(smem + BW_H, i_row, o, half);
+      for (int j = 0; j < 8; ++j) {
+        const float y = __shfl_xor_sync(0xffffffffu, f[8 + j], 16);
+        f8[j] = kside ? f[j] : y;
       }
+      {  // F, tf32-rounded, into the image's upper row of the pair
+        float fr[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) fr[j] = tf32_rna(f8[j]);
+        st8_f32_sw(smem + BW_FS + buf * 16384, img_row(i_row) + 16, 4 * half + 2 * hc, fr);
+      }
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = be * f8[j];
+      if (L == C)  // a full chunk goes out by one TMA store after the barrier below
+        store_row8<Tout>(reinterpret_cast<Tout*>(smem + BW_DV) + i_row * DVT + 16 * half + 8 * hc, o);
+      else if (i_row < L)  // the rows after a sequence's end belong to the next sequence: not written
+        store_row8<Tout>(static_cast<Tout*>(a.dv) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0 + 16 * half + 8 * hc, o);
+      const float h = -be * gi;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = h * f8[j];
+      st_hilo8(smem + BW_H, i_row, o, 2 * half + hc);
     }
     tc::fence_async_smem();
     tc::fence_before_sync();
