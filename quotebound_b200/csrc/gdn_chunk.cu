@@ -351,11 +351,31 @@ __global__ void __launch_bounds__(128, 4) gdn_chunk_prep(const __grid_constant__
         const float gam = __expf(bi - sb[j]);  // Gamma_ij (only j <= i is used)
         v[jj] = (kkside ? j < i : j <= i) ? gam * v[jj] : 0.f;
       }
-      if (kkside) {
+      // one instruction stream for the lane pair: the K K^T lane writes columns 0-15 of L and of P, the
+      // Q K^T lane columns 16-31 of both (each sends the other the half it does not write)
+      float x[16];
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) Lt[(32 * h + jj) * LS + i] = be * v[jj];
-      } else {
-        tc::st_row_bf16x2_32(pimg, pimg + 2048, img_row(i), v, 4 * h);
+      for (int jj = 0; jj < 16; ++jj) x[jj] = __shfl_xor_sync(0xffffffffu, kkside ? v[16 + jj] : v[jj], 16);
+      const int c0 = kkside ? 0 : 16;
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) Lt[(32 * h + c0 + jj) * LS + i] = be * (kkside ? v[jj] : x[jj]);
+      {
+        const int r = img_row(i);
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          uint32_t hw[4], lw[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int jj = 8 * cc + 2 * e;
+            const float p0 = kkside ? x[jj] : v[16 + jj], p1 = kkside ? x[jj + 1] : v[17 + jj];
+            const __nv_bfloat162 hh = __floats2bfloat162_rn(p0, p1);
+            hw[e] = *reinterpret_cast<const uint32_t*>(&hh);
+            lw[e] = tc::pack_bf16(p0 - __low2float(hh), p1 - __high2float(hh));
+          }
+          const int off = r * 128 + (((4 * h + (kkside ? 0 : 2) + cc) ^ (r & 7)) << 4);
+          *reinterpret_cast<uint4*>(pimg + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          *reinterpret_cast<uint4*>(pimg + 2048 + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
       }
     }
   }
@@ -498,6 +518,40 @@ __global__ void __launch_bounds__(128, 4) gdn_chunk_prep(const __grid_constant__
 }
 
 // ------------------------------------------------------------------------------------------------
+// 8 floats as the bf16 [hi | lo] pair of a 128-byte-swizzled operand row r: hi into chunk hc, lo into
+// chunk hc + 4 (columns 8 (hc & 3) .. + 7 of each 32-wide half).
+__device__ __forceinline__ void st_hilo8(uint8_t* tile, int r, const float (&v)[8], int hc) {
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const __nv_bfloat162 hh = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+    h[e] = *reinterpret_cast<const uint32_t*>(&hh);
+    l[e] = tc::pack_bf16(v[2 * e] - __low2float(hh), v[2 * e + 1] - __high2float(hh));
+  }
+  uint8_t* row = tile + r * 128;
+  *reinterpret_cast<uint4*>(row + ((hc ^ (r & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
+  *reinterpret_cast<uint4*>(row + (((hc + 4) ^ (r & 7)) << 4)) = make_uint4(l[0], l[1], l[2], l[3]);
+}
+// 8 floats into 16-byte chunks q0, q0 + 1 of row r of a 128-byte-row fp32 tile swizzled by r & 7.
+__device__ __forceinline__ void st8_f32_sw(uint8_t* tile, int r, int q0, const float (&v)[8]) {
+#pragma unroll
+  for (int q = 0; q < 2; ++q)
+    *reinterpret_cast<float4*>(tile + r * 128 + (((q0 + q) ^ (r & 7)) << 4)) =
+        make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+}
+template <typename Tout>
+__device__ __forceinline__ void store_row8(Tout* p, const float (&v)[8]);
+template <>
+__device__ __forceinline__ void store_row8<__nv_bfloat16>(__nv_bfloat16* p, const float (&v)[8]) {
+  *reinterpret_cast<uint4*>(p) = make_uint4(tc::pack_bf16(v[0], v[1]), tc::pack_bf16(v[2], v[3]),
+                                            tc::pack_bf16(v[4], v[5]), tc::pack_bf16(v[6], v[7]));
+}
+template <>
+__device__ __forceinline__ void store_row8<float>(float* p, const float (&v)[8]) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+
 // The forward state walk.  One CTA per (32 value rows, value head, sequence); thread t holds column t
 // of the 32 state rows (S^T[t][0..31]) in registers.
 struct StateArgs {
@@ -726,16 +780,18 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
     float yp[16];
     const size_t ptile = ((size_t)(cg * Hv + hv) * (DV / DVT) + blockIdx.x) * 2048;  // this CTA's tile
     {
+      // one instruction stream for the lane pair: the K-side lane forms E's columns 0-7 from its K S^T
+      // row, the Q-side lane columns 8-15 from the K-side lane's; the Q-side lane keeps gamma Q S^T
       tmem_ld_hl16(tl + cA, half, yp);
-      if (kside) {
-        float e[16];
+      float e8[8];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) e[j] = be * (vr[j] - gi * yp[j]);
-        tc::st_row_hilo16(smem + FW_E, i_row, e, half);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) yp[j] *= gi;
+      for (int j = 0; j < 8; ++j) {
+        const float ks = __shfl_xor_sync(0xffffffffu, yp[8 + j], 16);
+        e8[j] = be * ((kside ? vr[j] : vr[8 + j]) - gi * (kside ? yp[j] : ks));
       }
+      st_hilo8(smem + FW_E, i_row, e8, 2 * half + (kside ? 0 : 1));
+#pragma unroll
+      for (int j = 0; j < 16; ++j) yp[j] *= gi;
     }
     tc::fence_async_smem();
     tc::fence_before_sync();
@@ -801,14 +857,19 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
       for (int j = 0; j < 16; ++j) s[j] = fmaf(gC, s[j], u[j]);
 #pragma unroll
       for (int j = 0; j < 16; ++j) u[j] = o2[j] + __shfl_xor_sync(0xffffffffu, o2[j], 16);
-      if (!kside) {
+      // both lanes hold P D's row; the K-side lane writes columns 0-7 (with the Q-side lane's gamma Q S^T),
+      // the Q-side lane columns 8-15
+      const int hc = kside ? 0 : 1;
+      float y8[8];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) u[j] += yp[j];
-        if (L == C)  // a full chunk goes out by one TMA store after the next barrier
-          store_row16<Tout>(reinterpret_cast<Tout*>(smem + FW_Y) + i_row * DVT + 16 * half, u);
-        else if (i_row < L)  // the rows after a sequence's end belong to the next sequence: not written
-          store_row16<Tout>(static_cast<Tout*>(a.y) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0 + 16 * half, u);
+      for (int j = 0; j < 8; ++j) {
+        const float qy = __shfl_xor_sync(0xffffffffu, yp[j], 16);
+        y8[j] = kside ? u[j] + qy : u[8 + j] + yp[8 + j];
       }
+      if (L == C)  // a full chunk goes out by one TMA store after the next barrier
+        store_row8<Tout>(reinterpret_cast<Tout*>(smem + FW_Y) + i_row * DVT + 16 * half + 8 * hc, y8);
+      else if (i_row < L)  // the rows after a sequence's end belong to the next sequence: not written
+        store_row8<Tout>(static_cast<Tout*>(a.y) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0 + 16 * half + 8 * hc, y8);
     }
     ystage_tok = L == C ? tok0 : -1;
     tc::fence_async_smem();
@@ -886,40 +947,6 @@ __device__ __forceinline__ void ld16_bf16(const uint8_t* p, bool valid, float (&
   r.w[0] = valid ? reinterpret_cast<const uint4*>(p)[0] : z;
   r.w[1] = valid ? reinterpret_cast<const uint4*>(p)[1] : z;
   cvt_row16(r, v);
-}
-
-// 8 floats as the bf16 [hi | lo] pair of a 128-byte-swizzled operand row r: hi into chunk hc, lo into
-// chunk hc + 4 (columns 8 (hc & 3) .. + 7 of each 32-wide half).
-__device__ __forceinline__ void st_hilo8(uint8_t* tile, int r, const float (&v)[8], int hc) {
-  uint32_t h[4], l[4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const __nv_bfloat162 hh = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
-    h[e] = *reinterpret_cast<const uint32_t*>(&hh);
-    l[e] = tc::pack_bf16(v[2 * e] - __low2float(hh), v[2 * e + 1] - __high2float(hh));
-  }
-  uint8_t* row = tile + r * 128;
-  *reinterpret_cast<uint4*>(row + ((hc ^ (r & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
-  *reinterpret_cast<uint4*>(row + (((hc + 4) ^ (r & 7)) << 4)) = make_uint4(l[0], l[1], l[2], l[3]);
-}
-// 8 floats into 16-byte chunks q0, q0 + 1 of row r of a 128-byte-row fp32 tile swizzled by r & 7.
-__device__ __forceinline__ void st8_f32_sw(uint8_t* tile, int r, int q0, const float (&v)[8]) {
-#pragma unroll
-  for (int q = 0; q < 2; ++q)
-    *reinterpret_cast<float4*>(tile + r * 128 + (((q0 + q) ^ (r & 7)) << 4)) =
-        make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-}
-template <typename Tout>
-__device__ __forceinline__ void store_row8(Tout* p, const float (&v)[8]);
-template <>
-__device__ __forceinline__ void store_row8<__nv_bfloat16>(__nv_bfloat16* p, const float (&v)[8]) {
-  *reinterpret_cast<uint4*>(p) = make_uint4(tc::pack_bf16(v[0], v[1]), tc::pack_bf16(v[2], v[3]),
-                                            tc::pack_bf16(v[4], v[5]), tc::pack_bf16(v[6], v[7]));
-}
-template <>
-__device__ __forceinline__ void store_row8<float>(float* p, const float (&v)[8]) {
-  reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
-  reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
 }
 
 // The backward state walk: chunks in reverse, 32 rows of dS per CTA, 256 threads as in the forward walk
@@ -1459,12 +1486,21 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
         const float4 dvv = reinterpret_cast<const float4*>(buf + 16384)[idx];
         t5 += sv.x * dvv.x + sv.y * dvv.y + sv.z * dvv.z + sv.w * dvv.w;
       }
-      if (lower) {
-        float f[16], v[16];
-        ld16_f32_sw(buf + 32768, img_row(i_row) + 16, half, f);
-        ld16_bf16(buf + 57344 + i_row * 64 + 32 * half, rvalid, v);
+      {  // the lower lane of the pair takes columns 0-7, the upper one 8-15 (summed in the finalize)
+        const int hc = lower ? 0 : 1, r = img_row(i_row) + 16;
+        const uint8_t* frow = buf + 32768 + r * 128;
+        const float4 f0 = *reinterpret_cast<const float4*>(frow + (((4 * half + 2 * hc) ^ (r & 7)) << 4));
+        const float4 f1 = *reinterpret_cast<const float4*>(frow + (((4 * half + 2 * hc + 1) ^ (r & 7)) << 4));
+        const uint4 w = rvalid ? reinterpret_cast<const uint4*>(buf + 57344 + i_row * 64 + 32 * half)[hc]
+                               : make_uint4(0, 0, 0, 0);
+        const float f[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
+        const uint32_t u4[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-        for (int j = 0; j < 16; ++j) fv = fmaf(f[j], v[j], fv);
+        for (int e = 0; e < 4; ++e) {
+          const __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&u4[e]);
+          fv = fmaf(f[2 * e], __low2float(h2), fv);
+          fv = fmaf(f[2 * e + 1], __high2float(h2), fv);
+        }
       }
       ok = wait_all(&bar_mma, ph_mma, a.err, 34);
       ph_mma ^= 1;
@@ -1497,6 +1533,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
         tc::tmem_st32(tl + cQK + col, q0);
       }
       tc::tmem_wait_st();
+      fv += __shfl_xor_sync(0xffffffffu, fv, 16);
       if (lower) {
         srow[0][half][i_row] = ta;   // t3
         srow[1][half][i_row] = fv;   // F . V
