@@ -1039,13 +1039,8 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
       for (int j = 0; j < 16; ++j) ck[j * DK] = tf32_rna(ds[j]);
     }
     tc::st_row_hilo16(smem + BW_S, dk, ds, half);
-    tc::fence_async_smem();
-    tc::fence_before_sync();
-    ok = tc::mbar_wait(&bar_tma[buf], (uint32_t)((it >> 1) & 1), a.err, 20) &&
-         tc::mbar_wait(&bar_t, (uint32_t)(it & 1), a.err, 25) && tc::mbar_wait(&bar_p, (uint32_t)(it & 1), a.err, 26);
-    ok = __syncthreads_and(ok) != 0;
-    tc::fence_after_sync();
-    if (!ok) break;
+    // (each thread waits for the chunk's rows and gates itself: steps 1 and 2 share one barrier)
+    bool okw = tc::mbar_wait(&bar_tma[buf], (uint32_t)((it >> 1) & 1), a.err, 20);
     const float* gb = sg[buf];
     const float bi = gb[i_row], be = gb[64 + i_row], gi = __expf(bi), bC = gb[63];
     // 2. dO row i (zero past the end) as the plain bf16 operand of P^T dO, as gamma dO [hi | lo] and, exact
@@ -1074,8 +1069,10 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
     }
     tc::fence_async_smem();
     tc::fence_before_sync();
-    __syncthreads();
+    okw = okw && tc::mbar_wait(&bar_t, (uint32_t)(it & 1), a.err, 25) && tc::mbar_wait(&bar_p, (uint32_t)(it & 1), a.err, 26);
+    ok = __syncthreads_and(okw) != 0;
     tc::fence_after_sync();
+    if (!ok) break;
     const uint32_t kq = tc::smem_u32(smem + BW_KQ + buf * 32768);
     const uint32_t pimg = tc::smem_u32(smem + BW_P), timg = tc::smem_u32(smem + BW_T);
     // 3. [K; Q] dS^T (the K rows are X1 = K dS^T) and G = P^T dO (P_hi^T and P_lo^T accumulated)
