@@ -731,7 +731,9 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
   const uint32_t idT = tc::idesc(tc::kBF16, 128, 64, true, true);
   int64_t ystage_tok = -1;  // first token of the full chunk whose output rows wait in the staging tile
 
-  for (int64_t jc = 0; jc < nchunks && ok; ++jc) {
+  // The waits for an MMA round are per thread (the TMEM results are ready for every thread once it has
+  // seen the commit); their outcome joins the chunk's next barrier, where every thread breaks alike.
+  for (int64_t jc = 0; jc < nchunks; ++jc) {
     const int buf = (int)(jc & 1);
     const int64_t cg = c_first + jc;
     const int64_t tok0 = seq0 + jc * C;
@@ -747,7 +749,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
     tc::st_row_hilo16(smem + FW_S, dk, s, half);
     tc::fence_async_smem();
     tc::fence_before_sync();
-    ok = wait_all(&bar_tma[buf], (uint32_t)((jc >> 1) & 1), a.err, 10);
+    ok = __syncthreads_and(ok && tc::mbar_wait(&bar_tma[buf], (uint32_t)((jc >> 1) & 1), a.err, 10)) != 0;
     tc::fence_after_sync();
     if (!ok) break;
     const uint32_t kq = tc::smem_u32(smem + FW_KQ + buf * 32768);
@@ -772,10 +774,9 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
       raw.w[1] = i_row < L ? vp[1] : make_uint4(0, 0, 0, 0);
       cvt_row16(raw, vr);
     }
-    ok = wait_all(&bar_mma, ph, a.err, 11);
+    ok = ok && tc::mbar_wait(&bar_mma, ph, a.err, 11);
     ph ^= 1;
     tc::fence_after_sync();
-    if (!ok) break;
     // 3. K side: E = diag(beta) (V - diag(gamma) K S^T) as the [hi | lo] operand; Q side: gamma Q S^T
     float yp[16];
     const size_t ptile = ((size_t)(cg * Hv + hv) * (DV / DVT) + blockIdx.x) * 2048;  // this CTA's tile
@@ -795,18 +796,18 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
     }
     tc::fence_async_smem();
     tc::fence_before_sync();
-    __syncthreads();
+    ok = __syncthreads_and(ok) != 0;
     tc::fence_after_sync();
+    if (!ok) break;
     // 4. D = T E  ([T_hi; T_lo] stacked: row i's two products in lanes l and l + 16)
     if (tid == 0) {
       mma_run<4, kKmaj128>(tmem + cD, idA, tc::smem_u32(smem + FW_T + buf * 16384), tc::smem_u32(smem + FW_E), false);
       tc::mma_commit(&bar_mma);
     }
 
-    ok = wait_all(&bar_mma, ph, a.err, 12);
+    ok = ok && tc::mbar_wait(&bar_mma, ph, a.err, 12);
     ph ^= 1;
     tc::fence_after_sync();
-    if (!ok) break;
     {
       // both lanes of the pair hold row i of D; one instruction stream for both: the K-side lane writes
       // D as the [hi | lo] operand of P D and columns 0-7 of the tf32 copy, the Q-side lane
@@ -833,8 +834,9 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
     if (tid == 32) tc::bulk_wait_read();  // the staging buffers are rewritten below and next chunk
     tc::fence_async_smem();
     tc::fence_before_sync();
-    __syncthreads();
+    ok = __syncthreads_and(ok) != 0;
     tc::fence_after_sync();
+    if (!ok) break;
     // 5. S update^T = K^T D~ (M = 128 dk rows);  O2 = P D ([P_hi; P_lo] stacked)
     if (tid == 0) {
       mma_run<4, kKT>(tmem + cS, idT, kq, tc::smem_u32(smem + FW_DT), false);
@@ -845,10 +847,9 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
       tc::bulk_store(a.Ds + ptile, smem + FW_DS + buf * 8192, 8192);
       tc::bulk_commit();
     }
-    ok = wait_all(&bar_mma, ph, a.err, 13);
+    ok = ok && tc::mbar_wait(&bar_mma, ph, a.err, 13);
     ph ^= 1;
     tc::fence_after_sync();
-    if (!ok) break;
     {
       float u[16], o2[16];
       tmem_ld_hl16x2(tl + cS, tl + cO, half, u, o2);
@@ -875,12 +876,10 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
     tc::fence_async_smem();
     tc::fence_before_sync();
   }
-  if (ok && ystage_tok >= 0) {  // the last chunk's output rows
-    __syncthreads();
-    if (tid == 32) {
-      tc::tma_store_3d(&ymap, smem + FW_Y, dv0, hv, (int)ystage_tok);
-      tc::bulk_commit();
-    }
+  ok = __syncthreads_and(ok) != 0;  // (the last round's waits were per thread)
+  if (ok && ystage_tok >= 0 && tid == 32) {  // the last chunk's output rows
+    tc::tma_store_3d(&ymap, smem + FW_Y, dv0, hv, (int)ystage_tok);
+    tc::bulk_commit();
   }
   if (tid == 32) tc::bulk_wait();
   if (ok && a.hT) {
@@ -1025,7 +1024,8 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
   const uint32_t idF = tc::idesc(tc::kBF16, 64, 64, true, true);    // T^T x [hi | lo]
   const uint32_t idU = tc::idesc(tc::kBF16, 128, 64, true, true);   // Q^T, K^T x [hi | lo]
 
-  for (int64_t it = 0; it < nchunks && ok; ++it) {
+  // MMA-round waits per thread, joined at the chunk's next barrier (as in the forward walk)
+  for (int64_t it = 0; it < nchunks; ++it) {
     const int64_t jc = nchunks - 1 - it;
     const int buf = (int)(it & 1);
     const int64_t cg = c_first + jc;
@@ -1040,7 +1040,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
     }
     tc::st_row_hilo16(smem + BW_S, dk, ds, half);
     // (each thread waits for the chunk's rows and gates itself: steps 1 and 2 share one barrier)
-    bool okw = tc::mbar_wait(&bar_tma[buf], (uint32_t)((it >> 1) & 1), a.err, 20);
+    bool okw = ok && tc::mbar_wait(&bar_tma[buf], (uint32_t)((it >> 1) & 1), a.err, 20);
     const float* gb = sg[buf];
     const float bi = gb[i_row], be = gb[64 + i_row], gi = __expf(bi), bC = gb[63];
     // 2. dO row i (zero past the end) as the plain bf16 operand of P^T dO, as gamma dO [hi | lo] and, exact
@@ -1094,11 +1094,10 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
       tc::bulk_commit();
       if (jc > 0) issue_main(jc - 1, buf ^ 1);  // the previous chunk's [K; Q], gates and dO rows
     }
-    ok = wait_all(&bar_mma, ph, a.err, 21);
+    ok = ok && tc::mbar_wait(&bar_mma, ph, a.err, 21);
     ph ^= 1;
     tc::fence_after_sync();
-    if (!ok) break;
-    if (tid == 32 && jc > 0) issue_p(jc - 1);  // P's last reader has completed
+    if (ok && tid == 32 && jc > 0) issue_p(jc - 1);  // P's last reader has completed
     // 4. dD = diag(lambda) K dS^T + P^T dO (K side), as the [hi | lo] operand.  tcgen05.ld is a
     //    warp-wide aligned instruction: every lane executes the same loads, outside the branch.
     {
@@ -1133,8 +1132,9 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
     if (tid == 32) tc::bulk_wait_read();  // the staging buffer is rewritten next chunk
     tc::fence_async_smem();
     tc::fence_before_sync();
-    __syncthreads();
+    ok = __syncthreads_and(ok) != 0;
     tc::fence_after_sync();
+    if (!ok) break;
     // 5. F = T^T dD (T_hi^T and T_lo^T accumulated; M = 64: row j in the K-side lanes)
     if (tid == 0) {
       const uint32_t dd = tc::smem_u32(smem + BW_DD);
@@ -1145,11 +1145,10 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
           tc::mma_bf16(tmem + cF, desc_img_t(timg, part, ks), desc_hl(dd, ks), idF, (part | ks) ? 1u : 0u);
       tc::mma_commit(&bar_mma);
     }
-    ok = wait_all(&bar_mma, ph, a.err, 22);
+    ok = ok && tc::mbar_wait(&bar_mma, ph, a.err, 22);
     ph ^= 1;
     tc::fence_after_sync();
-    if (!ok) break;
-    if (tid == 32 && jc > 0) issue_t(jc - 1);  // T's last reader has completed
+    if (ok && tid == 32 && jc > 0) issue_t(jc - 1);  // T's last reader has completed
     {
       float f[16];
       tmem_ld_hl16(tl + cF, half, f);
@@ -1182,8 +1181,9 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
     }
     tc::fence_async_smem();
     tc::fence_before_sync();
-    __syncthreads();
+    ok = __syncthreads_and(ok) != 0;
     tc::fence_after_sync();
+    if (!ok) break;
     // 6. U = Q^T (gamma dO) (issued in step 3) + K^T H (M = 128 dk rows)
     if (tid == 0) {
       mma_run<4, kKT>(tmem + cU, idU, kq, tc::smem_u32(smem + BW_H), true);
@@ -1195,10 +1195,9 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
       if (L == C) tc::tma_store_3d(&dvmap, smem + BW_DV, dv0, hv, (int)tok0);
       tc::bulk_commit();
     }
-    ok = wait_all(&bar_mma, ph, a.err, 23);
+    ok = ok && tc::mbar_wait(&bar_mma, ph, a.err, 23);
     ph ^= 1;
     tc::fence_after_sync();
-    if (!ok) break;
     {
       float u[16];
       tmem_ld_hl16(tl + cU, half, u);
@@ -1208,6 +1207,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
     }
     tc::fence_before_sync();
   }
+  ok = __syncthreads_and(ok) != 0;  // (the last round's waits were per thread)
   if (tid == 32) tc::bulk_wait();
   if (ok && a.dh0) {
     float* dst = a.dh0 + (((size_t)n * Hv + hv) * DV + dv0 + 16 * half) * DK + dk;
