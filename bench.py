@@ -68,7 +68,7 @@ def bytes_per_token(Hk, Hv, Dk, Dv, act=2):
 
 # DRAM bytes (read + write) per launch of the dominant op, from one ncu capture of this bench's workload
 # (profiles/gdn_chunk_config1.md, profiles/gdn_verify_config4.md); None where no capture was made.
-TRAFFIC = {("c1", "layer_bwd"): 473.6e6, ("c4", "verify"): 550.8e6}
+TRAFFIC = {("c1", "layer_bwd"): 474.6e6, ("c4", "verify"): 550.8e6}
 
 
 def load_peaks():
