@@ -1450,14 +1450,15 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
     for (int sl = 0; sl < NSL && ok; ++sl) {
       const int q = r * NSL + sl, bs = q & 1;
       uint8_t* buf = smem + GR_BUF + bs * GR_BS;
-      ok = wait_all(&bar_s[bs], (uint32_t)((q >> 1) & 1), a.err, 37);
-      if (!ok) break;
+      // each thread waits for the slice's data itself; the barrier at the end of the slice keeps the
+      // buffers' reuse ordered and makes a failed wait everyone's
+      ok = ok && tc::mbar_wait(&bar_s[bs], (uint32_t)((q >> 1) & 1), a.err, 37);
       // the other buffer's last reader has finished (the finalize uses the second buffer, so the next
       // value head's first slice goes out during this head's last slice)
-      if (tid == 32 && q + 1 < ratio * NSL) issue_slice(q + 1);
+      if (ok && tid == 32 && q + 1 < ratio * NSL) issue_slice(q + 1);
       // a. over the slice's value rows (tf32, K = 32; every operand arrives in its final form): [dO; F] S,
       //    D dS (M = 64 in the upper lanes), [dO; F] D^T -- issued at once
-      if (tid == 0) {
+      if (tid == 0 && ok) {
         tc::fence_after_sync();
         const uint32_t s32 = tc::smem_u32(buf), d32 = tc::smem_u32(buf + 16384);
         const uint32_t aa = tc::smem_u32(buf + 32768), dt = tc::smem_u32(buf + 49152);
@@ -1499,7 +1500,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
           fv = fmaf(f[2 * e + 1], __high2float(h2), fv);
         }
       }
-      ok = wait_all(&bar_mma, ph_mma, a.err, 34);
+      ok = __syncthreads_and(ok && tc::mbar_wait(&bar_mma, ph_mma, a.err, 34)) != 0;
       ph_mma ^= 1;
       tc::fence_after_sync();
     }
