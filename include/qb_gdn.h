@@ -2,11 +2,11 @@
  * qb_gdn — the Gated DeltaNet recurrence on B200 (sm_100a) behind a C ABI.
  *
  * Drop-in for quotebound's recurrence entry points:
- *   gated_delta(q, k, v, g, beta, state, train)            src/deltanet.h:17-19, src/deltanet.cpp:68-80
+ *   gated_delta(q, k, v, g, beta, state, train)            src/deltanet.h:17-19, src/deltanet.cpp:49-61
  *   gated_delta_trainable(q, k, v, g, beta, state)         src/delta_grad.h:14-16, src/delta_grad.cpp:201-212
  *   gated_delta_vjp({q, k, v, g, beta, state}, dy, dstate) src/delta_grad.h:18-20, src/delta_grad.cpp:155-199
- * plus the per-token path of deltanet(..., rows) (src/deltanet.cpp:122-135, src/exact.cpp:144-159)
- * and the gate / beta / q-k norm graph around the recurrence (src/deltanet.cpp:22-33, 113-119).
+ * plus the per-token path of deltanet(..., rows) (src/deltanet.cpp:102-117, src/exact.cpp:144-159)
+ * and the gate / beta / q-k norm graph around the recurrence (src/deltanet.cpp:22-33, 94-100).
  *
  * Conventions (the reference's own C ABI, src/constrain_capi.h:7-9): every call that can fail
  * returns -1 and writes a NUL-terminated reason into err (cut to errlen); nothing throws across
@@ -93,7 +93,7 @@ int qb_gdn_bwd(const qb_gdn_desc* d, const void* q, const void* k, const void* v
                int64_t ws_bytes, void* stream, char* err, int errlen);
 
 /* The recurrence with the norm and gate graph around it fused in (deltanet()'s middle,
- * src/deltanet.cpp:113-119, compute_g :41-52): q, k are the raw conv outputs [B, T, Hk, Dk] (bf16),
+ * src/deltanet.cpp:94-100, compute_g :22-33): q, k are the raw conv outputs [B, T, Hk, Dk] (bf16),
  * normalised inside as the model does (rms_norm rounded to bf16, times the bf16 scalar 1/Dk for q and
  * 1/sqrt(Dk) for k); a, b [B, T, Hv] float32 give log g = -exp(A_log) softplus(a + dt_bias) and
  * beta = sigmoid(b); A_log, dt_bias [Hv] float32.  Needs the chunked path (bf16, Dk = Dv = 128).
@@ -112,7 +112,7 @@ int qb_gdn_layer_bwd(const qb_gdn_desc* d, const void* q, const void* k, const v
                      float* da, float* db, float* dA_log, float* ddt_bias, float* dh0, void* ws,
                      int64_t ws_bytes, void* stream, char* err, int errlen);
 
-/* One decode step for N independent sequences (gated_delta with T = 1, src/deltanet.cpp:68-80 as
+/* One decode step for N independent sequences (gated_delta with T = 1, src/deltanet.cpp:49-61 as
  * the decode path calls it, src/generate.cpp forward(..., cache)):
  *   q, k [N, Hk, Dk]; v [N, Hv, Dv]; g, beta [N, Hv]; state_in [N, Hv, Dv, Dk] float32;
  *   y [N, Hv, Dv] (out_dtype); state_out [N, Hv, Dv, Dk] (may equal state_in). */
@@ -121,7 +121,7 @@ int qb_gdn_step(int32_t N, int32_t Hk, int32_t Hv, int32_t Dk, int32_t Dv, int32
                 const float* beta, const float* state_in, void* y, float* state_out, void* stream,
                 char* err, int errlen);
 
-/* Exact speculative verify (deltanet(..., rows), src/deltanet.cpp:122-135; RowStates,
+/* Exact speculative verify (deltanet(..., rows), src/deltanet.cpp:102-117; RowStates,
  * src/model.h:84-89): V tokens of each of N sequences run as V one-token steps, bit for bit equal
  * to V calls of qb_gdn_step, and every row's state is kept:
  *   q, k [N, V, Hk, Dk]; v [N, V, Hv, Dv]; g, beta [N, V, Hv]; state_in [N, Hv, Dv, Dk];
@@ -138,8 +138,8 @@ int qb_gdn_keep_rows(int32_t N, int32_t V, int32_t Hv, int32_t Dk, int32_t Dv, c
                      const int32_t* keep, float* state_out, int32_t* status, void* stream, char* err,
                      int errlen);
 
-/* The gate / beta / q-k norm graph around the recurrence (src/deltanet.cpp:113-119, compute_g
- * :41-52), forward:
+/* The gate / beta / q-k norm graph around the recurrence (src/deltanet.cpp:94-100, compute_g
+ * :22-33), forward:
  *   qn = q * rsqrt(mean(q^2) + 1e-6) / Dk;  kn = k * rsqrt(mean(k^2) + 1e-6) / sqrt(Dk);
  *   beta = sigmoid(b);  g = exp(-exp(A_log) * softplus(a + dt_bias)).
  * q, k, qn, kn [P, Hk, Dk] (in_dtype for q, k; out_dtype for qn, kn); a, b, g, beta [P, Hv] float32;

@@ -245,7 +245,7 @@ __global__ void __launch_bounds__(128, 4) gdn_chunk_prep(const __grid_constant__
   auto gate_eval = [&](const float (&gr)[4], float& lg, float& bt) {
     lg = 0.f, bt = 0.f;
     if (tid < 64 && tid < L) {
-      if (layer) {  // log g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b) (src/deltanet.cpp:41-52, :118)
+      if (layer) {  // log g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b) (src/deltanet.cpp:22-33, :99)
         lg = -expf(gr[2]) * softplus_f(gr[0] + gr[3]);
         bt = sigmoid_f(gr[1]);
       } else {
@@ -259,7 +259,7 @@ __global__ void __launch_bounds__(128, 4) gdn_chunk_prep(const __grid_constant__
 
   bool ok = wait_all(&bar_tma, 0, a.err, 1);
   if (ok && layer) {
-    // q and k rows normalised in place as the model does (src/deltanet.cpp:113-116): rms_norm in fp32,
+    // q and k rows normalised in place as the model does (src/deltanet.cpp:94-97): rms_norm in fp32,
     // rounded to bf16, times the bf16 scalar 1/Dk (q) or 1/sqrt(Dk) (k), rounded again.  Thread t
     // owns half a row (one 128-byte slab row of 64 elements); the order inside a row does not matter,
     // so step c touches chunk c ^ (row & 7): eight consecutive rows then hit eight different banks.

@@ -6,7 +6,7 @@
 namespace qbgdn {
 
 // g == nullptr selects layer mode: q, k are the raw (pre-norm) rows and the gates come from
-// a, b, A_log, dt_bias (the norm and gate graph of src/deltanet.cpp:113-119 fused into the kernels).
+// a, b, A_log, dt_bias (the norm and gate graph of src/deltanet.cpp:94-100 fused into the kernels).
 struct ChunkFwdArgs {
   int B, T, Hk, Hv, Dk, Dv, N;
   int64_t n_chunks;

@@ -1,5 +1,5 @@
-// The gate / beta / q-k norm graph that feeds the recurrence (src/deltanet.cpp:113-119, compute_g
-// :41-52) and its chain rule.  HBM-bound elementwise work: one warp per (token, key head) row of
+// The gate / beta / q-k norm graph that feeds the recurrence (src/deltanet.cpp:94-100, compute_g
+// :22-33) and its chain rule.  HBM-bound elementwise work: one warp per (token, key head) row of
 // q and k, coalesced 16-byte loads, warp-shuffle reductions; per-head parameter gradients summed
 // in a fixed order (block partials, then one block over the partials) with no atomics.
 #include <stdarg.h>

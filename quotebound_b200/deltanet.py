@@ -8,8 +8,8 @@ Same names, argument order and meaning as the reference:
                                                                           — src/delta_grad.h:18-20
 
 Layouts: q, k [B, T, Hk, Dk]; v [B, T, Hv, Dv]; g, beta [B, T, Hv] float32; state [B, Hv, Dv, Dk]
-float32.  y comes back in q's dtype and the state in float32 (src/deltanet.cpp:68-80).  Like the
-reference, which feeds the op float32 (src/deltanet.cpp:73-79), inputs of mixed dtypes are computed in
+float32.  y comes back in q's dtype and the state in float32 (src/deltanet.cpp:49-61).  Like the
+reference, which feeds the op float32 (src/deltanet.cpp:54-60), inputs of mixed dtypes are computed in
 float32; bf16 q, k, v are read as bf16 directly (every bf16 value is exact in float32, so nothing is
 lost) and the recurrence itself always runs with a float32 state.
 
@@ -217,7 +217,7 @@ def gated_delta_trainable(q, k, v, g, beta, state=None, *, cu_seqlens=None, algo
 
 
 def gated_delta(q, k, v, g, beta, state=None, train=False, *, cu_seqlens=None, algo=0):
-    """y [B, T, Hv, Dv] in q's dtype and the new state [B, Hv, Dv, Dk] float32 (src/deltanet.cpp:68-80)."""
+    """y [B, T, Hv, Dv] in q's dtype and the new state [B, Hv, Dv, Dk] float32 (src/deltanet.cpp:49-61)."""
     if train:
         y, s = gated_delta_trainable(q, k, v, g, beta, state, cu_seqlens=cu_seqlens, algo=algo)
         return y.to(q.dtype), s

@@ -1,9 +1,9 @@
 """Decode-time recurrence over the C ABI: the one-token step, the exact multi-row verify and keep_rows.
 
 * ``step(q, k, v, g, beta, state)`` — gated_delta on one token with the cached state (the decode path,
-  src/deltanet.cpp:130 with S = 1).
+  src/deltanet.cpp:118-120 with S = 1).
 * ``verify(q, k, v, g, beta, state)`` — V drafted tokens run as V one-token steps, bit for bit equal to
-  V calls of ``step``, with every row's state kept (deltanet(..., rows), src/deltanet.cpp:122-135;
+  V calls of ``step``, with every row's state kept (deltanet(..., rows), src/deltanet.cpp:102-117;
   RowStates, src/model.h:84-89).
 * ``keep_rows(states, keep)`` — the state after ``keep[n]`` accepted tokens (src/exact.cpp:151-159).
 """

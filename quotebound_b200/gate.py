@@ -1,6 +1,6 @@
 """The gate / beta / q-k norm graph around the recurrence, over the C ABI.
 
-Forward (src/deltanet.cpp:113-119, compute_g :41-52):
+Forward (src/deltanet.cpp:94-100, compute_g :22-33):
     qn = q * rsqrt(mean(q^2) + 1e-6) / Dk;   kn = k * rsqrt(mean(k^2) + 1e-6) / sqrt(Dk)
     beta = sigmoid(b);   g = exp(-exp(A_log) * softplus(a + dt_bias))
 Backward: the chain rule of all of it, with this call's per-head sums of dA_log and ddt_bias (the

@@ -1,6 +1,6 @@
 """The recurrence with its norm and gate graph fused in, over the C ABI (qb_gdn_layer_fwd / _bwd).
 
-This is the middle of quotebound's deltanet() (src/deltanet.cpp:113-119, compute_g :41-52) from the conv
+This is the middle of quotebound's deltanet() (src/deltanet.cpp:94-100, compute_g :22-33) from the conv
 outputs to y: q, k are the raw rows, normalised inside as the model does (rms_norm rounded to bf16, times
 the bf16 scalar 1/Dk for q and 1/sqrt(Dk) for k); log g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b).
 The backward returns the gradients of the raw q, k, v, a, b and the per-head sums of dA_log, ddt_bias

@@ -4,14 +4,14 @@ No public dataset is involved: every workload is random data with the shapes and
 value distributions of the configurations this package is measured on.
 
 * q, k, v ~ N(0, 1); q and k are L2-normalised per head and q is scaled by
-  1/sqrt(Dk) (the model's rms_norm * 1/Dk and * 1/sqrt(Dk), src/deltanet.cpp:113-116,
+  1/sqrt(Dk) (the model's rms_norm * 1/Dk and * 1/sqrt(Dk), src/deltanet.cpp:94-97,
   give the same vectors up to the norm's 1e-6 epsilon).
 * a ~ N(0, 1), dt_bias ~ N(0, 0.5), A_log = log U(1, 16) per value head;
-  g = exp(-exp(A_log) * softplus(a + dt_bias)) (src/deltanet.cpp:41-52), beta = sigmoid(b), b ~ N(0, 1).
+  g = exp(-exp(A_log) * softplus(a + dt_bias)) (src/deltanet.cpp:22-33), beta = sigmoid(b), b ~ N(0, 1).
 * dO ~ N(0, 1).
 
 The reference's own recurrence tests draw g ~ U[g_lo, 1) instead
-(tests/test_deltanet.cpp:145-157); ``uniform_gate`` reproduces that family.
+(tests/test_deltanet.cpp:145-154); ``uniform_gate`` reproduces that family.
 """
 from __future__ import annotations
 

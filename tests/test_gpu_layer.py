@@ -1,7 +1,7 @@
 """The fused layer path (qb_gdn_layer_fwd / _bwd: norm + gates + recurrence) against the CPU oracle (GPU only).
 
 The reference computes q^, k^ in bf16 (rms_norm output in the activation dtype, times a bf16 scalar,
-src/deltanet.cpp:113-116), so the oracle's recurrence is fed those same bf16-rounded rows; the norm's
+src/deltanet.cpp:94-97), so the oracle's recurrence is fed those same bf16-rounded rows; the norm's
 chain rule is the straight-through one autodiff applies to the rounding.  Tolerance rel-L2 <= 2e-3.
 """
 import math

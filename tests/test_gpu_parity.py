@@ -2,7 +2,7 @@
 
 Tolerances (the build's contract): rel-L2 <= 1e-5 for float32 activations, <= 2e-3 for bf16
 activations; the reference's own recurrence bounds (1e-5 of the max for float32 forward and
-gradients, tests/test_deltanet.cpp:164-165,257) are checked on the float32 cases as well.  The
+gradients, tests/test_deltanet.cpp:43-44,136) are checked on the float32 cases as well.  The
 verify rows are checked bit for bit against one-token steps.
 """
 import os
@@ -110,7 +110,7 @@ def test_agree_forward(T, g_lo, dtype):
         assert rel(y, yo) <= tol and rel(s, so) <= tol
         if dtype == torch.float32:  # the reference's agree() bounds
             assert worst(y, yo) <= 1e-5 and worst(s, so) <= 1e-5
-        # 20 + rest steps against one call (tests/test_deltanet.cpp:168-173)
+        # 20 + rest steps against one call (tests/test_deltanet.cpp:47-52)
         y1, s1, _ = deltanet.gated_delta_fwd(d.q[:, :20], d.k[:, :20], d.v[:, :20], d.g[:, :20], d.beta[:, :20],
                                              d.h0, algo=algo)
         y2, s2, _ = deltanet.gated_delta_fwd(d.q[:, 20:], d.k[:, 20:], d.v[:, 20:], d.g[:, 20:], d.beta[:, 20:],
@@ -131,7 +131,7 @@ def test_bf16_fwd_bwd(T):
                                             (1, 333, 4, 4, 0.9)])
 def test_chunked_backward_reference_gates(B, T, Hk, Hv, g_lo):
     """The chunked backward on the reference's own gate family (g ~ U[g_lo, 1),
-    tests/test_deltanet.cpp:226-234), dg compared directly."""
+    tests/test_deltanet.cpp:106-113), dg compared directly."""
     p = synthetic.make(B, T, Hk, Hv, 128, 128, seed=100 + T, dtype=torch.bfloat16, uniform_gate=g_lo,
                        h0_std=0.1, dhT_std=0.1)
     assert_close(p, run_gpu(p, CHUNKED), oracle_all(p), 2e-3)

@@ -25,13 +25,13 @@ def rel(a, b):
 
 
 def worst(a, b):
-    """The reference's gradient metric: max |a - b| over max |b| (tests/test_deltanet.cpp:245-250)."""
+    """The reference's gradient metric: max |a - b| over max |b| (tests/test_deltanet.cpp:126-128)."""
     a = np.asarray(a, np.float64); b = np.asarray(b, np.float64)
     return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
 
 
 def problem_ref_style(B, T, Hk, Hv, Dk, Dv, g_lo, seed):
-    """Inputs as the reference's trainable_gradient draws them (tests/test_deltanet.cpp:226-234)."""
+    """Inputs as the reference's trainable_gradient draws them (tests/test_deltanet.cpp:106-113)."""
     gen = torch.Generator().manual_seed(seed)
     n = lambda *s: torch.randn(*s, generator=gen, dtype=torch.float64)
     unit = lambda x, s: x * torch.rsqrt((x * x).mean(-1, keepdim=True) + 1e-6) * s
@@ -60,13 +60,13 @@ def test_forward_matches_plain_ops(T, g_lo):
     y_ref, s_ref = torch_ref.gated_delta_ops(q, k, v, g, beta, s0)
     for acc64, tol in ((True, 1e-6), (False, 1e-5)):
         y, s = oracle.gated_delta_fwd(q, k, v, g, beta, s0, acc64=acc64)
-        # the reference's agree() bounds: 1e-5 of the max (tests/test_deltanet.cpp:164-165)
+        # the reference's agree() bounds: 1e-5 of the max (tests/test_deltanet.cpp:43-44)
         assert np.abs(y - y_ref.numpy()).max() <= tol * np.abs(y_ref.numpy()).max()
         assert np.abs(s - s_ref.numpy()).max() <= tol * np.abs(s_ref.numpy()).max()
 
 
 def test_state_carry_split():
-    """20 + rest steps against one call (tests/test_deltanet.cpp:168-173)."""
+    """20 + rest steps against one call (tests/test_deltanet.cpp:47-52)."""
     q, k, v, g, beta, s0, _, _ = problem_ref_style(2, 75, 2, 4, 32, 32, 0.9, seed=5)
     y, s = oracle.gated_delta_fwd(q, k, v, g, beta, s0, acc64=False)
     y1, s1 = oracle.gated_delta_fwd(q[:, :20], k[:, :20], v[:, :20], g[:, :20], beta[:, :20], s0, acc64=False)
@@ -75,7 +75,7 @@ def test_state_carry_split():
     assert np.array_equal(s2, s)
 
 
-# The reference's eight trainable_gradient shapes (tests/test_deltanet.cpp:266-275).
+# The reference's eight trainable_gradient shapes (tests/test_deltanet.cpp:145-154).
 TRAINABLE = [
     (1, 19, 16, 32, 128, 128, 0.5),
     (1, 64, 16, 32, 128, 128, 0.9),
@@ -95,7 +95,7 @@ def test_backward_matches_autodiff(shape):
     _, _, grads = autodiff(q, k, v, g, beta, s0, cy, cs)
     got = oracle.gated_delta_bwd(q, k, v, g, beta, s0, cy, cs, acc64=False)
     for name, a, b in zip(("q", "k", "v", "g", "beta", "state"), got, grads):
-        # the reference's bound for its backward: worst max-abs / max ≤ 1e-5 (tests/test_deltanet.cpp:257)
+        # the reference's bound for its backward: worst max-abs / max ≤ 1e-5 (tests/test_deltanet.cpp:136)
         assert worst(a, b.numpy()) <= 1e-5, name
 
 
