@@ -25,8 +25,9 @@
  * on it and never synchronise the device.  Host-side validation runs before any launch, so a call
  * that fails validation has enqueued nothing.
  *
- * Workspace: calls that need scratch take (ws, ws_bytes); query the size with
- * qb_gdn_workspace_bytes.  The same workspace must not be used by two calls in flight at once.
+ * Workspace: the recurrence calls take (ws, ws_bytes), 256-byte aligned; query the size with
+ * qb_gdn_workspace_bytes.  It opens with the call's status block (qb_gdn_status).  The same workspace
+ * must not be used by two calls in flight at once.
  */
 #ifndef QB_GDN_H
 #define QB_GDN_H
@@ -69,7 +70,8 @@ const char* qb_gdn_version(void);
 /* How many kernels this library has launched in this process so far (all devices and streams). */
 int64_t qb_gdn_launches(void);
 
-/* Bytes of workspace `op` needs for this shape (0 is possible); -1 on an invalid shape. */
+/* Bytes of workspace `op` needs for this shape (at least 256, the status block); -1 on an invalid
+ * shape. */
 int64_t qb_gdn_workspace_bytes(const qb_gdn_desc* d, int32_t op, char* err, int errlen);
 
 /* Bytes of the saved-for-backward buffer (the fp32 chunk-start states, [N_chunks, Hv, Dv, Dk],
@@ -161,14 +163,47 @@ int qb_gdn_gate_bwd(int64_t P, int32_t Hk, int32_t Hv, int32_t Dk, int32_t in_dt
 /* Workspace bytes qb_gdn_gate_bwd needs for P tokens and Hv heads. */
 int64_t qb_gdn_gate_workspace_bytes(int64_t P, int32_t Hv);
 
+/* Device status of the last qb_gdn_fwd / qb_gdn_bwd / qb_gdn_layer_fwd / qb_gdn_layer_bwd call that
+ * used this workspace.  Every such workspace opens with a 256-byte status block that the call clears on
+ * its stream before its first kernel.  The tensor-core kernels wait on copies and products with
+ * bounded waits (about one second of wall time or 2^24 polls); a wait that gives up records its code
+ * (the first one of the call wins), lets what it waited for land, frees its tensor memory and returns,
+ * so the call never hangs or traps -- but its outputs are then NOT valid.  Calls are asynchronous, so
+ * the code is read here: this synchronises `stream` (the stream of that call) and writes the code to
+ * *code.  The reference's counterpart is the runtime_error its backward throws
+ * (src/delta_grad.cpp:164-170), which has no asynchronous case.  Codes (0 = no failure):
+ *    1  prep: the K / Q tiles          2  prep: K K^T, Q K^T
+ *   10  forward walk: a chunk's tiles  11, 12, 13  forward walk: its three product rounds
+ *   20  reverse walk: a chunk's rows   25, 26  reverse walk: the T, P images
+ *   21, 22, 23  reverse walk: its three product rounds
+ *   30  gradient: the [K; Q] image     31  gradient: a value head's P image and gates
+ *   37  gradient: a slice's tiles      34, 35, 36  gradient: its product rounds (slice, K K^T, finalize)
+ * The row-parallel kernels have no such waits; their calls always leave 0. */
+int qb_gdn_status(const void* ws, int32_t* code, void* stream, char* err, int errlen);
+
+/* Test hook of the failure path above: from now on, in every call of this process, the bounded wait
+ * with this code gives up after `polls` polls (code 0 turns the hook off).  The wait then runs out on
+ * a normal input, as a lost arrival would make it, and a test can check that the call returns, that
+ * qb_gdn_status reports the code and that the next call is correct.  Not for production use.  No
+ * counterpart in the reference. */
+int qb_gdn_set_wait_limit(int32_t code, int32_t polls, char* err, int errlen);
+
+/* The finite check of the reference's training step (src/train.cpp:266-271 refuses a step whose loss
+ * or gradient norm is not finite), as a device count for host code to act on: writes the number of
+ * NaN or infinite entries among the n elements of x (QB_DTYPE_F32 or QB_DTYPE_BF16) into the device
+ * word *count (cleared first), asynchronously on `stream`. */
+int qb_gdn_count_nonfinite(const void* x, int64_t n, int32_t dtype, unsigned long long* count, void* stream,
+                           char* err, int errlen);
+
 /* qb_gdn_gate_bwd without a workspace argument, for callers that cannot allocate device memory:
  * code running inside a fixed memory budget or a pre-allocated pool, plugins handed only their input
  * and output buffers, and hosts that forbid cudaMalloc / cudaFree on the hot path because those calls
  * synchronise the device.  It allocates nothing: its partial sums go to a fixed array of 148 x 256 x 2
  * floats (296 KiB) in the library's own device memory, which every GPU that loads the library holds
  * until the process exits.  Value heads beyond 256 are refused with an error.  The first call on a
- * device looks up that array's device address (cudaGetSymbolAddress, with that device current); make
- * that first call before any stream capture.  All calls share the one array, so two calls that
+ * device looks up that array's device address (cudaGetSymbolAddress, with that device current), and
+ * so does the first call in a new context of the device (after cudaDeviceReset, say, the old address
+ * is gone); make that first call before any stream capture.  All calls share the one array, so two calls that
  * overlap on the GPU (other streams, other threads) race on it and must be ordered by the caller;
  * nothing in it needs clearing between calls.  Arguments and results are those of qb_gdn_gate_bwd.
  * This entry point has no counterpart in the reference. */

@@ -26,7 +26,7 @@ SYMBOLS = (
     "qb_gdn_version", "qb_gdn_launches", "qb_gdn_workspace_bytes", "qb_gdn_saved_bytes", "qb_gdn_fwd", "qb_gdn_bwd",
     "qb_gdn_step", "qb_gdn_verify", "qb_gdn_keep_rows", "qb_gdn_gate_fwd", "qb_gdn_gate_bwd",
     "qb_gdn_gate_workspace_bytes", "qb_gdn_gate_bwd_noalloc", "qb_gdn_layer_saved_bytes", "qb_gdn_layer_fwd",
-    "qb_gdn_layer_bwd",
+    "qb_gdn_layer_bwd", "qb_gdn_status", "qb_gdn_set_wait_limit", "qb_gdn_count_nonfinite",
 )
 
 
@@ -88,6 +88,12 @@ def load():
     L.qb_gdn_gate_bwd_noalloc.argtypes = [i64] + [i32] * 5 + [vp] * 16 + [vp, cp, ctypes.c_int]
     L.qb_gdn_gate_workspace_bytes.restype = i64
     L.qb_gdn_gate_workspace_bytes.argtypes = [i64, i32]
+    L.qb_gdn_status.restype = ctypes.c_int
+    L.qb_gdn_status.argtypes = [vp, ctypes.POINTER(i32), vp, cp, ctypes.c_int]
+    L.qb_gdn_set_wait_limit.restype = ctypes.c_int
+    L.qb_gdn_set_wait_limit.argtypes = [i32, i32, cp, ctypes.c_int]
+    L.qb_gdn_count_nonfinite.restype = ctypes.c_int
+    L.qb_gdn_count_nonfinite.argtypes = [vp, i64, i32, vp, vp, cp, ctypes.c_int]
     _lib = L
     return L
 
@@ -108,3 +114,29 @@ def version() -> str:
 def launches() -> int:
     """Kernels the library has launched in this process so far."""
     return int(load().qb_gdn_launches())
+
+
+# Meaning of the device status codes (include/qb_gdn.h, qb_gdn_status).
+STATUS_CODES = {
+    1: "prep: the K / Q tiles", 2: "prep: K K^T, Q K^T",
+    10: "forward walk: a chunk's tiles", 11: "forward walk: product round 1", 12: "forward walk: product round 2",
+    13: "forward walk: product round 3",
+    20: "reverse walk: a chunk's rows", 21: "reverse walk: product round 1", 22: "reverse walk: product round 2",
+    23: "reverse walk: product round 3", 25: "reverse walk: the T image", 26: "reverse walk: the P image",
+    30: "gradient: the [K; Q] image", 31: "gradient: a value head's P image and gates",
+    34: "gradient: a slice's products", 35: "gradient: K K^T", 36: "gradient: the finalize's products",
+    37: "gradient: a slice's tiles",
+}
+
+
+def status(ws, stream) -> int:
+    """The device status code the last call that used workspace ``ws`` (a CUDA tensor) left; syncs ``stream``."""
+    err, code = err_buf(), ctypes.c_int32(0)
+    check(load().qb_gdn_status(ctypes.c_void_p(ws.data_ptr()), ctypes.byref(code), stream, err, len(err)), err)
+    return int(code.value)
+
+
+def set_wait_limit(code: int, polls: int = 1) -> None:
+    """Test hook: the bounded wait with this code gives up after ``polls`` polls (code 0 = off)."""
+    err = err_buf()
+    check(load().qb_gdn_set_wait_limit(int(code), int(polls), err, len(err)), err)

@@ -43,7 +43,9 @@ bool chunked_bwd_ready();
 int64_t chunked_saved_bytes(int Hv, int Hk, int64_t n_chunks, int64_t tokens, bool layer);
 int64_t chunked_ws_bytes(int Hv, int Hk, int N, int64_t n_chunks, int64_t tokens, bool varlen, int op, bool with_saved,
                          bool layer);
-cudaError_t chunked_fwd(const ChunkFwdArgs& a, void* ws, cudaStream_t st);
+// Both report into a status block the caller has initialised (init_status): chunked_fwd into
+// `status` (the one opening ws, or a recomputing backward's own), chunked_bwd into the one opening ws.
+cudaError_t chunked_fwd(const ChunkFwdArgs& a, void* ws, cudaStream_t st, int* status);
 cudaError_t chunked_bwd(const ChunkBwdArgs& a, void* ws, cudaStream_t st);
 
 }  // namespace qbgdn

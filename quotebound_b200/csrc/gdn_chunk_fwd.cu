@@ -1,0 +1,258 @@
+// The forward walk of the tensor-core path: a sequence's chunks in order, 32 state rows per CTA.
+#include "gdn_chunk_impl.cuh"
+
+namespace qbgdn {
+
+// 256 threads: warp w reads TMEM lanes 32 (w & 3) .. + 31 and handles the value columns
+// 16 (w >> 2) .. + 15 of the CTA's 32; thread t holds S[dv0 + 16 (w >> 2) + j][t & 127].
+template <typename Tout>
+__global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_constant__ CUtensorMap vmap,
+                                                              const __grid_constant__ CUtensorMap ymap, StateArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(16) float sg[2][128];
+  __shared__ uint64_t bar_tma[2], bar_mma, bar_drain;
+  __shared__ uint32_t tmem_slot;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, half = warp >> 2, dk = tid & 127;
+  const int dv0 = blockIdx.x * DVT, hv = blockIdx.y, n = blockIdx.z;
+  const int Hv = a.geo.Hv, hk = hv / (Hv / a.geo.Hk);
+  int64_t c_first, nchunks, seq0, seq1;
+  seq_chunks(a.geo, n, c_first, nchunks, seq0, seq1);
+
+  // TMEM: [K; Q] S^T 0, D 64, S update 128, P D 192 (64 columns each: hi and lo halves)
+  const uint32_t cA = 0, cD = 64, cS = 128, cO = 192;
+  if (warp == 0) tc::tmem_alloc(&tmem_slot, 256);
+  if (tid == 0) {
+    tc::mbar_init(&bar_tma[0], 1);
+    tc::mbar_init(&bar_tma[1], 1);
+    tc::mbar_init(&bar_mma, 1);
+    tc::mbar_init(&bar_drain, 1);
+    tc::fence_mbar_init();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = tmem_slot;
+  const uint32_t tl = tc::taddr(tmem, 32 * quad, 0);  // this warp's lanes
+
+  float s[16];  // s[j] = S[dv0 + 16 half + j][dk]
+  {
+    const size_t base = (((size_t)n * Hv + hv) * DV + dv0 + 16 * half) * DK + dk;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) s[j] = a.h0 ? a.h0[base + (size_t)j * DK] : 0.f;
+  }
+
+  // One thread of warp 1 moves everything a chunk reads (the [K; Q], T and P images, the gates and the
+  // value rows) and the checkpoint, so that warp 0's thread issues the MMAs meanwhile and no thread
+  // waits on a global load inside the walk.
+  auto issue_loads = [&](int64_t jc, int buf) {
+    const int64_t cg = c_first + jc;
+    tc::mbar_arrive_expect_tx(&bar_tma[buf], 32768 + 2 * 16384 + 512 + 4096);
+    tc::bulk_load(smem + FW_KQ + buf * 32768, a.KQimg + (size_t)(cg * a.geo.Hk + hk) * 32768, 32768, &bar_tma[buf]);
+    tc::bulk_load(smem + FW_T + buf * 16384, a.Timg + (size_t)(cg * Hv + hv) * 16384, 16384, &bar_tma[buf]);
+    tc::bulk_load(smem + FW_P + buf * 16384, a.Pimg + (size_t)(cg * Hv + hv) * 16384, 16384, &bar_tma[buf]);
+    tc::bulk_load(sg[buf], a.gates + (cg * Hv + hv) * 128, 512, &bar_tma[buf]);
+    tc::tma_load_3d(smem + FW_V + buf * 4096, &vmap, &bar_tma[buf], dv0, hv, (int)(seq0 + jc * C));
+  };
+
+  // Lane l < 16 owns chunk row i = 16 quad + l for the K-side products (E, D) and lane l + 16 the same
+  // row for the Q-side ones (Y, D~, y).
+  const int i_row = 16 * quad + (lane & 15);
+  const bool kside = lane < 16;
+  if (nchunks > 0 && tid == 32) {
+    tc::prefetch_tmap(&vmap);
+    issue_loads(0, 0);
+  }
+  uint32_t ph = 0;
+  bool ok = true;
+  // failure path bookkeeping: chunks whose loads were issued, and whose load wait this thread ran
+  int64_t loads_issued = nchunks > 0 ? 1 : 0, loads_seen = 0;
+  const uint32_t idA = tc::idesc(tc::kBF16, 128, 64, false, true);
+  const uint32_t idT = tc::idesc(tc::kBF16, 128, 64, true, true);
+  int64_t ystage_tok = -1;  // first token of the full chunk whose output rows wait in the staging tile
+
+  // The waits for an MMA round are per thread (the TMEM results are ready for every thread once it has
+  // seen the commit); their outcome joins the chunk's next barrier, where every thread breaks alike.
+  for (int64_t jc = 0; jc < nchunks; ++jc) {
+    const int buf = (int)(jc & 1);
+    const int64_t cg = c_first + jc;
+    const int64_t tok0 = seq0 + jc * C;
+    const int L = (int)min((int64_t)C, seq1 - tok0);
+
+    // 1. the chunk-start state: staged for the bulk store of the checkpoint, and as the [hi | lo]
+    //    operand row dk
+    if (a.ckpt) {  // rounded to tf32: its one reader takes it as a tf32 operand
+      float* ck = reinterpret_cast<float*>(smem + FW_CK) + 16 * half * DK + dk;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) ck[j * DK] = tf32_rna(s[j]);
+    }
+    tc::st_row_hilo16(smem + FW_S, dk, s, half);
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    const bool waits = ok;
+    ok = __syncthreads_and(ok && tc::mbar_wait_or_drain(&bar_tma[buf], (uint32_t)((jc >> 1) & 1), a.err, 10)) != 0;
+    if (waits) loads_seen = jc + 1;
+    tc::fence_after_sync();
+    if (!ok) break;
+    const uint32_t kq = tc::smem_u32(smem + FW_KQ + buf * 32768);
+    // 2. [K; Q] S^T in one pass (M = 128, N = 64: the state's hi and lo halves)
+    if (tid == 0) {
+      mma_run<8, kKmaj128>(tmem + cA, idA, kq, tc::smem_u32(smem + FW_S), false);
+      tc::mma_commit(&bar_mma);
+    }
+    if (tid == 32) {
+      if (a.ckpt) tc::bulk_store(a.ckpt + ((cg * Hv + hv) * DV + dv0) * (size_t)DK, smem + FW_CK, DVT * DK * 4);
+      if (ystage_tok >= 0) tc::tma_store_3d(&ymap, smem + FW_Y, dv0, hv, (int)ystage_tok);  // last chunk's y
+      tc::bulk_commit();
+      if (jc + 1 < nchunks) issue_loads(jc + 1, buf ^ 1);  // the next chunk's tiles
+    }
+    if (jc + 1 < nchunks) loads_issued = jc + 2;
+    const float* gb = sg[buf];
+    const float bi = gb[i_row], be = gb[64 + i_row], gi = __expf(bi), bC = gb[63];
+    float vr[16];  // this row's values (rows past the sequence's end read as zero)
+    {
+      Row16 raw;
+      const uint4* vp = reinterpret_cast<const uint4*>(smem + FW_V + buf * 4096 + i_row * 64 + 32 * half);
+      raw.w[0] = i_row < L ? vp[0] : make_uint4(0, 0, 0, 0);
+      raw.w[1] = i_row < L ? vp[1] : make_uint4(0, 0, 0, 0);
+      cvt_row16(raw, vr);
+    }
+    ok = ok && tc::mbar_wait_or_drain(&bar_mma, ph, a.err, 11);
+    ph ^= 1;
+    tc::fence_after_sync();
+    // 3. K side: E = diag(beta) (V - diag(gamma) K S^T) as the [hi | lo] operand; Q side: gamma Q S^T
+    float yp[16];
+    const size_t ptile = ((size_t)(cg * Hv + hv) * (DV / DVT) + blockIdx.x) * 2048;  // this CTA's tile
+    {
+      // one instruction stream for the lane pair: the K-side lane forms E's columns 0-7 from its K S^T
+      // row, the Q-side lane columns 8-15 from the K-side lane's; the Q-side lane keeps gamma Q S^T
+      tmem_ld_hl16(tl + cA, half, yp);
+      float e8[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float ks = __shfl_xor_sync(0xffffffffu, yp[8 + j], 16);
+        e8[j] = be * ((kside ? vr[j] : vr[8 + j]) - gi * (kside ? yp[j] : ks));
+      }
+      st_hilo8(smem + FW_E, i_row, e8, 2 * half + (kside ? 0 : 1));
+#pragma unroll
+      for (int j = 0; j < 16; ++j) yp[j] *= gi;
+    }
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    ok = __syncthreads_and(ok) != 0;
+    tc::fence_after_sync();
+    if (!ok) break;
+    // 4. D = T E  ([T_hi; T_lo] stacked: row i's two products in lanes l and l + 16)
+    if (tid == 0) {
+      mma_run<4, kKmaj128>(tmem + cD, idA, tc::smem_u32(smem + FW_T + buf * 16384), tc::smem_u32(smem + FW_E), false);
+      tc::mma_commit(&bar_mma);
+    }
+
+    ok = ok && tc::mbar_wait_or_drain(&bar_mma, ph, a.err, 12);
+    ph ^= 1;
+    tc::fence_after_sync();
+    {
+      // both lanes of the pair hold row i of D; one instruction stream for both: the K-side lane writes
+      // D as the [hi | lo] operand of P D and columns 0-7 of the tf32 copy, the Q-side lane
+      // D~ = diag(lambda) D for the state update and columns 8-15 of the copy
+      float d[16];
+      tmem_ld_hl16_pair(tl + cD, half, d);
+      // (the other staging buffer's store was read before the last chunk's final barrier)
+      if (a.Ds) {  // tf32-rounded: the gradient kernel's tf32 operand, loaded as is
+        uint8_t* row = smem + FW_DS + buf * 8192 + i_row * 128;
+        const int q0 = 4 * half + (kside ? 0 : 2);
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          float x[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) x[e] = tf32_rna(kside ? d[4 * q + e] : d[8 + 4 * q + e]);
+          *reinterpret_cast<float4*>(row + (((q0 + q) ^ (i_row & 7)) << 4)) = make_float4(x[0], x[1], x[2], x[3]);
+        }
+      }
+      const float sc = kside ? 1.f : __expf(bC - bi);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) d[j] *= sc;
+      tc::st_row_hilo16(smem + (kside ? FW_D : FW_DT), i_row, d, half);
+    }
+    if (tid == 32) tc::bulk_wait_read();  // the staging buffers are rewritten below and next chunk
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    ok = __syncthreads_and(ok) != 0;
+    tc::fence_after_sync();
+    if (!ok) break;
+    // 5. S update^T = K^T D~ (M = 128 dk rows);  O2 = P D ([P_hi; P_lo] stacked)
+    if (tid == 0) {
+      mma_run<4, kKT>(tmem + cS, idT, kq, tc::smem_u32(smem + FW_DT), false);
+      mma_run<4, kKmaj128>(tmem + cO, idA, tc::smem_u32(smem + FW_P + buf * 16384), tc::smem_u32(smem + FW_D), false);
+      tc::mma_commit(&bar_mma);
+    }
+    if (tid == 32 && a.Ds) {
+      tc::bulk_store(a.Ds + ptile, smem + FW_DS + buf * 8192, 8192);
+      tc::bulk_commit();
+    }
+    ok = ok && tc::mbar_wait_or_drain(&bar_mma, ph, a.err, 13);
+    ph ^= 1;
+    tc::fence_after_sync();
+    {
+      float u[16], o2[16];
+      tmem_ld_hl16x2(tl + cS, tl + cO, half, u, o2);
+      const float gC = __expf(bC);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) s[j] = fmaf(gC, s[j], u[j]);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) u[j] = o2[j] + __shfl_xor_sync(0xffffffffu, o2[j], 16);
+      // both lanes hold P D's row; the K-side lane writes columns 0-7 (with the Q-side lane's gamma Q S^T),
+      // the Q-side lane columns 8-15
+      const int hc = kside ? 0 : 1;
+      float y8[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float qy = __shfl_xor_sync(0xffffffffu, yp[j], 16);
+        y8[j] = kside ? u[j] + qy : u[8 + j] + yp[8 + j];
+      }
+      if (L == C)  // a full chunk goes out by one TMA store after the next barrier
+        store_row8<Tout>(reinterpret_cast<Tout*>(smem + FW_Y) + i_row * DVT + 16 * half + 8 * hc, y8);
+      else if (i_row < L)  // the rows after a sequence's end belong to the next sequence: not written
+        store_row8<Tout>(static_cast<Tout*>(a.y) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0 + 16 * half + 8 * hc, y8);
+    }
+    ystage_tok = L == C ? tok0 : -1;
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+  }
+  ok = __syncthreads_and(ok) != 0;  // (the last round's waits were per thread)
+  if (!ok) {  // a wait gave up: everything still in flight lands before the TMEM and the CTA go
+    if (tid == 0) {  // every product this thread issued
+      tc::mma_commit(&bar_drain);
+      tc::mbar_drain(&bar_drain, 0);
+    }
+    if (tid == 32)
+      for (int64_t j = loads_seen; j < loads_issued; ++j) tc::mbar_drain(&bar_tma[j & 1], (uint32_t)((j >> 1) & 1));
+  }
+  if (ok && ystage_tok >= 0 && tid == 32) {  // the last chunk's output rows
+    tc::tma_store_3d(&ymap, smem + FW_Y, dv0, hv, (int)ystage_tok);
+    tc::bulk_commit();
+  }
+  if (tid == 32) tc::bulk_wait();
+  if (ok && a.hT) {
+    float* dst = a.hT + (((size_t)n * Hv + hv) * DV + dv0 + 16 * half) * DK + dk;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) dst[(size_t)j * DK] = s[j];
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tmem, 256);
+}
+
+cudaError_t launch_chunk_fwd_state(const CUtensorMap& vmap, const CUtensorMap& ymap, const StateArgs& a, int Hv, int N,
+                                   bool out_bf16, cudaStream_t st) {
+  auto kern = out_bf16 ? gdn_chunk_fwd_state<__nv_bfloat16> : gdn_chunk_fwd_state<float>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FW_SMEM);
+  if (e != cudaSuccess) return e;
+  kern<<<dim3(DV / DVT, Hv, N), 256, FW_SMEM, st>>>(vmap, ymap, a);
+  note_launch();
+  return cudaGetLastError();
+}
+
+}  // namespace qbgdn

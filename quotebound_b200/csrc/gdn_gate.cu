@@ -2,6 +2,7 @@
 // :22-33) and its chain rule.  HBM-bound elementwise work: one warp per (token, key head) row of
 // q and k, coalesced 16-byte loads, warp-shuffle reductions; per-head parameter gradients summed
 // in a fixed order (block partials, then one block over the partials) with no atomics.
+#include <cuda.h>
 #include <stdarg.h>
 #include <stdio.h>
 
@@ -198,7 +199,10 @@ static __device__ __align__(256) float g_gate_scratch[kGateScratchFloats];
 
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mu;
-float* g_scratch_ptr[kMaxDevices];  // device address of g_gate_scratch, per device
+// device address of g_gate_scratch per device, and the context it was looked up in: a device reset or
+// a re-created primary context loads the module anew, so a new context means a fresh lookup
+float* g_scratch_ptr[kMaxDevices];
+CUcontext g_scratch_ctx[kMaxDevices];
 
 int noalloc_fail(char* err, int errlen, const char* fmt, ...) {
   if (err && errlen > 0) {
@@ -211,18 +215,33 @@ int noalloc_fail(char* err, int errlen, const char* fmt, ...) {
   return -1;
 }
 
-// The device address of the scratch array on the current device, looked up once per device.
+// The device address of the scratch array on the current device, looked up once per device and
+// context (cudaGetSymbolAddress with that device current).
 cudaError_t scratch_on_current_device(float** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  static CUresult (*get_ctx)(CUcontext*) = nullptr;
+  if (!get_ctx) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return cudaErrorNotSupported;
+    get_ctx = reinterpret_cast<CUresult (*)(CUcontext*)>(fn);
+  }
+  CUcontext ctx = nullptr;
+  if (get_ctx(&ctx) != CUDA_SUCCESS) return cudaErrorDeviceUninitialized;
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_ptr[dev]) {
+  if (!ctx || !g_scratch_ptr[dev] || g_scratch_ctx[dev] != ctx) {
+    // (the lookup itself makes the device's primary context current when none is yet)
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_gate_scratch);
     if (e != cudaSuccess) return e;
+    if (get_ctx(&ctx) != CUDA_SUCCESS) return cudaErrorDeviceUninitialized;
     g_scratch_ptr[dev] = static_cast<float*>(p);
+    g_scratch_ctx[dev] = ctx;
   }
   *out = g_scratch_ptr[dev];
   return cudaSuccess;

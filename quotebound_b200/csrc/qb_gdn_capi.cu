@@ -13,9 +13,11 @@
 
 #include "../../include/qb_gdn.h"
 #include "gdn_chunk.cuh"
+#include "gdn_common.cuh"
 #include "gdn_gate.cuh"
 #include "gdn_simt.cuh"
 #include "launch_count.cuh"
+#include "status.cuh"
 
 using namespace qbgdn;
 
@@ -23,6 +25,45 @@ namespace qbgdn {
 static std::atomic<int64_t> g_launches{0};
 void note_launch(int64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 int64_t launches() { return g_launches.load(std::memory_order_relaxed); }
+
+// ---- the status block (status.cuh) ----
+static std::atomic<int> g_test_code{0};
+static std::atomic<uint32_t> g_test_polls{0};
+void set_test_wait_limit(int code, uint32_t polls) {
+  g_test_polls.store(polls);
+  g_test_code.store(code);
+}
+
+__global__ void status_init_kernel(int* status, int code, uint32_t polls) {
+  const int i = threadIdx.x;
+  if (i < kStatusBytes / 4) status[i] = i == 4 ? code : i == 5 ? (int)polls : 0;
+}
+
+cudaError_t init_status(int* status, cudaStream_t st) {
+  const int code = g_test_code.load();
+  if (code == 0) return cudaMemsetAsync(status, 0, kStatusBytes, st);
+  status_init_kernel<<<1, kStatusBytes / 4, 0, st>>>(status, code, g_test_polls.load());
+  note_launch();
+  return cudaGetLastError();
+}
+
+// Counts the entries of x that are NaN or infinite into *count (one atomic add per block).
+template <typename T>
+__global__ void count_nonfinite_kernel(const T* __restrict__ x, int64_t n, unsigned long long* count) {
+  unsigned c = 0;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    c += isfinite(to_f(x[i])) ? 0u : 1u;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+  __shared__ unsigned part[32];
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = c;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long t = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += part[w];
+    if (t) atomicAdd(count, t);
+  }
+}
 }  // namespace qbgdn
 
 namespace {
@@ -114,8 +155,10 @@ int64_t saved_bytes_of(const qb_gdn_desc* d, const Plan& p) {
 
 int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
 
-// Row-parallel workspace: [chunk_off (varlen)] [dq_part] [dk_part] [dg_part] [dbeta_part] [saved (recompute)]
+// Row-parallel workspace: [status block] [chunk_off (varlen)] [dq_part] [dk_part] [dg_part] [dbeta_part]
+// [saved (recompute)]
 struct SimtWs {
+  int* status;
   int64_t* chunk_off;
   float *dq_part, *dk_part, *dg_part, *dbeta_part;
   float* saved;
@@ -130,6 +173,7 @@ int64_t simt_ws_bytes(const qb_gdn_desc* d, const Plan& p, int op, bool with_sav
     return at;
   };
   SimtWs w{};
+  w.status = (int*)take(kStatusBytes);
   w.chunk_off = (int64_t*)take(p.varlen ? (p.N + 1) * 8 : 0);
   if (op == QB_OP_BWD) {
     const int64_t parts = p.tokens * d->Hv * (int64_t)p.NB;
@@ -209,13 +253,15 @@ int qb_gdn_layer_fwd(const qb_gdn_desc* d, const void* q, const void* k, const v
   if (!ws || ws_bytes < need || !aligned(ws, 256))
     return fail(err, errlen, "gated delta layer forward: a 256-byte aligned workspace of %lld bytes is needed (got %lld)",
                 (long long)need, (long long)ws_bytes);
+  cudaError_t e = init_status((int*)ws, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "gated delta layer forward", err, errlen);
   if (p.tokens == 0) return 0;
   ChunkFwdArgs f{};
   f.B = d->B, f.T = d->T, f.Hk = d->Hk, f.Hv = d->Hv, f.Dk = d->Dk, f.Dv = d->Dv, f.N = p.N, f.n_chunks = p.n_chunks;
   f.cu = d->cu_seqlens, f.q = q, f.k = k, f.v = v, f.h0 = h0, f.y = y, f.hT = hT, f.saved = saved;
   f.in_bf16 = 1, f.out_bf16 = d->out_dtype == QB_DTYPE_BF16;
   f.a_raw = a, f.b_raw = b, f.A_log = A_log, f.dt_bias = dt_bias;
-  cudaError_t e = chunked_fwd(f, ws, (cudaStream_t)stream);
+  e = chunked_fwd(f, ws, (cudaStream_t)stream, (int*)ws);
   return e == cudaSuccess ? 0 : cuda_fail(e, "gated delta layer forward", err, errlen);
 }
 
@@ -237,6 +283,7 @@ int qb_gdn_layer_bwd(const qb_gdn_desc* d, const void* q, const void* k, const v
     return fail(err, errlen, "gated delta layer backward: a 256-byte aligned workspace of %lld bytes is needed (got %lld)",
                 (long long)need, (long long)ws_bytes);
   cudaStream_t st = (cudaStream_t)stream;
+  if (cudaError_t e = init_status((int*)ws, st)) return cuda_fail(e, "gated delta layer backward", err, errlen);
   if (p.tokens == 0) {
     cudaError_t e = cudaMemsetAsync(dA_log, 0, d->Hv * 4, st);
     if (e == cudaSuccess) e = cudaMemsetAsync(ddt_bias, 0, d->Hv * 4, st);
@@ -272,12 +319,13 @@ int qb_gdn_fwd(const qb_gdn_desc* d, const void* q, const void* k, const void* v
       (hT && !aligned(hT, 16)) || (saved && !aligned(saved, 256)))
     return fail(err, errlen, "gated delta forward: q, k, v, y, h0, hT need 16-byte alignment and saved 256-byte");
   const int64_t need = ws_bytes_of(d, p, QB_OP_FWD, false);
-  if (need > 0 && (!ws || ws_bytes < need))
+  if (!ws || ws_bytes < need)
     return fail(err, errlen, "gated delta forward: workspace of %lld bytes needed (got %lld)", (long long)need,
                 (long long)ws_bytes);
-  if (need > 0 && !aligned(ws, 256)) return fail(err, errlen, "gated delta forward: workspace needs 256-byte alignment");
-  if (p.tokens == 0) return 0;
+  if (!aligned(ws, 256)) return fail(err, errlen, "gated delta forward: workspace needs 256-byte alignment");
   cudaStream_t st = (cudaStream_t)stream;
+  if (cudaError_t e = init_status((int*)ws, st)) return cuda_fail(e, "gated delta forward", err, errlen);
+  if (p.tokens == 0) return 0;
   if (p.chunked) {
     ChunkFwdArgs a{};
     a.B = d->B, a.T = d->T, a.Hk = d->Hk, a.Hv = d->Hv, a.Dk = d->Dk, a.Dv = d->Dv, a.N = p.N;
@@ -286,7 +334,7 @@ int qb_gdn_fwd(const qb_gdn_desc* d, const void* q, const void* k, const void* v
     a.q = q, a.k = k, a.v = v, a.g = g, a.beta = beta, a.h0 = h0, a.y = y, a.hT = hT;
     a.saved = saved;
     a.in_bf16 = d->in_dtype == QB_DTYPE_BF16, a.out_bf16 = d->out_dtype == QB_DTYPE_BF16;
-    cudaError_t e = chunked_fwd(a, ws, st);
+    cudaError_t e = chunked_fwd(a, ws, st, (int*)ws);
     return e == cudaSuccess ? 0 : cuda_fail(e, "gated delta forward (chunked)", err, errlen);
   }
   SimtWs w;
@@ -319,11 +367,12 @@ int qb_gdn_bwd(const qb_gdn_desc* d, const void* q, const void* k, const void* v
       (dh0 && !aligned(dh0, 16)) || (saved && !aligned(saved, 256)))
     return fail(err, errlen, "gated delta backward: tensors need 16-byte alignment and saved 256-byte");
   const int64_t need = ws_bytes_of(d, p, QB_OP_BWD, saved == nullptr);
-  if (need > 0 && (!ws || ws_bytes < need))
+  if (!ws || ws_bytes < need)
     return fail(err, errlen, "gated delta backward: workspace of %lld bytes needed (got %lld)", (long long)need,
                 (long long)ws_bytes);
-  if (need > 0 && !aligned(ws, 256)) return fail(err, errlen, "gated delta backward: workspace needs 256-byte alignment");
+  if (!aligned(ws, 256)) return fail(err, errlen, "gated delta backward: workspace needs 256-byte alignment");
   cudaStream_t st = (cudaStream_t)stream;
+  if (cudaError_t e = init_status((int*)ws, st)) return cuda_fail(e, "gated delta backward", err, errlen);
   if (p.tokens == 0) {
     if (dh0 && dhT) {
       cudaError_t e = cudaMemcpyAsync(dh0, dhT, (size_t)p.N * d->Hv * d->Dv * d->Dk * 4, cudaMemcpyDeviceToDevice, st);
@@ -368,7 +417,7 @@ int qb_gdn_bwd(const qb_gdn_desc* d, const void* q, const void* k, const void* v
       f.q = q, f.k = k, f.v = v, f.g = g, f.beta = beta, f.h0 = h0, f.y = dv, f.hT = nullptr;
       f.saved = ck;
       f.in_bf16 = in_bf16, f.out_bf16 = out_bf16;
-      if ((e = chunked_fwd(f, w.fwd_ws, st)) != cudaSuccess)
+      if ((e = chunked_fwd(f, w.fwd_ws, st, w.status)) != cudaSuccess)
         return cuda_fail(e, "gated delta backward (recompute)", err, errlen);
     } else {
       SimtArgs f = a;
@@ -389,6 +438,43 @@ int qb_gdn_bwd(const qb_gdn_desc* d, const void* q, const void* k, const void* v
   r.dq = dq, r.dk = dk, r.dg = dg, r.dbeta = dbeta;
   if ((e = simt_reduce_parts(r, out_bf16, st)) != cudaSuccess) return cuda_fail(e, "gated delta backward", err, errlen);
   return 0;
+}
+
+int qb_gdn_status(const void* ws, int32_t* code, void* stream, char* err, int errlen) {
+  if (!ws || !code) return fail(err, errlen, "gated delta status: ws and code must be non-null");
+  if (!aligned(ws, 256)) return fail(err, errlen, "gated delta status: ws is not a workspace (256-byte alignment)");
+  cudaStream_t st = (cudaStream_t)stream;
+  int32_t v = 0;
+  cudaError_t e = cudaMemcpyAsync(&v, ws, sizeof v, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(e, "gated delta status", err, errlen);
+  *code = v;
+  return 0;
+}
+
+int qb_gdn_set_wait_limit(int32_t code, int32_t polls, char* err, int errlen) {
+  if (code < 0 || polls < 1) return fail(err, errlen, "gated delta wait limit: code %d >= 0 and polls %d >= 1", code, polls);
+  set_test_wait_limit(code, (uint32_t)polls);
+  return 0;
+}
+
+int qb_gdn_count_nonfinite(const void* x, int64_t n, int32_t dtype, unsigned long long* count, void* stream, char* err,
+                           int errlen) {
+  if (n < 0 || !dtype_ok(dtype)) return fail(err, errlen, "gated delta finite check: bad arguments (n %lld, dtype %d)",
+                                             (long long)n, dtype);
+  if (!count || (n > 0 && !x)) return fail(err, errlen, "gated delta finite check: null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t e = cudaMemsetAsync(count, 0, sizeof *count, st);
+  if (e == cudaSuccess && n > 0) {
+    const unsigned blocks = (unsigned)std::min<int64_t>((n + 255) / 256, 148 * 8);
+    if (dtype == QB_DTYPE_BF16)
+      count_nonfinite_kernel<<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), n, count);
+    else
+      count_nonfinite_kernel<<<blocks, 256, 0, st>>>(static_cast<const float*>(x), n, count);
+    note_launch();
+    e = cudaGetLastError();
+  }
+  return e == cudaSuccess ? 0 : cuda_fail(e, "gated delta finite check", err, errlen);
 }
 
 static int check_rows(int32_t N, int32_t V, int32_t Hk, int32_t Hv, int32_t Dk, int32_t Dv, int32_t in_dtype,

@@ -62,19 +62,39 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 }
 
 // Bounded wait for the phase with the given parity to complete.  Gives up after about one second of
-// wall time (checked every 256 polls; each poll may itself suspend briefly) or 2^24 polls, writes
-// `code` into *err and returns false; the caller then skips its remaining work, frees its TMEM and
-// returns.  Never spins forever, never traps.
+// wall time (checked every 256 polls; each poll may itself suspend briefly) or 2^24 polls, records
+// `code` in the status block `err` (the first failure of a call wins) and returns false; the caller
+// then skips its remaining work, waits (again bounded, with no code) for the copies and products it
+// still has in flight, frees its TMEM and returns.  Never spins forever, never traps.
+//
+// err points at the status block that opens every workspace (status.cuh): err[0] the code,
+// err[4] / err[5] a test hook -- when err[4] equals `code`, this wait gives up after err[5] polls,
+// so that a test can make one named wait run out on a normal input.  The hook is read only once the
+// first poll has failed.
 constexpr uint32_t kMaxPolls = 1u << 24;
 constexpr uint64_t kMaxWaitNs = 1000000000ull;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
+  uint32_t limit = kMaxPolls;
+  if (err && code > 0 && *(volatile int*)(err + 4) == code) limit = *(volatile uint32_t*)(err + 5);
   const uint64_t t0 = globaltimer_ns();
-  for (uint32_t i = 1; i < kMaxPolls; ++i) {
+  for (uint32_t i = 1; i < limit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255) == 0 && globaltimer_ns() - t0 > kMaxWaitNs) break;
   }
-  if (err) atomicExch(err, code);
+  if (err) atomicCAS(err, 0, code);
+  return false;
+}
+// The failure path's wait for work still in flight: the full limits, nothing recorded.
+__device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity) {
+  return mbar_wait(bar, parity, nullptr, 0);
+}
+// mbar_wait for a phase whose copies or products were issued; when it gives up, the same phase is
+// waited for again (mbar_drain), so that they have landed before anything reads or reuses their
+// buffers.  Returns whether the first wait succeeded.
+__device__ __forceinline__ bool mbar_wait_or_drain(uint64_t* bar, uint32_t parity, int* err, int code) {
+  if (mbar_wait(bar, parity, err, code)) return true;
+  mbar_drain(bar, parity);
   return false;
 }
 

@@ -22,8 +22,8 @@ import ctypes
 
 import torch
 
-from . import _lib
-from ._lib import Desc, QbError, check, err_buf, load
+from . import _lib, checks
+from ._lib import Desc, QbError, err_buf, load
 
 __all__ = ["gated_delta", "gated_delta_trainable", "gated_delta_vjp", "gated_delta_fwd", "gated_delta_bwd",
            "saved_bytes", "workspace_bytes", "QbError"]
@@ -124,10 +124,12 @@ def _check_inputs(q, k, v, g, beta, state, n_seqs):
         raise ValueError("gated delta: tensors must be on a CUDA device (the library has no CPU path)")
 
 
-def gated_delta_fwd(q, k, v, g, beta, state=None, *, cu_seqlens=None, save=False, out_dtype=None, algo=0):
+def gated_delta_fwd(q, k, v, g, beta, state=None, *, cu_seqlens=None, save=False, out_dtype=None, algo=0,
+                    check=None):
     """The forward op.  Returns (y, final_state, saved) — saved is None unless ``save``.
 
-    With ``cu_seqlens`` (N + 1 offsets) the batch is B = 1 and ``state`` is [N, Hv, Dv, Dk]."""
+    With ``cu_seqlens`` (N + 1 offsets) the batch is B = 1 and ``state`` is [N, Hv, Dv, Dk].  ``check``
+    (default: ``QB_GDN_CHECK``) reads back the device status and checks y and the state for NaN / inf."""
     dev = q.device
     adt = _act_dtype(q, k, v)
     q, k, v = _prep(q, adt), _prep(k, adt), _prep(v, adt)
@@ -146,18 +148,21 @@ def gated_delta_fwd(q, k, v, g, beta, state=None, *, cu_seqlens=None, save=False
     hT = torch.empty(n_seqs, Hv, Dv, Dk, dtype=torch.float32, device=dev)
     saved = _empty_bytes(saved_bytes(d), dev) if save else None
     wsb = workspace_bytes(d, _lib.QB_OP_FWD)
-    ws = _empty_bytes(wsb, dev) if wsb > 0 else None
+    ws = _empty_bytes(wsb, dev)
     err = err_buf()
     rc = load().qb_gdn_fwd(ctypes.byref(d), _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(state), _ptr(y),
                            _ptr(hT), _ptr(saved), _ptr(ws), wsb, _stream(dev), err, len(err))
-    check(rc, err)
+    _lib.check(rc, err)
+    if checks.enabled(check):
+        checks.require_ok("gated delta forward", ws)
+        checks.require_finite("gated delta forward", y=y, state=hT)
     if y_dtype != y.dtype:
         y = y.to(y_dtype)
     return y, hT, saved
 
 
 def gated_delta_bwd(q, k, v, g, beta, state, dy, dstate=None, *, saved=None, cu_seqlens=None, algo=0,
-                    grad_dtype=None):
+                    grad_dtype=None, check=None):
     """Cotangents (dq, dk, dv, dg, dbeta, dstate0) of the forward given dy and dstate (the final state's)."""
     dev = q.device
     adt = _act_dtype(q, k, v, dy)
@@ -180,12 +185,15 @@ def gated_delta_bwd(q, k, v, g, beta, state, dy, dstate=None, *, saved=None, cu_
     B, T, Hk, Dk = q.shape
     dh0 = torch.empty(n_seqs, v.shape[2], v.shape[3], Dk, dtype=torch.float32, device=dev)
     wsb = workspace_bytes(d, _lib.QB_OP_BWD)
-    ws = _empty_bytes(wsb, dev) if wsb > 0 else None
+    ws = _empty_bytes(wsb, dev)
     err = err_buf()
     rc = load().qb_gdn_bwd(ctypes.byref(d), _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(state), _ptr(dy),
                            _ptr(dstate), _ptr(saved), _ptr(dq), _ptr(dk), _ptr(dv), _ptr(dg), _ptr(dbeta), _ptr(dh0),
                            _ptr(ws), wsb, _stream(dev), err, len(err))
-    check(rc, err)
+    _lib.check(rc, err)
+    if checks.enabled(check):
+        checks.require_ok("gated delta backward", ws)
+        checks.require_finite("gated delta backward", dq=dq, dk=dk, dv=dv, dg=dg, dbeta=dbeta, dstate=dh0)
     return dq, dk, dv, dg, dbeta, dh0
 
 

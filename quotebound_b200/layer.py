@@ -14,8 +14,8 @@ import ctypes
 
 import torch
 
-from . import _lib
-from ._lib import check, err_buf, load
+from . import _lib, checks
+from ._lib import err_buf, load
 from .deltanet import _cu_pair, _empty_bytes, _prep, _ptr, _stream, make_desc
 
 __all__ = ["gated_delta_layer_fwd", "gated_delta_layer_bwd", "gated_delta_layer"]
@@ -36,8 +36,8 @@ def _ws(d, op, dev):
 
 
 def gated_delta_layer_fwd(q, k, v, a, b, A_log, dt_bias, state=None, *, cu_seqlens=None, save=False,
-                          out_dtype=torch.bfloat16, algo=0):
-    """y [B, T, Hv, Dv], final state(s), saved (or None)."""
+                          out_dtype=torch.bfloat16, algo=0, check=None):
+    """y [B, T, Hv, Dv], final state(s), saved (or None).  ``check`` as in deltanet.gated_delta_fwd."""
     dev = q.device
     q, k, v = _prep(q, torch.bfloat16), _prep(k, torch.bfloat16), _prep(v, torch.bfloat16)
     a, b = _prep(a, torch.float32), _prep(b, torch.float32)
@@ -61,13 +61,16 @@ def gated_delta_layer_fwd(q, k, v, a, b, A_log, dt_bias, state=None, *, cu_seqle
     rc = load().qb_gdn_layer_fwd(ctypes.byref(d), _ptr(q), _ptr(k), _ptr(v), _ptr(a), _ptr(b), _ptr(A_log),
                                  _ptr(dt_bias), _ptr(state), _ptr(y), _ptr(hT), _ptr(saved), _ptr(ws), wsb,
                                  _stream(dev), err, len(err))
-    check(rc, err)
+    _lib.check(rc, err)
+    if checks.enabled(check):
+        checks.require_ok("gated delta layer forward", ws)
+        checks.require_finite("gated delta layer forward", y=y, state=hT)
     return y, hT, saved
 
 
 def gated_delta_layer_bwd(q, k, v, a, b, A_log, dt_bias, state, dy, dstate=None, *, saved=None, cu_seqlens=None,
-                          grad_dtype=torch.bfloat16, algo=0):
-    """(dq, dk, dv, da, db, dA_log, ddt_bias, dstate0)."""
+                          grad_dtype=torch.bfloat16, algo=0, check=None):
+    """(dq, dk, dv, da, db, dA_log, ddt_bias, dstate0).  ``check`` as in deltanet.gated_delta_fwd."""
     dev = q.device
     q, k, v, dy = (_prep(t, torch.bfloat16) for t in (q, k, v, dy))
     a, b = _prep(a, torch.float32), _prep(b, torch.float32)
@@ -95,7 +98,11 @@ def gated_delta_layer_bwd(q, k, v, a, b, A_log, dt_bias, state, dy, dstate=None,
                                  _ptr(dt_bias), _ptr(state), _ptr(dy), _ptr(dstate), _ptr(saved), _ptr(dq), _ptr(dk),
                                  _ptr(dv), _ptr(da), _ptr(db), _ptr(dA), _ptr(ddt), _ptr(dh0), _ptr(ws), int(n),
                                  _stream(dev), err, len(err))
-    check(rc, err)
+    _lib.check(rc, err)
+    if checks.enabled(check):
+        checks.require_ok("gated delta layer backward", ws)
+        checks.require_finite("gated delta layer backward", dq=dq, dk=dk, dv=dv, da=da, db=db, dA_log=dA,
+                              ddt_bias=ddt, dstate=dh0)
     return dq, dk, dv, da, db, dA, ddt, dh0
 
 

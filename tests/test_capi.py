@@ -161,3 +161,33 @@ def test_layer_path_refuses_what_the_chunked_kernels_cannot_take(L, bad):
 def test_unknown_op_is_refused(L):
     n, e = ws_or_err(L, desc(), 9)
     assert n == -1 and "unknown op" in e
+
+
+def test_status_and_checks_reject_bad_arguments(L):
+    """qb_gdn_status, qb_gdn_set_wait_limit and qb_gdn_count_nonfinite validate on the host."""
+    err = _lib.err_buf()
+    code = ctypes.c_int32(7)
+    assert L.qb_gdn_status(None, ctypes.byref(code), None, err, len(err)) == -1
+    assert b"non-null" in err.value and code.value == 7
+    assert L.qb_gdn_status(ctypes.c_void_p(4096 + 16), ctypes.byref(code), None, err, len(err)) == -1
+    assert b"alignment" in err.value
+    assert L.qb_gdn_set_wait_limit(-1, 1, err, len(err)) == -1
+    assert L.qb_gdn_set_wait_limit(1, 0, err, len(err)) == -1
+    assert L.qb_gdn_count_nonfinite(None, 10, _lib.QB_DTYPE_F32, None, None, err, len(err)) == -1
+    assert L.qb_gdn_count_nonfinite(None, -1, _lib.QB_DTYPE_F32, None, None, err, len(err)) == -1
+    assert L.qb_gdn_count_nonfinite(None, 1, 9, None, None, err, len(err)) == -1
+
+
+@pytest.mark.parametrize("op", [_lib.QB_OP_FWD, _lib.QB_OP_BWD, _lib.QB_OP_LAYER_FWD, _lib.QB_OP_LAYER_BWD])
+@pytest.mark.parametrize("dk,dt", [(128, _lib.QB_DTYPE_BF16), (32, _lib.QB_DTYPE_F32)])
+def test_every_workspace_holds_the_status_block(L, op, dk, dt):
+    """Every recurrence call's workspace opens with the 256-byte status block, even when the kernels
+    need no scratch (the row-parallel forward)."""
+    d = desc(Dk=dk, Dv=dk, in_dtype=dt, out_dtype=dt)
+    err = _lib.err_buf()
+    n = L.qb_gdn_workspace_bytes(ctypes.byref(d), op, err, len(err))
+    if op in (_lib.QB_OP_LAYER_FWD, _lib.QB_OP_LAYER_BWD):
+        # the fused layer path needs the tensor-core shape and, for its tensor maps, a CUDA driver
+        assert n == -1 if dk != 128 else (n == -1 and b"chunked" in err.value) or n >= 256
+    else:
+        assert n >= 256, err.value

@@ -4,7 +4,8 @@ only their input and output buffers, hosts that keep cudaMalloc/cudaFree (which 
 device) off the hot path.  Its partial sums live in a fixed array inside the library instead of a
 caller workspace.  Checked through the C ABI against qb_gdn_gate_bwd, the entry point with a
 workspace, on two calls in a row with different inputs and sizes (the shared array keeps the first
-call's contents, which must not leak into the second).
+call's contents, which must not leak into the second), and against the CPU oracle's gate backward
+with the gate tests' tolerance.
 
 Named to be collected last: a run that stops at the first failure has run every other test first.
 """
@@ -13,6 +14,7 @@ import ctypes
 import pytest
 import torch
 
+from oracle import oracle
 from quotebound_b200 import _lib, build
 
 pytestmark = pytest.mark.gpu
@@ -76,6 +78,11 @@ def test_no_alloc_matches_workspace_entry_on_two_calls():
             # the tolerance of the gate tests (rel-L2 <= 1e-5); the same kernels run, so the bits agree too
             assert _rel(got[n], want[n]) <= 1e-5, n
             assert torch.equal(got[n], want[n]), n
+        # and against the oracle (rel-L2 <= 1e-5, as the gate tests bound the entry point with a workspace)
+        f = lambda t: t.float().cpu().numpy()
+        ref = oracle.gate_bwd(*(f(x[n]) for n in ("q", "k", "a", "b", "A_log", "dt", "dqn", "dkn", "dg", "dbeta")))
+        for n, w in zip(("dq", "dk", "da", "db", "dA", "ddt"), ref):
+            assert _rel(got[n].cpu(), torch.from_numpy(w)) <= 1e-5, n
 
 
 def test_no_alloc_refuses_more_heads_than_its_scratch_holds():
