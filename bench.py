@@ -50,6 +50,7 @@ def parse():
                     help="c1 4B layer (default), c2 batched split over GPUs, c3 varlen (one GPU), c4 verify (one GPU)")
     ap.add_argument("--algo", type=int, default=0, help="0 auto, 1 row-parallel, 2 chunked")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-c2", action="store_true", help="skip the config 2 strong-scaling sub-result")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of a CUDA graph of the step")
     return ap.parse_args()
@@ -66,9 +67,11 @@ def bytes_per_token(Hk, Hv, Dk, Dv, act=2):
     return fwd, bwd
 
 
-# DRAM bytes (read + write) per launch of the dominant op, from one ncu capture of this bench's workload
-# (profiles/gdn_chunk_config1.md, profiles/gdn_verify_config4.md); None where no capture was made.
+# DRAM bytes (read + write) per launch of the dominant op, copied from one ncu capture of this bench's
+# workload (dram__bytes_read.sum + dram__bytes_write.sum); a constant, so it goes stale when the kernels
+# change and is refreshed from a new capture then.  None where no capture was made.
 TRAFFIC = {("c1", "layer_bwd"): 474.6e6, ("c4", "verify"): 550.8e6}
+TRAFFIC_NOTE = "constant from one ncu capture of this workload (not measured in this run)"
 
 
 def load_peaks():
@@ -82,22 +85,61 @@ def load_peaks():
 
 # ---- clocks during the timed region ----
 class ClockSampler:
+    """SM clock and throttle reasons sampled during the timed region.  NVML is polled about every 0.5 ms (the
+    timed region of one workload is tens of milliseconds, too short for nvidia-smi's 200 ms period);
+    nvidia-smi -lms 200 is the fallback when NVML cannot be loaded."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, index):
         self.index = index
         self.proc = None
+        self.thread = None
         self.lines = []
+        self.sm = []
+        self.reasons = set()
+        self.max_mhz = None
+        self.source = None
+        self._stop = threading.Event()
 
     def start(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            bits = {"hw_slowdown": pynvml.nvmlClocksThrottleReasonHwSlowdown,
+                    "hw_thermal_slowdown": getattr(pynvml, "nvmlClocksThrottleReasonHwThermalSlowdown", 0x40),
+                    "sw_thermal_slowdown": getattr(pynvml, "nvmlClocksThrottleReasonSwThermalSlowdown", 0x20),
+                    "sw_power_cap": pynvml.nvmlClocksThrottleReasonSwPowerCap}
+
+            def poll():
+                while not self._stop.is_set():
+                    try:
+                        self.sm.append(float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)))
+                        r = pynvml.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+                        for n, b in bits.items():
+                            if r & b:
+                                self.reasons.add(n)
+                    except Exception:
+                        pass
+                    time.sleep(0.0005)
+
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            self.source = "nvml, polled about every 0.5 ms"
+            return
+        except Exception:
+            self.thread = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+            self.source = "nvidia-smi -lms 200"
         except Exception:
             self.proc = None
 
@@ -106,30 +148,33 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
-                continue
+        self._stop.set()
+        if self.proc is not None:
+            self.proc.terminate()
             try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        sm.sort()
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            for line in self.lines:
+                f = [x.strip() for x in line.split(",")]
+                if len(f) < 9:
+                    continue
+                try:
+                    self.sm.append(float(f[1]))
+                    self.max_mhz = float(f[2])
+                except ValueError:
+                    continue
+                for n, v in zip(self.NAMES, f[5:9]):
+                    if v.lower() == "active":
+                        self.reasons.add(n)
+        elif self.thread is not None:
+            self.thread.join(timeout=1)
+        if self.source is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no clock source"]}
+        sm = sorted(self.sm)
         med = sm[len(sm) // 2] if sm else None
-        return {"sm_mhz": med, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": len(sm),
+                "source": self.source}
 
 
 # ---- the step ----
@@ -208,50 +253,42 @@ def flush_l2(buf):
     buf.zero_()
 
 
-def run_ours(args):
-    world, rank, local = rank_info()
-    dist = world > 1
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if dist:
-        import datetime
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                             device_id=dev)
-    from quotebound_b200 import _lib, build
-    build.ensure()
-    _lib.load()
-    B, T, Hk, Hv, Dk, Dv, seed, rank_tokens = workload_shape(args.workload, world, rank)
+def _measure(args, workload, world, rank, dev, dist, steps, warmup):
+    """One workload on this rank: the step captured in a CUDA graph, W warm-up then K timed steps (L2
+    flushed before each, outside its events), the per-op split from eager steps.  Returns a dict."""
+    from quotebound_b200 import _lib, partition
+    B, T, Hk, Hv, Dk, Dv, seed, _ = workload_shape(workload, world, rank)
     W = Work(B, T, Hk, Hv, Dk, Dv, seed, dev, args.algo)
     flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
-    red = torch.empty(2 * (64 if args.workload == "c2" else Hv), dtype=torch.float32, device=dev)
+    Hv_all = 64 if workload == "c2" else Hv
+    red = torch.empty(2 * Hv_all, dtype=torch.float32, device=dev)
+    shard = partition.plan(B=8, Hk=16, Hv=64, world=world)[rank] if workload == "c2" else None
+    reduces = dist and (workload == "c1" or partition.needs_allreduce(partition.plan(B=8, Hk=16, Hv=64, world=world)))
 
     def allreduce(dA, ddt):
-        if not dist:
+        if not reduces:
             return
-        if args.workload == "c2":
-            from quotebound_b200 import partition
-            s = partition.plan(B=8, Hk=16, Hv=64, world=world)[rank]
+        if shard is not None:
             red.zero_()
-            red[s.hv0:s.hv1] = dA
-            red[64 + s.hv0:64 + s.hv1] = ddt
+            red[shard.hv0:shard.hv1] = dA
+            red[64 + shard.hv0:64 + shard.hv1] = ddt
         else:
             red[:Hv] = dA
             red[Hv:] = ddt
         torch.distributed.all_reduce(red)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         out = W.step()
         allreduce(out[5], out[6])
     torch.cuda.synchronize()
 
     # The step's launches captured once in a CUDA graph and replayed (the library's host-side work --
-    # argument checks, tensor maps, workspace allocation -- then costs nothing per step); the gradient
-    # all-reduce runs eagerly after each replay.
-    # With several ranks the all-reduce is captured too (NCCL supports capture; the communicator was
-    # created by the eager warm-up); if that capture fails, the graph holds the step alone.
+    # argument checks, tensor maps, workspace allocation -- then costs nothing per step).  With several
+    # ranks the all-reduce is captured too (NCCL supports capture; the communicator was created by the
+    # eager warm-up); if that capture fails, the graph holds the step alone and the all-reduce runs eagerly.
     graph, gout, graph_launches, graph_reduces = None, None, 0, False
     if not args.no_graph:
-        for with_reduce in ((True, False) if dist else (False,)):
+        for with_reduce in ((True, False) if reduces else (False,)):
             try:
                 side = torch.cuda.Stream()
                 side.wait_stream(torch.cuda.current_stream())
@@ -275,16 +312,14 @@ def run_ours(args):
                 graph, gout = None, None
                 torch.cuda.synchronize()
 
-    sampler = ClockSampler(local)
+    sampler = ClockSampler(dev.index)
     if dist:
         torch.distributed.barrier()
     torch.cuda.synchronize()
     sampler.start()
-    time.sleep(0.3)
     n0 = _lib.launches()
-    step_events = []
-    op_events = []
-    for _ in range(args.steps):
+    step_events, op_events = [], []
+    for _ in range(steps):
         flush_l2(flush)
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
@@ -301,11 +336,11 @@ def run_ours(args):
     torch.cuda.synchronize()
     if dist:
         torch.distributed.barrier()
-    launches = (_lib.launches() - n0) + graph_launches * args.steps
+    launches = (_lib.launches() - n0) + graph_launches * steps
     clocks = sampler.stop()
-    ms = sum(a.elapsed_time(b) for a, b in step_events) / args.steps
+    ms = sum(a.elapsed_time(b) for a, b in step_events) / steps
     if graph is not None:  # the per-op split from eager steps (after eager warm-up: the graph's pool is its own)
-        for k in range(3 + args.steps):
+        for k in range(3 + steps):
             flush_l2(flush)
             out = W.step(op_events if k >= 3 else None)
             allreduce(out[5], out[6])
@@ -319,75 +354,112 @@ def run_ours(args):
         t = torch.tensor([ms], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms_max = float(t.item())
-    if args.workload == "c1":
-        total_tokens = world * B * T
-        tokens_label = total_tokens
-    else:
-        total_tokens = 8 * 4096
-        tokens_label = total_tokens
-    value = total_tokens / (ms_max / 1e3)
+    total_tokens = world * B * T if workload == "c1" else 8 * 4096
+    return {"W": W, "allreduce": allreduce, "graph": graph, "gout": gout, "graph_reduces": graph_reduces,
+            "ms_max": ms_max, "per_op": per_op, "launches": launches, "clocks": clocks, "B": B, "T": T, "Hk": Hk,
+            "Hv": Hv, "Dk": Dk, "Dv": Dv, "value": total_tokens / (ms_max / 1e3), "reduces": reduces,
+            "flush": flush}
 
+
+def _roofline(workload, per_op, B, T, Hk, Hv, Dk, Dv):
+    hbm, tf, src = load_peaks()
+    fpt = fwd_flops_per_token_head(Dk, Dv)
+    dom = max(per_op, key=per_op.get)  # the dominant op of the step and its algorithmic work per launch
+    toks = B * T
+    flops = {"gdn_fwd": fpt * toks * Hv, "gdn_bwd": 2 * fpt * toks * Hv, "layer_fwd": fpt * toks * Hv,
+             "layer_bwd": 2 * fpt * toks * Hv}
+    fb, bb = bytes_per_token(Hk, Hv, Dk, Dv)
+    bytes_ = {"gdn_fwd": fb * toks, "gdn_bwd": bb * toks, "layer_fwd": fb * toks, "layer_bwd": bb * toks,
+              "gate_fwd": toks * (2 * Hk * Dk * 2 * 2 + Hv * 4 * 4),
+              "gate_bwd": toks * (4 * Hk * Dk * 2 + 2 * Hk * Dk * 2 + Hv * 4 * 6)}
+    dom_ms = per_op[dom]
+    if dom in flops:
+        ach = flops[dom] / (dom_ms / 1e3) / 1e12
+        return {"kernel": dom, "bound": "tensor", "achieved": round(ach, 3), "peak": tf, "unit": "TFLOP/s",
+                "frac": round(ach / tf, 5), "peak_source": src, "traffic": TRAFFIC.get((workload, dom)),
+                "traffic_source": TRAFFIC_NOTE, "ms_per_launch": round(dom_ms, 4),
+                "flop_per_launch": flops[dom], "bytes_per_launch": bytes_[dom],
+                "hbm_achieved_gbs": round(bytes_[dom] / (dom_ms / 1e3) / 1e9, 1),
+                "hbm_frac": round(bytes_[dom] / (dom_ms / 1e3) / 1e9 / hbm, 5)}
+    ach = bytes_[dom] / (dom_ms / 1e3) / 1e9
+    return {"kernel": dom, "bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+            "frac": round(ach / hbm, 5), "peak_source": src, "traffic": TRAFFIC.get((workload, dom)),
+            "traffic_source": TRAFFIC_NOTE, "ms_per_launch": round(dom_ms, 4)}
+
+
+def run_ours(args):
+    world, rank, local = rank_info()
+    dist = world > 1
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if dist:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=dev)
+    from quotebound_b200 import _lib, build
+    build.ensure()
+    _lib.load()
+    m = _measure(args, args.workload, world, rank, dev, dist, args.steps, args.warmup)
     # e2e through the public API with host buffers (pinned), every step: H2D inputs, D2H gradients
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(W, args, dev, dist, world, allreduce)
+        e2e = run_e2e(m["W"], args, dev, dist, world, m["allreduce"])
+    graph = m.pop("graph")
+    m.pop("gout")
+    # config 2 beside config 1: B=8, T=4096, Hv=64 split by (batch x head group) over the same ranks,
+    # fixed total work (strong scaling) -- the curve that exercises the partitioner and its all-reduce
+    c2 = None
+    if args.workload == "c1" and not args.no_c2:
+        del graph
+        torch.cuda.synchronize()
+        n2 = _measure(args, "c2", world, rank, dev, dist, max(3, args.steps // 2), max(3, args.warmup))
+        n2.pop("graph"), n2.pop("gout")
+        c2 = n2
+        graph = None
 
     if rank == 0:
-        hbm, tf, src = load_peaks()
-        Hk_, Hv_ = (16, 32) if args.workload == "c1" else (16, 64)
-        fpt = fwd_flops_per_token_head(Dk, Dv)
-        # dominant op of the step and its algorithmic work per launch
-        dom = max(per_op, key=per_op.get)
-        launch_tokens = B * T if args.workload == "c1" else B * T
-        heads = Hv
-        flops = {"gdn_fwd": fpt * launch_tokens * heads, "gdn_bwd": 2 * fpt * launch_tokens * heads,
-                 "layer_fwd": fpt * launch_tokens * heads, "layer_bwd": 2 * fpt * launch_tokens * heads}
-        fb, bb = bytes_per_token(Hk, Hv, Dk, Dv)
-        bytes_ = {"gdn_fwd": fb * launch_tokens, "gdn_bwd": bb * launch_tokens, "layer_fwd": fb * launch_tokens,
-                  "layer_bwd": bb * launch_tokens,
-                  "gate_fwd": launch_tokens * (2 * Hk * Dk * 2 * 2 + Hv * 4 * 4),
-                  "gate_bwd": launch_tokens * (4 * Hk * Dk * 2 + 2 * Hk * Dk * 2 + Hv * 4 * 6)}
-        dom_ms = per_op[dom]
-        if dom in flops:
-            ach = flops[dom] / (dom_ms / 1e3) / 1e12
-            roof = {"kernel": dom, "bound": "tensor", "achieved": round(ach, 3), "peak": tf, "unit": "TFLOP/s",
-                    "frac": round(ach / tf, 5), "peak_source": src, "traffic": TRAFFIC.get((args.workload, dom)),
-                    "ms_per_launch": round(dom_ms, 4),
-                    "hbm_achieved_gbs": round(bytes_[dom] / (dom_ms / 1e3) / 1e9, 1),
-                    "hbm_frac": round(bytes_[dom] / (dom_ms / 1e3) / 1e9 / hbm, 5)}
-        else:
-            ach = bytes_[dom] / (dom_ms / 1e3) / 1e9
-            roof = {"kernel": dom, "bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
-                    "frac": round(ach / hbm, 5), "peak_source": src, "traffic": TRAFFIC.get((args.workload, dom)),
-                    "ms_per_launch": round(dom_ms, 4)}
+        workload = args.workload
         line = {
-            "metric": "GDN fwd+bwd tokens/s at 4B layer shape" if args.workload == "c1"
+            "metric": "GDN fwd+bwd tokens/s at 4B layer shape" if workload == "c1"
             else "GDN fwd+bwd tokens/s, B=8 T=4096 Hv=64 split over GPUs",
-            "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms_max, 4), "higher_is_better": True,
-            "scaling": "weak" if args.workload == "c1" else "strong", "vs_baseline": None, "dtype": "bf16",
+            "value": round(m["value"], 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(m["ms_max"], 4), "higher_is_better": True,
+            "scaling": "weak" if workload == "c1" else "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded; q,k,v,dO ~ N(0,1), q/k normalised, g = exp(-e^A_log softplus(a+dt_bias)))",
-            "config": {"workload": "config1: B=1/GPU T=2048 Hk=16 Hv=32 Dk=Dv=128" if args.workload == "c1"
+            "config": {"workload": "config1: B=1/GPU T=2048 Hk=16 Hv=32 Dk=Dv=128" if workload == "c1"
                        else "config2: B=8 T=4096 Hk=16 Hv=64 Dk=Dv=128, (batch x head-group) split",
-                       "global_batch": world * B if args.workload == "c1" else 8, "seq_len": T,
-                       "parallelism": f"dp{world}" if args.workload == "c1" else f"bh{world}",
+                       "global_batch": world * m["B"] if workload == "c1" else 8, "seq_len": m["T"],
+                       "parallelism": f"dp{world}" if workload == "c1" else f"bh{world}",
                        "l2": "flushed before every step (512 MiB write, outside the step events)",
-                       "launch": ("CUDA graph of the step" + (" and its all-reduce" if graph_reduces else "") +
-                                  ", replayed") if graph is not None else "eager",
+                       "launch": "CUDA graph of the step" + (" and its all-reduce" if m["graph_reduces"] else "")
+                       + ", replayed",
                        "algo": {0: "auto", 1: "rows", 2: "chunked"}[args.algo],
                        "step": ("layer_fwd(save) + layer_bwd" if args.algo != 1 else
-                                "gate_fwd + gdn_fwd(save) + gdn_bwd + gate_bwd") + (" + allreduce" if dist else "")},
-            "per_op_ms": {k: round(v, 4) for k, v in per_op.items()},
-            "gpu_launches": int(launches),
-            "clocks": clocks,
-            "roofline": roof,
+                                "gate_fwd + gdn_fwd(save) + gdn_bwd + gate_bwd")
+                       + (" + allreduce" if m["reduces"] else "")},
+            "per_op_ms": {k: round(v, 4) for k, v in m["per_op"].items()},
+            "gpu_launches": int(m["launches"]),
+            "clocks": m["clocks"],
+            "roofline": _roofline(workload, m["per_op"], m["B"], m["T"], m["Hk"], m["Hv"], m["Dk"], m["Dv"]),
             "e2e": e2e,
         }
+        if c2 is not None:
+            line["config2_strong"] = {
+                "metric": "GDN fwd+bwd tokens/s, config2 (B=8 T=4096 Hk=16 Hv=64) split over the GPUs",
+                "value": round(c2["value"], 1), "unit": "tokens/s", "n_gpus": world, "scaling": "strong",
+                "ms_per_step": round(c2["ms_max"], 4), "steps": max(3, args.steps // 2),
+                "per_rank": {"batch_rows": c2["B"], "key_heads": c2["Hk"], "value_heads": c2["Hv"]},
+                "allreduce": c2["reduces"], "per_op_ms": {k: round(v, 4) for k, v in c2["per_op"].items()},
+                "gpu_launches": int(c2["launches"]), "clocks": c2["clocks"],
+                "roofline": _roofline("c2", c2["per_op"], c2["B"], c2["T"], c2["Hk"], c2["Hv"], c2["Dk"], c2["Dv"])}
         if not args.no_cpu_baseline and world == 1:
-            line["cpu_baseline"] = cpu_baseline(args.workload)
+            line["cpu_baseline"] = cpu_baseline(workload)
         print(json.dumps(line), flush=True)
     # a graph that holds an NCCL call is released before its process group
-    del graph, gout
+    del graph
+    m.clear()
+    if c2 is not None:
+        c2.clear()
     torch.cuda.synchronize()
     if dist:
         torch.distributed.barrier()
@@ -505,40 +577,43 @@ def _oracle_sample(T, threads, seconds):
 
 
 def cpu_baseline(workload):
+    """The CPU oracle on every host core over config 1 itself (T=2048), about ten seconds of passes."""
     from oracle import oracle
     oracle.build()
     threads = os.cpu_count() or 1
-    T = 256
+    T = 2048
     tps, n, el = _oracle_sample(T, threads, 10.0)
     return {"value": round(tps, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"config1 heads (Hk=16, Hv=32, Dk=Dv=128), T={T} fwd+bwd, float32 C oracle, OpenMP "
+            "sample": f"config1 (B=1, T={T}, Hk=16, Hv=32, Dk=Dv=128) fwd+bwd, float32 C oracle, OpenMP "
                       f"{threads} threads, {n} passes in {el:.1f} s"}
 
 
 def run_reference(args):
     """The reference's CPU path for this recurrence (its MLX/Metal build cannot run here): the C oracle
-    restating it, on every host core, same metric and workload shape, bounded samples per step."""
+    restating it, on every host core, on config 1 itself (B=1, T=2048, Hk=16, Hv=32, Dk=Dv=128): each
+    step is one forward + backward pass over the whole sequence."""
     world, rank, local = rank_info()
     if rank != 0:
         return
     from oracle import oracle
     oracle.build()
     threads = os.cpu_count() or 1
-    T = 256
+    T = 2048
     for _ in range(args.warmup):
         _oracle_sample(T, threads, 0.0)
-    rates = []
+    times = []
     for _ in range(args.steps):
-        tps, n, el = _oracle_sample(T, threads, 0.0)
-        rates.append(tps)
-    rates.sort()
-    v = rates[len(rates) // 2]
+        t0 = time.perf_counter()
+        _oracle_sample(T, threads, 0.0)
+        times.append(time.perf_counter() - t0)
+    ms = 1e3 * sum(times) / len(times)
+    v = T / (ms / 1e3)
     line = {"impl": "reference", "metric": "GDN fwd+bwd tokens/s at 4B layer shape", "value": round(v, 1),
             "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "higher_is_better": True, "dtype": "f32",
-            "config": {"workload": "config1 heads: Hk=16 Hv=32 Dk=Dv=128; sampled T=256 per step"},
+            "ms_per_step": round(ms, 3), "higher_is_better": True, "dtype": "f32",
+            "config": {"workload": "config1: B=1 T=2048 Hk=16 Hv=32 Dk=Dv=128", "same_config": True},
             "cpu_baseline": {"value": round(v, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
-                             "sample": f"one fwd+bwd of T={T} steps per timed step (median of {args.steps})"},
+                             "sample": f"one fwd+bwd of config 1 (T={T}) per timed step, mean of {args.steps}"},
             "e2e": {"value": round(v, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "the reference's recurrence runs on MLX/Metal (macOS only); its CPU restatement is timed"}
     print(json.dumps(line), flush=True)
@@ -554,7 +629,6 @@ def _timed(step, steps, warmup, dev):
     torch.cuda.synchronize()
     sampler = ClockSampler(dev.index)
     sampler.start()
-    time.sleep(0.3)
     n0 = _lib.launches()
     evs, ops = [], []
     for _ in range(steps):
