@@ -250,21 +250,23 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
     if (!ok) break;
     tc::fence_after_sync();
     float* scratch = reinterpret_cast<float*>(smem + GR_SCR);  // [64][65], then 4 x 64 column partials
-    float rsum = 0.f, dbl = 0.f;
+    float dbl = 0.f;
     {
       // Lane l holds dP[i][32 half + 0..31], lane l + 16 holds F D^T there; one exchange leaves each
       // lane both for 16 columns: j0 = 32 half (lower lane), 32 half + 16 (upper lane).  K K^T row i
-      // is in lane l alone; its second 16 columns go to lane l + 16.
-      float v[32], kk32[32], dp[16], fd[16], kk[16];
+      // is in lane l, Q K^T row i in lane l + 16; two exchanges give each lane both for its columns.
+      float v[32], kk32[32], dp[16], fd[16], kk[16], qk[16];
       tc::tmem_ld32(tl + cPF + 32 * half, v);
       tc::tmem_ld32(tl + cKK + 32 * half, kk32);
 #pragma unroll
       for (int k = 0; k < 16; ++k) {
         const float x = __shfl_xor_sync(0xffffffffu, lower ? v[16 + k] : v[k], 16);
         const float y = __shfl_xor_sync(0xffffffffu, kk32[16 + k], 16);
+        const float z = __shfl_xor_sync(0xffffffffu, kk32[k], 16);
         dp[k] = lower ? v[k] : x;
         fd[k] = lower ? x : v[16 + k];
         kk[k] = lower ? kk32[k] : y;
+        qk[k] = lower ? z : kk32[16 + k];
       }
       const int j0 = 32 * half + (lower ? 0 : 16);
       // this row's P (hi + lo from the image) for the 16 columns, loaded up front
@@ -287,34 +289,30 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
           }
         }
       }
+      // f_ij: the coefficient of the gate product Gamma_ij in the loss (P and L terms, strict lower;
+      // the diagonal spans no step), at scratch[i][j + 1] -- column 0 takes the gamma terms below
       float ph[16], kh[16], xs[16];
 #pragma unroll
       for (int k = 0; k < 16; ++k) {
         const int j = j0 + k;
         const float gam = j <= i_row ? __expf(bi - sg[j]) : 0.f;
-        const float xp = j <= i_row ? dp[k] * pv[k] : 0.f;
         const float dl = j < i_row ? -fd[k] : 0.f;
         const float lv = gam * kk[k];  // L_ij / beta_i = Gamma_ij (K K^T)_ij
-        const float xl = dl * be * lv;
         dbl = fmaf(dl, lv, dbl);
-        xs[k] = xp + xl;
-        rsum += xs[k];
+        xs[k] = j < i_row ? fmaf(dp[k], qk[k], dl * be * kk[k]) : 0.f;
         ph[k] = dp[k] * gam;        // dP^
         kh[k] = dl * be * gam;      // dKK
       }
+      (void)pv;
 #pragma unroll
-      for (int k = 0; k < 16; ++k) scratch[i_row * 65 + j0 + k] = xs[k];
+      for (int k = 0; k < 16; ++k) scratch[i_row * 65 + 1 + j0 + k] = xs[k];
       const int rr = img_row(i_row), c0 = j0 >> 3;
       st_hilo16_chunks(smem + GR_FHI, smem + GR_FLO, rr, ph, c0);
       st_hilo16_chunks(smem + GR_FHI, smem + GR_FLO, rr + 16, kh, c0);
     }
-    {  // the row sums of both lanes of the pair, per column half
-      const float rs = rsum + __shfl_xor_sync(0xffffffffu, rsum, 16);
+    {  // the L terms of d beta, both lanes of the pair, per column half
       const float db2 = dbl + __shfl_xor_sync(0xffffffffu, dbl, 16);
-      if (lower) {
-        srow[4][half][i_row] = rs;
-        srow[5][half][i_row] = db2;
-      }
+      if (lower) srow[5][half][i_row] = db2;
     }
     {
       float t5w = t5;
@@ -349,7 +347,62 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
       }
       tc::mma_commit(&bar_mma);
     }
-    // column sums of the Gamma terms (fixed order: four 16-row partials, then their sum); row totals; d b
+    // The gate gradient, formed directly (a gate near zero keeps full relative precision; no division):
+    //   dg_t = sum_{i >= t} Gamma_{i,t} A_{i,t},  A_{i,t} = sum_{e <= t} f[i][e] Gamma_{t-1, e-1}
+    // (e = 0 is the chunk start, Gamma_{t-1,-1} = gamma_{t-1}).  A is a linear recurrence in t,
+    // A_{i,t+1} = g_t A_{i,t} + f[i][t+1], run as four 16-step segments per row (the four lanes of a
+    // quad) joined by their carries.
+    // 1. column 0 (the gamma terms), the end-state terms of row 63, and each row's gate g_t
+    if (tid < 64) {
+      const int i = tid;
+      const float be_ = sg[64 + i];
+      const float t3_ = srow[0][0][i] + srow[0][1][i];
+      const float t2_ = srow[2][0][i] + srow[2][1][i];
+      const float t4_ = srow[3][0][i] + srow[3][1][i];
+      float st5 = 0.f;
+      for (int w = 0; w < 8; ++w) st5 += sred[w];
+      scratch[i * 65] = t3_ - be_ * t2_ + (i == 63 ? st5 : 0.f);
+      scratch[63 * 65 + 1 + i] += t4_;  // lambda_i: the end state's products (row 63 is the chunk's end)
+      float lg = 0.f;  // past the sequence's end the gate is 1
+      if (i < L) lg = a.g ? fmaxf(logf(in0), -88.f) : -expf(eA) * softplus_f(in0 + dtb);
+      sdb[i] = __expf(lg);
+    }
+    __syncthreads();
+    // 2. thread (row i, segment part): its 16 values of A, then the contributions Gamma_{i,t} A_{i,t}
+    //    in place over the consumed coefficients
+    {
+      const int i = tid >> 2, part = tid & 3, s0 = 16 * part;
+      const float* fr = scratch + i * 65;
+      float B[16], R[16];
+      float b = 0.f, rr = 1.f;  // local sum over this segment's e, and Gamma_{t-1, s0-1}
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const int t = s0 + u;
+        b = u == 0 ? fr[t] : fmaf(sdb[t - 1], b, fr[t]);
+        rr = u == 0 ? 1.f : rr * sdb[t - 1];
+        B[u] = b, R[u] = rr;
+      }
+      const float gl = sdb[s0 + 15];
+      const float bout = gl * b, rout = gl * rr;  // this segment's share of A and decay at t = s0 + 16
+      float cin = 0.f;
+      const int q0 = (lane & ~3);
+#pragma unroll
+      for (int q = 0; q < 3; ++q) {
+        const float bq = __shfl_sync(0xffffffffu, bout, q0 + q);
+        const float rq = __shfl_sync(0xffffffffu, rout, q0 + q);
+        if (q < part) cin = fmaf(rq, cin, bq);
+      }
+      const float bi_ = sg[i];
+      float* fw = scratch + i * 65;
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const int t = s0 + u;
+        const float A = fmaf(R[u], cin, B[u]);
+        fw[t] = i >= t ? __expf(bi_ - sg[t]) * A : 0.f;
+      }
+    }
+    __syncthreads();
+    // 3. dg_t = the column sums (fixed order: four 16-row partials, then their sum)
     {
       const int col = tid & 63, part = tid >> 6;
       float cs = 0.f;
@@ -358,52 +411,19 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
       scratch[64 * 65 + part * 64 + col] = cs;
     }
     __syncthreads();
-    float lt4 = 0.f, dbv = 0.f;
-    if (tid < 64) {
-      const int i = tid;
-      const float* cp = scratch + 64 * 65;
-      const float csum = (cp[i] + cp[64 + i]) + (cp[128 + i] + cp[192 + i]);
-      const float bi_ = sg[i], be_ = sg[64 + i], gi_ = __expf(bi_), lam_ = __expf(bC - bi_);
-      const float t3_ = srow[0][0][i] + srow[0][1][i];
-      const float t2_ = srow[2][0][i] + srow[2][1][i];
-      const float t4_ = srow[3][0][i] + srow[3][1][i];
-      const float rs = srow[4][0][i] + srow[4][1][i];
-      dbv = rs - csum + gi_ * t3_ - be_ * gi_ * t2_ - lam_ * t4_;
-      lt4 = lam_ * t4_;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) lt4 += __shfl_xor_sync(0xffffffffu, lt4, o);
-    if (lane == 0 && warp < 2) sred[8 + warp] = lt4;
-    __syncthreads();
-    if (tid == 63) {
-      float st5 = 0.f;
-      for (int w = 0; w < 8; ++w) st5 += sred[w];
-      dbv += (sred[8] + sred[9]) + __expf(bC) * st5;
-    }
-    // d log g_i = sum over rows i' >= i of d b_i': a suffix scan over the 64 rows (two warps)
-    if (tid < 64) {
-      float x = dbv;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float y = __shfl_down_sync(0xffffffffu, x, o);
-        if (lane + o < 32) x += y;
-      }
-      if (tid == 32) sdb[0] = x;  // the upper warp's total (rows 32..63)
-      sdb[1 + tid] = x;
-    }
-    __syncthreads();
     float pa = 0.f, pd = 0.f;  // layer mode: this row's share of the head's dA_log, ddt_bias
     if (tid < 64 && tid < L) {
       const int i = tid;
-      const float dl = sdb[1 + i] + (i < 32 ? sdb[0] : 0.f);  // d log g_i
+      const float* cp = scratch + 64 * 65;
+      const float dgi = (cp[i] + cp[64 + i]) + (cp[128 + i] + cp[192 + i]);  // dg_i
+      const float dl = sdb[i] * dgi;                                      // d log g_i = g_i dg_i
       const int64_t gi_idx = (tok0 + i) * Hv + hv;
       // d beta = F . (V - gamma R) + the L terms;  F . R = K . (F S) = t2
       const float gi_ = __expf(sg[i]);
       const float t1_ = (srow[1][0][i] + srow[1][1][i]) - gi_ * (srow[2][0][i] + srow[2][1][i]);
       const float dbe = t1_ + srow[5][0][i] + srow[5][1][i];
       if (a.g) {
-        // dg = d log g / g; a gate of exactly 0 (log g clamped) gets 0, which keeps g * dg = 0 exact
-        a.dg[gi_idx] = in0 > 0.f ? dl / in0 : 0.f;
+        a.dg[gi_idx] = dgi;
         a.dbeta[gi_idx] = dbe;
       } else {
         // log g = -e^A softplus(x), x = a + dt_bias: da = d log g * (-e^A sigmoid(x)); beta = sigmoid(b)

@@ -70,47 +70,6 @@ __device__ __forceinline__ float tf32_rna(float x) {
   return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
 }
 
-// Chunk geometry: chunk index -> sequence, first token, valid steps.
-struct Geo {
-  int T, Hk, Hv, N;
-  int ncs;                   // chunks per sequence (fixed-length batches)
-  const int32_t* cu;         // varlen offsets or null
-  const int64_t* chunk_off;  // varlen: first chunk of each sequence [N + 1]
-};
-
-__device__ __forceinline__ void chunk_info(const Geo& g, int64_t c, int& n, int64_t& tok0, int& L) {
-  if (!g.cu) {
-    n = (int)(c / g.ncs);
-    const int j = (int)(c - (int64_t)n * g.ncs);
-    tok0 = (int64_t)n * g.T + (int64_t)j * C;
-    L = min(C, g.T - j * C);
-    return;
-  }
-  int lo = 0, hi = g.N - 1;  // last n with chunk_off[n] <= c
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (g.chunk_off[mid] <= c) lo = mid; else hi = mid - 1;
-  }
-  n = lo;
-  tok0 = g.cu[n] + (c - g.chunk_off[n]) * C;
-  L = (int)min((int64_t)C, (int64_t)g.cu[n + 1] - tok0);
-}
-
-__device__ __forceinline__ void seq_chunks(const Geo& g, int n, int64_t& c_first, int64_t& nchunks, int64_t& seq0,
-                                           int64_t& seq1) {
-  if (g.cu) {
-    c_first = g.chunk_off[n];
-    nchunks = g.chunk_off[n + 1] - c_first;
-    seq0 = g.cu[n];
-    seq1 = g.cu[n + 1];
-  } else {
-    c_first = (int64_t)n * g.ncs;
-    nchunks = g.ncs;
-    seq0 = (int64_t)n * g.T;
-    seq1 = seq0 + g.T;
-  }
-}
-
 // Inclusive prefix sum over 64 values held by threads 0..63 (warps 0 and 1); result in out[64].
 __device__ __forceinline__ void scan64(float x, float* out, float* tmp) {
   const int tid = threadIdx.x, lane = tid & 31;

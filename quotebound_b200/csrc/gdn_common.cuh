@@ -8,6 +8,47 @@ namespace qbgdn {
 
 constexpr int kChunk = 64;  // steps per chunk (src/delta_grad.cpp:11)
 
+// Chunk geometry: chunk index -> sequence, first token, valid steps.
+struct Geo {
+  int T, Hk, Hv, N;
+  int ncs;                   // chunks per sequence (fixed-length batches)
+  const int32_t* cu;         // varlen offsets or null
+  const int64_t* chunk_off;  // varlen: first chunk of each sequence [N + 1]
+};
+
+__device__ __forceinline__ void chunk_info(const Geo& g, int64_t c, int& n, int64_t& tok0, int& L) {
+  if (!g.cu) {
+    n = (int)(c / g.ncs);
+    const int j = (int)(c - (int64_t)n * g.ncs);
+    tok0 = (int64_t)n * g.T + (int64_t)j * kChunk;
+    L = min(kChunk, g.T - j * kChunk);
+    return;
+  }
+  int lo = 0, hi = g.N - 1;  // last n with chunk_off[n] <= c
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (g.chunk_off[mid] <= c) lo = mid; else hi = mid - 1;
+  }
+  n = lo;
+  tok0 = g.cu[n] + (c - g.chunk_off[n]) * kChunk;
+  L = (int)min((int64_t)kChunk, (int64_t)g.cu[n + 1] - tok0);
+}
+
+__device__ __forceinline__ void seq_chunks(const Geo& g, int n, int64_t& c_first, int64_t& nchunks, int64_t& seq0,
+                                           int64_t& seq1) {
+  if (g.cu) {
+    c_first = g.chunk_off[n];
+    nchunks = g.chunk_off[n + 1] - c_first;
+    seq0 = g.cu[n];
+    seq1 = g.cu[n + 1];
+  } else {
+    c_first = (int64_t)n * g.ncs;
+    nchunks = g.ncs;
+    seq0 = (int64_t)n * g.T;
+    seq1 = seq0 + g.T;
+  }
+}
+
 // ---- element access for the two activation dtypes ---------------------------------------------
 __device__ __forceinline__ float to_f(float x) { return x; }
 __device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }

@@ -6,9 +6,7 @@
 //                      whose rounding the one-token step and the verify rows reproduce bit for bit).
 //  * gdn_step        — one decode token (qb_gdn_step).
 //  * gdn_verify      — V tokens run as V steps, every row's state kept (qb_gdn_verify).
-//  * gdn_simt_bwd    — the reverse recurrence (qb_gdn_bwd's generic path): each chunk of 64 steps
-//                      is replayed from its saved start in sub-chunks of 8, then walked back.
-//  * gdn_reduce_parts — the fixed-order sums of the per-row-block partials (deterministic).
+// The generic backward is the CUDA-core chunked one of gdn_cc.cu.
 #include "gdn_common.cuh"
 #include "gdn_simt.cuh"
 #include "launch_count.cuh"
@@ -110,212 +108,6 @@ __global__ void __launch_bounds__(256) gdn_verify(SimtArgs a) {
   }
 }
 
-// ------------------------------------------------------------------------------------------------
-// Reverse recurrence.  With dS the cotangent of the state row, going back over step t:
-//   dS += dy q;  dq += dy S_t;  dd = dS . k;  du = -beta dd;
-//   dk += dS delta + du (g S_{t-1});  dS += du k;  dg += dS . S_{t-1};  dS *= g;
-//   dv = beta dd;  dbeta += dd (v - u).
-// The rows of a block are summed in shared memory in row order; row blocks and the value heads of
-// a key head are summed afterwards by gdn_reduce_parts, again in a fixed order.
-constexpr int kSub = 8;
-constexpr int kNSub = kChunk / kSub;
-
-template <int NPT, typename Tin, typename Tout>
-__global__ void __launch_bounds__(256) gdn_simt_bwd(SimtArgs a) {
-  extern __shared__ float red[];  // [rows_per_block][2 * Dk + 2]
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int RPB = a.rows_per_block;
-  const int blk = blockIdx.x, r = blk * RPB + warp;  // Dv % RPB == 0 (host guarantees)
-  const int hv = blockIdx.y, n = blockIdx.z;
-  const int hk = hv / (a.Hv / a.Hk);
-  const int NB = a.Dv / RPB;
-  const int Dk = a.Dk;
-  const SeqRange sr = seq_range(a.cu, n, a.T);
-  const Tin* __restrict__ q = static_cast<const Tin*>(a.q);
-  const Tin* __restrict__ k = static_cast<const Tin*>(a.k);
-  const Tin* __restrict__ v = static_cast<const Tin*>(a.v);
-  const Tin* __restrict__ dy = static_cast<const Tin*>(a.dy);
-  Tout* __restrict__ dv = static_cast<Tout*>(a.dv);
-  const int c0 = lane * NPT;
-  const size_t srow = ((size_t)n * a.Hv + hv) * a.Dv + r;
-  const int64_t L = sr.t1 - sr.t0;
-  const int64_t NC = (L + kChunk - 1) / kChunk;
-  const int64_t chunk_base = a.chunk_off ? a.chunk_off[n] : (int64_t)n * ((a.T + kChunk - 1) / kChunk);
-  const int W2 = 2 * Dk + 2;
-
-  float ds[NPT];
-  if (a.dhT) {
-    load_vec<NPT>(a.dhT + srow * Dk + c0, ds);
-  } else {
-#pragma unroll
-    for (int i = 0; i < NPT; ++i) ds[i] = 0.f;
-  }
-
-  for (int64_t c = NC - 1; c >= 0; --c) {
-    const int64_t ta = sr.t0 + c * kChunk, te = min(sr.t1, ta + kChunk);
-    float s[NPT];
-    load_vec<NPT>(a.ckpt + (((chunk_base + c) * a.Hv + hv) * a.Dv + r) * (size_t)Dk + c0, s);
-    // sub-chunk starts of this chunk
-    float sub[kNSub][NPT];
-#pragma unroll
-    for (int m = 0; m < kNSub; ++m) {
-#pragma unroll
-      for (int i = 0; i < NPT; ++i) sub[m][i] = s[i];
-#pragma unroll
-      for (int j = 0; j < kSub; ++j) {
-        const int64_t t = ta + m * kSub + j;
-        if (t < te) {
-          const size_t tok = (size_t)sr.b * a.T + t;
-          float kk[NPT];
-          load_vec<NPT>(k + (tok * a.Hk + hk) * Dk + c0, kk);
-          const size_t gb = tok * a.Hv + hv;
-          const float gt = a.g[gb], bt = a.beta[gb];
-          const float vt = to_f(v[gb * a.Dv + r]);
-          float u = 0.f;
-#pragma unroll
-          for (int i = 0; i < NPT; ++i) {
-            s[i] *= gt;
-            u = fmaf(s[i], kk[i], u);
-          }
-          u = warp_sum(u);
-          const float d = (vt - u) * bt;
-#pragma unroll
-          for (int i = 0; i < NPT; ++i) s[i] = fmaf(kk[i], d, s[i]);
-        }
-      }
-    }
-#pragma unroll
-    for (int m = kNSub - 1; m >= 0; --m) {
-      const int64_t ts = ta + m * kSub;
-      if (ts >= te) continue;  // uniform across the block: every warp has the same (n, hv)
-      float st[kSub + 1][NPT], del[kSub], uu[kSub];
-#pragma unroll
-      for (int i = 0; i < NPT; ++i) st[0][i] = sub[m][i];
-#pragma unroll
-      for (int j = 0; j < kSub; ++j) {
-        const int64_t t = ts + j;
-        del[j] = uu[j] = 0.f;
-#pragma unroll
-        for (int i = 0; i < NPT; ++i) st[j + 1][i] = st[j][i];
-        if (t < te) {
-          const size_t tok = (size_t)sr.b * a.T + t;
-          float kk[NPT];
-          load_vec<NPT>(k + (tok * a.Hk + hk) * Dk + c0, kk);
-          const size_t gb = tok * a.Hv + hv;
-          const float gt = a.g[gb], bt = a.beta[gb];
-          const float vt = to_f(v[gb * a.Dv + r]);
-          float u = 0.f;
-#pragma unroll
-          for (int i = 0; i < NPT; ++i) {
-            st[j + 1][i] = st[j][i] * gt;
-            u = fmaf(st[j + 1][i], kk[i], u);
-          }
-          u = warp_sum(u);
-          const float d = (vt - u) * bt;
-#pragma unroll
-          for (int i = 0; i < NPT; ++i) st[j + 1][i] = fmaf(kk[i], d, st[j + 1][i]);
-          del[j] = d;
-          uu[j] = u;
-        }
-      }
-#pragma unroll
-      for (int j = kSub - 1; j >= 0; --j) {
-        const int64_t t = ts + j;
-        if (t >= te) continue;  // uniform across the block
-        const size_t tok = (size_t)sr.b * a.T + t;
-        float kk[NPT], qq[NPT];
-        load_vec<NPT>(k + (tok * a.Hk + hk) * Dk + c0, kk);
-        load_vec<NPT>(q + (tok * a.Hk + hk) * Dk + c0, qq);
-        const size_t gb = tok * a.Hv + hv;
-        const float gt = a.g[gb], bt = a.beta[gb];
-        const float vt = to_f(v[gb * a.Dv + r]), dyt = to_f(dy[gb * a.Dv + r]);
-        float pq[NPT], pk[NPT];
-        float dd = 0.f;
-#pragma unroll
-        for (int i = 0; i < NPT; ++i) {
-          ds[i] = fmaf(dyt, qq[i], ds[i]);
-          pq[i] = dyt * st[j + 1][i];
-          dd = fmaf(ds[i], kk[i], dd);
-        }
-        dd = warp_sum(dd);
-        const float du = -bt * dd;
-        float dgr = 0.f;
-#pragma unroll
-        for (int i = 0; i < NPT; ++i) {
-          pk[i] = fmaf(ds[i], del[j], du * (st[j][i] * gt));
-          ds[i] = fmaf(du, kk[i], ds[i]);
-          dgr = fmaf(ds[i], st[j][i], dgr);
-          ds[i] *= gt;
-        }
-        dgr = warp_sum(dgr);
-        if (lane == 0) dv[gb * a.Dv + r] = from_f<Tout>(bt * dd);
-        float* my = red + warp * W2;
-#pragma unroll
-        for (int i = 0; i < NPT; ++i) {
-          my[c0 + i] = pq[i];
-          my[Dk + c0 + i] = pk[i];
-        }
-        if (lane == 0) {
-          my[2 * Dk] = dgr;
-          my[2 * Dk + 1] = dd * (vt - uu[j]);
-        }
-        __syncthreads();
-        const size_t part = (tok * a.Hv + hv) * NB + blk;
-        for (int col = threadIdx.x; col < W2; col += blockDim.x) {
-          float acc = 0.f;
-          for (int w = 0; w < RPB; ++w) acc += red[w * W2 + col];
-          if (col < Dk)
-            a.dq_part[part * Dk + col] = acc;
-          else if (col < 2 * Dk)
-            a.dk_part[part * Dk + col - Dk] = acc;
-          else if (col == 2 * Dk)
-            a.dg_part[part] = acc;
-          else
-            a.dbeta_part[part] = acc;
-        }
-        __syncthreads();
-      }
-    }
-  }
-  if (a.dh0) store_vec<NPT>(a.dh0 + srow * Dk + c0, ds);
-}
-
-// dq[tok, hk] = sum over the value heads of key head hk, then over row blocks, in that order;
-// dg, dbeta[tok, hv] = sum over row blocks.  One thread per output element.
-template <typename Tout>
-__global__ void gdn_reduce_parts(ReduceArgs a) {
-  const int64_t total_qk = a.tokens * a.Hk * a.Dk;
-  const int64_t total_g = a.tokens * a.Hv;
-  const int ratio = a.Hv / a.Hk;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total_qk + total_g;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    if (i < total_qk) {
-      const int64_t col = i % a.Dk, th = i / a.Dk;  // th = tok * Hk + hk
-      const int64_t tok = th / a.Hk, hk = th % a.Hk;
-      float sq = 0.f, sk = 0.f;
-      for (int j = 0; j < ratio; ++j) {
-        const int64_t hv = hk * ratio + j;
-        const int64_t base = ((tok * a.Hv + hv) * a.NB) * a.Dk + col;
-        for (int b = 0; b < a.NB; ++b) {
-          sq += a.dq_part[base + (int64_t)b * a.Dk];
-          sk += a.dk_part[base + (int64_t)b * a.Dk];
-        }
-      }
-      static_cast<Tout*>(a.dq)[i] = from_f<Tout>(sq);
-      static_cast<Tout*>(a.dk)[i] = from_f<Tout>(sk);
-    } else {
-      const int64_t j = i - total_qk;  // tok * Hv + hv
-      float sg = 0.f, sb = 0.f;
-      for (int b = 0; b < a.NB; ++b) {
-        sg += a.dg_part[j * a.NB + b];
-        sb += a.dbeta_part[j * a.NB + b];
-      }
-      a.dg[j] = sg;
-      a.dbeta[j] = sb;
-    }
-  }
-}
-
 // chunk_off[n] = sum over sequences m < n of ceil(len_m / 64); one thread (n is small).
 __global__ void gdn_chunk_offsets(const int32_t* cu, int N, int64_t* chunk_off) {
   if (blockIdx.x == 0 && threadIdx.x == 0) {
@@ -361,15 +153,6 @@ static cudaError_t launch_kind(SimtKind kind, const SimtArgs& a, dim3 grid, dim3
       gdn_verify<NPT, Tin, Tout><<<grid, block, 0, st>>>(a);
       note_launch();
       break;
-    case SimtKind::Bwd:
-      if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(gdn_simt_bwd<NPT, Tin, Tout>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-      }
-      gdn_simt_bwd<NPT, Tin, Tout><<<grid, block, smem, st>>>(a);
-      note_launch();
-      break;
   }
   return cudaGetLastError();
 }
@@ -396,23 +179,11 @@ cudaError_t simt_launch(SimtKind kind, const SimtArgs& a, int n_seqs, int in_bf1
                         cudaStream_t st) {
   const int RPB = a.rows_per_block;
   dim3 grid((a.Dv + RPB - 1) / RPB, a.Hv, n_seqs), block(32 * RPB);
-  const size_t smem = kind == SimtKind::Bwd ? sizeof(float) * RPB * (2 * a.Dk + 2) : 0;
+  const size_t smem = 0;
   if (in_bf16 && out_bf16) return launch_npt<__nv_bfloat16, __nv_bfloat16>(kind, a, grid, block, smem, st);
   if (in_bf16) return launch_npt<__nv_bfloat16, float>(kind, a, grid, block, smem, st);
   if (out_bf16) return launch_npt<float, __nv_bfloat16>(kind, a, grid, block, smem, st);
   return launch_npt<float, float>(kind, a, grid, block, smem, st);
-}
-
-cudaError_t simt_reduce_parts(const ReduceArgs& a, int out_bf16, cudaStream_t st) {
-  const int64_t total = a.tokens * (a.Hk * a.Dk + a.Hv);
-  const int threads = 256;
-  const int64_t blocks = std::min<int64_t>((total + threads - 1) / threads, 148 * 16);
-  if (out_bf16)
-    gdn_reduce_parts<__nv_bfloat16><<<(unsigned)blocks, threads, 0, st>>>(a);
-  else
-    gdn_reduce_parts<float><<<(unsigned)blocks, threads, 0, st>>>(a);
-  note_launch();
-  return cudaGetLastError();
 }
 
 cudaError_t launch_chunk_offsets(const int32_t* cu, int N, int64_t* chunk_off, cudaStream_t st) {

@@ -12,6 +12,7 @@
 #include <atomic>
 
 #include "../../include/qb_gdn.h"
+#include "gdn_cc.cuh"
 #include "gdn_chunk.cuh"
 #include "gdn_common.cuh"
 #include "gdn_gate.cuh"
@@ -94,8 +95,7 @@ struct Plan {
   int64_t n_chunks;     // sum over sequences of ceil(len / 64)
   bool varlen;
   bool chunked;         // tensor-core chunked path
-  int rpb;              // rows per block (row-parallel path)
-  int NB;               // row blocks (row-parallel backward)
+  int rpb;              // rows per block (row-parallel forward)
 };
 
 int check_desc(const qb_gdn_desc* d, Plan* p, char* err, int errlen) {
@@ -144,7 +144,6 @@ int check_desc(const qb_gdn_desc* d, Plan* p, char* err, int errlen) {
                 d->Dk, d->Dv);
   p->chunked = d->algo == QB_ALGO_CHUNKED || (d->algo == QB_ALGO_AUTO && chunk_ok);
   p->rpb = simt_rows_per_block(d->Dv);
-  p->NB = d->Dv / p->rpb;
   return 0;
 }
 
@@ -155,14 +154,13 @@ int64_t saved_bytes_of(const qb_gdn_desc* d, const Plan& p) {
 
 int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
 
-// Row-parallel workspace: [status block] [chunk_off (varlen)] [dq_part] [dk_part] [dg_part] [dbeta_part]
-// [saved (recompute)]
+// Workspace of the row-parallel forward and the CUDA-core backward: [status block] [chunk_off (varlen)]
+// [the backward's chunk intermediates (gdn_cc.cuh)] [saved (recompute)]
 struct SimtWs {
   int* status;
   int64_t* chunk_off;
-  float *dq_part, *dk_part, *dg_part, *dbeta_part;
+  char* cc;
   float* saved;
-  char* fwd_ws;
 };
 
 int64_t simt_ws_bytes(const qb_gdn_desc* d, const Plan& p, int op, bool with_saved, SimtWs* out, char* base) {
@@ -176,17 +174,8 @@ int64_t simt_ws_bytes(const qb_gdn_desc* d, const Plan& p, int op, bool with_sav
   w.status = (int*)take(kStatusBytes);
   w.chunk_off = (int64_t*)take(p.varlen ? (p.N + 1) * 8 : 0);
   if (op == QB_OP_BWD) {
-    const int64_t parts = p.tokens * d->Hv * (int64_t)p.NB;
-    w.dq_part = (float*)take(parts * d->Dk * 4);
-    w.dk_part = (float*)take(parts * d->Dk * 4);
-    w.dg_part = (float*)take(parts * 4);
-    w.dbeta_part = (float*)take(parts * 4);
-    if (with_saved) {
-      w.saved = (float*)take(saved_bytes_of(d, p));
-      // recomputing with the chunked forward needs that forward's own workspace too
-      if (p.chunked)
-        w.fwd_ws = take(chunked_ws_bytes(d->Hv, d->Hk, p.N, p.n_chunks, p.tokens, p.varlen, QB_OP_FWD, false, false));
-    }
+    w.cc = take(cc_ws_layout(d->Hk, d->Hv, d->Dk, d->Dv, p.n_chunks, nullptr, nullptr));
+    if (with_saved) w.saved = (float*)take(saved_bytes_of(d, p));
   }
   if (out) *out = w;
   return off;
@@ -409,34 +398,20 @@ int qb_gdn_bwd(const qb_gdn_desc* d, const void* q, const void* k, const void* v
   float* ck = (float*)saved;
   if (!ck) {  // recompute the chunk starts with the same forward, y discarded into the dv buffer
     ck = w.saved;
-    if (p.chunked) {
-      ChunkFwdArgs f{};
-      f.B = d->B, f.T = d->T, f.Hk = d->Hk, f.Hv = d->Hv, f.Dk = d->Dk, f.Dv = d->Dv, f.N = p.N;
-      f.n_chunks = p.n_chunks;
-      f.cu = d->cu_seqlens;
-      f.q = q, f.k = k, f.v = v, f.g = g, f.beta = beta, f.h0 = h0, f.y = dv, f.hT = nullptr;
-      f.saved = ck;
-      f.in_bf16 = in_bf16, f.out_bf16 = out_bf16;
-      if ((e = chunked_fwd(f, w.fwd_ws, st, w.status)) != cudaSuccess)
-        return cuda_fail(e, "gated delta backward (recompute)", err, errlen);
-    } else {
-      SimtArgs f = a;
-      f.y = dv;  // same shape and dtype as y; overwritten by the backward below
-      f.ckpt = ck;
-      if ((e = simt_launch(SimtKind::Fwd, f, p.N, in_bf16, out_bf16, st)) != cudaSuccess)
-        return cuda_fail(e, "gated delta backward (recompute)", err, errlen);
-    }
+    SimtArgs f = a;
+    f.y = dv;  // same shape and dtype as y; overwritten by the backward below
+    f.ckpt = ck;
+    if ((e = simt_launch(SimtKind::Fwd, f, p.N, in_bf16, out_bf16, st)) != cudaSuccess)
+      return cuda_fail(e, "gated delta backward (recompute)", err, errlen);
   }
-  a.ckpt = ck;
-  a.dy = dy, a.dhT = dhT, a.dv = dv, a.dh0 = dh0;
-  a.dq_part = w.dq_part, a.dk_part = w.dk_part, a.dg_part = w.dg_part, a.dbeta_part = w.dbeta_part;
-  if ((e = simt_launch(SimtKind::Bwd, a, p.N, in_bf16, out_bf16, st)) != cudaSuccess)
-    return cuda_fail(e, "gated delta backward", err, errlen);
-  ReduceArgs r{};
-  r.tokens = p.tokens, r.Hk = d->Hk, r.Hv = d->Hv, r.Dk = d->Dk, r.NB = p.NB;
-  r.dq_part = w.dq_part, r.dk_part = w.dk_part, r.dg_part = w.dg_part, r.dbeta_part = w.dbeta_part;
-  r.dq = dq, r.dk = dk, r.dg = dg, r.dbeta = dbeta;
-  if ((e = simt_reduce_parts(r, out_bf16, st)) != cudaSuccess) return cuda_fail(e, "gated delta backward", err, errlen);
+  CcArgs c{};
+  cc_ws_layout(d->Hk, d->Hv, d->Dk, d->Dv, p.n_chunks, w.cc, &c);
+  c.geo = Geo{d->T, d->Hk, d->Hv, p.N, (d->T + kChunkSteps - 1) / kChunkSteps, d->cu_seqlens,
+              p.varlen ? w.chunk_off : nullptr};
+  c.n_chunks = p.n_chunks, c.Dk = d->Dk, c.Dv = d->Dv;
+  c.q = q, c.k = k, c.v = v, c.dy = dy, c.g = g, c.beta = beta, c.ckpt = ck, c.dhT = dhT;
+  c.dq = dq, c.dk = dk, c.dv = dv, c.dg = dg, c.dbeta = dbeta, c.dh0 = dh0;
+  if ((e = cc_bwd(c, p.N, in_bf16, out_bf16, st)) != cudaSuccess) return cuda_fail(e, "gated delta backward", err, errlen);
   return 0;
 }
 

@@ -55,6 +55,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking probe of the same phase (try_wait may suspend the thread for a while before it
+// answers no).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -70,11 +84,11 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // err points at the status block that opens every workspace (status.cuh): err[0] the code,
 // err[4] / err[5] a test hook -- when err[4] equals `code`, this wait gives up after err[5] polls,
 // so that a test can make one named wait run out on a normal input.  The hook is read only once the
-// first poll has failed.
+// first poll (non-blocking) has failed.
 constexpr uint32_t kMaxPolls = 1u << 24;
 constexpr uint64_t kMaxWaitNs = 1000000000ull;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_test_wait(bar, parity)) return true;
   uint32_t limit = kMaxPolls;
   if (err && code > 0 && *(volatile int*)(err + 4) == code) limit = *(volatile uint32_t*)(err + 5);
   const uint64_t t0 = globaltimer_ns();

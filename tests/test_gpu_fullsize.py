@@ -70,3 +70,47 @@ def test_config2_rows_alone_equal_batch():
             assert torch.equal(a, b[sl]), (r, n)
         if r in (0, B - 1):
             check(one, oracle_layer(pr, q[sl], k[sl], v[sl], dy[sl]))
+
+
+def test_config1_plain_path_dg_direct():
+    """qb_gdn_fwd / qb_gdn_bwd (normalised q, k and the gates as inputs, gated_delta_vjp's contract) at
+    config 1 with its gate distribution (g = exp(-e^A_log softplus(a + dt_bias)) reaches 1e-30), on the
+    tensor-core path and the CUDA-core path: every output, dg included, directly at rel-L2 <= 2e-3."""
+    import numpy as np
+
+    from oracle import oracle
+    from quotebound_b200 import _lib, deltanet
+    p = synthetic.make(1, 2048, 16, 32, 128, 128, seed=0, dtype=torch.bfloat16, h0_std=0.02, dhT_std=0.02)
+    assert float(p.g.min()) < 1e-20  # the distribution the tests of dg must cover
+    f = lambda t: None if t is None else t.float().cpu().numpy()
+    yo, hTo = oracle.gated_delta_fwd(f(p.q), f(p.k), f(p.v), f(p.g), f(p.beta), f(p.h0))
+    go = oracle.gated_delta_bwd(f(p.q), f(p.k), f(p.v), f(p.g), f(p.beta), f(p.h0), f(p.dy), f(p.dhT))
+    d = p.to("cuda")
+    for algo in (_lib.QB_ALGO_CHUNKED, _lib.QB_ALGO_ROWS):
+        y, hT, saved = deltanet.gated_delta_fwd(d.q, d.k, d.v, d.g, d.beta, d.h0, save=True, algo=algo)
+        grads = deltanet.gated_delta_bwd(d.q, d.k, d.v, d.g, d.beta, d.h0, d.dy, d.dhT, saved=saved, algo=algo)
+        assert rel(y, yo) <= TOL and rel(hT, hTo) <= TOL, algo
+        for n, a, b in zip(("dq", "dk", "dv", "dg", "dbeta", "dh0"), grads, go):
+            assert rel(a, b) <= TOL, (algo, n, rel(a, b))
+        # the smallest gates' dg entries on their own scale too
+        small = np.asarray(p.g.float().numpy() < 1e-10)
+        dg, dgo = grads[3].float().cpu().numpy(), go[3]
+        assert rel(torch.from_numpy(dg[small]), torch.from_numpy(dgo[small])) <= TOL, algo
+
+
+def test_config4_verify_full_bit_exact():
+    """Config 4 at its size: 32 sequences x 8 drafted tokens, Hk=16, Hv=32, Dk=Dv=128, bf16 inputs,
+    cached state ~ N(0, 0.05): the verify rows equal 8 one-token steps bit for bit, outputs and every
+    kept state (tests/test_exact.cpp:80-123's pattern)."""
+    from quotebound_b200 import exact
+    N, V, Hk, Hv, D = 32, 8, 16, 32, 128
+    p = synthetic.make(N, V, Hk, Hv, D, D, seed=0, dtype=torch.bfloat16, with_dy=False)
+    gen = torch.Generator().manual_seed(1)
+    state = (torch.randn(N, Hv, D, D, generator=gen) * 0.05).cuda()
+    d = p.to("cuda")
+    y, states = exact.verify(d.q, d.k, d.v, d.g, d.beta, state)
+    cur = state.clone()
+    for j in range(V):
+        yj, cur = exact.step(d.q[:, j], d.k[:, j], d.v[:, j], d.g[:, j], d.beta[:, j], cur)
+        assert torch.equal(yj, y[:, j]), j
+        assert torch.equal(cur, states[:, j]), j

@@ -54,12 +54,10 @@ def run_gpu(p, algo, cu=None):
     return y, hT, grads
 
 
-def assert_close(p, got, want, tol, names=("dq", "dk", "dv", "dg", "dbeta", "dh0"), ref_worst=False,
-                 dlogg=False):
-    """dlogg: compare g * dg (= d loss / d log g) instead of dg.  The chunked backward computes the
-    log-gate gradient and divides by g, so with gates near zero (the bench's distribution reaches
-    g ~ 1e-30) dg itself carries d log g's absolute error divided by g; g * dg is the quantity it
-    computes to the stated tolerance, and the one the gate backward consumes."""
+def assert_close(p, got, want, tol, names=("dq", "dk", "dv", "dg", "dbeta", "dh0"), ref_worst=False):
+    """Every output against the oracle at rel-L2 <= tol, dg directly (both backward paths form the gate
+    gradient from the gate products that span each step, so gates near zero -- the bench's
+    distribution reaches g ~ 1e-30 -- keep full relative precision)."""
     y, hT, grads = got
     yo, hTo, go = want
     assert rel(y, yo) <= tol, ("y", rel(y, yo))
@@ -67,9 +65,6 @@ def assert_close(p, got, want, tol, names=("dq", "dk", "dv", "dg", "dbeta", "dh0
     for n, a, b in zip(names, grads, go):
         if n == "dh0" and p.h0 is None and p.dhT is None:
             continue
-        if n == "dg" and dlogg:
-            gg = p.g.float()
-            a, b = a.float().cpu() * gg, torch.from_numpy(b) * gg
         assert rel(a, b) <= tol, (n, rel(a, b))
         if ref_worst:
             assert worst(a, b) <= 1e-5, (n, worst(a, b))
@@ -124,7 +119,7 @@ def test_bf16_fwd_bwd(T):
     p = synthetic.make(1, T, 16, 32, 128, 128, seed=T, dtype=torch.bfloat16, h0_std=0.02, dhT_std=0.02)
     want = oracle_all(p)
     for algo in (ROWS, CHUNKED):
-        assert_close(p, run_gpu(p, algo), want, 2e-3, dlogg=algo == CHUNKED)
+        assert_close(p, run_gpu(p, algo), want, 2e-3)
 
 
 @pytest.mark.parametrize("B,T,Hk,Hv,g_lo", [(2, 150, 16, 32, 0.99), (1, 129, 16, 32, 0.9), (2, 64, 8, 32, 0.5),
@@ -144,7 +139,7 @@ def test_varlen_matches_oracle():
                        cu_seqlens=cu)
     want = oracle_all(p, cu)
     for algo in (ROWS, CHUNKED):
-        assert_close(p, run_gpu(p, algo, cu), want, 2e-3, dlogg=algo == CHUNKED)
+        assert_close(p, run_gpu(p, algo, cu), want, 2e-3)
     pf = synthetic.make(1, cu[-1], 2, 4, 32, 32, seed=8, h0_std=0.1, dhT_std=0.1, cu_seqlens=cu)
     assert_close(pf, run_gpu(pf, ROWS, cu), oracle_all(pf, cu), 1e-5, ref_worst=True)
 
