@@ -163,6 +163,64 @@ int qb_gdn_gate_bwd(int64_t P, int32_t Hk, int32_t Hv, int32_t Dk, int32_t in_dt
 /* Workspace bytes qb_gdn_gate_bwd needs for P tokens and Hv heads. */
 int64_t qb_gdn_gate_workspace_bytes(int64_t P, int32_t Hv);
 
+/* ---- Around the recurrence: the conv before it and the gated norm after it ----------------------
+ *
+ * The causal depthwise conv1d + SiLU of deltanet() (src/deltanet.cpp:74-93), fused with the q / k / v
+ * split.  x [B, T, conv_dim] holds the projected channels q | k | v (conv_dim = 2 Hk Dk + Hv Dv, the
+ * reference's in_proj_qkv output); w [conv_dim, K] the per-channel taps (the reference's [conv_dim, K,
+ * 1]); the conv state [N, K - 1, conv_dim] the last K - 1 inputs of each sequence (LayerCache.conv,
+ * src/model.h:72-76).  Each token's window is its K - 1 predecessors in the same sequence, the carried
+ * state before a sequence's start (zeros when state_in is NULL); u = conv rounded to dtype, output
+ * silu(u) rounded to dtype, written to q [B, T, Hk, Dk], k [B, T, Hk, Dk], v [B, T, Hv, Dv] -- the raw
+ * rows qb_gdn_layer_fwd normalises.  Varlen as in qb_gdn_desc.  Hk Dk and Hv Dv multiples of 8. */
+typedef struct qb_gdn_conv_desc {
+  int32_t B, T, Hk, Hv, Dk, Dv;
+  int32_t K; /* taps: 2, 3 or 4 (Qwen3.5: 4) */
+  int32_t n_seqs;
+  const int32_t* cu_seqlens;
+  const int32_t* cu_seqlens_host;
+  int32_t dtype; /* x, w, q, k, v, the states and their cotangents: QB_DTYPE_BF16 or QB_DTYPE_F32 */
+} qb_gdn_conv_desc;
+
+/* Workspace bytes of qb_gdn_conv_fwd / qb_gdn_conv_bwd (the backward's figure covers dw). */
+int64_t qb_gdn_conv_workspace_bytes(const qb_gdn_conv_desc* d, char* err, int errlen);
+
+/* Forward; state_out (NULL = not written) receives the new conv state (src/deltanet.cpp:75-77). */
+int qb_gdn_conv_fwd(const qb_gdn_conv_desc* d, const void* x, const void* w, const void* state_in, void* q, void* k,
+                    void* v, void* state_out, void* ws, int64_t ws_bytes, void* stream, char* err, int errlen);
+
+/* Backward: dx [B, T, conv_dim] from the cotangents dq, dk, dv and dstate_out (the new state's; NULL =
+ * zero); dw [conv_dim, K] float32 summed over every token in a fixed order (NULL = not computed);
+ * dstate_in [N, K - 1, conv_dim] (NULL = not written). */
+int qb_gdn_conv_bwd(const qb_gdn_conv_desc* d, const void* x, const void* w, const void* state_in, const void* dq,
+                    const void* dk, const void* dv, const void* dstate_out, void* dx, float* dw, void* dstate_in,
+                    void* ws, int64_t ws_bytes, void* stream, char* err, int errlen);
+
+/* The conv's part of the exact speculative verify (deltanet(..., rows), src/deltanet.cpp:79-87): B = N
+ * sequences of T = V drafted tokens each (x [N, V, conv_dim]) run as V one-token steps of
+ * qb_gdn_conv_fwd, bit for bit, every token's conv window kept: states [N, V, K - 1, conv_dim], row j
+ * the state after token j (RowStates.conv, src/model.h:84-89).  state_in is required. */
+int qb_gdn_conv_verify(const qb_gdn_conv_desc* d, const void* x, const void* w, const void* state_in, void* q, void* k,
+                       void* v, void* states, void* stream, char* err, int errlen);
+
+/* keep_rows for the conv state (src/exact.cpp:151-159: cache.conv = rows.conv[n - 1]): state_out[n] =
+ * states[n, keep[n] - 1]; keep as in qb_gdn_keep_rows. */
+int qb_gdn_keep_conv_rows(int32_t N, int32_t V, int32_t K, int32_t conv_dim, int32_t dtype, const void* states,
+                          const int32_t* keep, void* state_out, int32_t* status, void* stream, char* err, int errlen);
+
+/* The gated RMSNorm after the recurrence (src/deltanet.cpp:35-45, :122; Qwen3NextRMSNormGated): per
+ * (token, value head) row, n = rms_norm(y, w, eps) rounded to dtype, o = silu(z) n in float32 rounded
+ * to dtype.  y, z, o [P, Hv, Dv] (dtype), w [Dv] float32, Dv in {32, 64, 128, 256}. */
+int qb_gdn_gated_norm_fwd(int64_t P, int32_t Hv, int32_t Dv, float eps, int32_t dtype, const void* y, const void* z,
+                          const float* w, void* o, void* stream, char* err, int errlen);
+/* Workspace bytes of the backward's dw. */
+int64_t qb_gdn_gated_norm_workspace_bytes(int64_t P, int32_t Hv, int32_t Dv);
+/* Backward: dy, dz (dtype) and dw [Dv] float32 summed over the rows in a fixed order (NULL = not
+ * computed; then ws may be NULL). */
+int qb_gdn_gated_norm_bwd(int64_t P, int32_t Hv, int32_t Dv, float eps, int32_t dtype, const void* y, const void* z,
+                          const float* w, const void* dout, void* dy, void* dz, float* dw, void* ws, int64_t ws_bytes,
+                          void* stream, char* err, int errlen);
+
 /* Device status of the last qb_gdn_fwd / qb_gdn_bwd / qb_gdn_layer_fwd / qb_gdn_layer_bwd call that
  * used this workspace.  Every such workspace opens with a 256-byte status block that the call clears on
  * its stream before its first kernel.  The tensor-core kernels wait on copies and products with

@@ -364,6 +364,162 @@ int gdn_oracle_gate_bwd(int64_t M, int Dk, int64_t P, int Hv, const float* q, co
   return 0;
 }
 
+
+/* ---------------------------------------------------------------------------
+ * Around the recurrence.  round_bf16 = 1 rounds what the reference keeps in the activations' dtype
+ * (bf16): the conv's output before its SiLU and the SiLU's output; the norm's output before the gate
+ * and the gated output.  Everything else in double.
+ * ------------------------------------------------------------------------- */
+static float bf16_round(float x) { /* round to nearest even at 8 mantissa bits */
+  uint32_t u;
+  memcpy(&u, &x, 4);
+  if ((u & 0x7f800000u) == 0x7f800000u) return x;
+  u += 0x7fffu + ((u >> 16) & 1u);
+  u &= 0xffff0000u;
+  memcpy(&x, &u, 4);
+  return x;
+}
+static double rnd(double x, int round_bf16) { return round_bf16 ? (double)bf16_round((float)x) : (double)(float)x; }
+
+/* The causal depthwise conv1d + SiLU (src/deltanet.cpp:74-93): per sequence n, xpad = [state_in[n]
+ * (K - 1 rows; zeros when NULL); its x rows], u_t[c] = sum_m xpad[t + m][c] w[c][m], y = silu(u),
+ * split into q | k | v by channel; state_out[n] = the last K - 1 rows of xpad (src/deltanet.cpp:75-77).
+ * x [tokens, conv_dim] with conv_dim = 2 key_dim + value_dim; w [conv_dim, K]. */
+static void conv_seq(const gdn_shape* s, int n, int64_t* t0, int64_t* t1) {
+  int64_t b;
+  seq_range(s, n, &b, t0, t1);
+  if (!s->cu) { *t0 = (int64_t)n * s->T; *t1 = *t0 + s->T; }
+}
+
+int gdn_oracle_conv_fwd(int B, int T, const int32_t* cu, int N, int key_dim, int value_dim, int K, int round_bf16,
+                        const float* x, const float* w, const float* state_in, float* q, float* k, float* v,
+                        float* state_out) {
+  const gdn_shape sh = {B, T, 1, 1, 1, 1, N, cu};
+  const int cd = 2 * key_dim + value_dim, NS = num_seqs(&sh);
+  for (int n = 0; n < NS; ++n) {
+    int64_t t0, t1;
+    conv_seq(&sh, n, &t0, &t1);
+    const int64_t Ls = t1 - t0;
+    for (int c = 0; c < cd; ++c) {
+      /* xpad value at padded position p */
+#define XPAD(p) ((p) < K - 1 ? (state_in ? (double)state_in[((int64_t)n * (K - 1) + (p)) * cd + c] : 0.0) \
+                             : (double)x[(t0 + (p) - (K - 1)) * cd + c])
+      for (int64_t t = 0; t < Ls; ++t) {
+        double u = 0;
+        for (int m = 0; m < K; ++m) u += XPAD(t + m) * (double)w[(int64_t)c * K + m];
+        u = rnd(u, round_bf16);
+        const float y = (float)rnd(u / (1.0 + exp(-u)), round_bf16);
+        const int64_t tok = t0 + t;
+        if (c < key_dim) q[tok * key_dim + c] = y;
+        else if (c < 2 * key_dim) k[tok * key_dim + c - key_dim] = y;
+        else v[tok * value_dim + c - 2 * key_dim] = y;
+      }
+      if (state_out)
+        for (int j = 0; j < K - 1; ++j) state_out[((int64_t)n * (K - 1) + j) * cd + c] = (float)XPAD(Ls + j);
+#undef XPAD
+    }
+  }
+  return 0;
+}
+
+/* Its backward: du = dy silu'(u) (u rounded as in the forward; a rounding passes the cotangent
+ * through), dxpad[t + m] += du_t w[m], dw[c][m] += du_t xpad[t + m]; the new state's cotangent adds onto
+ * xpad's last K - 1 rows; xpad's first K - 1 rows are the carried state's cotangent. */
+int gdn_oracle_conv_bwd(int B, int T, const int32_t* cu, int N, int key_dim, int value_dim, int K, int round_bf16,
+                        const float* x, const float* w, const float* state_in, const float* dq, const float* dk,
+                        const float* dv, const float* dstate_out, float* dx, float* dw, float* dstate_in) {
+  const gdn_shape sh = {B, T, 1, 1, 1, 1, N, cu};
+  const int cd = 2 * key_dim + value_dim, NS = num_seqs(&sh);
+  double* dwa = (double*)calloc((size_t)cd * K, sizeof(double));
+  for (int n = 0; n < NS; ++n) {
+    int64_t t0, t1;
+    conv_seq(&sh, n, &t0, &t1);
+    const int64_t Ls = t1 - t0;
+    double* dxp = (double*)malloc(sizeof(double) * (size_t)(Ls + K - 1));
+    for (int c = 0; c < cd; ++c) {
+#define XPAD(p) ((p) < K - 1 ? (state_in ? (double)state_in[((int64_t)n * (K - 1) + (p)) * cd + c] : 0.0) \
+                             : (double)x[(t0 + (p) - (K - 1)) * cd + c])
+      for (int64_t p = 0; p < Ls + K - 1; ++p) dxp[p] = 0;
+      for (int64_t t = 0; t < Ls; ++t) {
+        double u = 0;
+        for (int m = 0; m < K; ++m) u += XPAD(t + m) * (double)w[(int64_t)c * K + m];
+        u = rnd(u, round_bf16);
+        const int64_t tok = t0 + t;
+        const double g = c < key_dim ? dq[tok * key_dim + c]
+                         : c < 2 * key_dim ? dk[tok * key_dim + c - key_dim]
+                                           : dv[tok * value_dim + c - 2 * key_dim];
+        const double sg = 1.0 / (1.0 + exp(-u));
+        const double du = g * sg * (1.0 + u * (1.0 - sg));
+        for (int m = 0; m < K; ++m) {
+          dxp[t + m] += du * w[(int64_t)c * K + m];
+          dwa[(int64_t)c * K + m] += du * XPAD(t + m);
+        }
+      }
+      if (dstate_out)
+        for (int j = 0; j < K - 1; ++j) dxp[Ls + j] += dstate_out[((int64_t)n * (K - 1) + j) * cd + c];
+      for (int64_t p = 0; p < Ls + K - 1; ++p) {
+        if (p < K - 1) {
+          if (dstate_in) dstate_in[((int64_t)n * (K - 1) + p) * cd + c] = (float)dxp[p];
+        } else {
+          dx[(t0 + p - (K - 1)) * cd + c] = (float)dxp[p];
+        }
+      }
+#undef XPAD
+    }
+    free(dxp);
+  }
+  if (dw)
+    for (int64_t i = 0; i < (int64_t)cd * K; ++i) dw[i] = (float)dwa[i];
+  free(dwa);
+  return 0;
+}
+
+/* The gated RMSNorm (src/deltanet.cpp:35-45, :122): per row of Dv, n = y rsqrt(mean(y^2) + eps) w
+ * (rounded), o = silu(z) n (rounded). */
+int gdn_oracle_gated_norm_fwd(int64_t rows, int Dv, float eps, int round_bf16, const float* y, const float* z,
+                              const float* w, float* o) {
+  for (int64_t r = 0; r < rows; ++r) {
+    const float* yr = y + r * Dv;
+    double ss = 0;
+    for (int i = 0; i < Dv; ++i) ss += (double)yr[i] * yr[i];
+    const double rs = 1.0 / sqrt(ss / Dv + eps);
+    for (int i = 0; i < Dv; ++i) {
+      const double nv = rnd(yr[i] * rs * w[i], round_bf16);
+      const double zz = z[r * Dv + i];
+      o[r * Dv + i] = (float)rnd(zz / (1.0 + exp(-zz)) * nv, round_bf16);
+    }
+  }
+  return 0;
+}
+
+int gdn_oracle_gated_norm_bwd(int64_t rows, int Dv, float eps, int round_bf16, const float* y, const float* z,
+                              const float* w, const float* dout, float* dy, float* dz, float* dw) {
+  double* dwa = (double*)calloc((size_t)Dv, sizeof(double));
+  for (int64_t r = 0; r < rows; ++r) {
+    const float* yr = y + r * Dv;
+    double ss = 0, dot = 0;
+    for (int i = 0; i < Dv; ++i) ss += (double)yr[i] * yr[i];
+    const double rs = 1.0 / sqrt(ss / Dv + eps);
+    for (int i = 0; i < Dv; ++i) {
+      const double zz = z[r * Dv + i], sg = 1.0 / (1.0 + exp(-zz));
+      const double nv = rnd(yr[i] * rs * w[i], round_bf16);
+      const double g = dout[r * Dv + i], dn = g * zz * sg;
+      dz[r * Dv + i] = (float)(g * nv * sg * (1.0 + zz * (1.0 - sg)));
+      dot += (double)yr[i] * w[i] * dn;
+      dwa[i] += dn * yr[i] * rs;
+    }
+    for (int i = 0; i < Dv; ++i) {
+      const double zz = z[r * Dv + i], sg = 1.0 / (1.0 + exp(-zz));
+      const double dn = (double)dout[r * Dv + i] * zz * sg;
+      dy[r * Dv + i] = (float)(rs * w[i] * dn - rs * rs * rs * dot * yr[i] / Dv);
+    }
+  }
+  if (dw)
+    for (int i = 0; i < Dv; ++i) dw[i] = (float)dwa[i];
+  free(dwa);
+  return 0;
+}
+
 int gdn_oracle_max_threads(void) {
 #ifdef _OPENMP
   return omp_get_max_threads();

@@ -49,6 +49,11 @@ def lib():
         L.gdn_oracle_gate_fwd.argtypes = [i64, i, i64, i, p, p, p, p, p, p, p, p, p, p, p]
         L.gdn_oracle_gate_bwd.argtypes = [i64, i, i64, i, p, p, p, p, p, p, p, p, p, p,
                                           p, p, p, p, p, p]
+        L.gdn_oracle_conv_fwd.argtypes = [i, i, ip, i, i, i, i, i, p, p, p, p, p, p, p]
+        L.gdn_oracle_conv_bwd.argtypes = [i, i, ip, i, i, i, i, i, p, p, p, p, p, p, p, p, p, p]
+        f = ctypes.c_float
+        L.gdn_oracle_gated_norm_fwd.argtypes = [i64, i, f, i, p, p, p, p]
+        L.gdn_oracle_gated_norm_bwd.argtypes = [i64, i, f, i, p, p, p, p, p, p, p]
         L.gdn_oracle_max_threads.restype = ctypes.c_int
         _lib = L
     return _lib
@@ -136,3 +141,60 @@ def gate_bwd(q, k, a, b, A_log, dt_bias, dqn, dkn, dg, dbeta):
     lib().gdn_oracle_gate_bwd(M, Dk, Pn, Hv, qp, kp, ap, bp, Ap, dp, dqp, dkp, dgp, dbp,
                               P(dq), P(dk), P(da), P(db), P(dA), P(ddt))
     return dq, dk, da, db, dA, ddt
+
+
+def _cu_conv(cu_seqlens):
+    if cu_seqlens is None:
+        return None, None
+    c = np.ascontiguousarray(np.asarray(cu_seqlens, dtype=np.int32))
+    return c, c.ctypes.data_as(_i32p)
+
+
+def conv_fwd(x, w, state_in, Hk, Dk, Hv, Dv, round_bf16=False, cu_seqlens=None):
+    """The causal depthwise conv1d + SiLU split into (q, k, v, state_out) (src/deltanet.cpp:74-93).
+    x [B, T, conv_dim]; w [conv_dim, K]; state_in [N, K - 1, conv_dim] or None."""
+    x, xp = _f(x); w, wp = _f(w); state_in, sp = _f(state_in)
+    B, T, cd = x.shape
+    K = w.shape[1]
+    cu, cup = _cu_conv(cu_seqlens)
+    N = B if cu is None else len(cu) - 1
+    kd, vd = Hk * Dk, Hv * Dv
+    q = np.zeros((B, T, Hk, Dk), np.float32); k = np.zeros_like(q); v = np.zeros((B, T, Hv, Dv), np.float32)
+    so = np.zeros((N, K - 1, cd), np.float32)
+    P = lambda a: a.ctypes.data_as(_f32p)
+    lib().gdn_oracle_conv_fwd(B, T, cup, N, kd, vd, K, int(round_bf16), xp, wp, sp, P(q), P(k), P(v), P(so))
+    return q, k, v, so
+
+
+def conv_bwd(x, w, state_in, dq, dk, dv, dstate_out, Hk, Dk, Hv, Dv, round_bf16=False, cu_seqlens=None):
+    """(dx, dw, dstate_in) of conv_fwd given the cotangents of q, k, v and of the new state."""
+    x, xp = _f(x); w, wp = _f(w); state_in, sp = _f(state_in)
+    dq, dqp = _f(dq); dk, dkp = _f(dk); dv, dvp = _f(dv); dstate_out, dsp = _f(dstate_out)
+    B, T, cd = x.shape
+    K = w.shape[1]
+    cu, cup = _cu_conv(cu_seqlens)
+    N = B if cu is None else len(cu) - 1
+    dx = np.zeros_like(x); dw = np.zeros_like(w); dsi = np.zeros((N, K - 1, cd), np.float32)
+    P = lambda a: a.ctypes.data_as(_f32p)
+    lib().gdn_oracle_conv_bwd(B, T, cup, N, Hk * Dk, Hv * Dv, K, int(round_bf16), xp, wp, sp, dqp, dkp, dvp, dsp,
+                              P(dx), P(dw), P(dsi))
+    return dx, dw, dsi
+
+
+def gated_norm_fwd(y, z, w, eps, round_bf16=False):
+    """o = silu(z) rms_norm(y, w, eps) per row of Dv (src/deltanet.cpp:35-45, :122)."""
+    y, yp = _f(y); z, zp = _f(z); w, wp = _f(w)
+    Dv = y.shape[-1]
+    o = np.zeros_like(y)
+    lib().gdn_oracle_gated_norm_fwd(y.size // Dv, Dv, float(eps), int(round_bf16), yp, zp, wp, o.ctypes.data_as(_f32p))
+    return o
+
+
+def gated_norm_bwd(y, z, w, dout, eps, round_bf16=False):
+    """(dy, dz, dw) of gated_norm_fwd."""
+    y, yp = _f(y); z, zp = _f(z); w, wp = _f(w); dout, dp = _f(dout)
+    Dv = y.shape[-1]
+    dy = np.zeros_like(y); dz = np.zeros_like(y); dw = np.zeros_like(w)
+    P = lambda a: a.ctypes.data_as(_f32p)
+    lib().gdn_oracle_gated_norm_bwd(y.size // Dv, Dv, float(eps), int(round_bf16), yp, zp, wp, dp, P(dy), P(dz), P(dw))
+    return dy, dz, dw

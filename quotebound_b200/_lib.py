@@ -27,6 +27,8 @@ SYMBOLS = (
     "qb_gdn_step", "qb_gdn_verify", "qb_gdn_keep_rows", "qb_gdn_gate_fwd", "qb_gdn_gate_bwd",
     "qb_gdn_gate_workspace_bytes", "qb_gdn_gate_bwd_noalloc", "qb_gdn_layer_saved_bytes", "qb_gdn_layer_fwd",
     "qb_gdn_layer_bwd", "qb_gdn_status", "qb_gdn_set_wait_limit", "qb_gdn_count_nonfinite",
+    "qb_gdn_conv_workspace_bytes", "qb_gdn_conv_fwd", "qb_gdn_conv_bwd", "qb_gdn_conv_verify", "qb_gdn_keep_conv_rows",
+    "qb_gdn_gated_norm_fwd", "qb_gdn_gated_norm_workspace_bytes", "qb_gdn_gated_norm_bwd",
 )
 
 
@@ -36,6 +38,14 @@ class Desc(ctypes.Structure):
         ("Dk", ctypes.c_int32), ("Dv", ctypes.c_int32), ("n_seqs", ctypes.c_int32),
         ("cu_seqlens", ctypes.c_void_p), ("cu_seqlens_host", ctypes.c_void_p),
         ("in_dtype", ctypes.c_int32), ("out_dtype", ctypes.c_int32), ("algo", ctypes.c_int32),
+    ]
+
+
+class ConvDesc(ctypes.Structure):
+    _fields_ = [
+        ("B", ctypes.c_int32), ("T", ctypes.c_int32), ("Hk", ctypes.c_int32), ("Hv", ctypes.c_int32),
+        ("Dk", ctypes.c_int32), ("Dv", ctypes.c_int32), ("K", ctypes.c_int32), ("n_seqs", ctypes.c_int32),
+        ("cu_seqlens", ctypes.c_void_p), ("cu_seqlens_host", ctypes.c_void_p), ("dtype", ctypes.c_int32),
     ]
 
 
@@ -94,6 +104,24 @@ def load():
     L.qb_gdn_set_wait_limit.argtypes = [i32, i32, cp, ctypes.c_int]
     L.qb_gdn_count_nonfinite.restype = ctypes.c_int
     L.qb_gdn_count_nonfinite.argtypes = [vp, i64, i32, vp, vp, cp, ctypes.c_int]
+    cdp = ctypes.POINTER(ConvDesc)
+    L.qb_gdn_conv_workspace_bytes.restype = i64
+    L.qb_gdn_conv_workspace_bytes.argtypes = [cdp, cp, ctypes.c_int]
+    L.qb_gdn_conv_fwd.restype = ctypes.c_int
+    L.qb_gdn_conv_fwd.argtypes = [cdp] + [vp] * 8 + [i64, vp, cp, ctypes.c_int]
+    L.qb_gdn_conv_bwd.restype = ctypes.c_int
+    L.qb_gdn_conv_bwd.argtypes = [cdp] + [vp] * 11 + [i64, vp, cp, ctypes.c_int]
+    L.qb_gdn_conv_verify.restype = ctypes.c_int
+    L.qb_gdn_conv_verify.argtypes = [cdp] + [vp] * 7 + [vp, cp, ctypes.c_int]
+    L.qb_gdn_keep_conv_rows.restype = ctypes.c_int
+    L.qb_gdn_keep_conv_rows.argtypes = [i32] * 5 + [vp] * 4 + [vp, cp, ctypes.c_int]
+    f32 = ctypes.c_float
+    L.qb_gdn_gated_norm_fwd.restype = ctypes.c_int
+    L.qb_gdn_gated_norm_fwd.argtypes = [i64, i32, i32, f32, i32] + [vp] * 4 + [vp, cp, ctypes.c_int]
+    L.qb_gdn_gated_norm_workspace_bytes.restype = i64
+    L.qb_gdn_gated_norm_workspace_bytes.argtypes = [i64, i32, i32]
+    L.qb_gdn_gated_norm_bwd.restype = ctypes.c_int
+    L.qb_gdn_gated_norm_bwd.argtypes = [i64, i32, i32, f32, i32] + [vp] * 7 + [vp, i64, vp, cp, ctypes.c_int]
     _lib = L
     return L
 
