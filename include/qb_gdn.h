@@ -41,7 +41,7 @@ extern "C" {
 enum { QB_DTYPE_F32 = 0, QB_DTYPE_BF16 = 1 };
 
 /* Which calls a workspace / saved-state size is asked for. */
-enum { QB_OP_FWD = 0, QB_OP_BWD = 1, QB_OP_LAYER_FWD = 2, QB_OP_LAYER_BWD = 3 };
+enum { QB_OP_FWD = 0, QB_OP_BWD = 1, QB_OP_LAYER_FWD = 2, QB_OP_LAYER_BWD = 3, QB_OP_BWD_CKPT = 4 };
 
 /* Which kernels run the recurrence.  AUTO takes the tensor-core chunked path where the shape has
  * one (Dk = Dv = 128) and the row-parallel path elsewhere; the other two force one path (CHUNKED
@@ -74,8 +74,9 @@ int64_t qb_gdn_launches(void);
  * shape. */
 int64_t qb_gdn_workspace_bytes(const qb_gdn_desc* d, int32_t op, char* err, int errlen);
 
-/* Bytes of the saved-for-backward buffer (the fp32 chunk-start states, [N_chunks, Hv, Dv, Dk],
- * the counterpart of src/delta_grad.cpp:172-181's ckpt) that a training forward fills. */
+/* Bytes of the saved-for-backward buffer a training forward fills: the chunk-start states (ckpt, see
+ * qb_gdn_ckpt_bytes; the counterpart of src/delta_grad.cpp:172-181's ckpt) followed, on the tensor-core
+ * path, by data derived from the inputs (gates, operand images, the chunks' delta rows). */
 int64_t qb_gdn_saved_bytes(const qb_gdn_desc* d, char* err, int errlen);
 
 /* gated_delta: y and the final state(s).  h0 NULL = zero initial state; hT NULL = not written.
@@ -93,6 +94,22 @@ int qb_gdn_bwd(const qb_gdn_desc* d, const void* q, const void* k, const void* v
                const float* beta, const float* h0, const void* dy, const float* dhT, const void* saved,
                void* dq, void* dk, void* dv, float* dg, float* dbeta, float* dh0, void* ws,
                int64_t ws_bytes, void* stream, char* err, int errlen);
+
+/* The chunk-start states as a format of their own, for callers that checkpoint activations
+ * (src/model.cpp:397-404 wraps every layer in mx::checkpoint) and so keep only what the backward cannot
+ * cheaply redo: ckpt [N_chunks, Hv, Dv, Dk] float32, the state at the start of every 64-step chunk,
+ * chunks numbered sequence by sequence (fixed-length batches: [B, ceil(T / 64), Hv, Dv, Dk], exactly
+ * the reference's ckpt, src/delta_grad.cpp:172-181).  Every saved buffer of a training qb_gdn_fwd
+ * begins with it (its first qb_gdn_ckpt_bytes bytes; on the tensor-core path rounded to tf32, which is
+ * how its backward reads it); the rest of saved is derived data.
+ * qb_gdn_bwd_from_ckpt is gated_delta_vjp (src/delta_grad.cpp:155-199) given those states: the derived
+ * data is recomputed chunk by chunk in parallel (no sequential forward), then the backward runs.
+ * Workspace: qb_gdn_workspace_bytes(d, QB_OP_BWD_CKPT).  h0 is not read (ckpt[chunk 0] is it). */
+int64_t qb_gdn_ckpt_bytes(const qb_gdn_desc* d, char* err, int errlen);
+int qb_gdn_bwd_from_ckpt(const qb_gdn_desc* d, const void* q, const void* k, const void* v, const float* g,
+                         const float* beta, const float* h0, const void* dy, const float* dhT, const float* ckpt,
+                         void* dq, void* dk, void* dv, float* dg, float* dbeta, float* dh0, void* ws, int64_t ws_bytes,
+                         void* stream, char* err, int errlen);
 
 /* The recurrence with the norm and gate graph around it fused in (deltanet()'s middle,
  * src/deltanet.cpp:94-100, compute_g :22-33): q, k are the raw conv outputs [B, T, Hk, Dk] (bf16),

@@ -17,6 +17,7 @@ QB_OP_FWD = 0
 QB_OP_BWD = 1
 QB_OP_LAYER_FWD = 2
 QB_OP_LAYER_BWD = 3
+QB_OP_BWD_CKPT = 4
 QB_ALGO_AUTO = 0
 QB_ALGO_ROWS = 1
 QB_ALGO_CHUNKED = 2
@@ -28,7 +29,8 @@ SYMBOLS = (
     "qb_gdn_gate_workspace_bytes", "qb_gdn_gate_bwd_noalloc", "qb_gdn_layer_saved_bytes", "qb_gdn_layer_fwd",
     "qb_gdn_layer_bwd", "qb_gdn_status", "qb_gdn_set_wait_limit", "qb_gdn_count_nonfinite",
     "qb_gdn_conv_workspace_bytes", "qb_gdn_conv_fwd", "qb_gdn_conv_bwd", "qb_gdn_conv_verify", "qb_gdn_keep_conv_rows",
-    "qb_gdn_gated_norm_fwd", "qb_gdn_gated_norm_workspace_bytes", "qb_gdn_gated_norm_bwd",
+    "qb_gdn_gated_norm_fwd", "qb_gdn_gated_norm_workspace_bytes", "qb_gdn_gated_norm_bwd", "qb_gdn_ckpt_bytes",
+    "qb_gdn_bwd_from_ckpt",
 )
 
 
@@ -104,6 +106,10 @@ def load():
     L.qb_gdn_set_wait_limit.argtypes = [i32, i32, cp, ctypes.c_int]
     L.qb_gdn_count_nonfinite.restype = ctypes.c_int
     L.qb_gdn_count_nonfinite.argtypes = [vp, i64, i32, vp, vp, cp, ctypes.c_int]
+    L.qb_gdn_ckpt_bytes.restype = i64
+    L.qb_gdn_ckpt_bytes.argtypes = [dp, cp, ctypes.c_int]
+    L.qb_gdn_bwd_from_ckpt.restype = ctypes.c_int
+    L.qb_gdn_bwd_from_ckpt.argtypes = [dp] + [vp] * 16 + [i64, vp, cp, ctypes.c_int]
     cdp = ctypes.POINTER(ConvDesc)
     L.qb_gdn_conv_workspace_bytes.restype = i64
     L.qb_gdn_conv_workspace_bytes.argtypes = [cdp, cp, ctypes.c_int]

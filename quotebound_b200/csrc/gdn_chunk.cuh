@@ -18,6 +18,9 @@ struct ChunkFwdArgs {
   void* saved;
   int in_bf16, out_bf16;
   const float *a_raw, *b_raw, *A_log, *dt_bias;
+  // non-null: recompute mode -- given these chunk-start states [chunks, Hv, Dv, Dk], fill saved (without
+  // its checkpoint part) chunk by chunk in parallel; y is not written (hT must be null)
+  const float* ckpt_in;
 };
 
 // Layer mode as above: dg, dbeta then receive da, db, and dA_log, ddt_bias the head sums.
@@ -33,6 +36,9 @@ struct ChunkBwdArgs {
   int in_bf16, out_bf16;
   const float *a_raw, *b_raw, *A_log, *dt_bias;
   float *dA_log, *ddt_bias;
+  // with saved null: the caller's chunk-start states [chunks, Hv, Dv, Dk] (the rest is recomputed from
+  // them chunk by chunk), or null to recompute everything with the forward walk
+  const float* ckpt_in;
 };
 
 bool chunked_supported(int Dk, int Dv);
@@ -42,7 +48,7 @@ bool chunked_bwd_ready();
 // layer: the saved buffer / workspace of the layer-mode path (adds the normalised q, k rows)
 int64_t chunked_saved_bytes(int Hv, int Hk, int64_t n_chunks, int64_t tokens, bool layer);
 int64_t chunked_ws_bytes(int Hv, int Hk, int N, int64_t n_chunks, int64_t tokens, bool varlen, int op, bool with_saved,
-                         bool layer);
+                         bool layer, bool ckpt_external = false);
 // Both report into a status block the caller has initialised (init_status): chunked_fwd into
 // `status` (the one opening ws, or a recomputing backward's own), chunked_bwd into the one opening ws.
 cudaError_t chunked_fwd(const ChunkFwdArgs& a, void* ws, cudaStream_t st, int* status);

@@ -19,7 +19,15 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
   const int dv0 = blockIdx.x * DVT, hv = blockIdx.y, n = blockIdx.z;
   const int Hv = a.geo.Hv, hk = hv / (Hv / a.geo.Hk);
   int64_t c_first, nchunks, seq0, seq1;
-  seq_chunks(a.geo, n, c_first, nchunks, seq0, seq1);
+  if (a.ckpt_in) {  // recompute mode: this CTA's one chunk (blockIdx.z), its start state from the checkpoint
+    int nn, Lc;
+    int64_t t0;
+    c_first = blockIdx.z;
+    chunk_info(a.geo, c_first, nn, t0, Lc);
+    nchunks = 1, seq0 = t0, seq1 = t0 + Lc;
+  } else {
+    seq_chunks(a.geo, n, c_first, nchunks, seq0, seq1);
+  }
 
   // TMEM: [K; Q] S^T 0, D 64, S update 128, P D 192 (64 columns each: hi and lo halves)
   const uint32_t cA = 0, cD = 64, cS = 128, cO = 192;
@@ -41,7 +49,12 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
   {
     const size_t base = (((size_t)n * Hv + hv) * DV + dv0 + 16 * half) * DK + dk;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) s[j] = a.h0 ? a.h0[base + (size_t)j * DK] : 0.f;
+    for (int j = 0; j < 16; ++j) s[j] = (a.h0 && !a.ckpt_in) ? a.h0[base + (size_t)j * DK] : 0.f;
+    if (a.ckpt_in) {
+      const float* ck = a.ckpt_in + (((size_t)c_first * Hv + hv) * DV + dv0 + 16 * half) * DK + dk;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) s[j] = ck[(size_t)j * DK];
+    }
   }
 
   // One thread of warp 1 moves everything a chunk reads (the [K; Q], T and P images, the gates and the
@@ -212,12 +225,15 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
         const float qy = __shfl_xor_sync(0xffffffffu, yp[j], 16);
         y8[j] = kside ? u[j] + qy : u[8 + j] + yp[8 + j];
       }
-      if (L == C)  // a full chunk goes out by one TMA store after the next barrier
+      if (a.ckpt_in) {
+        // recompute mode: D is the product, y is not written
+      } else if (L == C) {  // a full chunk goes out by one TMA store after the next barrier
         store_row8<Tout>(reinterpret_cast<Tout*>(smem + FW_Y) + i_row * DVT + 16 * half + 8 * hc, y8);
-      else if (i_row < L)  // the rows after a sequence's end belong to the next sequence: not written
+      } else if (i_row < L) {  // the rows after a sequence's end belong to the next sequence: not written
         store_row8<Tout>(static_cast<Tout*>(a.y) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0 + 16 * half + 8 * hc, y8);
+      }
     }
-    ystage_tok = L == C ? tok0 : -1;
+    ystage_tok = (L == C && !a.ckpt_in) ? tok0 : -1;
     tc::fence_async_smem();
     tc::fence_before_sync();
   }
@@ -250,7 +266,8 @@ cudaError_t launch_chunk_fwd_state(const CUtensorMap& vmap, const CUtensorMap& y
   auto kern = out_bf16 ? gdn_chunk_fwd_state<__nv_bfloat16> : gdn_chunk_fwd_state<float>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FW_SMEM);
   if (e != cudaSuccess) return e;
-  kern<<<dim3(DV / DVT, Hv, N), 256, FW_SMEM, st>>>(vmap, ymap, a);
+  // recompute mode: one CTA per (slice, value head, chunk)
+  kern<<<dim3(DV / DVT, Hv, a.ckpt_in ? (unsigned)a.geo_chunks : (unsigned)N), 256, FW_SMEM, st>>>(vmap, ymap, a);
   note_launch();
   return cudaGetLastError();
 }

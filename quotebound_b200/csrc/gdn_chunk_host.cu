@@ -75,7 +75,8 @@ struct Saved {
   float* Ds;
 };
 
-int64_t saved_layout(int Hv, int Hk, int64_t n_chunks, char* base, Saved* s) {
+// with_ckpt false: the layout without its chunk-start states (a backward given them by the caller).
+int64_t saved_layout(int Hv, int Hk, int64_t n_chunks, char* base, Saved* s, bool with_ckpt = true) {
   int64_t off = 0;
   auto take = [&](int64_t bytes) {
     char* at = base ? base + off : nullptr;
@@ -83,7 +84,7 @@ int64_t saved_layout(int Hv, int Hk, int64_t n_chunks, char* base, Saved* s) {
     return at;
   };
   Saved x;
-  x.ckpt = (float*)take(n_chunks * Hv * (int64_t)DV * DK * 4);
+  x.ckpt = (float*)take(with_ckpt ? n_chunks * Hv * (int64_t)DV * DK * 4 : 0);
   x.gates = (float*)take(n_chunks * Hv * 128 * 4);
   x.Timg = (uint8_t*)take(n_chunks * Hv * 16384);
   x.Pimg = (uint8_t*)take(n_chunks * Hv * 16384);
@@ -111,7 +112,7 @@ struct Ws {
 };
 
 int64_t ws_layout(int Hv, int Hk, int N, int64_t n_chunks, bool layer, bool varlen, int op, bool with_saved,
-                  char* base, Ws* w) {
+                  char* base, Ws* w, bool ckpt_external = false) {
   int64_t off = 0;
   auto take = [&](int64_t bytes) {
     char* at = base ? base + off : nullptr;
@@ -131,7 +132,7 @@ int64_t ws_layout(int Hv, int Hk, int N, int64_t n_chunks, bool layer, bool varl
     x.Aimg = (uint8_t*)take(n_chunks * Hv * (DV / DVT) * 16384);
     x.head_part = (float*)take(layer ? n_chunks * Hv * 2 * 4 : 0);
     if (with_saved) {
-      x.saved = take(saved_layout(Hv, Hk, n_chunks, nullptr, nullptr));
+      x.saved = take(saved_layout(Hv, Hk, n_chunks, nullptr, nullptr, !ckpt_external));
       x.fwd_ws = take(ws_layout(Hv, Hk, N, n_chunks, layer, varlen, 0, false, nullptr, nullptr));
     }
   }
@@ -149,8 +150,8 @@ int64_t chunked_saved_bytes(int Hv, int Hk, int64_t n_chunks, int64_t tokens, bo
 }
 
 int64_t chunked_ws_bytes(int Hv, int Hk, int N, int64_t n_chunks, int64_t tokens, bool varlen, int op, bool with_saved,
-                         bool layer) {
-  return ws_layout(Hv, Hk, N, n_chunks, layer, varlen, op, with_saved, nullptr, nullptr);
+                         bool layer, bool ckpt_external) {
+  return ws_layout(Hv, Hk, N, n_chunks, layer, varlen, op, with_saved, nullptr, nullptr, ckpt_external);
 }
 
 cudaError_t chunked_fwd(const ChunkFwdArgs& a, void* ws, cudaStream_t st, int* status) {
@@ -163,8 +164,8 @@ cudaError_t chunked_fwd(const ChunkFwdArgs& a, void* ws, cudaStream_t st, int* s
   float *gates = w.gates, *ckpt = nullptr;
   uint8_t *Ti = w.Timg, *Pi = w.Pimg, *KQi = w.KQimg;
   if (a.saved) {
-    saved_layout(a.Hv, a.Hk, a.n_chunks, (char*)a.saved, &sv);
-    gates = sv.gates, ckpt = sv.ckpt;
+    saved_layout(a.Hv, a.Hk, a.n_chunks, (char*)a.saved, &sv, a.ckpt_in == nullptr);
+    gates = sv.gates, ckpt = a.ckpt_in ? nullptr : sv.ckpt;
     Ti = sv.Timg, Pi = sv.Pimg, KQi = sv.KQimg;
   }
   cudaError_t e;
@@ -180,7 +181,9 @@ cudaError_t chunked_fwd(const ChunkFwdArgs& a, void* ws, cudaStream_t st, int* s
   CUtensorMap vmap, ymap;
   if (!map_rows(&vmap, a.v, rows, a.Hv, a.Dv, DVT, C) || !map_rows(&ymap, a.y, rows, a.Hv, a.Dv, DVT, C, !a.out_bf16))
     return cudaErrorInvalidValue;
-  StateArgs sa{geo, a.v, gates, a.h0, a.y, a.hT, ckpt, Ti, Pi, KQi, a.saved ? sv.Ds : nullptr, err};
+  StateArgs sa{geo, a.v, gates, a.h0, a.y, a.hT, ckpt, Ti, Pi, KQi, a.saved ? sv.Ds : nullptr, err, a.ckpt_in,
+               a.n_chunks};
+  if (a.ckpt_in && (a.n_chunks == 0 || a.hT)) return cudaErrorInvalidValue;  // recompute mode writes D alone
   return launch_chunk_fwd_state(vmap, ymap, sa, a.Hv, a.N, a.out_bf16, st);
 }
 
@@ -189,7 +192,8 @@ cudaError_t chunked_bwd(const ChunkBwdArgs& a, void* ws, cudaStream_t st) {
   const bool layer = a.g == nullptr;
   const int64_t rows = (int64_t)a.B * a.T;
   Ws w;
-  ws_layout(a.Hv, a.Hk, a.N, a.n_chunks, layer, a.cu != nullptr, 1, a.saved == nullptr, (char*)ws, &w);
+  ws_layout(a.Hv, a.Hk, a.N, a.n_chunks, layer, a.cu != nullptr, 1, a.saved == nullptr, (char*)ws, &w,
+            a.ckpt_in != nullptr);
   cudaError_t e;
   const void* saved = a.saved;
   if (!saved) {  // recompute the forward's intermediates with the same forward (y is discarded into dv)
@@ -198,11 +202,13 @@ cudaError_t chunked_bwd(const ChunkBwdArgs& a, void* ws, cudaStream_t st) {
     f.cu = a.cu, f.q = a.q, f.k = a.k, f.v = a.v, f.g = a.g, f.beta = a.beta, f.h0 = a.h0, f.y = a.dv;
     f.saved = w.saved, f.in_bf16 = a.in_bf16, f.out_bf16 = a.out_bf16;
     f.a_raw = a.a_raw, f.b_raw = a.b_raw, f.A_log = a.A_log, f.dt_bias = a.dt_bias;
-    if ((e = chunked_fwd(f, w.fwd_ws, st, w.err)) != cudaSuccess) return e;
+    f.ckpt_in = a.ckpt_in;  // given the chunk-start states: every chunk recomputed on its own (no walk)
+    if (a.n_chunks > 0 && (e = chunked_fwd(f, w.fwd_ws, st, w.err)) != cudaSuccess) return e;
     saved = w.saved;
   }
   Saved sv;
-  saved_layout(a.Hv, a.Hk, a.n_chunks, (char*)saved, &sv);
+  saved_layout(a.Hv, a.Hk, a.n_chunks, (char*)saved, &sv, a.ckpt_in == nullptr);
+  if (a.ckpt_in) sv.ckpt = const_cast<float*>(a.ckpt_in);
   if (a.cu && (e = launch_chunk_offsets(a.cu, a.N, w.chunk_off, st)) != cudaSuccess) return e;
   Geo geo{a.T, a.Hk, a.Hv, a.N, (a.T + C - 1) / C, a.cu, a.cu ? w.chunk_off : nullptr};
   CUtensorMap dmap, vmap, dvmap;

@@ -409,6 +409,10 @@ struct StateArgs {
   // training: D = T E for the backward (or null), fp32 tiles [chunks, Hv, Dv / 32 slices][64 rows][32]
   float* Ds;
   int* err;
+  // recompute mode (non-null): every chunk on its own, its start state read from these chunk-start states
+  // [chunks, Hv, Dv, Dk]; D is written, y, the final state and the checkpoint are not
+  const float* ckpt_in;
+  int64_t geo_chunks;  // the number of chunks (the grid's z extent in recompute mode)
 };
 
 // The backward state walk: chunks in reverse, 32 rows of dS per CTA (thread t holds dS[dv0+j][t]).

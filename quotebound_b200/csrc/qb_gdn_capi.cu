@@ -217,6 +217,11 @@ int64_t qb_gdn_workspace_bytes(const qb_gdn_desc* d, int32_t op, char* err, int 
                             op == QB_OP_LAYER_BWD, true);
   }
   if (check_desc(d, &p, err, errlen)) return -1;
+  if (op == QB_OP_BWD_CKPT) {
+    if (chunked_bwd_of(p))
+      return chunked_ws_bytes(d->Hv, d->Hk, p.N, p.n_chunks, p.tokens, p.varlen, QB_OP_BWD, true, false, true);
+    return simt_ws_bytes(d, p, QB_OP_BWD, false, nullptr, nullptr);
+  }
   if (op != QB_OP_FWD && op != QB_OP_BWD) return fail(err, errlen, "gated delta: unknown op %d", op);
   // the backward's figure covers recomputing the saved states (saved == NULL)
   return ws_bytes_of(d, p, op, op == QB_OP_BWD);
@@ -413,6 +418,71 @@ int qb_gdn_bwd(const qb_gdn_desc* d, const void* q, const void* k, const void* v
   c.dq = dq, c.dk = dk, c.dv = dv, c.dg = dg, c.dbeta = dbeta, c.dh0 = dh0;
   if ((e = cc_bwd(c, p.N, in_bf16, out_bf16, st)) != cudaSuccess) return cuda_fail(e, "gated delta backward", err, errlen);
   return 0;
+}
+
+int64_t qb_gdn_ckpt_bytes(const qb_gdn_desc* d, char* err, int errlen) {
+  Plan p;
+  if (check_desc(d, &p, err, errlen)) return -1;
+  return p.n_chunks * d->Hv * (int64_t)d->Dv * d->Dk * 4;
+}
+
+int qb_gdn_bwd_from_ckpt(const qb_gdn_desc* d, const void* q, const void* k, const void* v, const float* g,
+                         const float* beta, const float* h0, const void* dy, const float* dhT, const float* ckpt,
+                         void* dq, void* dk, void* dv, float* dg, float* dbeta, float* dh0, void* ws, int64_t ws_bytes,
+                         void* stream, char* err, int errlen) {
+  Plan p;
+  if (check_desc(d, &p, err, errlen)) return -1;
+  if (!q || !k || !v || !g || !beta || !dy || !ckpt || !dq || !dk || !dv || !dg || !dbeta)
+    return fail(err, errlen, "gated delta backward from ckpt: inputs, ckpt and every gradient but dh0 must be non-null");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(dy, 16) || !aligned(dq, 16) ||
+      !aligned(dk, 16) || !aligned(dv, 16) || !aligned(ckpt, 16) || (dhT && !aligned(dhT, 16)) ||
+      (dh0 && !aligned(dh0, 16)))
+    return fail(err, errlen, "gated delta backward from ckpt: tensors need 16-byte alignment");
+  const bool chunked = chunked_bwd_of(p);
+  if (chunked && p.n_chunks > 65535)
+    return fail(err, errlen, "gated delta backward from ckpt: at most 65535 chunks per call (got %lld)",
+                (long long)p.n_chunks);
+  const int64_t need = chunked ? chunked_ws_bytes(d->Hv, d->Hk, p.N, p.n_chunks, p.tokens, p.varlen, QB_OP_BWD, true,
+                                                  false, true)
+                               : simt_ws_bytes(d, p, QB_OP_BWD, false, nullptr, nullptr);
+  if (!ws || ws_bytes < need || !aligned(ws, 256))
+    return fail(err, errlen, "gated delta backward from ckpt: a 256-byte aligned workspace of %lld bytes is needed "
+                "(got %lld)", (long long)need, (long long)ws_bytes);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (cudaError_t e = init_status((int*)ws, st)) return cuda_fail(e, "gated delta backward from ckpt", err, errlen);
+  if (p.tokens == 0) {
+    if (!dh0) return 0;
+    const size_t bytes = (size_t)p.N * d->Hv * d->Dv * d->Dk * 4;
+    cudaError_t e = dhT ? cudaMemcpyAsync(dh0, dhT, bytes, cudaMemcpyDeviceToDevice, st) : cudaMemsetAsync(dh0, 0, bytes, st);
+    return e == cudaSuccess ? 0 : cuda_fail(e, "gated delta backward from ckpt", err, errlen);
+  }
+  const int in_bf16 = d->in_dtype == QB_DTYPE_BF16, out_bf16 = d->out_dtype == QB_DTYPE_BF16;
+  cudaError_t e;
+  if (chunked) {
+    ChunkBwdArgs a{};
+    a.B = d->B, a.T = d->T, a.Hk = d->Hk, a.Hv = d->Hv, a.Dk = d->Dk, a.Dv = d->Dv, a.N = p.N;
+    a.n_chunks = p.n_chunks;
+    a.cu = d->cu_seqlens;
+    a.q = q, a.k = k, a.v = v, a.g = g, a.beta = beta, a.h0 = h0, a.dy = dy, a.dhT = dhT, a.saved = nullptr;
+    a.dq = dq, a.dk = dk, a.dv = dv, a.dg = dg, a.dbeta = dbeta, a.dh0 = dh0;
+    a.in_bf16 = in_bf16, a.out_bf16 = out_bf16;
+    a.ckpt_in = ckpt;
+    e = chunked_bwd(a, ws, st);
+    return e == cudaSuccess ? 0 : cuda_fail(e, "gated delta backward from ckpt (chunked)", err, errlen);
+  }
+  SimtWs w;
+  simt_ws_bytes(d, p, QB_OP_BWD, false, &w, (char*)ws);
+  if (p.varlen && (e = launch_chunk_offsets(d->cu_seqlens, p.N, w.chunk_off, st)) != cudaSuccess)
+    return cuda_fail(e, "gated delta backward from ckpt", err, errlen);
+  CcArgs c{};
+  cc_ws_layout(d->Hk, d->Hv, d->Dk, d->Dv, p.n_chunks, w.cc, &c);
+  c.geo = Geo{d->T, d->Hk, d->Hv, p.N, (d->T + kChunkSteps - 1) / kChunkSteps, d->cu_seqlens,
+              p.varlen ? w.chunk_off : nullptr};
+  c.n_chunks = p.n_chunks, c.Dk = d->Dk, c.Dv = d->Dv;
+  c.q = q, c.k = k, c.v = v, c.dy = dy, c.g = g, c.beta = beta, c.ckpt = ckpt, c.dhT = dhT;
+  c.dq = dq, c.dk = dk, c.dv = dv, c.dg = dg, c.dbeta = dbeta, c.dh0 = dh0;
+  e = cc_bwd(c, p.N, in_bf16, out_bf16, st);
+  return e == cudaSuccess ? 0 : cuda_fail(e, "gated delta backward from ckpt", err, errlen);
 }
 
 int qb_gdn_status(const void* ws, int32_t* code, void* stream, char* err, int errlen) {

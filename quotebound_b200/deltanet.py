@@ -26,7 +26,7 @@ from . import _lib, checks
 from ._lib import Desc, QbError, err_buf, load
 
 __all__ = ["gated_delta", "gated_delta_trainable", "gated_delta_vjp", "gated_delta_fwd", "gated_delta_bwd",
-           "saved_bytes", "workspace_bytes", "QbError"]
+           "gated_delta_bwd_from_ckpt", "ckpt_bytes", "saved_ckpt", "saved_bytes", "workspace_bytes", "QbError"]
 
 
 def _dtype_code(t: torch.dtype) -> int:
@@ -194,6 +194,57 @@ def gated_delta_bwd(q, k, v, g, beta, state, dy, dstate=None, *, saved=None, cu_
     if checks.enabled(check):
         checks.require_ok("gated delta backward", ws)
         checks.require_finite("gated delta backward", dq=dq, dk=dk, dv=dv, dg=dg, dbeta=dbeta, dstate=dh0)
+    return dq, dk, dv, dg, dbeta, dh0
+
+
+def ckpt_bytes(desc: Desc) -> int:
+    err = err_buf()
+    n = load().qb_gdn_ckpt_bytes(ctypes.byref(desc), err, len(err))
+    if n < 0:
+        raise ValueError(err.value.decode())
+    return int(n)
+
+
+def saved_ckpt(saved, q, v, cu_seqlens=None, algo=0):
+    """The chunk-start states [N_chunks, Hv, Dv, Dk] float32 at the head of a training forward's saved
+    buffer (a view, no copy)."""
+    cu_dev, cu_host = _cu_pair(cu_seqlens, q.device)
+    d = make_desc(q, v, cu_dev, cu_host, _act_dtype(q, v), None, algo)
+    n = ckpt_bytes(d)
+    return saved[:n].view(torch.float32).view(-1, v.shape[2], v.shape[3], q.shape[3])
+
+
+def gated_delta_bwd_from_ckpt(q, k, v, g, beta, dy, ckpt, dstate=None, *, cu_seqlens=None, algo=0, grad_dtype=None,
+                              check=None):
+    """gated_delta_vjp given the chunk-start states ckpt [N_chunks, Hv, Dv, Dk] float32 (the reference's
+    ckpt, src/delta_grad.cpp:172-181): (dq, dk, dv, dg, dbeta, dstate0)."""
+    dev = q.device
+    adt = _act_dtype(q, k, v, dy)
+    q, k, v, dy = _prep(q, adt), _prep(k, adt), _prep(v, adt), _prep(dy, adt)
+    g, beta = _prep(g, torch.float32), _prep(beta, torch.float32)
+    ckpt, dstate = _prep(ckpt, torch.float32), _prep(dstate, torch.float32)
+    cu_dev, cu_host = _cu_pair(cu_seqlens, dev)
+    n_seqs = q.shape[0] if cu_host is None else cu_host.numel() - 1
+    _check_inputs(q, k, v, g, beta, None, n_seqs)
+    gdt = grad_dtype or adt
+    d = make_desc(q, v, cu_dev, cu_host, adt, gdt, algo)
+    if ckpt.numel() * 4 != ckpt_bytes(d):
+        raise ValueError(f"gated delta: ckpt must hold {ckpt_bytes(d) // 4} floats (got {ckpt.numel()})")
+    dq, dk = torch.empty(q.shape, dtype=gdt, device=dev), torch.empty(k.shape, dtype=gdt, device=dev)
+    dv = torch.empty(v.shape, dtype=gdt, device=dev)
+    dg = torch.empty(g.shape, dtype=torch.float32, device=dev)
+    dbeta = torch.empty(beta.shape, dtype=torch.float32, device=dev)
+    dh0 = torch.empty(n_seqs, v.shape[2], v.shape[3], q.shape[3], dtype=torch.float32, device=dev)
+    wsb = workspace_bytes(d, _lib.QB_OP_BWD_CKPT)
+    ws = _empty_bytes(wsb, dev)
+    err = err_buf()
+    rc = load().qb_gdn_bwd_from_ckpt(ctypes.byref(d), _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), None, _ptr(dy),
+                                     _ptr(dstate), _ptr(ckpt), _ptr(dq), _ptr(dk), _ptr(dv), _ptr(dg), _ptr(dbeta),
+                                     _ptr(dh0), _ptr(ws), wsb, _stream(dev), err, len(err))
+    _lib.check(rc, err)
+    if checks.enabled(check):
+        checks.require_ok("gated delta backward from ckpt", ws)
+        checks.require_finite("gated delta backward from ckpt", dq=dq, dk=dk, dv=dv, dg=dg, dbeta=dbeta, dstate=dh0)
     return dq, dk, dv, dg, dbeta, dh0
 
 

@@ -285,3 +285,50 @@ def test_gate_fwd_bwd(dtype):
         assert rel(x, w) <= 1e-5
     for x, w in zip(got_b, want_b):
         assert rel(x, w) <= 1e-5
+
+
+# ---- the chunk-start states as a shared format (qb_gdn_ckpt_bytes, qb_gdn_bwd_from_ckpt) ----
+def oracle_ckpt(p, cu=None):
+    """The state at the start of every 64-step chunk, by the oracle run chunk by chunk with the state
+    carried -- as the reference builds its ckpt (src/delta_grad.cpp:172-181)."""
+    f = lambda t: None if t is None else t.float().cpu().numpy()
+    q, k, v, g, beta = f(p.q), f(p.k), f(p.v), f(p.g), f(p.beta)
+    B, T, Hk, Dk = q.shape
+    Hv, Dv = v.shape[2], v.shape[3]
+    seqs = [(b, 0, T) for b in range(B)] if cu is None else [(0, cu[n], cu[n + 1]) for n in range(len(cu) - 1)]
+    out = []
+    for n, (b, t0, t1) in enumerate(seqs):
+        s = np.zeros((1, Hv, Dv, Dk), np.float32) if p.h0 is None else f(p.h0)[n:n + 1]
+        for c0 in range(t0, t1, 64):
+            out.append(s[0])
+            c1 = min(t1, c0 + 64)
+            sl = lambda a: np.ascontiguousarray(a[b:b + 1, c0:c1])
+            _, s = oracle.gated_delta_fwd(sl(q), sl(k), sl(v), sl(g), sl(beta), s)
+    return np.stack(out)
+
+
+@pytest.mark.parametrize("algo,dtype,tol", [(ROWS, torch.float32, 1e-5), (CHUNKED, torch.bfloat16, 2e-3)])
+@pytest.mark.parametrize("lengths", [None, [130, 1, 64, 257, 40]])
+def test_backward_from_ckpt(algo, dtype, tol, lengths):
+    """gated_delta_vjp given the chunk-start states alone: from the oracle's ckpt, and from the head of a
+    training forward's saved buffer (the states it stores there match the oracle's)."""
+    cu = synthetic.cu_from_lengths(lengths) if lengths else None
+    T = cu[-1] if cu else 200
+    B = 1 if cu else 2
+    Hk, Hv, D = (4, 8, 64) if algo == ROWS else (4, 8, 128)
+    p = synthetic.make(B, T, Hk, Hv, D, D, seed=31, dtype=dtype, h0_std=0.1, dhT_std=0.1, cu_seqlens=cu,
+                       uniform_gate=0.9)
+    want = oracle_all(p, cu)[2]
+    ck = oracle_ckpt(p, cu)
+    d = p.to("cuda")
+    got = deltanet.gated_delta_bwd_from_ckpt(d.q, d.k, d.v, d.g, d.beta, d.dy, torch.from_numpy(ck).cuda(), d.dhT,
+                                             cu_seqlens=cu, algo=algo, check=True)
+    for n, a, b in zip(("dq", "dk", "dv", "dg", "dbeta", "dh0"), got, want):
+        assert rel(a, b) <= tol, (n, rel(a, b))
+    _, _, saved = deltanet.gated_delta_fwd(d.q, d.k, d.v, d.g, d.beta, d.h0, save=True, cu_seqlens=cu, algo=algo)
+    head = deltanet.saved_ckpt(saved, d.q, d.v, cu_seqlens=cu, algo=algo)
+    assert rel(head, ck) <= (1e-6 if algo == ROWS else 1e-3)  # the tensor-core path stores them tf32-rounded
+    again = deltanet.gated_delta_bwd_from_ckpt(d.q, d.k, d.v, d.g, d.beta, d.dy, head.clone(), d.dhT, cu_seqlens=cu,
+                                               algo=algo)
+    for n, a, b in zip(("dq", "dk", "dv", "dg", "dbeta", "dh0"), again, want):
+        assert rel(a, b) <= tol, (n, rel(a, b))
