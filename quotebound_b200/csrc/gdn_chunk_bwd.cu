@@ -15,6 +15,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
   __shared__ __align__(16) float sg[2][128];
   __shared__ uint64_t bar_tma[2], bar_t, bar_p, bar_mma, bar_drain;
   __shared__ uint32_t tmem_slot;
+  __shared__ int s_hook[2];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quad = warp & 3, half = warp >> 2, dk = tid & 127;
@@ -33,6 +34,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
     tc::mbar_init(&bar_p, 1);
     tc::mbar_init(&bar_mma, 1);
     tc::mbar_init(&bar_drain, 1);
+    tc::load_hook(s_hook, a.err);
     tc::fence_mbar_init();
   }
   tc::fence_before_sync();
@@ -100,7 +102,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
     tc::st_row_hilo16(smem + BW_S, dk, ds, half);
     // (each thread waits for the chunk's rows and gates itself: steps 1 and 2 share one barrier)
     const bool waits = ok;
-    bool okw = ok && tc::mbar_wait_or_drain(&bar_tma[buf], (uint32_t)((it >> 1) & 1), a.err, 20);
+    bool okw = ok && tc::mbar_wait_or_drain(&bar_tma[buf], (uint32_t)((it >> 1) & 1), a.err, 20, s_hook);
     const float* gb = sg[buf];
     const float bi = gb[i_row], be = gb[64 + i_row], gi = __expf(bi), bC = gb[63];
     // 2. dO row i (zero past the end) as the plain bf16 operand of P^T dO, as gamma dO [hi | lo] and, exact
@@ -130,8 +132,8 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
     tc::fence_async_smem();
     tc::fence_before_sync();
     if (waits) {  // (the T and P waits run even when the row wait gave up, so that all three have landed)
-      const bool okt = tc::mbar_wait_or_drain(&bar_t, (uint32_t)(it & 1), a.err, 25);
-      const bool okp = tc::mbar_wait_or_drain(&bar_p, (uint32_t)(it & 1), a.err, 26);
+      const bool okt = tc::mbar_wait_or_drain(&bar_t, (uint32_t)(it & 1), a.err, 25, s_hook);
+      const bool okp = tc::mbar_wait_or_drain(&bar_p, (uint32_t)(it & 1), a.err, 26, s_hook);
       okw = okw && okt && okp;
       seen = it + 1;
     }
@@ -160,7 +162,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
       if (jc > 0) issue_main(jc - 1, buf ^ 1);  // the previous chunk's [K; Q], gates and dO rows
     }
     if (jc > 0) main_issued = it + 2;
-    ok = ok && tc::mbar_wait_or_drain(&bar_mma, ph, a.err, 21);
+    ok = ok && tc::mbar_wait_or_drain(&bar_mma, ph, a.err, 21, s_hook);
     ph ^= 1;
     tc::fence_after_sync();
     if (ok && tid == 32 && jc > 0) {  // P's last reader has completed
@@ -214,7 +216,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
           tc::mma_bf16(tmem + cF, desc_img_t(timg, part, ks), desc_hl(dd, ks), idF, (part | ks) ? 1u : 0u);
       tc::mma_commit(&bar_mma);
     }
-    ok = ok && tc::mbar_wait_or_drain(&bar_mma, ph, a.err, 22);
+    ok = ok && tc::mbar_wait_or_drain(&bar_mma, ph, a.err, 22, s_hook);
     ph ^= 1;
     tc::fence_after_sync();
     if (ok && tid == 32 && jc > 0) {  // T's last reader has completed
@@ -267,7 +269,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_state(const __grid_const
       if (L == C) tc::tma_store_3d(&dvmap, smem + BW_DV, dv0, hv, (int)tok0);
       tc::bulk_commit();
     }
-    ok = ok && tc::mbar_wait_or_drain(&bar_mma, ph, a.err, 23);
+    ok = ok && tc::mbar_wait_or_drain(&bar_mma, ph, a.err, 23, s_hook);
     ph ^= 1;
     tc::fence_after_sync();
     {

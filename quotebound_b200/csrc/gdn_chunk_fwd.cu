@@ -13,6 +13,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
   __shared__ __align__(16) float sg[2][128];
   __shared__ uint64_t bar_tma[2], bar_mma, bar_drain;
   __shared__ uint32_t tmem_slot;
+  __shared__ int s_hook[2];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quad = warp & 3, half = warp >> 2, dk = tid & 127;
@@ -37,6 +38,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
     tc::mbar_init(&bar_tma[1], 1);
     tc::mbar_init(&bar_mma, 1);
     tc::mbar_init(&bar_drain, 1);
+    tc::load_hook(s_hook, a.err);
     tc::fence_mbar_init();
   }
   tc::fence_before_sync();
@@ -105,7 +107,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
     tc::fence_async_smem();
     tc::fence_before_sync();
     const bool waits = ok;
-    ok = __syncthreads_and(ok && tc::mbar_wait_or_drain(&bar_tma[buf], (uint32_t)((jc >> 1) & 1), a.err, 10)) != 0;
+    ok = __syncthreads_and(ok && tc::mbar_wait_or_drain(&bar_tma[buf], (uint32_t)((jc >> 1) & 1), a.err, 10, s_hook)) != 0;
     if (waits) loads_seen = jc + 1;
     tc::fence_after_sync();
     if (!ok) break;
@@ -132,7 +134,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
       raw.w[1] = i_row < L ? vp[1] : make_uint4(0, 0, 0, 0);
       cvt_row16(raw, vr);
     }
-    ok = ok && tc::mbar_wait_or_drain(&bar_mma, ph, a.err, 11);
+    ok = ok && tc::mbar_wait_or_drain(&bar_mma, ph, a.err, 11, s_hook);
     ph ^= 1;
     tc::fence_after_sync();
     // 3. K side: E = diag(beta) (V - diag(gamma) K S^T) as the [hi | lo] operand; Q side: gamma Q S^T
@@ -163,7 +165,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
       tc::mma_commit(&bar_mma);
     }
 
-    ok = ok && tc::mbar_wait_or_drain(&bar_mma, ph, a.err, 12);
+    ok = ok && tc::mbar_wait_or_drain(&bar_mma, ph, a.err, 12, s_hook);
     ph ^= 1;
     tc::fence_after_sync();
     {
@@ -205,7 +207,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
       tc::bulk_store(a.Ds + ptile, smem + FW_DS + buf * 8192, 8192);
       tc::bulk_commit();
     }
-    ok = ok && tc::mbar_wait_or_drain(&bar_mma, ph, a.err, 13);
+    ok = ok && tc::mbar_wait_or_drain(&bar_mma, ph, a.err, 13, s_hook);
     ph ^= 1;
     tc::fence_after_sync();
     {

@@ -19,6 +19,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
   __shared__ float snorm[2][2][128];
   __shared__ uint64_t bar_kq, bar_h, bar_kk, bar_s[2], bar_mma, bar_drain;
   __shared__ uint32_t tmem_slot;
+  __shared__ int s_hook[2];
   __shared__ int s_last;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -44,6 +45,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
     tc::mbar_init(&bar_s[1], 1);
     tc::mbar_init(&bar_mma, 1);
     tc::mbar_init(&bar_drain, 1);
+    tc::load_hook(s_hook, a.err);
     tc::fence_mbar_init();
   }
   tc::fence_before_sync();
@@ -97,7 +99,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
   // failure path bookkeeping: value heads and slices whose loads were issued, and those whose waits
   // this thread ran (the issuing thread's view is the one used)
   int h_issued = 1, h_seen = 0, s_issued = 1, s_seen = 0;
-  bool ok = wait_all(&bar_kq, 0, a.err, 30);
+  bool ok = wait_all(&bar_kq, 0, a.err, 30, s_hook);
   const uint32_t kq = tc::smem_u32(smem + GR_KQ);
   // K K^T (the same for every value head of the group): the image's K row groups (2 KB each) copied
   // unchanged into a K-only tile (the swizzle is relative to 1 KB, so whole groups keep it), then
@@ -128,7 +130,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
 
   for (int r = 0; r < ratio && ok; ++r) {
     const int hv = hk * ratio + r;
-    ok = wait_all(&bar_h, (uint32_t)(r & 1), a.err, 31);
+    ok = wait_all(&bar_h, (uint32_t)(r & 1), a.err, 31, s_hook);
     h_seen = r + 1;
     if (!ok) break;
     const float* sg = sgt[r & 1];
@@ -148,6 +150,11 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
         dtb = __ldg(a.dt_bias + hv);
       }
     }
+    if (tid < 64) {  // this row's gate g_t for the gate gradient's recurrence (1 past the sequence's end)
+      float lg = 0.f;
+      if (tid < L) lg = a.g ? fmaxf(logf(in0), -88.f) : -expf(eA) * softplus_f(in0 + dtb);
+      sdb[tid] = __expf(lg);
+    }
 
     for (int sl = 0; sl < NSL && ok; ++sl) {
       const int q = r * NSL + sl, bs = q & 1;
@@ -155,7 +162,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
       // each thread waits for the slice's data itself; the barrier at the end of the slice keeps the
       // buffers' reuse ordered and makes a failed wait everyone's
       if (ok) s_seen = q + 1;
-      ok = ok && tc::mbar_wait_or_drain(&bar_s[bs], (uint32_t)((q >> 1) & 1), a.err, 37);
+      ok = ok && tc::mbar_wait_or_drain(&bar_s[bs], (uint32_t)((q >> 1) & 1), a.err, 37, s_hook);
       // the other buffer's last reader has finished (the finalize uses the second buffer, so the next
       // value head's first slice goes out during this head's last slice)
       if (ok && tid == 32 && q + 1 < ratio * NSL) {
@@ -206,11 +213,18 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
           fv = fmaf(f[2 * e + 1], __high2float(h2), fv);
         }
       }
-      ok = __syncthreads_and(ok && tc::mbar_wait_or_drain(&bar_mma, ph_mma, a.err, 34)) != 0;
+      ok = __syncthreads_and(ok && tc::mbar_wait_or_drain(&bar_mma, ph_mma, a.err, 34, s_hook)) != 0;
       ph_mma ^= 1;
       tc::fence_after_sync();
     }
     if (!ok) break;
+
+    {  // the slices' S (.) dS, per warp (read by the gate gradient after the next barrier)
+      float t5w = t5;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) t5w += __shfl_xor_sync(0xffffffffu, t5w, o);
+      if (lane == 0) sred[warp] = t5w;
+    }
 
     // e. finalize this value head
     // e1. the row terms from the unscaled products, and their scaled sum into dQ (lower lanes) and dK
@@ -246,7 +260,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
         srow[3][half][i_row] = tb;   // t4
       }
     }
-    ok = wait_all(&bar_kk, 0u, a.err, 35);
+    ok = wait_all(&bar_kk, 0u, a.err, 35, s_hook);
     if (!ok) break;
     tc::fence_after_sync();
     float* scratch = reinterpret_cast<float*>(smem + GR_SCR);  // [64][65], then 4 x 64 column partials
@@ -304,8 +318,18 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
         kh[k] = dl * be * gam;      // dKK
       }
       (void)pv;
+      if (i_row == 63) {  // row 63 is the chunk's end: the end state's products lambda_j
+#pragma unroll
+        for (int k = 0; k < 16; ++k) xs[k] += srow[3][0][j0 + k] + srow[3][1][j0 + k];
+      }
 #pragma unroll
       for (int k = 0; k < 16; ++k) scratch[i_row * 65 + 1 + j0 + k] = xs[k];
+      if (lower && half == 0) {  // column 0: the gamma terms (and the end state's gamma_C <S, dS>)
+        float c0v = (srow[0][0][i_row] + srow[0][1][i_row]) - be * (srow[2][0][i_row] + srow[2][1][i_row]);
+        if (i_row == 63)
+          for (int w = 0; w < 8; ++w) c0v += sred[w];
+        scratch[i_row * 65] = c0v;
+      }
       const int rr = img_row(i_row), c0 = j0 >> 3;
       st_hilo16_chunks(smem + GR_FHI, smem + GR_FLO, rr, ph, c0);
       st_hilo16_chunks(smem + GR_FHI, smem + GR_FLO, rr + 16, kh, c0);
@@ -313,12 +337,6 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
     {  // the L terms of d beta, both lanes of the pair, per column half
       const float db2 = dbl + __shfl_xor_sync(0xffffffffu, dbl, 16);
       if (lower) srow[5][half][i_row] = db2;
-    }
-    {
-      float t5w = t5;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) t5w += __shfl_xor_sync(0xffffffffu, t5w, o);
-      if (lane == 0) sred[warp] = t5w;
     }
     tc::fence_async_smem();
     tc::fence_before_sync();
@@ -351,24 +369,9 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
     //   dg_t = sum_{i >= t} Gamma_{i,t} A_{i,t},  A_{i,t} = sum_{e <= t} f[i][e] Gamma_{t-1, e-1}
     // (e = 0 is the chunk start, Gamma_{t-1,-1} = gamma_{t-1}).  A is a linear recurrence in t,
     // A_{i,t+1} = g_t A_{i,t} + f[i][t+1], run as four 16-step segments per row (the four lanes of a
-    // quad) joined by their carries.
-    // 1. column 0 (the gamma terms), the end-state terms of row 63, and each row's gate g_t
-    if (tid < 64) {
-      const int i = tid;
-      const float be_ = sg[64 + i];
-      const float t3_ = srow[0][0][i] + srow[0][1][i];
-      const float t2_ = srow[2][0][i] + srow[2][1][i];
-      const float t4_ = srow[3][0][i] + srow[3][1][i];
-      float st5 = 0.f;
-      for (int w = 0; w < 8; ++w) st5 += sred[w];
-      scratch[i * 65] = t3_ - be_ * t2_ + (i == 63 ? st5 : 0.f);
-      scratch[63 * 65 + 1 + i] += t4_;  // lambda_i: the end state's products (row 63 is the chunk's end)
-      float lg = 0.f;  // past the sequence's end the gate is 1
-      if (i < L) lg = a.g ? fmaxf(logf(in0), -88.f) : -expf(eA) * softplus_f(in0 + dtb);
-      sdb[i] = __expf(lg);
-    }
-    __syncthreads();
-    // 2. thread (row i, segment part): its 16 values of A, then the contributions Gamma_{i,t} A_{i,t}
+    // quad) joined by their carries.  The coefficients f (column 0: the gamma terms, row 63: the end
+    // state's) and the gates g_t are in shared memory since the last barrier.
+    // 1. thread (row i, segment part): its 16 values of A, then the contributions Gamma_{i,t} A_{i,t}
     //    in place over the consumed coefficients
     {
       const int i = tid >> 2, part = tid & 3, s0 = 16 * part;
@@ -402,7 +405,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
       }
     }
     __syncthreads();
-    // 3. dg_t = the column sums (fixed order: four 16-row partials, then their sum)
+    // 2. dg_t = the column sums (fixed order: four 16-row partials, then their sum)
     {
       const int col = tid & 63, part = tid >> 6;
       float cs = 0.f;
@@ -453,7 +456,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
       }
     }
     tc::fence_async_smem();  // the scratch writes before the next TMA into this buffer
-    ok = wait_all(&bar_mma, ph_mma, a.err, 36);
+    ok = wait_all(&bar_mma, ph_mma, a.err, 36, s_hook);
     ph_mma ^= 1;
     tc::fence_after_sync();
   }

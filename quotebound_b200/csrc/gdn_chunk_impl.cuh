@@ -142,8 +142,8 @@ __device__ __forceinline__ int img_row(int i) { return 32 * (i >> 4) + (i & 15);
 
 // Every thread waits for the phase (a wait that gives up drains it, tc::mbar_wait_or_drain); the
 // CTA-wide outcome.
-__device__ __forceinline__ bool wait_all(uint64_t* bar, uint32_t parity, int* err, int code) {
-  return __syncthreads_and(tc::mbar_wait_or_drain(bar, parity, err, code)) != 0;
+__device__ __forceinline__ bool wait_all(uint64_t* bar, uint32_t parity, int* err, int code, const int* hook) {
+  return __syncthreads_and(tc::mbar_wait_or_drain(bar, parity, err, code, hook)) != 0;
 }
 
 

@@ -16,6 +16,7 @@ __global__ void __launch_bounds__(128, 4) gdn_chunk_prep(const __grid_constant__
   __shared__ __align__(16) float sX[2][16][16];  // the inverse's 16 x 16 intermediate products
   __shared__ uint64_t bar_tma, bar_mma;
   __shared__ uint32_t tmem_slot;
+  __shared__ int s_hook[2];
   constexpr int LS = 64;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -29,6 +30,7 @@ __global__ void __launch_bounds__(128, 4) gdn_chunk_prep(const __grid_constant__
   if (tid == 0) {
     tc::mbar_init(&bar_tma, 1);
     tc::mbar_init(&bar_mma, 1);
+    tc::load_hook(s_hook, a.err);
     tc::fence_mbar_init();
   }
   tc::fence_before_sync();
@@ -71,7 +73,7 @@ __global__ void __launch_bounds__(128, 4) gdn_chunk_prep(const __grid_constant__
   float gr[4];
   gate_load(hk * ratio, gr);
 
-  bool ok = wait_all(&bar_tma, 0, a.err, 1);
+  bool ok = wait_all(&bar_tma, 0, a.err, 1, s_hook);
   if (ok && layer) {
     // q and k rows normalised in place as the model does (src/deltanet.cpp:94-97): rms_norm in fp32,
     // rounded to bf16, times the bf16 scalar 1/Dk (q) or 1/sqrt(Dk) (k), rounded again.  Thread t
@@ -134,7 +136,7 @@ __global__ void __launch_bounds__(128, 4) gdn_chunk_prep(const __grid_constant__
       dst[idx] = *reinterpret_cast<const uint4*>((part ? qtile : ktile) + sl * 8192 + g * 2048 + rem);
     }
   }
-  ok = __syncthreads_and(ok && tc::mbar_wait_or_drain(&bar_mma, 0, a.err, 2)) != 0;
+  ok = __syncthreads_and(ok && tc::mbar_wait_or_drain(&bar_mma, 0, a.err, 2, s_hook)) != 0;
   tc::fence_after_sync();
   // The products are the same for every value head of the key head; the gates are not.  Each value
   // head in turn: its gated L and P, T, the images.

@@ -81,23 +81,34 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // then skips its remaining work, waits (again bounded, with no code) for the copies and products it
 // still has in flight, frees its TMEM and returns.  Never spins forever, never traps.
 //
-// err points at the status block that opens every workspace (status.cuh): err[0] the code,
-// err[4] / err[5] a test hook -- when err[4] equals `code`, this wait gives up after err[5] polls,
-// so that a test can make one named wait run out on a normal input.  The hook is read only once the
-// first poll (non-blocking) has failed.
+// err points at the status block that opens every workspace (status.cuh), word 0 the code.  hook is
+// the kernel's shared-memory copy of the block's test hook (words 4 and 5, read once per CTA by
+// load_hook): when hook[0] equals `code`, this wait gives up after hook[1] polls, so that a test can
+// make one named wait run out on a normal input.  The first poll does not suspend, so a wait whose
+// data is still in flight always reaches the hook.
 constexpr uint32_t kMaxPolls = 1u << 24;
 constexpr uint64_t kMaxWaitNs = 1000000000ull;
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
+                                          const int* hook = nullptr) {
   if (mbar_test_wait(bar, parity)) return true;
   uint32_t limit = kMaxPolls;
-  if (err && code > 0 && *(volatile int*)(err + 4) == code) limit = *(volatile uint32_t*)(err + 5);
-  const uint64_t t0 = globaltimer_ns();
+  if (hook && code > 0 && hook[0] == code) limit = (uint32_t)hook[1];
+  uint64_t t0 = 0;  // the wall clock starts at the 256th poll (a short wait never reads it)
   for (uint32_t i = 1; i < limit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255) == 0 && globaltimer_ns() - t0 > kMaxWaitNs) break;
+    if ((i & 255) == 0) {
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) t0 = now;
+      else if (now - t0 > kMaxWaitNs) break;
+    }
   }
   if (err) atomicCAS(err, 0, code);
   return false;
+}
+// The test hook of the status block into shared memory (one thread, before the CTA's first barrier).
+__device__ __forceinline__ void load_hook(int* hook, const int* err) {
+  hook[0] = err ? err[4] : 0;
+  hook[1] = err ? err[5] : 0;
 }
 // The failure path's wait for work still in flight: the full limits, nothing recorded.
 __device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity) {
@@ -106,8 +117,9 @@ __device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity) {
 // mbar_wait for a phase whose copies or products were issued; when it gives up, the same phase is
 // waited for again (mbar_drain), so that they have landed before anything reads or reuses their
 // buffers.  Returns whether the first wait succeeded.
-__device__ __forceinline__ bool mbar_wait_or_drain(uint64_t* bar, uint32_t parity, int* err, int code) {
-  if (mbar_wait(bar, parity, err, code)) return true;
+__device__ __forceinline__ bool mbar_wait_or_drain(uint64_t* bar, uint32_t parity, int* err, int code,
+                                                   const int* hook = nullptr) {
+  if (mbar_wait(bar, parity, err, code, hook)) return true;
   mbar_drain(bar, parity);
   return false;
 }
