@@ -87,6 +87,38 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
   const uint32_t idA = tc::idesc(tc::kBF16, 128, 64, false, true);
   const uint32_t idT = tc::idesc(tc::kBF16, 128, 64, true, true);
   int64_t ystage_tok = -1;  // first token of the full chunk whose output rows wait in the staging tile
+  // The output product P D of a chunk is issued after the chunk's state update and read back during the
+  // next chunk, so that neither it nor the output rows sit on the chain of dependent chunks: yq holds
+  // that chunk's gamma Q S^T rows (Q-side lanes) until then, prev_tok / prev_L its place.
+  const bool outputs = a.ckpt_in == nullptr;  // recompute mode makes no output rows
+  float yq[16];
+  int64_t prev_tok = -1;
+  int prev_L = 0;
+  // the output rows of the chunk whose P D is in TMEM at cO: into the staging tile (full chunks, stored
+  // by one TMA store after the next barrier) or straight to global memory (the rows of a short chunk
+  // before the sequence's end)
+  auto out_rows = [&](float (&y8)[8]) {
+    float o2[16], u[16];
+    tmem_ld_hl16(tl + cO, half, o2);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) u[j] = o2[j] + __shfl_xor_sync(0xffffffffu, o2[j], 16);
+    // both lanes hold P D's row; the K-side lane forms columns 0-7 (with the Q-side lane's gamma Q S^T),
+    // the Q-side lane columns 8-15
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float qy = __shfl_xor_sync(0xffffffffu, yq[j], 16);
+      y8[j] = kside ? u[j] + qy : u[8 + j] + yq[8 + j];
+    }
+  };
+  auto put_rows = [&](const float (&y8)[8]) {
+    const int hc = kside ? 0 : 1;
+    if (prev_L == C) {
+      store_row8<Tout>(reinterpret_cast<Tout*>(smem + FW_Y) + i_row * DVT + 16 * half + 8 * hc, y8);
+    } else if (i_row < prev_L) {  // the rows after a sequence's end belong to the next sequence
+      store_row8<Tout>(static_cast<Tout*>(a.y) + ((prev_tok + i_row) * Hv + hv) * (size_t)DV + dv0 + 16 * half + 8 * hc,
+                       y8);
+    }
+  };
 
   // The waits for an MMA round are per thread (the TMEM results are ready for every thread once it has
   // seen the commit); their outcome joins the chunk's next barrier, where every thread breaks alike.
@@ -112,18 +144,17 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
     tc::fence_after_sync();
     if (!ok) break;
     const uint32_t kq = tc::smem_u32(smem + FW_KQ + buf * 32768);
-    // 2. [K; Q] S^T in one pass (M = 128, N = 64: the state's hi and lo halves)
+    // 2. [K; Q] S^T in one pass (M = 128, N = 64: the state's hi and lo halves); the commit also
+    //    covers the last chunk's P D, issued after it
     if (tid == 0) {
       mma_run<8, kKmaj128>(tmem + cA, idA, kq, tc::smem_u32(smem + FW_S), false);
       tc::mma_commit(&bar_mma);
     }
     if (tid == 32) {
       if (a.ckpt) tc::bulk_store(a.ckpt + ((cg * Hv + hv) * DV + dv0) * (size_t)DK, smem + FW_CK, DVT * DK * 4);
-      if (ystage_tok >= 0) tc::tma_store_3d(&ymap, smem + FW_Y, dv0, hv, (int)ystage_tok);  // last chunk's y
+      if (ystage_tok >= 0) tc::tma_store_3d(&ymap, smem + FW_Y, dv0, hv, (int)ystage_tok);  // an earlier chunk's y
       tc::bulk_commit();
-      if (jc + 1 < nchunks) issue_loads(jc + 1, buf ^ 1);  // the next chunk's tiles
     }
-    if (jc + 1 < nchunks) loads_issued = jc + 2;
     const float* gb = sg[buf];
     const float bi = gb[i_row], be = gb[64 + i_row], gi = __expf(bi), bC = gb[63];
     float vr[16];  // this row's values (rows past the sequence's end read as zero)
@@ -154,6 +185,10 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
 #pragma unroll
       for (int j = 0; j < 16; ++j) yp[j] *= gi;
     }
+    // the next chunk's tiles: its buffers' last readers (this chunk's one before, and that chunk's P D,
+    // which the wait above covers) are done
+    if (tid == 32 && ok && jc + 1 < nchunks) issue_loads(jc + 1, buf ^ 1);
+    if (ok && jc + 1 < nchunks) loads_issued = jc + 2;
     tc::fence_async_smem();
     tc::fence_before_sync();
     ok = __syncthreads_and(ok) != 0;
@@ -164,6 +199,12 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
       mma_run<4, kKmaj128>(tmem + cD, idA, tc::smem_u32(smem + FW_T + buf * 16384), tc::smem_u32(smem + FW_E), false);
       tc::mma_commit(&bar_mma);
     }
+    // meanwhile the last chunk's output rows (its P D completed before this chunk's K S^T)
+    float y8[8];
+    const bool rows = outputs && prev_tok >= 0;
+    if (rows) out_rows(y8);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) yq[j] = yp[j];
 
     ok = ok && tc::mbar_wait_or_drain(&bar_mma, ph, a.err, 12, s_hook);
     ph ^= 1;
@@ -197,45 +238,36 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
     ok = __syncthreads_and(ok) != 0;
     tc::fence_after_sync();
     if (!ok) break;
-    // 5. S update^T = K^T D~ (M = 128 dk rows);  O2 = P D ([P_hi; P_lo] stacked)
+    // 5. S update^T = K^T D~ (M = 128 dk rows), committed alone; then O2 = P D ([P_hi; P_lo] stacked),
+    //    whose completion the next chunk's first commit (or the one after the walk's last barrier)
+    //    covers.  (Not a second commit here: a thread that polled late would find the barrier two
+    //    phases on, the parity it waits for current again.)
     if (tid == 0) {
       mma_run<4, kKT>(tmem + cS, idT, kq, tc::smem_u32(smem + FW_DT), false);
-      mma_run<4, kKmaj128>(tmem + cO, idA, tc::smem_u32(smem + FW_P + buf * 16384), tc::smem_u32(smem + FW_D), false);
       tc::mma_commit(&bar_mma);
+      if (outputs)
+        mma_run<4, kKmaj128>(tmem + cO, idA, tc::smem_u32(smem + FW_P + buf * 16384), tc::smem_u32(smem + FW_D), false);
     }
     if (tid == 32 && a.Ds) {
       tc::bulk_store(a.Ds + ptile, smem + FW_DS + buf * 8192, 8192);
       tc::bulk_commit();
     }
+    ystage_tok = -1;
+    if (rows) {
+      put_rows(y8);
+      if (prev_L == C) ystage_tok = prev_tok;
+    }
+    prev_tok = tok0, prev_L = L;
     ok = ok && tc::mbar_wait_or_drain(&bar_mma, ph, a.err, 13, s_hook);
     ph ^= 1;
     tc::fence_after_sync();
     {
-      float u[16], o2[16];
-      tmem_ld_hl16x2(tl + cS, tl + cO, half, u, o2);
+      float u[16];
+      tmem_ld_hl16(tl + cS, half, u);
       const float gC = __expf(bC);
 #pragma unroll
       for (int j = 0; j < 16; ++j) s[j] = fmaf(gC, s[j], u[j]);
-#pragma unroll
-      for (int j = 0; j < 16; ++j) u[j] = o2[j] + __shfl_xor_sync(0xffffffffu, o2[j], 16);
-      // both lanes hold P D's row; the K-side lane writes columns 0-7 (with the Q-side lane's gamma Q S^T),
-      // the Q-side lane columns 8-15
-      const int hc = kside ? 0 : 1;
-      float y8[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float qy = __shfl_xor_sync(0xffffffffu, yp[j], 16);
-        y8[j] = kside ? u[j] + qy : u[8 + j] + yp[8 + j];
-      }
-      if (a.ckpt_in) {
-        // recompute mode: D is the product, y is not written
-      } else if (L == C) {  // a full chunk goes out by one TMA store after the next barrier
-        store_row8<Tout>(reinterpret_cast<Tout*>(smem + FW_Y) + i_row * DVT + 16 * half + 8 * hc, y8);
-      } else if (i_row < L) {  // the rows after a sequence's end belong to the next sequence: not written
-        store_row8<Tout>(static_cast<Tout*>(a.y) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0 + 16 * half + 8 * hc, y8);
-      }
     }
-    ystage_tok = (L == C && !a.ckpt_in) ? tok0 : -1;
     tc::fence_async_smem();
     tc::fence_before_sync();
   }
@@ -248,9 +280,27 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_fwd_state(const __grid_const
     if (tid == 32)
       for (int64_t j = loads_seen; j < loads_issued; ++j) tc::mbar_drain(&bar_tma[j & 1], (uint32_t)((j >> 1) & 1));
   }
-  if (ok && ystage_tok >= 0 && tid == 32) {  // the last chunk's output rows
-    tc::tma_store_3d(&ymap, smem + FW_Y, dv0, hv, (int)ystage_tok);
-    tc::bulk_commit();
+  if (ok && outputs && prev_tok >= 0) {  // the last chunk's output rows, after the staged ones go out
+    if (tid == 0) tc::mma_commit(&bar_mma);  // every thread saw the round before complete
+    if (ystage_tok >= 0 && tid == 32) {
+      tc::tma_store_3d(&ymap, smem + FW_Y, dv0, hv, (int)ystage_tok);
+      tc::bulk_commit();
+      tc::bulk_wait_read();
+    }
+    ok = tc::mbar_wait_or_drain(&bar_mma, ph, a.err, 14, s_hook);
+    tc::fence_after_sync();
+    float y8[8];
+    out_rows(y8);
+    tc::fence_before_sync();
+    ok = __syncthreads_and(ok) != 0;  // (the staging tile is free)
+    tc::fence_after_sync();
+    if (ok) put_rows(y8);
+    tc::fence_async_smem();
+    __syncthreads();
+    if (ok && prev_L == C && tid == 32) {
+      tc::tma_store_3d(&ymap, smem + FW_Y, dv0, hv, (int)prev_tok);
+      tc::bulk_commit();
+    }
   }
   if (tid == 32) tc::bulk_wait();
   if (ok && a.hT) {
