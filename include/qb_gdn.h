@@ -249,8 +249,8 @@ int qb_gdn_gated_norm_bwd(int64_t P, int32_t Hv, int32_t Dv, float eps, int32_t 
  * (src/delta_grad.cpp:164-170), which has no asynchronous case.  Codes (0 = no failure):
  *    1  prep: the K / Q tiles          2  prep: K K^T, Q K^T
  *   10  forward walk: a chunk's tiles  11, 12, 13  forward walk: its three product rounds
- *   14  forward walk: the last chunk's output product
- *   20  reverse walk: a chunk's rows   25, 26  reverse walk: the T, P images
+ *   14  forward walk: the last chunk's output product   15  forward walk: a chunk's P image
+ *   20  reverse walk: a chunk's images and gates   26  reverse walk: a chunk's P image and rows
  *   21, 22, 23  reverse walk: its three product rounds
  *   30  gradient: the [K; Q] image     31  gradient: a value head's P image and gates
  *   37  gradient: a slice's tiles      34, 35, 36  gradient: its product rounds (slice, K K^T, finalize)

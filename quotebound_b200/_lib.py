@@ -155,8 +155,10 @@ STATUS_CODES = {
     1: "prep: the K / Q tiles", 2: "prep: K K^T, Q K^T",
     10: "forward walk: a chunk's tiles", 11: "forward walk: product round 1", 12: "forward walk: product round 2",
     13: "forward walk: product round 3", 14: "forward walk: the last chunk's output product",
-    20: "reverse walk: a chunk's rows", 21: "reverse walk: product round 1", 22: "reverse walk: product round 2",
-    23: "reverse walk: product round 3", 25: "reverse walk: the T image", 26: "reverse walk: the P image",
+    15: "forward walk: a chunk's P image",
+    20: "reverse walk: a chunk's images and gates", 21: "reverse walk: product round 1",
+    22: "reverse walk: product round 2", 23: "reverse walk: product round 3",
+    26: "reverse walk: a chunk's P image and rows",
     30: "gradient: the [K; Q] image", 31: "gradient: a value head's P image and gates",
     34: "gradient: a slice's products", 35: "gradient: K K^T", 36: "gradient: the finalize's products",
     37: "gradient: a slice's tiles",

@@ -82,8 +82,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
   };
   auto issue_head = [&](int r) {
     const int hv = hk * ratio + r;
-    tc::mbar_arrive_expect_tx(&bar_h, 16384 + 512);
-    tc::bulk_load(smem + GR_P, a.Pimg + (size_t)(c * Hv + hv) * 16384, 16384, &bar_h);
+    tc::mbar_arrive_expect_tx(&bar_h, 512);
     tc::bulk_load(sgt[r & 1], a.gates + (c * Hv + hv) * 128, 512, &bar_h);
   };
   if (tid == 32) {
@@ -283,26 +282,6 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
         qk[k] = lower ? z : kk32[16 + k];
       }
       const int j0 = 32 * half + (lower ? 0 : 16);
-      // this row's P (hi + lo from the image) for the 16 columns, loaded up front
-      float pv[16];
-      {
-        const int rr = img_row(i_row);
-        const uint8_t* prow = smem + GR_P + rr * 128;
-#pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-          const int ch = (j0 >> 3) + cc;
-          const uint4 hi = *reinterpret_cast<const uint4*>(prow + ((ch ^ (rr & 7)) << 4));
-          const uint4 lo = *reinterpret_cast<const uint4*>(prow + 2048 + ((ch ^ (rr & 7)) << 4));
-          const uint32_t hw[4] = {hi.x, hi.y, hi.z, hi.w}, lw[4] = {lo.x, lo.y, lo.z, lo.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&hw[e]);
-            const __nv_bfloat162 l2 = *reinterpret_cast<const __nv_bfloat162*>(&lw[e]);
-            pv[8 * cc + 2 * e] = __low2float(h2) + __low2float(l2);
-            pv[8 * cc + 2 * e + 1] = __high2float(h2) + __high2float(l2);
-          }
-        }
-      }
       // f_ij: the coefficient of the gate product Gamma_ij in the loss (P and L terms, strict lower;
       // the diagonal spans no step), at scratch[i][j + 1] -- column 0 takes the gamma terms below
       float ph[16], kh[16], xs[16];
@@ -317,7 +296,6 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
         ph[k] = dp[k] * gam;        // dP^
         kh[k] = dl * be * gam;      // dKK
       }
-      (void)pv;
       if (i_row == 63) {  // row 63 is the chunk's end: the end state's products lambda_j
 #pragma unroll
         for (int k = 0; k < 16; ++k) xs[k] += srow[3][0][j0 + k] + srow[3][1][j0 + k];
@@ -342,7 +320,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
-    // the P image has been read: the next value head's P and gates (into the other gate buffer)
+    // the next value head's gates (into the other gate buffer)
     if (r + 1 < ratio) {
       if (tid == 32) issue_head(r + 1);
       h_issued = r + 2;

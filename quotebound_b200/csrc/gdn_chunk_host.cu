@@ -34,10 +34,11 @@ bool map_act(CUtensorMap* m, const void* base, int64_t rows, int heads, int dim,
            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// bf16 rows [rows, heads, dim] read as unswizzled boxes of box_cols x box_rows of one head (the
-// value or output-gradient rows of a chunk); rows past the end read as zero.
+// bf16 rows [rows, heads, dim] read as boxes of box_cols x box_rows of one head (the value or
+// output-gradient rows of a chunk), unswizzled or (sw64) in the 64-byte swizzle of an MN-major MMA
+// operand with 64-byte rows; rows past the end read as zero.
 bool map_rows(CUtensorMap* m, const void* base, int64_t rows, int heads, int dim, int box_cols, int box_rows,
-              bool f32 = false) {
+              bool f32 = false, bool sw64 = false) {
   EncodeTiled f = encode_fn();
   if (!f) return false;
   const cuuint64_t eb = f32 ? 4 : 2;
@@ -47,8 +48,8 @@ bool map_rows(CUtensorMap* m, const void* base, int64_t rows, int heads, int dim
   cuuint32_t es[3] = {1, 1, 1};
   return f(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base),
            dims, strides, box, es,
-           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+           CU_TENSOR_MAP_INTERLEAVE_NONE, sw64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // State rows [rows, 128] fp32 (a chunk-state buffer); box = 32 columns x 32 rows in the 32-byte-atom
@@ -212,7 +213,7 @@ cudaError_t chunked_bwd(const ChunkBwdArgs& a, void* ws, cudaStream_t st) {
   if (a.cu && (e = launch_chunk_offsets(a.cu, a.N, w.chunk_off, st)) != cudaSuccess) return e;
   Geo geo{a.T, a.Hk, a.Hv, a.N, (a.T + C - 1) / C, a.cu, a.cu ? w.chunk_off : nullptr};
   CUtensorMap dmap, vmap, dvmap;
-  if (!map_rows(&dmap, a.dy, rows, a.Hv, a.Dv, DVT, C) || !map_rows(&vmap, a.v, rows, a.Hv, a.Dv, DVT, C) ||
+  if (!map_rows(&dmap, a.dy, rows, a.Hv, a.Dv, DVT, C, false, true) || !map_rows(&vmap, a.v, rows, a.Hv, a.Dv, DVT, C) ||
       !map_rows(&dvmap, a.dv, rows, a.Hv, a.Dv, DVT, C, !a.out_bf16))
     return cudaErrorInvalidValue;
   BwdStateArgs ba{geo, a.dy, sv.gates, a.dhT, a.dv, a.dh0, w.dsbuf, sv.Timg, sv.Pimg, sv.KQimg, w.Aimg, w.err};
@@ -228,7 +229,7 @@ cudaError_t chunked_bwd(const ChunkBwdArgs& a, void* ws, cudaStream_t st) {
   if (!map_state_mn(&smap_mn, sv.ckpt, a.n_chunks * a.Hv * (int64_t)DV) ||
       !map_state_mn(&dmap_mn, w.dsbuf, a.n_chunks * a.Hv * (int64_t)DV))
     return cudaErrorInvalidValue;
-  GradArgs ga{geo, a.g, sv.gates, sv.Pimg, sv.KQimg, sv.Ds, w.Aimg, a.dq, a.dk, a.dg, a.dbeta, w.err,
+  GradArgs ga{geo, a.g, sv.gates, sv.KQimg, sv.Ds, w.Aimg, a.dq, a.dk, a.dg, a.dbeta, w.err,
               static_cast<const __nv_bfloat16*>(a.q), static_cast<const __nv_bfloat16*>(a.k),
               a.a_raw, a.b_raw, a.A_log, a.dt_bias, w.head_part, a.dA_log, a.ddt_bias,
               reinterpret_cast<unsigned*>(w.err + 2)};

@@ -37,7 +37,8 @@
 //                        registers; three tcgen05 rounds per chunk (K S^T, Q S^T | T E | P D, K^T D~).
 //                        Writes y and, for training, the chunk-start states.
 //   gdn_chunk_bwd_state  (Dv/32, Hv, sequences): the chunks in reverse with 32 rows of dS; three rounds
-//                        (K dS^T, P^T dO | T^T dD | Q^T (gamma dO), K^T H).  Writes dv, dS per chunk, dh0.
+//                        on the chain (K dS^T | T^T dD | K^T H), with P^T dO (a chunk ahead) and
+//                        Q^T (gamma dO) beside it.  Writes dv, dS per chunk, dh0.
 //   gdn_chunk_bwd_grad   (chunks, Hk): everything else per chunk, the value heads of a key head in turn
 //                        so dq and dk are summed over the group in TMEM in a fixed order; K K^T is
 //                        recomputed there from the [K; Q] image (one MMA per CTA).
@@ -212,11 +213,10 @@ constexpr int FW_S = 131072;       // 16 KB bf16 state [hi | lo], MN-major [128 
 constexpr int FW_E = 147456;       // 8 KB bf16 E [hi | lo], MN-major [64][64]
 constexpr int FW_D = 155648;       // 8 KB bf16 D [hi | lo]
 constexpr int FW_DT = 163840;      // 8 KB bf16 D~ = diag(lambda) D [hi | lo]
-constexpr int FW_CK = 172032;      // 16 KB fp32 chunk-start state staging [32 dv][128 dk] (bulk store)
-constexpr int FW_V = 188416;       // 2 x 4 KB bf16 value rows [64][32] (TMA)
-constexpr int FW_DS = 196608;      // 2 x 8 KB fp32 D rows [64][32] staging (bulk store, training)
-constexpr int FW_Y = 212992;       // 8 KB output rows [64][32] staging (TMA store of full chunks)
-constexpr int FW_SMEM = 221184 + 1024;
+constexpr int FW_V = 172032;       // 2 x 4 KB bf16 value rows [64][32] (TMA)
+constexpr int FW_Y = 180224;       // 8 KB output rows [64][32] staging (TMA store of full chunks)
+constexpr int FW_CK = 188416;      // 16 KB fp32 chunk-start state staging [32 dv][128 dk] (bulk store)
+constexpr int FW_SMEM = 204800 + 1024;
 
 // Descriptors of the stacked operands.  The [K; Q] tile holds, per 64-column slab (16 KB), the row
 // groups K 0-15, Q 0-15, K 16-31, Q 16-31, ... (2 KB each).
@@ -278,18 +278,16 @@ __device__ __forceinline__ void tmem_ld_hl16_pair(uint32_t taddr, int half, floa
 
 // ---- the reverse walk's helpers ------------------------------------------------------------------
 constexpr int BW_KQ = 0;           // 2 x 32 KB bf16 [K; Q] image
-constexpr int BW_T = 65536;        // 16 KB bf16 [T_hi; T_lo] image (reloaded once the chunk's F is done)
-constexpr int BW_P = 81920;        // 16 KB bf16 [P_hi; P_lo] image (reloaded once P^T dO is done)
-constexpr int BW_S = 98304;        // 16 KB bf16 dS [hi | lo], MN-major [128 dk][64]
-constexpr int BW_DO = 114688;      // 8 KB bf16 dO, MN-major [64][32] (128-byte rows, half used)
-constexpr int BW_GD = 122880;      // 8 KB bf16 gamma dO [hi | lo]
-constexpr int BW_DD = 131072;      // 8 KB bf16 dD [hi | lo]
-constexpr int BW_H = 139264;       // 8 KB bf16 H = -beta gamma F [hi | lo]
-constexpr int BW_CK = 147456;      // 16 KB fp32 dS staging [32 dv][128 dk] (bulk store)
-constexpr int BW_V = 163840;       // 2 x 4 KB bf16 dO rows [64][32] (TMA)
-constexpr int BW_FS = 172032;      // 2 x 16 KB [dO; F] operand image staging (bulk store)
-constexpr int BW_DV = 204800;      // 8 KB dv rows [64][32] staging (TMA store of full chunks)
-constexpr int BW_SMEM = 212992 + 1024;
+constexpr int BW_T = 65536;        // 2 x 16 KB bf16 [T_hi; T_lo] image
+constexpr int BW_P = 98304;        // 2 x 16 KB bf16 [P_hi; P_lo] image
+constexpr int BW_S = 131072;       // 16 KB bf16 dS [hi | lo], MN-major [128 dk][64]
+constexpr int BW_GD = 147456;      // 8 KB bf16 gamma dO [hi | lo]
+constexpr int BW_DD = 155648;      // 8 KB bf16 dD [hi | lo]
+constexpr int BW_H = 163840;       // 8 KB bf16 H = -beta gamma F [hi | lo]
+constexpr int BW_V = 172032;       // 2 x 4 KB bf16 dO rows [64][32], 64-byte swizzle (TMA)
+constexpr int BW_FS = 180224;      // 2 x 16 KB [dO; F] operand image staging (bulk store)
+constexpr int BW_DV = 212992;      // 8 KB dv rows [64][32] staging (TMA store of full chunks)
+constexpr int BW_SMEM = 221184 + 1024;
 
 // K-step ks of the transpose of one half (part 0 = hi, 1 = lo) of a [hi; lo] image as the M = 64
 // MN-major A operand: the image's rows (chunk steps) are K.
@@ -317,7 +315,7 @@ __device__ __forceinline__ void ld16_bf16(const uint8_t* p, bool valid, float (&
 // ---- the gradient kernel's helpers ---------------------------------------------------------------
 // Shared memory of the gradient kernel.
 constexpr int GR_KQ = 0;           // 32 KB bf16 [K; Q] image
-constexpr int GR_P = 32768;        // 16 KB bf16 [P_hi; P_lo] image of the value head
+constexpr int GR_FREE = 32768;     // 16 KB unused
 constexpr int GR_BUF = 49152;      // 2 x 60 KB slice buffers: S, dS (tf32, MN-major [32 dv][128 dk], +0, +16 KB),
 constexpr int GR_BS = 61440;       //   the [dO; F] image (+32 KB), D (K-major [64][32], +48 KB), V rows (+56 KB)
 constexpr int GR_KO = 172032;      // 16 KB bf16 K rows alone (K-major): the B operand of K K^T
@@ -443,7 +441,7 @@ struct GradArgs {
   Geo geo;
   const float* g;           // [B*T, Hv] (dg = d log g / g); null in layer mode
   const float* gates;       // [chunks, Hv, 2, 64]
-  const uint8_t *Pimg, *KQimg;  // the forward's operand images
+  const uint8_t* KQimg;     // the forward's [K; Q] operand image
   const float* Ds;          // D (tf32-rounded), fp32 tiles [chunks, Hv, Dv / 32][64][32], rows swizzled
   const uint8_t* Aimg;      // [dO; F] operand images [chunks, Hv, Dv / 32] x 16 KB
   void *dq, *dk;            // [B*T, Hk, Dk]

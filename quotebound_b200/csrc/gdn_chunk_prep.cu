@@ -165,7 +165,9 @@ __global__ void __launch_bounds__(128, 4) gdn_chunk_prep(const __grid_constant__
       for (int jj = 0; jj < 32; ++jj) {
         const int j = 32 * h + jj;
         const float gam = __expf(bi - sb[j]);  // Gamma_ij (only j <= i is used)
-        v[jj] = (kkside ? j < i : j <= i) ? gam * v[jj] : 0.f;
+        // (P's rows past the sequence's end are zero: the reverse walk multiplies P^T with the raw rows
+        // of the output gradient there, which belong to the next sequence)
+        v[jj] = (kkside ? j < i : (j <= i && i < L)) ? gam * v[jj] : 0.f;
       }
       // one instruction stream for the lane pair: the K K^T lane writes columns 0-15 of L and of P, the
       // Q K^T lane columns 16-31 of both (each sends the other the half it does not write)

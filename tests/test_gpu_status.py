@@ -31,7 +31,7 @@ def _pass(x, check=False):
     return (y, hT) + tuple(g[:7])
 
 
-@pytest.mark.parametrize("code,where", [(1, "forward"), (11, "forward"), (13, "forward"), (21, "backward"),
+@pytest.mark.parametrize("code,where", [(1, "forward"), (11, "forward"), (12, "forward"), (22, "backward"),
                                         (34, "backward")])
 def test_a_wait_that_runs_out_is_reported_and_the_next_call_is_clean(code, where):
     x = _inputs()
