@@ -10,7 +10,7 @@ namespace qbgdn {
 // [K; Q] dS^T -> dD -> F = T^T dD -> H -> K^T H -> dS; the products that need no dS -- G = P^T dO (from
 // the value-gradient rows as they land, a chunk ahead) and Q^T (gamma dO) -- run where the tensor pipe
 // would idle, and the epilogue work that feeds no product of the chain (the dS copy for the gradient
-// kernel, the dO rows' staging) fills the wait for the first round.  Besides dv, the per-chunk dS and
+// kernel, the dO rows' staging) fills the waits for the products.  Besides dv, the per-chunk dS and
 // dh0 it leaves the gradient kernel F = T^T dD.
 template <typename Tout>
 __global__ void __launch_bounds__(320, 1) gdn_chunk_bwd_state(const __grid_constant__ CUtensorMap dmap,
@@ -83,15 +83,13 @@ __global__ void __launch_bounds__(320, 1) gdn_chunk_bwd_state(const __grid_const
   // G = P^T dO of iteration it into cG: P_hi^T and P_lo^T accumulated (M = 64), the value-gradient
   // rows as the MN-major N = 32 operand (64-byte rows in the 64-byte swizzle, 512 bytes per 8 rows).
   // P's rows past the sequence's end are zero, so the next sequence's rows there add nothing.
-  auto mma_g = [&](int64_t it) {
+  auto mma_g = [&](int64_t it, int part) {  // part 0: P_hi^T dO (fresh), 1: + P_lo^T dO
     const int b = (int)(it & 1);
     const uint32_t pimg = tc::smem_u32(smem + BW_P + b * 16384), vt = tc::smem_u32(smem + BW_V + b * 4096);
 #pragma unroll
-    for (int part = 0; part < 2; ++part)
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        tc::mma_bf16(tmem + cG, desc_img_t(pimg, part, ks), tc::sdesc(vt + ks * 1024, 4096, 512, 4), idG,
-                     (part | ks) ? 1u : 0u);
+    for (int ks = 0; ks < 4; ++ks)
+      tc::mma_bf16(tmem + cG, desc_img_t(pimg, part, ks), tc::sdesc(vt + ks * 1024, 4096, 512, 4), idG,
+                   (part | ks) ? 1u : 0u);
   };
 
   bool ok = true;
@@ -105,7 +103,7 @@ __global__ void __launch_bounds__(320, 1) gdn_chunk_bwd_state(const __grid_const
   }
   if (issuer && nchunks > 0) {
     ok = tc::mbar_wait_or_drain(&bar_g[0], 0, a.err, 26, s_hook);
-    if (ok) mma_g(0);  // completes before the first chunk's round-3 commit
+    if (ok) mma_g(0, 0), mma_g(0, 1);  // completes before the first chunk's round-3 commit
   }
   const int i_row = 16 * quad + (lane & 15);
   const bool kside = lane < 16;
@@ -221,6 +219,12 @@ __global__ void __launch_bounds__(320, 1) gdn_chunk_bwd_state(const __grid_const
         tc::mma_commit(&bar_mma);
         mma_run<4, kQT>(tmem + cU, idU, kq, tc::smem_u32(smem + BW_GD), false);
       }
+      // G of the next chunk (cG was read in step 4), its first half here (it runs during the F
+      // epilogue, ahead of K^T H), the second after K^T H
+      if (it + 1 < nchunks) {
+        ok = tc::mbar_wait_or_drain(&bar_g[b ^ 1], (uint32_t)(((it + 1) >> 1) & 1), a.err, 26, s_hook);
+        if (ok) mma_g(it + 1, 0);
+      }
     }
     if (epi) {
       // meanwhile dS (tf32-rounded: its one reader takes it as a tf32 operand) into the gradient
@@ -267,14 +271,11 @@ __global__ void __launch_bounds__(320, 1) gdn_chunk_bwd_state(const __grid_const
     tc::fence_after_sync();
     if (!ok) break;
     // 6. U = Q^T (gamma dO) (issued in step 5) + K^T H (M = 128 dk rows); the stores of this chunk's
-    //    image and dv rows; then G of the next chunk, which runs during the dS update
+    //    image and dv rows
     if (issuer) {
       mma_run<4, kKT>(tmem + cU, idU, kq, tc::smem_u32(smem + BW_H), true);
       tc::mma_commit(&bar_mma);
-      if (it + 1 < nchunks) {
-        ok = tc::mbar_wait_or_drain(&bar_g[b ^ 1], (uint32_t)(((it + 1) >> 1) & 1), a.err, 26, s_hook);
-        if (ok) mma_g(it + 1);  // cG was read in step 4
-      }
+      if (it + 1 < nchunks) mma_g(it + 1, 1);
     }
     if (copier) {
       tc::bulk_store(a.Aimg + ((size_t)(cg * Hv + hv) * (DV / DVT) + blockIdx.x) * 16384, smem + BW_FS + b * 16384,

@@ -143,16 +143,8 @@ __global__ void __launch_bounds__(320, 1) gdn_chunk_fwd_state(const __grid_const
     const int64_t tok0 = seq0 + jc * C;
     const int L = (int)min((int64_t)C, seq1 - tok0);
 
-    // 1. the chunk-start state as the [hi | lo] operand row dk, and (training) staged for the bulk store
-    //    of the checkpoint, rounded to tf32: its one reader takes it as a tf32 operand
-    if (epi) {
-      tc::st_row_hilo16(smem + FW_S, dk, s, half);
-      if (a.ckpt) {
-        float* ck = reinterpret_cast<float*>(smem + FW_CK) + 16 * half * DK + dk;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) ck[j * DK] = tf32_rna(s[j]);
-      }
-    }
+    // 1. the chunk-start state as the [hi | lo] operand row dk
+    if (epi) tc::st_row_hilo16(smem + FW_S, dk, s, half);
     tc::fence_async_smem();
     tc::fence_before_sync();
     ok = __syncthreads_and(ok) != 0;
@@ -170,7 +162,6 @@ __global__ void __launch_bounds__(320, 1) gdn_chunk_fwd_state(const __grid_const
       }
     }
     if (copier) {
-      if (a.ckpt) tc::bulk_store(a.ckpt + ((cg * Hv + hv) * DV + dv0) * (size_t)DK, smem + FW_CK, DVT * DK * 4);
       if (ystage_tok >= 0) tc::tma_store_3d(&ymap, smem + FW_Y, dv0, hv, (int)ystage_tok);  // an earlier chunk's rows
       tc::bulk_commit();
       // the next chunk's tiles into the buffers of the chunk before this one (whose readers are done);
@@ -185,6 +176,13 @@ __global__ void __launch_bounds__(320, 1) gdn_chunk_fwd_state(const __grid_const
     }
     float bi = 0.f, be = 0.f, gi = 0.f, bC = 0.f, yp[16];
     if (epi) {
+      // meanwhile (training) the chunk-start state, rounded to tf32 (its one reader takes it as a tf32
+      // operand), staged for the bulk store of the checkpoint after the next barrier
+      if (a.ckpt) {
+        float* ck = reinterpret_cast<float*>(smem + FW_CK) + 16 * half * DK + dk;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) ck[j * DK] = tf32_rna(s[j]);
+      }
       ok = ok && tc::mbar_wait_or_drain(&bar_tma[buf], (uint32_t)((jc >> 1) & 1), a.err, 10, s_hook);
       const float* gb = sg[buf];
       bi = gb[i_row], be = gb[64 + i_row], gi = __expf(bi), bC = gb[63];
@@ -222,6 +220,10 @@ __global__ void __launch_bounds__(320, 1) gdn_chunk_fwd_state(const __grid_const
     if (issuer) {
       mma_run<4, kKmaj128>(tmem + cD, idA, tc::smem_u32(smem + FW_T + buf * 16384), tc::smem_u32(smem + FW_E), false);
       tc::mma_commit(&bar_mma);
+    }
+    if (copier && a.ckpt) {
+      tc::bulk_store(a.ckpt + ((cg * Hv + hv) * DV + dv0) * (size_t)DK, smem + FW_CK, DVT * DK * 4);
+      tc::bulk_commit();
     }
     if (copier) tc::bulk_wait_read();  // the staging tiles are rewritten below and next chunk
     float y8[8], ds8[8];
