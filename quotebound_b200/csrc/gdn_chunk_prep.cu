@@ -161,10 +161,17 @@ __global__ void __launch_bounds__(128, 4) gdn_chunk_prep(const __grid_constant__
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       tc::tmem_ld32(tc::taddr(tmem, 32 * warp, 32 * h), v);
+      // Gamma_ij = e^(b_i - b_j) for this 32-column half (only j <= i is used): both lanes of the pair
+      // need the same row's, so each forms 16 (the exponentials bound this phase) and they swap them
+      float gh[16], go[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) gh[k] = __expf(bi - sb[32 * h + (kkside ? 0 : 16) + k]);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) go[k] = __shfl_xor_sync(0xffffffffu, gh[k], 16);
 #pragma unroll
       for (int jj = 0; jj < 32; ++jj) {
         const int j = 32 * h + jj;
-        const float gam = __expf(bi - sb[j]);  // Gamma_ij (only j <= i is used)
+        const float gam = ((jj < 16) == kkside) ? gh[jj & 15] : go[jj & 15];
         // (P's rows past the sequence's end are zero: the reverse walk multiplies P^T with the raw rows
         // of the output gradient there, which belong to the next sequence)
         v[jj] = (kkside ? j < i : (j <= i && i < L)) ? gam * v[jj] : 0.f;
