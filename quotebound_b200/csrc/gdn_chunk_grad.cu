@@ -10,7 +10,9 @@ namespace qbgdn {
 template <typename Tout>
 __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_constant__ CUtensorMap smap_mn,
                                                              const __grid_constant__ CUtensorMap dmap_mn,
-                                                             const __grid_constant__ CUtensorMap vmap, GradArgs a) {
+                                                             const __grid_constant__ CUtensorMap vmap,
+                                                             const __grid_constant__ CUtensorMap dqmap,
+                                                             const __grid_constant__ CUtensorMap dkmap, GradArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(16) float sgt[2][128];  // the value heads' gates: b[64], beta[64] (double-buffered)
@@ -451,6 +453,11 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
   // f. dq (lower lanes) and dk (upper lanes) rows of this key head, 64 columns per thread (layer mode:
   //    through the norms to the raw q, k)
   if (!a.g) cp_async_wait_all();
+  // A full chunk of a bf16 result leaves by four TMA stores of 64 x 64 tiles, staged where the raw rows
+  // were (read before the norm's barrier below): plain stores of a thread's 64-column row put 16 bytes
+  // into each of 32 rows 4 KB apart per instruction, and cost this phase thousands of cycles.  Other
+  // chunks' rows (a sequence's last, whose rows past its end belong to the next) go out by plain stores.
+  const bool tile_out = sizeof(Tout) == 2 && L == C;
   if (ok) {
     Tout* out = static_cast<Tout*>(lower ? a.dq : a.dk) + rowoff;
     float v0[32], v1[32];
@@ -493,13 +500,32 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
         v1[j] = sc * rn * (v1[j] - c2 * x1[j]);
       }
     }
-    if (rvalid) {
+    if (tile_out) {  // row i_row of the dq (lower) or dk (upper) tile, columns 64 half .. + 63
+      uint8_t* row = smem + GR_RAW + (lower ? 0 : 16384) + half * 8192 + i_row * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const float* x = c < 4 ? v0 + 8 * c : v1 + 8 * (c - 4);
+        *reinterpret_cast<uint4*>(row + ((c ^ (i_row & 7)) << 4)) =
+            make_uint4(tc::pack_bf16(x[0], x[1]), tc::pack_bf16(x[2], x[3]), tc::pack_bf16(x[4], x[5]),
+                       tc::pack_bf16(x[6], x[7]));
+      }
+    } else if (rvalid) {
       store_row32<Tout>(out, v0);
       store_row32<Tout>(out + 32, v1);
     }
   }
+  tc::fence_async_smem();
   tc::fence_before_sync();
   __syncthreads();
+  if (ok && tile_out && tid == 32) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      tc::tma_store_3d(&dqmap, smem + GR_RAW + h * 8192, 64 * h, hk, (int)tok0);
+      tc::tma_store_3d(&dkmap, smem + GR_RAW + 16384 + h * 8192, 64 * h, hk, (int)tok0);
+    }
+    tc::bulk_commit();
+    tc::bulk_wait();  // the staging stays in place until the stores have read it
+  }
   if (warp == 0) tc::tmem_dealloc(tmem, 512);
   if (!a.g) {
     // layer mode: the CTA that finishes last sums every chunk's head terms, in chunk order (the same
@@ -531,11 +557,12 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
 }
 
 cudaError_t launch_chunk_bwd_grad(const CUtensorMap& smap_mn, const CUtensorMap& dmap_mn, const CUtensorMap& vmap,
-                                  const GradArgs& a, int64_t n_chunks, int Hk, bool out_bf16, cudaStream_t st) {
+                                  const CUtensorMap& dqmap, const CUtensorMap& dkmap, const GradArgs& a,
+                                  int64_t n_chunks, int Hk, bool out_bf16, cudaStream_t st) {
   auto kern = out_bf16 ? gdn_chunk_bwd_grad<__nv_bfloat16> : gdn_chunk_bwd_grad<float>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GR_SMEM);
   if (e != cudaSuccess) return e;
-  kern<<<dim3((unsigned)n_chunks, Hk), 256, GR_SMEM, st>>>(smap_mn, dmap_mn, vmap, a);
+  kern<<<dim3((unsigned)n_chunks, Hk), 256, GR_SMEM, st>>>(smap_mn, dmap_mn, vmap, dqmap, dkmap, a);
   note_launch();
   return cudaGetLastError();
 }

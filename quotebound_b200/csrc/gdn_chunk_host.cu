@@ -233,7 +233,12 @@ cudaError_t chunked_bwd(const ChunkBwdArgs& a, void* ws, cudaStream_t st) {
               static_cast<const __nv_bfloat16*>(a.q), static_cast<const __nv_bfloat16*>(a.k),
               a.a_raw, a.b_raw, a.A_log, a.dt_bias, w.head_part, a.dA_log, a.ddt_bias,
               reinterpret_cast<unsigned*>(w.err + 2)};
-  return launch_chunk_bwd_grad(smap_mn, dmap_mn, vmap, ga, a.n_chunks, a.Hk, a.out_bf16, st);
+  // the tiles of full chunks' dq, dk rows (bf16 results; a float32 result is stored row by row and the
+  // maps are not read)
+  CUtensorMap dqmap = vmap, dkmap = vmap;
+  if (a.out_bf16 && (!map_act(&dqmap, a.dq, rows, a.Hk, a.Dk) || !map_act(&dkmap, a.dk, rows, a.Hk, a.Dk)))
+    return cudaErrorInvalidValue;
+  return launch_chunk_bwd_grad(smap_mn, dmap_mn, vmap, dqmap, dkmap, ga, a.n_chunks, a.Hk, a.out_bf16, st);
 }
 
 }  // namespace qbgdn

@@ -463,6 +463,7 @@ cudaError_t launch_chunk_fwd_state(const CUtensorMap& vmap, const CUtensorMap& y
 cudaError_t launch_chunk_bwd_state(const CUtensorMap& dmap, const CUtensorMap& dvmap, const BwdStateArgs& a, int Hv,
                                    int N, bool out_bf16, cudaStream_t st);
 cudaError_t launch_chunk_bwd_grad(const CUtensorMap& smap_mn, const CUtensorMap& dmap_mn, const CUtensorMap& vmap,
-                                  const GradArgs& a, int64_t n_chunks, int Hk, bool out_bf16, cudaStream_t st);
+                                  const CUtensorMap& dqmap, const CUtensorMap& dkmap, const GradArgs& a,
+                                  int64_t n_chunks, int Hk, bool out_bf16, cudaStream_t st);
 
 }  // namespace qbgdn
