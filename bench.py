@@ -1,6 +1,6 @@
 """Gated DeltaNet forward + backward tokens/s on B200 (one process per GPU).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c1|c2|c3|c4]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c1|c2|c3|c4|conv_norm]
 
 One step is the whole training pass of the recurrence's layer slice over one batch, through the fused
 layer entry points (the norm and gate graph inside the chunked kernels):
@@ -15,6 +15,8 @@ Workloads (synthetic, seeded; shapes and value distributions of the measured con
   c2  B=8, T=4096, Hk=16, Hv=64 split over the GPUs by (batch x value-head group); strong scaling.
   c3  16 sequences of U[128, 4096] tokens packed with cu_seqlens (one GPU).
   c4  exact speculative verify of 8 drafted tokens for 32 sequences, every state kept (one GPU).
+  conv_norm  the layer's steps either side of the recurrence at the 4B shape, 4 x 2048 tokens: the causal
+      conv + SiLU with the q/k/v split and the gated RMSNorm, forward and backward (one GPU; HBM-bound).
 
 `value` is tokens/s of the whole job (tokens of all ranks / max over ranks of the device time);
 `e2e` is the same metric through the public API with host buffers: every step copies its inputs
@@ -46,8 +48,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c1", choices=["c1", "c2", "c3", "c4"],
-                    help="c1 4B layer (default), c2 batched split over GPUs, c3 varlen (one GPU), c4 verify (one GPU)")
+    ap.add_argument("--workload", default="c1", choices=["c1", "c2", "c3", "c4", "conv_norm"],
+                    help="c1 4B layer (default), c2 batched split over GPUs, c3 varlen (one GPU), c4 verify (one GPU), "
+                         "conv_norm the conv and gated norm around the recurrence (one GPU)")
     ap.add_argument("--algo", type=int, default=0, help="0 auto, 1 row-parallel, 2 chunked")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-c2", action="store_true", help="skip the config 2 strong-scaling sub-result")
@@ -649,10 +652,66 @@ def _timed(step, steps, warmup, dev):
     return ms, {k: sum(v) / len(v) for k, v in per_op.items()}, launches, clocks
 
 
+def conv_norm_line(args, dev, hbm, src):
+    """The causal conv + SiLU (with the q/k/v split) and the gated RMSNorm, forward and backward, at the 4B
+    layer shape (Hk=16, Hv=32, Dk=Dv=128, conv_dim 8192, 4 taps) over B = 4 sequences of 2048 tokens: every
+    activation is 64-128 MB, so each op streams HBM.  The roofline is each op's algorithmic bytes (its
+    inputs read and outputs written once) over its CUDA-event time."""
+    from quotebound_b200 import conv, norm
+    B, T, Hk, Hv, D, K = 4, 2048, 16, 32, 128, 4
+    cdim = 2 * Hk * D + Hv * D
+    gen = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(B, T, cdim, generator=gen, device=dev).to(torch.bfloat16)
+    w = (torch.randn(cdim, K, generator=gen, device=dev) * 0.5).to(torch.bfloat16)
+    st = torch.randn(B, K - 1, cdim, generator=gen, device=dev).to(torch.bfloat16)
+    dq = torch.randn(B, T, Hk, D, generator=gen, device=dev).to(torch.bfloat16)
+    dk = torch.randn(B, T, Hk, D, generator=gen, device=dev).to(torch.bfloat16)
+    dv = torch.randn(B, T, Hv, D, generator=gen, device=dev).to(torch.bfloat16)
+    y = torch.randn(B, T, Hv, D, generator=gen, device=dev).to(torch.bfloat16)
+    z = torch.randn(B, T, Hv, D, generator=gen, device=dev).to(torch.bfloat16)
+    do = torch.randn(B, T, Hv, D, generator=gen, device=dev).to(torch.bfloat16)
+    nw = torch.rand(D, generator=gen, device=dev) + 0.5
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+
+    def step(events):  # L2 flushed before every op (outside its events): each op's inputs come from HBM
+        for name, fn in (("conv_fwd", lambda: conv.conv_fwd(x, w, st, Hk=Hk, Dk=D, Hv=Hv, Dv=D)),
+                         ("conv_bwd", lambda: conv.conv_bwd(x, w, st, dq, dk, dv, Hk=Hk, Dk=D, Hv=Hv, Dv=D)),
+                         ("norm_fwd", lambda: norm.gated_norm_fwd(y, z, nw)),
+                         ("norm_bwd", lambda: norm.gated_norm_bwd(y, z, nw, do))):
+            flush.zero_()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            if events is not None:
+                events.append((name, e0, e1))
+
+    _, per_op, launches, clocks = _timed(step, args.steps, args.warmup, dev)
+    ms = sum(per_op.values())  # the four ops' device time per step (the flushes between them excluded)
+    act, row = B * T * cdim * 2, B * T * Hv * D * 2
+    nbytes = {"conv_fwd": 2 * act, "conv_bwd": 3 * act, "norm_fwd": 3 * row, "norm_bwd": 5 * row}
+    roof = {k: {"achieved_gbs": round(nbytes[k] / (per_op[k] / 1e3) / 1e9, 1),
+                "frac": round(nbytes[k] / (per_op[k] / 1e3) / 1e9 / hbm, 4), "bytes": nbytes[k]} for k in nbytes}
+    dom = max(per_op, key=per_op.get)
+    return {"metric": "GDN layer conv + gated norm fwd+bwd tokens/s", "value": round(B * T / (ms / 1e3), 1),
+            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded)",
+            "config": {"workload": f"conv_norm: B={B} T={T} Hk={Hk} Hv={Hv} Dk=Dv={D} conv_dim={cdim} taps={K}",
+                       "l2": "flushed before every op",
+                       "step": "conv_fwd + conv_bwd + gated_norm_fwd + gated_norm_bwd (sum of the ops' event times)"},
+            "per_op_ms": {k: round(v, 4) for k, v in per_op.items()}, "gpu_launches": int(launches),
+            "clocks": clocks,
+            "roofline": {"kernel": dom, "bound": "hbm", "achieved": roof[dom]["achieved_gbs"], "peak": hbm,
+                         "unit": "GB/s", "frac": roof[dom]["frac"], "peak_source": src, "traffic": None,
+                         "bytes_per_launch": nbytes[dom], "per_op": roof}}
+
+
 def run_single(args):
     world, rank, local = rank_info()
     if world > 1:
-        raise SystemExit("workloads c3 and c4 run on one GPU")
+        raise SystemExit("workloads c3, c4 and conv_norm run on one GPU")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     from quotebound_b200 import _lib, build, exact, synthetic
@@ -680,6 +739,8 @@ def run_single(args):
                 "clocks": clocks,
                 "roofline": {"kernel": dom, "bound": "tensor", "achieved": round(ach, 3), "peak": tf,
                              "unit": "TFLOP/s", "frac": round(ach / tf, 5), "peak_source": src, "traffic": None}}
+    elif args.workload == "conv_norm":
+        line = conv_norm_line(args, dev, hbm, src)
     else:
         N, V, Hk, Hv, D = 32, 8, 16, 32, 128
         p = synthetic.make(N, V, Hk, Hv, D, D, seed=0, device=dev, with_dy=False)
@@ -720,7 +781,7 @@ if __name__ == "__main__":
     a = parse()
     if a.impl == "reference":
         run_reference(a)
-    elif a.workload in ("c3", "c4"):
+    elif a.workload in ("c3", "c4", "conv_norm"):
         run_single(a)
     else:
         run_ours(a)

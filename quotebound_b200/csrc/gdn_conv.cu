@@ -9,9 +9,12 @@
 // form runs V tokens as V one-token steps bit for bit and keeps every token's conv window
 // (src/deltanet.cpp:79-87, RowStates.conv in src/model.h:84-89).
 //
-// HBM-bound: one thread owns 8 consecutive channels (one 16-byte bf16 vector) over a chunk of 64
-// tokens of one sequence, with the K - 1 previous inputs in registers, so x is read once (plus K - 1
-// rows of halo per chunk) and each output written once, all coalesced along the channels.
+// HBM-bound: one thread owns N consecutive channels (8 in the forward: one 16-byte bf16 vector; 4 in the
+// backward, whose per-thread state is four times larger) over a chunk of 64 tokens of one sequence, with
+// the K - 1 previous inputs in registers, so x is read once (plus K - 1 rows of halo per chunk) and each
+// output written once, all coalesced along the channels.  The rows are loaded eight tokens at a time
+// (all eight loads in flight before the first is used): one load in flight per thread leaves these
+// kernels bound by memory latency at a fraction of the bandwidth.
 #include "../../include/qb_gdn.h"
 #include "capi_util.cuh"
 #include "gdn_common.cuh"
@@ -22,8 +25,11 @@ namespace qbgdn {
 
 namespace {
 
-constexpr int CV = 8;     // channels per thread
+constexpr int CV = 8;     // channels per thread (forward, verify)
+constexpr int CVB = 4;    // channels per thread (backward)
 constexpr int NTC = 256;  // threads per block
+constexpr int PF = 4;     // tokens loaded per batch (forward)
+constexpr int PFB = 4;    // tokens loaded per batch (backward)
 
 struct ConvArgs {
   Geo geo;
@@ -43,21 +49,65 @@ __device__ __forceinline__ float round_to<float>(float x) { return x; }
 template <>
 __device__ __forceinline__ float round_to<__nv_bfloat16>(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
-template <typename T>
-__device__ __forceinline__ void ld8(const T* p, float (&o)[CV]);
+// N channels of a row (N = 4 or 8): a raw vector load, converted when used.
+template <int N, typename T>
+struct RawV;
 template <>
-__device__ __forceinline__ void ld8<__nv_bfloat16>(const __nv_bfloat16* p, float (&o)[CV]) {
-  load_vec<8, __nv_bfloat16>(p, o);
+struct RawV<8, __nv_bfloat16> {
+  uint4 w;
+  __device__ __forceinline__ void load(const __nv_bfloat16* p) { w = *reinterpret_cast<const uint4*>(p); }
+  __device__ __forceinline__ void zero() { w = make_uint4(0, 0, 0, 0); }
+  __device__ __forceinline__ void cvt(float (&o)[8]) const {
+    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&u[e]);
+      o[2 * e] = __low2float(h), o[2 * e + 1] = __high2float(h);
+    }
+  }
+};
+template <>
+struct RawV<4, __nv_bfloat16> {
+  uint2 w;
+  __device__ __forceinline__ void load(const __nv_bfloat16* p) { w = *reinterpret_cast<const uint2*>(p); }
+  __device__ __forceinline__ void zero() { w = make_uint2(0, 0); }
+  __device__ __forceinline__ void cvt(float (&o)[4]) const {
+    const uint32_t u[2] = {w.x, w.y};
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&u[e]);
+      o[2 * e] = __low2float(h), o[2 * e + 1] = __high2float(h);
+    }
+  }
+};
+template <>
+struct RawV<8, float> {
+  float4 a, b;
+  __device__ __forceinline__ void load(const float* p) {
+    a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+  }
+  __device__ __forceinline__ void zero() { a = b = make_float4(0.f, 0.f, 0.f, 0.f); }
+  __device__ __forceinline__ void cvt(float (&o)[8]) const {
+    o[0] = a.x, o[1] = a.y, o[2] = a.z, o[3] = a.w, o[4] = b.x, o[5] = b.y, o[6] = b.z, o[7] = b.w;
+  }
+};
+template <>
+struct RawV<4, float> {
+  float4 a;
+  __device__ __forceinline__ void load(const float* p) { a = *reinterpret_cast<const float4*>(p); }
+  __device__ __forceinline__ void zero() { a = make_float4(0.f, 0.f, 0.f, 0.f); }
+  __device__ __forceinline__ void cvt(float (&o)[4]) const { o[0] = a.x, o[1] = a.y, o[2] = a.z, o[3] = a.w; }
+};
+template <int N, typename T>
+__device__ __forceinline__ void ldv(const T* p, float (&o)[N]) {
+  RawV<N, T> r;
+  r.load(p);
+  r.cvt(o);
 }
+template <int N, typename T>
+__device__ __forceinline__ void stv(T* p, const float (&v)[N]);
 template <>
-__device__ __forceinline__ void ld8<float>(const float* p, float (&o)[CV]) {
-  const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
-  o[0] = a.x, o[1] = a.y, o[2] = a.z, o[3] = a.w, o[4] = b.x, o[5] = b.y, o[6] = b.z, o[7] = b.w;
-}
-template <typename T>
-__device__ __forceinline__ void st8(T* p, const float (&v)[CV]);
-template <>
-__device__ __forceinline__ void st8<__nv_bfloat16>(__nv_bfloat16* p, const float (&v)[CV]) {
+__device__ __forceinline__ void stv<8, __nv_bfloat16>(__nv_bfloat16* p, const float (&v)[8]) {
   uint32_t u[4];
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
@@ -67,19 +117,33 @@ __device__ __forceinline__ void st8<__nv_bfloat16>(__nv_bfloat16* p, const float
   *reinterpret_cast<uint4*>(p) = make_uint4(u[0], u[1], u[2], u[3]);
 }
 template <>
-__device__ __forceinline__ void st8<float>(float* p, const float (&v)[CV]) {
+__device__ __forceinline__ void stv<4, __nv_bfloat16>(__nv_bfloat16* p, const float (&v)[4]) {
+  uint32_t u[2];
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+    u[e] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  *reinterpret_cast<uint2*>(p) = make_uint2(u[0], u[1]);
+}
+template <>
+__device__ __forceinline__ void stv<8, float>(float* p, const float (&v)[8]) {
   reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
   reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
 }
+template <>
+__device__ __forceinline__ void stv<4, float>(float* p, const float (&v)[4]) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+}
 
-// One output of 8 channels from the window xp[0 .. K-1] (oldest first): the conv in a fixed FMA order
+// One output of N channels from the window xp[0 .. K-1] (oldest first): the conv in a fixed FMA order
 // rounded to T, then its SiLU rounded to T.  Every kernel below calls exactly this, so the sequence
 // form, a one-token step and the verify rows give the same bits.
-template <int K, typename T>
-__device__ __forceinline__ void conv_silu(const float (&xp)[K][CV], const float (&wv)[K][CV], float (&u)[CV],
-                                          float (&y)[CV]) {
+template <int K, typename T, int N>
+__device__ __forceinline__ void conv_silu(const float (&xp)[K][N], const float (&wv)[K][N], float (&u)[N],
+                                          float (&y)[N]) {
 #pragma unroll
-  for (int e = 0; e < CV; ++e) {
+  for (int e = 0; e < N; ++e) {
     float acc = 0.f;
 #pragma unroll
     for (int m = 0; m < K; ++m) acc = __fmaf_rn(xp[m][e], wv[m][e], acc);
@@ -97,42 +161,42 @@ __device__ __forceinline__ T* route(T* q, T* k, T* v, const ConvArgs& a, int64_t
   return v + t * a.value_dim + (c - 2 * a.key_dim);
 }
 
-template <int K, typename T>
-__device__ __forceinline__ void load_w(const ConvArgs& a, int cg, float (&wv)[K][CV]) {
+template <int K, typename T, int N>
+__device__ __forceinline__ void load_w(const ConvArgs& a, int cg, float (&wv)[K][N]) {
   const T* w = static_cast<const T*>(a.w);
 #pragma unroll
-  for (int e = 0; e < CV; ++e)
+  for (int e = 0; e < N; ++e)
 #pragma unroll
     for (int m = 0; m < K; ++m) wv[m][e] = to_f(w[(size_t)(cg + e) * K + m]);
 }
 
 // The K - 1 inputs before token tok0 of the sequence starting at s0 (state rows before the start).
-template <int K, typename T>
+template <int K, typename T, int N>
 __device__ __forceinline__ void load_halo(const ConvArgs& a, int n, int64_t s0, int64_t tok0, int cg,
-                                          float (&xp)[K][CV]) {
+                                          float (&xp)[K][N]) {
   const T* x = static_cast<const T*>(a.x);
   const T* st = static_cast<const T*>(a.state_in);
 #pragma unroll
   for (int j = 0; j < K - 1; ++j) {
     const int64_t t = tok0 - (K - 1) + j;
     if (t >= s0) {
-      ld8<T>(x + t * a.conv_dim + cg, xp[j]);
+      ldv<N, T>(x + t * a.conv_dim + cg, xp[j]);
     } else if (st) {
       const int64_t p = t - s0 + (K - 1);  // row of the carried state
-      ld8<T>(st + ((int64_t)n * (K - 1) + p) * a.conv_dim + cg, xp[j]);
+      ldv<N, T>(st + ((int64_t)n * (K - 1) + p) * a.conv_dim + cg, xp[j]);
     } else {
 #pragma unroll
-      for (int e = 0; e < CV; ++e) xp[j][e] = 0.f;
+      for (int e = 0; e < N; ++e) xp[j][e] = 0.f;
     }
   }
 }
 
-template <int K>
-__device__ __forceinline__ void shift(float (&xp)[K][CV]) {
+template <int K, int N>
+__device__ __forceinline__ void shift(float (&xp)[K][N]) {
 #pragma unroll
   for (int j = 0; j < K - 1; ++j)
 #pragma unroll
-    for (int e = 0; e < CV; ++e) xp[j][e] = xp[j + 1][e];
+    for (int e = 0; e < N; ++e) xp[j][e] = xp[j + 1][e];
 }
 
 }  // namespace
@@ -141,29 +205,38 @@ __device__ __forceinline__ void shift(float (&xp)[K][CV]) {
 // Forward: grid (chunks, conv_dim / (256 * 8)); chunk c covers up to 64 tokens of one sequence.
 template <int K, typename T>
 __global__ void __launch_bounds__(NTC) gdn_conv_fwd(ConvArgs a) {
-  const int cg = (blockIdx.y * NTC + threadIdx.x) * CV;
+  constexpr int N = CV;
+  const int cg = (blockIdx.y * NTC + threadIdx.x) * N;
   if (cg >= a.conv_dim) return;
   const int64_t c = blockIdx.x;
   int n, L;
   int64_t tok0, cf, nc, s0, s1;
   chunk_info(a.geo, c, n, tok0, L);
   seq_chunks(a.geo, n, cf, nc, s0, s1);
-  float wv[K][CV], xp[K][CV], u[CV], y[CV];
-  load_w<K, T>(a, cg, wv);
-  load_halo<K, T>(a, n, s0, tok0, cg, xp);
+  float wv[K][N], xp[K][N], u[N], y[N];
+  load_w<K, T, N>(a, cg, wv);
+  load_halo<K, T, N>(a, n, s0, tok0, cg, xp);
   const T* x = static_cast<const T*>(a.x);
   T *q = static_cast<T*>(a.q), *k = static_cast<T*>(a.k), *v = static_cast<T*>(a.v);
-  for (int i = 0; i < L; ++i) {
-    const int64_t t = tok0 + i;
-    ld8<T>(x + t * a.conv_dim + cg, xp[K - 1]);
-    conv_silu<K, T>(xp, wv, u, y);
-    st8<T>(route(q, k, v, a, t, cg), y);
-    shift<K>(xp);
+  for (int i0 = 0; i0 < L; i0 += PF) {  // PF rows loaded at once, then used
+    RawV<N, T> r[PF];
+#pragma unroll
+    for (int j = 0; j < PF; ++j)
+      if (i0 + j < L) r[j].load(x + (tok0 + i0 + j) * a.conv_dim + cg);
+#pragma unroll
+    for (int j = 0; j < PF; ++j) {
+      if (i0 + j < L) {
+        r[j].cvt(xp[K - 1]);
+        conv_silu<K, T, N>(xp, wv, u, y);
+        stv<N, T>(route(q, k, v, a, tok0 + i0 + j, cg), y);
+        shift<K, N>(xp);
+      }
+    }
   }
   if (a.state_out && c == cf + nc - 1) {  // the last chunk of the sequence: its window is the new state
     T* so = static_cast<T*>(a.state_out);
 #pragma unroll
-    for (int j = 0; j < K - 1; ++j) st8<T>(so + ((int64_t)n * (K - 1) + j) * a.conv_dim + cg, xp[j]);
+    for (int j = 0; j < K - 1; ++j) stv<N, T>(so + ((int64_t)n * (K - 1) + j) * a.conv_dim + cg, xp[j]);
   }
 }
 
@@ -185,8 +258,9 @@ __global__ void __launch_bounds__(NTC) gdn_conv_empty(const int32_t* cu, int con
 // start; the new state's cotangent (dstate_out) adds onto the last K - 1 inputs.  Each chunk
 // recomputes u for its own outputs and the K - 1 after it (same sequence).
 template <int K, typename T>
-__global__ void __launch_bounds__(NTC) gdn_conv_bwd(ConvArgs a) {
-  const int cg = (blockIdx.y * NTC + threadIdx.x) * CV;
+__global__ void __launch_bounds__(NTC, 2) gdn_conv_bwd(ConvArgs a) {
+  constexpr int N = CVB, PF = PFB;
+  const int cg = (blockIdx.y * NTC + threadIdx.x) * N;
   if (cg >= a.conv_dim) return;
   const int64_t c = blockIdx.x;
   int n, L;
@@ -195,72 +269,92 @@ __global__ void __launch_bounds__(NTC) gdn_conv_bwd(ConvArgs a) {
   seq_chunks(a.geo, n, cf, nc, s0, s1);
   const int64_t Ls = s1 - s0;
   const bool first = c == cf;
-  float wv[K][CV], xp[K][CV], u[CV], y[CV], du[K][CV], dw[K][CV];
-  load_w<K, T>(a, cg, wv);
-  load_halo<K, T>(a, n, s0, tok0, cg, xp);
+  float wv[K][N], xp[K][N], u[N], du[K][N], dw[K][N];
+  load_w<K, T, N>(a, cg, wv);
+  load_halo<K, T, N>(a, n, s0, tok0, cg, xp);
 #pragma unroll
   for (int m = 0; m < K; ++m)
 #pragma unroll
-    for (int e = 0; e < CV; ++e) du[m][e] = dw[m][e] = 0.f;
+    for (int e = 0; e < N; ++e) du[m][e] = dw[m][e] = 0.f;
   const T* x = static_cast<const T*>(a.x);
   const T *dq = static_cast<const T*>(a.dq), *dk = static_cast<const T*>(a.dk), *dv = static_cast<const T*>(a.dv);
   const T* dso = static_cast<const T*>(a.dstate_out);
   T* dx = static_cast<T*>(a.dx);
   T* dsi = static_cast<T*>(a.dstate_in);
   // inputs emitted: this chunk's tokens, and for the sequence's first chunk the K - 1 state rows
-  const int64_t in_lo = first ? tok0 - (K - 1) : tok0, in_hi = tok0 + L;
-  for (int64_t t = tok0; t < tok0 + L + K - 1; ++t) {
-    // du for output t (zero past the sequence's end)
-    shift<K>(du);
-    if (t < s1) {
-      ld8<T>(x + t * a.conv_dim + cg, xp[K - 1]);
-      conv_silu<K, T>(xp, wv, u, y);
-      float g[CV];
-      ld8<T>(route(dq, dk, dv, a, t, cg), g);
+  const int64_t in_lo = first ? tok0 - (K - 1) : tok0, in_hi = tok0 + L, t_end = tok0 + L + K - 1;
+  for (int64_t t0 = tok0; t0 < t_end; t0 += PF) {
+    // this batch's rows of x and of the output gradient, loaded at once (outputs past the sequence's
+    // end have none)
+    RawV<N, T> rx[PF], rg[PF];
 #pragma unroll
-      for (int e = 0; e < CV; ++e) {
-        const float s = 1.f / (1.f + __expf(-u[e]));
-        du[K - 1][e] = g[e] * s * (1.f + u[e] * (1.f - s));
+    for (int j = 0; j < PF; ++j) {
+      const int64_t t = t0 + j;
+      if (t < t_end && t < s1) {
+        rx[j].load(x + t * a.conv_dim + cg);
+        rg[j].load(route(dq, dk, dv, a, t, cg));
       }
-      if (t < tok0 + L) {
-#pragma unroll
-        for (int m = 0; m < K; ++m)
-#pragma unroll
-          for (int e = 0; e < CV; ++e) dw[m][e] = fmaf(du[K - 1][e], xp[m][e], dw[m][e]);
-      }
-      shift<K>(xp);
-    } else {
-#pragma unroll
-      for (int e = 0; e < CV; ++e) du[K - 1][e] = 0.f;
     }
-    // input t - (K - 1) has now seen every output that reads it: du[K-1-m] is du_{t-m}
-    const int64_t ti = t - (K - 1);
-    if (ti >= in_lo && ti < in_hi) {
-      float d[CV];
 #pragma unroll
-      for (int e = 0; e < CV; ++e) {
-        float acc = 0.f;
+    for (int j = 0; j < PF; ++j) {
+      const int64_t t = t0 + j;
+      if (t >= t_end) continue;
+      // du for output t (zero past the sequence's end): u recomputed as the forward rounds it, its
+      // sigmoid s as the forward forms it, du = dy s (1 + u (1 - s))
+      shift<K, N>(du);
+      if (t < s1) {
+        rx[j].cvt(xp[K - 1]);
+        float g[N];
+        rg[j].cvt(g);
 #pragma unroll
-        for (int m = 0; m < K; ++m) acc = fmaf(du[K - 1 - m][e], wv[m][e], acc);
-        d[e] = acc;
+        for (int e = 0; e < N; ++e) {
+          float acc = 0.f;
+#pragma unroll
+          for (int m = 0; m < K; ++m) acc = __fmaf_rn(xp[m][e], wv[m][e], acc);
+          u[e] = round_to<T>(acc);
+          const float s = __frcp_rn(__fadd_rn(1.f, __expf(-u[e])));
+          du[K - 1][e] = g[e] * s * (1.f + u[e] * (1.f - s));
+        }
+        if (t < tok0 + L) {
+#pragma unroll
+          for (int m = 0; m < K; ++m)
+#pragma unroll
+            for (int e = 0; e < N; ++e) dw[m][e] = fmaf(du[K - 1][e], xp[m][e], dw[m][e]);
+        }
+        shift<K, N>(xp);
+      } else {
+#pragma unroll
+        for (int e = 0; e < N; ++e) du[K - 1][e] = 0.f;
       }
-      const int64_t p = ti - s0 + (K - 1);  // padded position; the new state is positions Ls .. Ls + K - 2
-      if (dso && p >= Ls) {
-        float ds[CV];
-        ld8<T>(dso + ((int64_t)n * (K - 1) + (p - Ls)) * a.conv_dim + cg, ds);
+      // input t - (K - 1) has now seen every output that reads it: du[K-1-m] is du_{t-m}
+      const int64_t ti = t - (K - 1);
+      if (ti >= in_lo && ti < in_hi) {
+        float d[N];
 #pragma unroll
-        for (int e = 0; e < CV; ++e) d[e] += ds[e];
+        for (int e = 0; e < N; ++e) {
+          float acc = 0.f;
+#pragma unroll
+          for (int m = 0; m < K; ++m) acc = fmaf(du[K - 1 - m][e], wv[m][e], acc);
+          d[e] = acc;
+        }
+        const int64_t p = ti - s0 + (K - 1);  // padded position; the new state is positions Ls .. Ls + K - 2
+        if (dso && p >= Ls) {
+          float ds[N];
+          ldv<N, T>(dso + ((int64_t)n * (K - 1) + (p - Ls)) * a.conv_dim + cg, ds);
+#pragma unroll
+          for (int e = 0; e < N; ++e) d[e] += ds[e];
+        }
+        if (ti >= s0)
+          stv<N, T>(dx + ti * a.conv_dim + cg, d);
+        else if (dsi)
+          stv<N, T>(dsi + ((int64_t)n * (K - 1) + p) * a.conv_dim + cg, d);
       }
-      if (ti >= s0)
-        st8<T>(dx + ti * a.conv_dim + cg, d);
-      else if (dsi)
-        st8<T>(dsi + ((int64_t)n * (K - 1) + p) * a.conv_dim + cg, d);
     }
   }
   if (a.dw_part) {
     float* dp = a.dw_part + (c * a.conv_dim + cg) * K;
 #pragma unroll
-    for (int e = 0; e < CV; ++e)
+    for (int e = 0; e < N; ++e)
 #pragma unroll
       for (int m = 0; m < K; ++m) dp[e * K + m] = dw[m][e];
   }
@@ -284,19 +378,19 @@ __global__ void __launch_bounds__(NTC) gdn_conv_verify(ConvArgs a, int V) {
   if (cg >= a.conv_dim) return;
   const int n = blockIdx.x;
   float wv[K][CV], xp[K][CV], u[CV], y[CV];
-  load_w<K, T>(a, cg, wv);
-  load_halo<K, T>(a, n, (int64_t)n * V, (int64_t)n * V, cg, xp);
+  load_w<K, T, CV>(a, cg, wv);
+  load_halo<K, T, CV>(a, n, (int64_t)n * V, (int64_t)n * V, cg, xp);
   const T* x = static_cast<const T*>(a.x);
   T *q = static_cast<T*>(a.q), *k = static_cast<T*>(a.k), *v = static_cast<T*>(a.v);
   T* states = static_cast<T*>(a.state_out);
   for (int j = 0; j < V; ++j) {
     const int64_t t = (int64_t)n * V + j;
-    ld8<T>(x + t * a.conv_dim + cg, xp[K - 1]);
-    conv_silu<K, T>(xp, wv, u, y);
-    st8<T>(route(q, k, v, a, t, cg), y);
-    shift<K>(xp);
+    ldv<CV, T>(x + t * a.conv_dim + cg, xp[K - 1]);
+    conv_silu<K, T, CV>(xp, wv, u, y);
+    stv<CV, T>(route(q, k, v, a, t, cg), y);
+    shift<K, CV>(xp);
 #pragma unroll
-    for (int r = 0; r < K - 1; ++r) st8<T>(states + ((t * (K - 1)) + r) * a.conv_dim + cg, xp[r]);
+    for (int r = 0; r < K - 1; ++r) stv<CV, T>(states + ((t * (K - 1)) + r) * a.conv_dim + cg, xp[r]);
   }
 }
 
@@ -449,7 +543,7 @@ int qb_gdn_conv_fwd(const qb_gdn_conv_desc* d, const void* x, const void* w, con
     }
     return 0;
   }
-  const dim3 grid((unsigned)p.n_chunks, (p.conv_dim + NTC * CV - 1) / (NTC * CV));
+  const dim3 grid((unsigned)p.n_chunks, (p.conv_dim + NTC * CVB - 1) / (NTC * CVB));
   return capi_cuda(dispatch(d->dtype, 0, d->K, a, grid, 0, st), "gated delta conv forward", err, errlen);
 }
 
@@ -493,7 +587,7 @@ int qb_gdn_conv_bwd(const qb_gdn_conv_desc* d, const void* x, const void* w, con
                              err, errlen);
     return 0;
   }
-  const dim3 grid((unsigned)p.n_chunks, (p.conv_dim + NTC * CV - 1) / (NTC * CV));
+  const dim3 grid((unsigned)p.n_chunks, (p.conv_dim + NTC * CVB - 1) / (NTC * CVB));
   if ((e = dispatch(d->dtype, 1, d->K, a, grid, 0, st)) != cudaSuccess)
     return capi_cuda(e, "gated delta conv backward", err, errlen);
   if (dw) {
