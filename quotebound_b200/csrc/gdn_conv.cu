@@ -28,8 +28,6 @@ namespace {
 constexpr int CV = 8;     // channels per thread (forward, verify)
 constexpr int CVB = 4;    // channels per thread (backward)
 constexpr int NTC = 256;  // threads per block
-constexpr int PF = 4;     // tokens loaded per batch (forward)
-constexpr int PFB = 4;    // tokens loaded per batch (backward)
 
 struct ConvArgs {
   Geo geo;
@@ -56,6 +54,7 @@ template <>
 struct RawV<8, __nv_bfloat16> {
   uint4 w;
   __device__ __forceinline__ void load(const __nv_bfloat16* p) { w = *reinterpret_cast<const uint4*>(p); }
+  __device__ __forceinline__ void lds(const uint8_t* p, int) { w = *reinterpret_cast<const uint4*>(p); }
   __device__ __forceinline__ void zero() { w = make_uint4(0, 0, 0, 0); }
   __device__ __forceinline__ void cvt(float (&o)[8]) const {
     const uint32_t u[4] = {w.x, w.y, w.z, w.w};
@@ -70,6 +69,7 @@ template <>
 struct RawV<4, __nv_bfloat16> {
   uint2 w;
   __device__ __forceinline__ void load(const __nv_bfloat16* p) { w = *reinterpret_cast<const uint2*>(p); }
+  __device__ __forceinline__ void lds(const uint8_t* p, int) { w = *reinterpret_cast<const uint2*>(p); }
   __device__ __forceinline__ void zero() { w = make_uint2(0, 0); }
   __device__ __forceinline__ void cvt(float (&o)[4]) const {
     const uint32_t u[2] = {w.x, w.y};
@@ -86,6 +86,9 @@ struct RawV<8, float> {
   __device__ __forceinline__ void load(const float* p) {
     a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
   }
+  __device__ __forceinline__ void lds(const uint8_t* p, int stride) {
+    a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + stride);
+  }
   __device__ __forceinline__ void zero() { a = b = make_float4(0.f, 0.f, 0.f, 0.f); }
   __device__ __forceinline__ void cvt(float (&o)[8]) const {
     o[0] = a.x, o[1] = a.y, o[2] = a.z, o[3] = a.w, o[4] = b.x, o[5] = b.y, o[6] = b.z, o[7] = b.w;
@@ -95,6 +98,7 @@ template <>
 struct RawV<4, float> {
   float4 a;
   __device__ __forceinline__ void load(const float* p) { a = *reinterpret_cast<const float4*>(p); }
+  __device__ __forceinline__ void lds(const uint8_t* p, int) { a = *reinterpret_cast<const float4*>(p); }
   __device__ __forceinline__ void zero() { a = make_float4(0.f, 0.f, 0.f, 0.f); }
   __device__ __forceinline__ void cvt(float (&o)[4]) const { o[0] = a.x, o[1] = a.y, o[2] = a.z, o[3] = a.w; }
 };
@@ -136,6 +140,36 @@ __device__ __forceinline__ void stv<4, float>(float* p, const float (&v)[4]) {
   *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
 }
 
+// A thread's queue of rows in flight: each row's N-channel vector copied by cp.async into this thread's
+// own slot of a shared-memory ring (S slots), read back by the same thread once its commit group has
+// completed (cp.async.wait_group) -- no barrier and no spin: the hardware counts the groups.  A vector
+// of VB bytes is stored as VB / WB words of WB bytes, word w of slot s of thread t at
+// ((s * NWD + w) * NTC + t) * WB, so that a warp's reads of one word are contiguous.
+template <int N, typename T, int S>
+struct RowRing {
+  static constexpr int VB = N * (int)sizeof(T), WB = VB >= 16 ? 16 : VB, NWD = VB / WB;
+  static constexpr int BYTES = S * NWD * NTC * WB;
+  uint8_t* mine;  // this thread's word 0 of slot 0
+  __device__ __forceinline__ RowRing(uint8_t* ring) : mine(ring + threadIdx.x * WB) {}
+  __device__ __forceinline__ uint8_t* slot(int i) const { return mine + (i % S) * NWD * NTC * WB; }
+  __device__ __forceinline__ void copy(int i, const T* src) const {  // the row vector at src into slot i
+    const uint8_t* g = reinterpret_cast<const uint8_t*>(src);
+#pragma unroll
+    for (int w = 0; w < NWD; ++w) {
+      const uint32_t d = (uint32_t)__cvta_generic_to_shared(slot(i) + w * NTC * WB);
+      if constexpr (WB == 16)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(g + w * WB) : "memory");
+      else
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(d), "l"(g + w * WB) : "memory");
+    }
+  }
+  __device__ __forceinline__ static void commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+  // every group but the newest `pending` has completed
+  template <int pending>
+  __device__ __forceinline__ static void wait() { asm volatile("cp.async.wait_group %0;" ::"n"(pending) : "memory"); }
+  __device__ __forceinline__ void read(int i, RawV<N, T>& r) const { r.lds(slot(i), NTC * WB); }
+};
+
 // One output of N channels from the window xp[0 .. K-1] (oldest first): the conv in a fixed FMA order
 // rounded to T, then its SiLU rounded to T.  Every kernel below calls exactly this, so the sequence
 // form, a one-token step and the verify rows give the same bits.
@@ -148,7 +182,7 @@ __device__ __forceinline__ void conv_silu(const float (&xp)[K][N], const float (
 #pragma unroll
     for (int m = 0; m < K; ++m) acc = __fmaf_rn(xp[m][e], wv[m][e], acc);
     u[e] = round_to<T>(acc);
-    const float s = __frcp_rn(__fadd_rn(1.f, __expf(-u[e])));
+    const float s = __fdividef(1.f, __fadd_rn(1.f, __expf(-u[e])));
     y[e] = round_to<T>(__fmul_rn(u[e], s));
   }
 }
@@ -204,8 +238,10 @@ __device__ __forceinline__ void shift(float (&xp)[K][N]) {
 // ------------------------------------------------------------------------------------------------
 // Forward: grid (chunks, conv_dim / (256 * 8)); chunk c covers up to 64 tokens of one sequence.
 template <int K, typename T>
-__global__ void __launch_bounds__(NTC) gdn_conv_fwd(ConvArgs a) {
-  constexpr int N = CV;
+__global__ void __launch_bounds__(NTC, 2) gdn_conv_fwd(ConvArgs a) {
+  constexpr int N = CV, S = 12 * 16 / (N * (int)sizeof(T));  // rows in flight per thread (48 KB a block)
+  using Ring = RowRing<N, T, S>;
+  __shared__ __align__(16) uint8_t ring_mem[Ring::BYTES];
   const int cg = (blockIdx.y * NTC + threadIdx.x) * N;
   if (cg >= a.conv_dim) return;
   const int64_t c = blockIdx.x;
@@ -218,20 +254,25 @@ __global__ void __launch_bounds__(NTC) gdn_conv_fwd(ConvArgs a) {
   load_halo<K, T, N>(a, n, s0, tok0, cg, xp);
   const T* x = static_cast<const T*>(a.x);
   T *q = static_cast<T*>(a.q), *k = static_cast<T*>(a.k), *v = static_cast<T*>(a.v);
-  for (int i0 = 0; i0 < L; i0 += PF) {  // PF rows loaded at once, then used
-    RawV<N, T> r[PF];
-#pragma unroll
-    for (int j = 0; j < PF; ++j)
-      if (i0 + j < L) r[j].load(x + (tok0 + i0 + j) * a.conv_dim + cg);
-#pragma unroll
-    for (int j = 0; j < PF; ++j) {
-      if (i0 + j < L) {
-        r[j].cvt(xp[K - 1]);
-        conv_silu<K, T, N>(xp, wv, u, y);
-        stv<N, T>(route(q, k, v, a, tok0 + i0 + j, cg), y);
-        shift<K, N>(xp);
-      }
-    }
+  // the chunk's rows stream through the ring: row i + S is copied once row i has been used (the
+  // groups of rows past the chunk are empty, so that the count stays one group per row)
+  const Ring ring(ring_mem);
+#pragma unroll 1
+  for (int i = 0; i < S; ++i) {
+    if (i < L) ring.copy(i, x + (tok0 + i) * a.conv_dim + cg);
+    Ring::commit();
+  }
+#pragma unroll 1
+  for (int i = 0; i < L; ++i) {
+    Ring::template wait<S - 1>();  // row i's group is complete
+    RawV<N, T> r;
+    ring.read(i, r);
+    r.cvt(xp[K - 1]);
+    conv_silu<K, T, N>(xp, wv, u, y);
+    stv<N, T>(route(q, k, v, a, tok0 + i, cg), y);
+    shift<K, N>(xp);
+    if (i + S < L) ring.copy(i + S, x + (tok0 + i + S) * a.conv_dim + cg);  // slot i % S, read above
+    Ring::commit();
   }
   if (a.state_out && c == cf + nc - 1) {  // the last chunk of the sequence: its window is the new state
     T* so = static_cast<T*>(a.state_out);
@@ -259,7 +300,9 @@ __global__ void __launch_bounds__(NTC) gdn_conv_empty(const int32_t* cu, int con
 // recomputes u for its own outputs and the K - 1 after it (same sequence).
 template <int K, typename T>
 __global__ void __launch_bounds__(NTC, 2) gdn_conv_bwd(ConvArgs a) {
-  constexpr int N = CVB, PF = PFB;
+  constexpr int N = CVB, S = 12 * 8 / (N * (int)sizeof(T));  // rows of x and dy in flight (48 KB a block)
+  using Ring = RowRing<N, T, S>;
+  __shared__ __align__(16) uint8_t ring_mem[2 * Ring::BYTES];
   const int cg = (blockIdx.y * NTC + threadIdx.x) * N;
   if (cg >= a.conv_dim) return;
   const int64_t c = blockIdx.x;
@@ -283,36 +326,40 @@ __global__ void __launch_bounds__(NTC, 2) gdn_conv_bwd(ConvArgs a) {
   T* dsi = static_cast<T*>(a.dstate_in);
   // inputs emitted: this chunk's tokens, and for the sequence's first chunk the K - 1 state rows
   const int64_t in_lo = first ? tok0 - (K - 1) : tok0, in_hi = tok0 + L, t_end = tok0 + L + K - 1;
-  for (int64_t t0 = tok0; t0 < t_end; t0 += PF) {
-    // this batch's rows of x and of the output gradient, loaded at once (outputs past the sequence's
-    // end have none)
-    RawV<N, T> rx[PF], rg[PF];
-#pragma unroll
-    for (int j = 0; j < PF; ++j) {
-      const int64_t t = t0 + j;
-      if (t < t_end && t < s1) {
-        rx[j].load(x + t * a.conv_dim + cg);
-        rg[j].load(route(dq, dk, dv, a, t, cg));
-      }
+  // rows tok0 .. t_lim - 1 of x and of the output gradient (outputs past the sequence's end have none)
+  // stream through two rings, one commit group per row
+  const int nrows = (int)(min(t_end, s1) - tok0);
+  const Ring ringx(ring_mem), ringg(ring_mem + Ring::BYTES);
+#pragma unroll 1
+  for (int i = 0; i < S; ++i) {
+    if (i < nrows) {
+      ringx.copy(i, x + (tok0 + i) * a.conv_dim + cg);
+      ringg.copy(i, route(dq, dk, dv, a, tok0 + i, cg));
     }
-#pragma unroll
-    for (int j = 0; j < PF; ++j) {
-      const int64_t t = t0 + j;
-      if (t >= t_end) continue;
+    Ring::commit();
+  }
+  {
+#pragma unroll 1
+    for (int64_t t = tok0; t < t_end; ++t) {
+      const int i = (int)(t - tok0);
       // du for output t (zero past the sequence's end): u recomputed as the forward rounds it, its
       // sigmoid s as the forward forms it, du = dy s (1 + u (1 - s))
       shift<K, N>(du);
-      if (t < s1) {
-        rx[j].cvt(xp[K - 1]);
+      if (i < nrows) {
+        Ring::template wait<S - 1>();  // row i's group is complete
+        RawV<N, T> rx, rg;
+        ringx.read(i, rx);
+        ringg.read(i, rg);
+        rx.cvt(xp[K - 1]);
         float g[N];
-        rg[j].cvt(g);
+        rg.cvt(g);
 #pragma unroll
         for (int e = 0; e < N; ++e) {
           float acc = 0.f;
 #pragma unroll
           for (int m = 0; m < K; ++m) acc = __fmaf_rn(xp[m][e], wv[m][e], acc);
           u[e] = round_to<T>(acc);
-          const float s = __frcp_rn(__fadd_rn(1.f, __expf(-u[e])));
+          const float s = __fdividef(1.f, __fadd_rn(1.f, __expf(-u[e])));
           du[K - 1][e] = g[e] * s * (1.f + u[e] * (1.f - s));
         }
         if (t < tok0 + L) {
@@ -322,6 +369,11 @@ __global__ void __launch_bounds__(NTC, 2) gdn_conv_bwd(ConvArgs a) {
             for (int e = 0; e < N; ++e) dw[m][e] = fmaf(du[K - 1][e], xp[m][e], dw[m][e]);
         }
         shift<K, N>(xp);
+        if (i + S < nrows) {  // slots i % S, read above
+          ringx.copy(i + S, x + (tok0 + i + S) * a.conv_dim + cg);
+          ringg.copy(i + S, route(dq, dk, dv, a, tok0 + i + S, cg));
+        }
+        Ring::commit();
       } else {
 #pragma unroll
         for (int e = 0; e < N; ++e) du[K - 1][e] = 0.f;
@@ -543,7 +595,7 @@ int qb_gdn_conv_fwd(const qb_gdn_conv_desc* d, const void* x, const void* w, con
     }
     return 0;
   }
-  const dim3 grid((unsigned)p.n_chunks, (p.conv_dim + NTC * CVB - 1) / (NTC * CVB));
+  const dim3 grid((unsigned)p.n_chunks, (p.conv_dim + NTC * CV - 1) / (NTC * CV));
   return capi_cuda(dispatch(d->dtype, 0, d->K, a, grid, 0, st), "gated delta conv forward", err, errlen);
 }
 

@@ -19,6 +19,8 @@ namespace {
 
 constexpr int NW = 8;           // warps per block
 constexpr int NB_MAX = 148 * 4; // blocks of the backward (its dw partials)
+constexpr int RF = 4;           // rows per warp in flight (forward)
+constexpr int RB = 2;           // rows per warp in flight (backward)
 
 template <typename T>
 __device__ __forceinline__ float rnd(float x);
@@ -27,7 +29,8 @@ __device__ __forceinline__ float rnd<float>(float x) { return x; }
 template <>
 __device__ __forceinline__ float rnd<__nv_bfloat16>(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
-__device__ __forceinline__ float sigm(float x) { return 1.f / (1.f + __expf(-x)); }
+// 1 / (1 + e^-x) with the approximate reciprocal (about 1 ulp; 0 once 1 + e^-x passes 2^126)
+__device__ __forceinline__ float sigm(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 
 // NV consecutive elements of a row as one vector load / store (NV = 1, 2, 4, 8).
 template <int NV, typename T>
@@ -106,9 +109,9 @@ struct NormArgs {
 };
 
 // Lane l holds elements NV l .. NV l + NV - 1 of a row (one vector per tensor, coalesced across the
-// warp); a warp takes two rows per iteration so that both rows' loads are in flight together.
+// warp); a warp takes RF rows per iteration so that all their loads are in flight together.
 template <int NV, typename T>
-__global__ void __launch_bounds__(NW * 32) gdn_gated_norm_fwd(NormArgs a) {
+__global__ void __launch_bounds__(NW * 32, 4) gdn_gated_norm_fwd(NormArgs a) {  // 4 blocks per SM
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = blockIdx.x * (int64_t)NW + (threadIdx.x >> 5), nwarps = (int64_t)gridDim.x * NW;
   const T* y = static_cast<const T*>(a.y);
@@ -117,10 +120,11 @@ __global__ void __launch_bounds__(NW * 32) gdn_gated_norm_fwd(NormArgs a) {
   float w[NV];
 #pragma unroll
   for (int j = 0; j < NV; ++j) w[j] = a.w[NV * lane + j];
-  for (int64_t r0 = warp0; r0 < a.rows; r0 += 2 * nwarps) {
-    float yv[2][NV], zv[2][NV], ss[2] = {0.f, 0.f};
+  constexpr int R = NV >= 8 ? 2 : RF;  // (Dv = 256: two rows keep it within 64 registers)
+  for (int64_t r0 = warp0; r0 < a.rows; r0 += R * nwarps) {
+    float yv[R][NV], zv[R][NV], ss[R];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
+    for (int h = 0; h < R; ++h) {
       const int64_t r = r0 + h * nwarps;
       if (r < a.rows) {
         ldrow<NV, T>(y + r * a.Dv + NV * lane, yv[h]);
@@ -131,13 +135,14 @@ __global__ void __launch_bounds__(NW * 32) gdn_gated_norm_fwd(NormArgs a) {
       }
     }
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
+    for (int h = 0; h < R; ++h) {
+      ss[h] = 0.f;
 #pragma unroll
       for (int j = 0; j < NV; ++j) ss[h] = fmaf(yv[h][j], yv[h][j], ss[h]);
       ss[h] = warp_sum(ss[h]);
     }
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
+    for (int h = 0; h < R; ++h) {
       const int64_t r = r0 + h * nwarps;
       if (r >= a.rows) continue;
       const float rs = rsqrtf(ss[h] / a.Dv + a.eps);
@@ -165,10 +170,11 @@ __global__ void __launch_bounds__(NW * 32) gdn_gated_norm_bwd(NormArgs a) {
   float w[NV], dwa[NV];
 #pragma unroll
   for (int j = 0; j < NV; ++j) w[j] = a.w[NV * lane + j], dwa[j] = 0.f;
-  for (int64_t r0 = warp0; r0 < a.rows; r0 += 2 * nwarps) {
-    float yv[2][NV], zv[2][NV], gv[2][NV], ss[2] = {0.f, 0.f};
+  constexpr int R = RB;
+  for (int64_t r0 = warp0; r0 < a.rows; r0 += R * nwarps) {
+    float yv[R][NV], zv[R][NV], gv[R][NV], ss[R];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
+    for (int h = 0; h < R; ++h) {
       const int64_t r = r0 + h * nwarps;
       if (r < a.rows) {
         ldrow<NV, T>(y + r * a.Dv + NV * lane, yv[h]);
@@ -180,13 +186,14 @@ __global__ void __launch_bounds__(NW * 32) gdn_gated_norm_bwd(NormArgs a) {
       }
     }
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
+    for (int h = 0; h < R; ++h) {
+      ss[h] = 0.f;
 #pragma unroll
       for (int j = 0; j < NV; ++j) ss[h] = fmaf(yv[h][j], yv[h][j], ss[h]);
       ss[h] = warp_sum(ss[h]);
     }
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
+    for (int h = 0; h < R; ++h) {
       const int64_t r = r0 + h * nwarps;
       if (r >= a.rows) continue;  // (uniform across the warp: r is the warp's)
       const float rs = rsqrtf(ss[h] / a.Dv + a.eps);
