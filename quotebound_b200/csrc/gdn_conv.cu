@@ -27,6 +27,7 @@ namespace {
 
 constexpr int CV = 8;     // channels per thread (forward, verify)
 constexpr int CVB = 4;    // channels per thread (backward)
+constexpr int CVF = 4;    // channels per thread (forward)
 constexpr int NTC = 256;  // threads per block
 
 struct ConvArgs {
@@ -238,8 +239,8 @@ __device__ __forceinline__ void shift(float (&xp)[K][N]) {
 // ------------------------------------------------------------------------------------------------
 // Forward: grid (chunks, conv_dim / (256 * 8)); chunk c covers up to 64 tokens of one sequence.
 template <int K, typename T>
-__global__ void __launch_bounds__(NTC, 2) gdn_conv_fwd(ConvArgs a) {
-  constexpr int N = CV, S = 12 * 16 / (N * (int)sizeof(T));  // rows in flight per thread (48 KB a block)
+__global__ void __launch_bounds__(NTC, 4) gdn_conv_fwd(ConvArgs a) {
+  constexpr int N = CVF, S = 12 * 8 / (N * (int)sizeof(T));  // rows in flight per thread (24 KB a block)
   using Ring = RowRing<N, T, S>;
   __shared__ __align__(16) uint8_t ring_mem[Ring::BYTES];
   const int cg = (blockIdx.y * NTC + threadIdx.x) * N;
@@ -299,7 +300,7 @@ __global__ void __launch_bounds__(NTC) gdn_conv_empty(const int32_t* cu, int con
 // start; the new state's cotangent (dstate_out) adds onto the last K - 1 inputs.  Each chunk
 // recomputes u for its own outputs and the K - 1 after it (same sequence).
 template <int K, typename T>
-__global__ void __launch_bounds__(NTC, 2) gdn_conv_bwd(ConvArgs a) {
+__global__ void __launch_bounds__(NTC, 3) gdn_conv_bwd(ConvArgs a) {
   constexpr int N = CVB, S = 12 * 8 / (N * (int)sizeof(T));  // rows of x and dy in flight (48 KB a block)
   using Ring = RowRing<N, T, S>;
   __shared__ __align__(16) uint8_t ring_mem[2 * Ring::BYTES];
@@ -412,12 +413,22 @@ __global__ void __launch_bounds__(NTC, 2) gdn_conv_bwd(ConvArgs a) {
   }
 }
 
-// dw[ch][m] = the per-chunk partials summed in chunk order.
-__global__ void gdn_conv_dw_sum(const float* part, int64_t n_chunks, int64_t per, float* dw) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < per; i += (int64_t)gridDim.x * blockDim.x) {
-    float s = 0.f;
-    for (int64_t c = 0; c < n_chunks; ++c) s += part[c * per + i];
-    dw[i] = s;
+// dw[ch][m] = the per-chunk partials summed in a fixed order: a block takes 32 consecutive (ch, m) columns,
+// its warp g sums chunks g, g + 8, g + 16, ... in order, then the eight warp sums are added in warp order.
+__global__ void __launch_bounds__(256) gdn_conv_dw_sum(const float* part, int64_t n_chunks, int64_t per, float* dw) {
+  __shared__ float red[8][32];
+  const int lane = threadIdx.x & 31, g = threadIdx.x >> 5;
+  const int64_t i = blockIdx.x * (int64_t)32 + lane;
+  float s = 0.f;
+  if (i < per)
+    for (int64_t c = g; c < n_chunks; c += 8) s += part[c * per + i];
+  red[g][lane] = s;
+  __syncthreads();
+  if (g == 0 && i < per) {
+    float t = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) t += red[q][lane];
+    dw[i] = t;
   }
 }
 
@@ -595,7 +606,7 @@ int qb_gdn_conv_fwd(const qb_gdn_conv_desc* d, const void* x, const void* w, con
     }
     return 0;
   }
-  const dim3 grid((unsigned)p.n_chunks, (p.conv_dim + NTC * CV - 1) / (NTC * CV));
+  const dim3 grid((unsigned)p.n_chunks, (p.conv_dim + NTC * CVF - 1) / (NTC * CVF));
   return capi_cuda(dispatch(d->dtype, 0, d->K, a, grid, 0, st), "gated delta conv forward", err, errlen);
 }
 
@@ -644,7 +655,7 @@ int qb_gdn_conv_bwd(const qb_gdn_conv_desc* d, const void* x, const void* w, con
     return capi_cuda(e, "gated delta conv backward", err, errlen);
   if (dw) {
     const int64_t per = (int64_t)p.conv_dim * d->K;
-    gdn_conv_dw_sum<<<(unsigned)std::min<int64_t>((per + 255) / 256, 148 * 4), 256, 0, st>>>(part, p.n_chunks, per, dw);
+    gdn_conv_dw_sum<<<(unsigned)((per + 31) / 32), 256, 0, st>>>(part, p.n_chunks, per, dw);
     note_launch();
     if ((e = cudaGetLastError()) != cudaSuccess) return capi_cuda(e, "gated delta conv backward", err, errlen);
   }
