@@ -152,12 +152,12 @@ struct RowRing {
   static constexpr int BYTES = S * NWD * NTC * WB;
   uint8_t* mine;  // this thread's word 0 of slot 0
   __device__ __forceinline__ RowRing(uint8_t* ring) : mine(ring + threadIdx.x * WB) {}
-  __device__ __forceinline__ uint8_t* slot(int i) const { return mine + (i % S) * NWD * NTC * WB; }
-  __device__ __forceinline__ void copy(int i, const T* src) const {  // the row vector at src into slot i
+  __device__ __forceinline__ uint8_t* slot(int s) const { return mine + s * NWD * NTC * WB; }
+  __device__ __forceinline__ void copy(int s, const T* src) const {  // the row vector at src into slot s
     const uint8_t* g = reinterpret_cast<const uint8_t*>(src);
 #pragma unroll
     for (int w = 0; w < NWD; ++w) {
-      const uint32_t d = (uint32_t)__cvta_generic_to_shared(slot(i) + w * NTC * WB);
+      const uint32_t d = (uint32_t)__cvta_generic_to_shared(slot(s) + w * NTC * WB);
       if constexpr (WB == 16)
         asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(g + w * WB) : "memory");
       else
@@ -168,7 +168,8 @@ struct RowRing {
   // every group but the newest `pending` has completed
   template <int pending>
   __device__ __forceinline__ static void wait() { asm volatile("cp.async.wait_group %0;" ::"n"(pending) : "memory"); }
-  __device__ __forceinline__ void read(int i, RawV<N, T>& r) const { r.lds(slot(i), NTC * WB); }
+  __device__ __forceinline__ void read(int s, RawV<N, T>& r) const { r.lds(slot(s), NTC * WB); }
+  __device__ __forceinline__ static int next(int s) { return s + 1 == S ? 0 : s + 1; }
 };
 
 // One output of N channels from the window xp[0 .. K-1] (oldest first): the conv in a fixed FMA order
@@ -184,7 +185,7 @@ __device__ __forceinline__ void conv_silu(const float (&xp)[K][N], const float (
     for (int m = 0; m < K; ++m) acc = __fmaf_rn(xp[m][e], wv[m][e], acc);
     u[e] = round_to<T>(acc);
     const float s = __fdividef(1.f, __fadd_rn(1.f, __expf(-u[e])));
-    y[e] = round_to<T>(__fmul_rn(u[e], s));
+    y[e] = __fmul_rn(u[e], s);  // rounded to T once, by the store (stv)
   }
 }
 
@@ -263,17 +264,19 @@ __global__ void __launch_bounds__(NTC, 4) gdn_conv_fwd(ConvArgs a) {
     if (i < L) ring.copy(i, x + (tok0 + i) * a.conv_dim + cg);
     Ring::commit();
   }
-#pragma unroll 1
+  int sl = 0;  // row i's slot, i % S
+#pragma unroll 4
   for (int i = 0; i < L; ++i) {
     Ring::template wait<S - 1>();  // row i's group is complete
     RawV<N, T> r;
-    ring.read(i, r);
+    ring.read(sl, r);
     r.cvt(xp[K - 1]);
     conv_silu<K, T, N>(xp, wv, u, y);
     stv<N, T>(route(q, k, v, a, tok0 + i, cg), y);
     shift<K, N>(xp);
-    if (i + S < L) ring.copy(i + S, x + (tok0 + i + S) * a.conv_dim + cg);  // slot i % S, read above
+    if (i + S < L) ring.copy(sl, x + (tok0 + i + S) * a.conv_dim + cg);  // slot i % S, read above
     Ring::commit();
+    sl = Ring::next(sl);
   }
   if (a.state_out && c == cf + nc - 1) {  // the last chunk of the sequence: its window is the new state
     T* so = static_cast<T*>(a.state_out);
@@ -340,7 +343,8 @@ __global__ void __launch_bounds__(NTC, 3) gdn_conv_bwd(ConvArgs a) {
     Ring::commit();
   }
   {
-#pragma unroll 1
+    int sl = 0;  // row i's slot, i % S
+#pragma unroll 4
     for (int64_t t = tok0; t < t_end; ++t) {
       const int i = (int)(t - tok0);
       // du for output t (zero past the sequence's end): u recomputed as the forward rounds it, its
@@ -349,8 +353,8 @@ __global__ void __launch_bounds__(NTC, 3) gdn_conv_bwd(ConvArgs a) {
       if (i < nrows) {
         Ring::template wait<S - 1>();  // row i's group is complete
         RawV<N, T> rx, rg;
-        ringx.read(i, rx);
-        ringg.read(i, rg);
+        ringx.read(sl, rx);
+        ringg.read(sl, rg);
         rx.cvt(xp[K - 1]);
         float g[N];
         rg.cvt(g);
@@ -371,10 +375,11 @@ __global__ void __launch_bounds__(NTC, 3) gdn_conv_bwd(ConvArgs a) {
         }
         shift<K, N>(xp);
         if (i + S < nrows) {  // slots i % S, read above
-          ringx.copy(i + S, x + (tok0 + i + S) * a.conv_dim + cg);
-          ringg.copy(i + S, route(dq, dk, dv, a, tok0 + i + S, cg));
+          ringx.copy(sl, x + (tok0 + i + S) * a.conv_dim + cg);
+          ringg.copy(sl, route(dq, dk, dv, a, tok0 + i + S, cg));
         }
         Ring::commit();
+        sl = Ring::next(sl);
       } else {
 #pragma unroll
         for (int e = 0; e < N; ++e) du[K - 1][e] = 0.f;
