@@ -88,9 +88,9 @@ def load_peaks():
 
 # ---- clocks during the timed region ----
 class ClockSampler:
-    """SM clock and throttle reasons sampled during the timed region.  NVML is polled about every 0.5 ms (the
-    timed region of one workload is tens of milliseconds, too short for nvidia-smi's 200 ms period);
-    nvidia-smi -lms 200 is the fallback when NVML cannot be loaded."""
+    """SM clock and throttle reasons sampled during the timed region.  NVML is polled back to back (the
+    timed region of one workload is milliseconds to tens of milliseconds, too short for nvidia-smi's 200 ms
+    period); nvidia-smi -lms 200 is the fallback when NVML cannot be loaded."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
@@ -105,6 +105,7 @@ class ClockSampler:
         self.reasons = set()
         self.max_mhz = None
         self.source = None
+        self.n_reason_polls = 0
         self._stop = threading.Event()
 
     def start(self):
@@ -118,21 +119,28 @@ class ClockSampler:
                     "sw_thermal_slowdown": getattr(pynvml, "nvmlClocksThrottleReasonSwThermalSlowdown", 0x20),
                     "sw_power_cap": pynvml.nvmlClocksThrottleReasonSwPowerCap}
 
-            def poll():
-                while not self._stop.is_set():
+            def poll():  # the SM clock every poll, the throttle reasons every fourth (and on the last)
+                k = 0
+                while True:
+                    last = self._stop.is_set()
                     try:
                         self.sm.append(float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)))
-                        r = pynvml.nvmlDeviceGetCurrentClocksThrottleReasons(h)
-                        for n, b in bits.items():
-                            if r & b:
-                                self.reasons.add(n)
+                        if k % 4 == 0 or last:
+                            r = pynvml.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+                            self.n_reason_polls += 1
+                            for n, b in bits.items():
+                                if r & b:
+                                    self.reasons.add(n)
                     except Exception:
                         pass
-                    time.sleep(0.0005)
+                    if last:
+                        break
+                    k += 1
+                    time.sleep(0.0001)
 
             self.thread = threading.Thread(target=poll, daemon=True)
             self.thread.start()
-            self.source = "nvml, polled about every 0.5 ms"
+            self.source = "nvml: SM clock polled back to back, throttle reasons every fourth poll"
             return
         except Exception:
             self.thread = None
@@ -176,8 +184,11 @@ class ClockSampler:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no clock source"]}
         sm = sorted(self.sm)
         med = sm[len(sm) // 2] if sm else None
-        return {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": len(sm),
-                "source": self.source}
+        out = {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": len(sm),
+               "source": self.source}
+        if self.n_reason_polls:
+            out["reason_samples"] = self.n_reason_polls
+        return out
 
 
 # ---- the step ----
@@ -540,7 +551,7 @@ def run_e2e(W, args, dev, dist, world, allreduce):
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(comp)
-    n = max(3, args.steps // 2)
+    n = max(3, args.steps)  # K steps, as the device-timed line; the pipeline's fill and drain included
     run(n, e0)
     e1.record(comp)
     torch.cuda.synchronize()
