@@ -26,8 +26,10 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quad = warp & 3, half = warp >> 2;
-  const int64_t c = blockIdx.x;
-  const int hk = blockIdx.y, Hv = a.geo.Hv, ratio = Hv / a.geo.Hk;
+  // a 1-D grid, key heads fastest: the first CTAs take the lowest chunks of every key head, whose state
+  // cotangents and [dO; F] rows the reverse walk (chunks high to low) wrote last and L2 may still hold
+  const int64_t c = blockIdx.x / a.geo.Hk;
+  const int hk = (int)(blockIdx.x % a.geo.Hk), Hv = a.geo.Hv, ratio = Hv / a.geo.Hk;
   int n, L;
   int64_t tok0;
   chunk_info(a.geo, c, n, tok0, L);
@@ -532,12 +534,12 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
     // result whichever CTA it is):  dA_log[h], ddt_bias[h] = sum over chunks of head_part[c][h][0 | 1]
     if (tid == 0) {
       __threadfence();
-      s_last = atomicAdd(a.done, 1u) == gridDim.x * gridDim.y - 1;
+      s_last = atomicAdd(a.done, 1u) == gridDim.x - 1;
     }
     __syncthreads();
     if (s_last) {
       __threadfence();
-      const int64_t nc = gridDim.x;
+      const int64_t nc = gridDim.x / a.geo.Hk;
       for (int j = tid; j < 2 * Hv; j += blockDim.x) {
         const float* p = a.head_part + j;  // head j >> 1, term j & 1
         float s = 0.f;
@@ -562,7 +564,7 @@ cudaError_t launch_chunk_bwd_grad(const CUtensorMap& smap_mn, const CUtensorMap&
   auto kern = out_bf16 ? gdn_chunk_bwd_grad<__nv_bfloat16> : gdn_chunk_bwd_grad<float>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GR_SMEM);
   if (e != cudaSuccess) return e;
-  kern<<<dim3((unsigned)n_chunks, Hk), 256, GR_SMEM, st>>>(smap_mn, dmap_mn, vmap, dqmap, dkmap, a);
+  kern<<<(unsigned)(n_chunks * Hk), 256, GR_SMEM, st>>>(smap_mn, dmap_mn, vmap, dqmap, dkmap, a);
   note_launch();
   return cudaGetLastError();
 }
