@@ -9,12 +9,14 @@
 // form runs V tokens as V one-token steps bit for bit and keeps every token's conv window
 // (src/deltanet.cpp:79-87, RowStates.conv in src/model.h:84-89).
 //
-// HBM-bound: one thread owns N consecutive channels (8 in the forward: one 16-byte bf16 vector; 4 in the
-// backward, whose per-thread state is four times larger) over a chunk of 64 tokens of one sequence, with
-// the K - 1 previous inputs in registers, so x is read once (plus K - 1 rows of halo per chunk) and each
-// output written once, all coalesced along the channels.  The rows are loaded eight tokens at a time
-// (all eight loads in flight before the first is used): one load in flight per thread leaves these
-// kernels bound by memory latency at a fraction of the bandwidth.
+// One thread owns 4 consecutive channels (one 8-byte bf16 vector) over a chunk of 64 tokens of one
+// sequence, with the K - 1 previous inputs in registers, so x is read once (plus K - 1 rows of halo per
+// chunk) and each output written once, all coalesced along the channels.  Each thread's rows stream
+// through a queue of its own in shared memory (cp.async into its slot of a ring, a dozen rows in
+// flight), so these kernels are not bound by memory latency; what bounds them is the instruction issue
+// of the per-element arithmetic (the conv, its bf16 rounding, the SiLU's exponential and reciprocal).
+#include <type_traits>
+
 #include "../../include/qb_gdn.h"
 #include "capi_util.cuh"
 #include "gdn_common.cuh"
@@ -342,59 +344,63 @@ __global__ void __launch_bounds__(NTC, 3) gdn_conv_bwd(ConvArgs a) {
     }
     Ring::commit();
   }
-  {
-    int sl = 0;  // row i's slot, i % S
-#pragma unroll 4
-    for (int64_t t = tok0; t < t_end; ++t) {
-      const int i = (int)(t - tok0);
-      // du for output t (zero past the sequence's end): u recomputed as the forward rounds it, its
-      // sigmoid s as the forward forms it, du = dy s (1 + u (1 - s))
-      shift<K, N>(du);
-      if (i < nrows) {
-        Ring::template wait<S - 1>();  // row i's group is complete
-        RawV<N, T> rx, rg;
-        ringx.read(sl, rx);
-        ringg.read(sl, rg);
-        rx.cvt(xp[K - 1]);
-        float g[N];
-        rg.cvt(g);
+  int sl = 0;  // row i's slot, i % S
+  // one token: du for output t (zero past the sequence's end; u recomputed as the forward rounds it, its
+  // sigmoid s as the forward forms it, du = dy s (1 + u (1 - s))), then dx of input t - (K - 1), which has
+  // now seen every output that reads it (du[K-1-m] is du_{t-m}).  FAST: a token of the chunk from its
+  // K-th on, for which every test below has a known outcome (its row exists, it feeds dw, its input
+  // ti = t - (K - 1) lies in the chunk, in the sequence, and before the carried state's rows).
+  auto token = [&](int64_t t, auto fast) {
+    constexpr bool FAST = decltype(fast)::value;
+    const int i = (int)(t - tok0);
+    shift<K, N>(du);
+    if (FAST || i < nrows) {
+      Ring::template wait<S - 1>();  // row i's group is complete
+      RawV<N, T> rx, rg;
+      ringx.read(sl, rx);
+      ringg.read(sl, rg);
+      rx.cvt(xp[K - 1]);
+      float g[N];
+      rg.cvt(g);
 #pragma unroll
-        for (int e = 0; e < N; ++e) {
-          float acc = 0.f;
+      for (int e = 0; e < N; ++e) {
+        float acc = 0.f;
 #pragma unroll
-          for (int m = 0; m < K; ++m) acc = __fmaf_rn(xp[m][e], wv[m][e], acc);
-          u[e] = round_to<T>(acc);
-          const float s = __fdividef(1.f, __fadd_rn(1.f, __expf(-u[e])));
-          du[K - 1][e] = g[e] * s * (1.f + u[e] * (1.f - s));
-        }
-        if (t < tok0 + L) {
-#pragma unroll
-          for (int m = 0; m < K; ++m)
-#pragma unroll
-            for (int e = 0; e < N; ++e) dw[m][e] = fmaf(du[K - 1][e], xp[m][e], dw[m][e]);
-        }
-        shift<K, N>(xp);
-        if (i + S < nrows) {  // slots i % S, read above
-          ringx.copy(sl, x + (tok0 + i + S) * a.conv_dim + cg);
-          ringg.copy(sl, route(dq, dk, dv, a, tok0 + i + S, cg));
-        }
-        Ring::commit();
-        sl = Ring::next(sl);
-      } else {
-#pragma unroll
-        for (int e = 0; e < N; ++e) du[K - 1][e] = 0.f;
+        for (int m = 0; m < K; ++m) acc = __fmaf_rn(xp[m][e], wv[m][e], acc);
+        u[e] = round_to<T>(acc);
+        const float s = __fdividef(1.f, __fadd_rn(1.f, __expf(-u[e])));
+        du[K - 1][e] = g[e] * s * (1.f + u[e] * (1.f - s));
       }
-      // input t - (K - 1) has now seen every output that reads it: du[K-1-m] is du_{t-m}
-      const int64_t ti = t - (K - 1);
-      if (ti >= in_lo && ti < in_hi) {
-        float d[N];
+      if (FAST || t < tok0 + L) {
 #pragma unroll
-        for (int e = 0; e < N; ++e) {
-          float acc = 0.f;
+        for (int m = 0; m < K; ++m)
 #pragma unroll
-          for (int m = 0; m < K; ++m) acc = fmaf(du[K - 1 - m][e], wv[m][e], acc);
-          d[e] = acc;
-        }
+          for (int e = 0; e < N; ++e) dw[m][e] = fmaf(du[K - 1][e], xp[m][e], dw[m][e]);
+      }
+      shift<K, N>(xp);
+      if (i + S < nrows) {  // slots i % S, read above
+        ringx.copy(sl, x + (tok0 + i + S) * a.conv_dim + cg);
+        ringg.copy(sl, route(dq, dk, dv, a, tok0 + i + S, cg));
+      }
+      Ring::commit();
+      sl = Ring::next(sl);
+    } else {
+#pragma unroll
+      for (int e = 0; e < N; ++e) du[K - 1][e] = 0.f;
+    }
+    const int64_t ti = t - (K - 1);
+    if (FAST || (ti >= in_lo && ti < in_hi)) {
+      float d[N];
+#pragma unroll
+      for (int e = 0; e < N; ++e) {
+        float acc = 0.f;
+#pragma unroll
+        for (int m = 0; m < K; ++m) acc = fmaf(du[K - 1 - m][e], wv[m][e], acc);
+        d[e] = acc;
+      }
+      if constexpr (FAST) {
+        stv<N, T>(dx + ti * a.conv_dim + cg, d);
+      } else {
         const int64_t p = ti - s0 + (K - 1);  // padded position; the new state is positions Ls .. Ls + K - 2
         if (dso && p >= Ls) {
           float ds[N];
@@ -408,7 +414,16 @@ __global__ void __launch_bounds__(NTC, 3) gdn_conv_bwd(ConvArgs a) {
           stv<N, T>(dsi + ((int64_t)n * (K - 1) + p) * a.conv_dim + cg, d);
       }
     }
-  }
+  };
+  // the chunk's first K - 1 tokens, its later ones (fast), then the K - 1 outputs after it
+  const int64_t f0 = tok0 + (K - 1), f1 = tok0 + L;
+  int64_t t = tok0;
+#pragma unroll 1
+  for (; t < f0 && t < t_end; ++t) token(t, std::false_type{});
+#pragma unroll 4
+  for (; t < f1; ++t) token(t, std::true_type{});
+#pragma unroll 1
+  for (; t < t_end; ++t) token(t, std::false_type{});
   if (a.dw_part) {
     float* dp = a.dw_part + (c * a.conv_dim + cg) * K;
 #pragma unroll
