@@ -5,9 +5,9 @@
 // (autodiff through those ops, the roundings passing the cotangent through):
 //   dn = do silu(z),  dz = do n silu'(z),
 //   dy = r (w dn) - y r^3 (sum_e y_e w_e dn_e) / Dv,  dw = sum over rows of dn y r.
-// HBM-bound: one warp per row, Dv / 32 consecutive elements per lane (one vector load per tensor), two
-// rows per warp in flight, warp-shuffle row sums; dw summed per block in a fixed row order, then over
-// blocks by one block per column in a fixed tree order (deterministic, no atomics).
+// HBM-bound: one warp per row, Dv / 32 consecutive elements per lane (one vector load per tensor), a
+// full SM of warps, warp-shuffle row sums; dw summed per block in a fixed row order, then over blocks by
+// one block per column in a fixed tree order (deterministic, no atomics).
 #include "../../include/qb_gdn.h"
 #include "capi_util.cuh"
 #include "gdn_common.cuh"
@@ -18,9 +18,14 @@ namespace qbgdn {
 namespace {
 
 constexpr int NW = 8;           // warps per block
-constexpr int NB_MAX = 148 * 4; // blocks of the backward (its dw partials)
-constexpr int RF = 4;           // rows per warp in flight (forward)
-constexpr int RB = 2;           // rows per warp in flight (backward)
+// One row per warp at a time, and as many warps as fit (eight 256-thread blocks per SM in the forward,
+// six in the backward, whose dw partials need the registers): measured on B200 at Dv = 128, more
+// resident warps keep more loads in flight than more rows per warp do.
+// Dv = 256 (eight elements per lane) needs more registers: four and three blocks.
+constexpr int RF = 1;           // rows per warp in flight (forward)
+constexpr int RB = 1;           // rows per warp in flight (backward)
+__host__ __device__ constexpr int fwd_blocks_per_sm(int nv) { return nv >= 8 ? 4 : 8; }
+__host__ __device__ constexpr int bwd_blocks_per_sm(int nv) { return nv >= 8 ? 3 : 6; }
 
 template <typename T>
 __device__ __forceinline__ float rnd(float x);
@@ -109,9 +114,9 @@ struct NormArgs {
 };
 
 // Lane l holds elements NV l .. NV l + NV - 1 of a row (one vector per tensor, coalesced across the
-// warp); a warp takes RF rows per iteration so that all their loads are in flight together.
+// warp); a warp takes RF rows per iteration, all their loads in flight together.
 template <int NV, typename T>
-__global__ void __launch_bounds__(NW * 32, 4) gdn_gated_norm_fwd(NormArgs a) {  // 4 blocks per SM
+__global__ void __launch_bounds__(NW * 32, fwd_blocks_per_sm(NV)) gdn_gated_norm_fwd(NormArgs a) {
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = blockIdx.x * (int64_t)NW + (threadIdx.x >> 5), nwarps = (int64_t)gridDim.x * NW;
   const T* y = static_cast<const T*>(a.y);
@@ -120,7 +125,7 @@ __global__ void __launch_bounds__(NW * 32, 4) gdn_gated_norm_fwd(NormArgs a) {  
   float w[NV];
 #pragma unroll
   for (int j = 0; j < NV; ++j) w[j] = a.w[NV * lane + j];
-  constexpr int R = NV >= 8 ? 2 : RF;  // (Dv = 256: two rows keep it within 64 registers)
+  constexpr int R = RF;
   for (int64_t r0 = warp0; r0 < a.rows; r0 += R * nwarps) {
     float yv[R][NV], zv[R][NV], ss[R];
 #pragma unroll
@@ -158,7 +163,7 @@ __global__ void __launch_bounds__(NW * 32, 4) gdn_gated_norm_fwd(NormArgs a) {  
 }
 
 template <int NV, typename T>
-__global__ void __launch_bounds__(NW * 32) gdn_gated_norm_bwd(NormArgs a) {
+__global__ void __launch_bounds__(NW * 32, bwd_blocks_per_sm(NV)) gdn_gated_norm_bwd(NormArgs a) {
   __shared__ float red[NW][NV * 32];
   const int lane = threadIdx.x & 31, wi = threadIdx.x >> 5;
   const int64_t warp0 = blockIdx.x * (int64_t)NW + wi, nwarps = (int64_t)gridDim.x * NW;
@@ -244,14 +249,16 @@ __global__ void __launch_bounds__(256) gdn_gated_norm_dw(const float* part, int 
   if (t == 0) dw[i] = sh[0];
 }
 
-int norm_blocks(int64_t rows) {
+// blocks of a launch: a warp per row, at most one wave (the backward's count is also its dw partials')
+int norm_blocks(int64_t rows, int Dv, bool bwd) {
+  const int per_sm = bwd ? bwd_blocks_per_sm(Dv / 32) : fwd_blocks_per_sm(Dv / 32);
   const int64_t b = (rows + NW - 1) / NW;
-  return (int)std::max<int64_t>(1, std::min<int64_t>(b, NB_MAX));
+  return (int)std::max<int64_t>(1, std::min<int64_t>(b, 148 * per_sm));
 }
 
 template <typename T>
 cudaError_t launch_norm(bool bwd, const NormArgs& a, cudaStream_t st) {
-  const int nb = norm_blocks(a.rows);
+  const int nb = norm_blocks(a.rows, a.Dv, bwd);
 #define QB_NORM_CASE(NV)                                                                   \
   case NV:                                                                                 \
     if (bwd) gdn_gated_norm_bwd<NV, T><<<nb, NW * 32, 0, st>>>(a);                         \
@@ -307,7 +314,7 @@ int qb_gdn_gated_norm_fwd(int64_t P, int32_t Hv, int32_t Dv, float eps, int32_t 
 
 int64_t qb_gdn_gated_norm_workspace_bytes(int64_t P, int32_t Hv, int32_t Dv) {
   if (P < 0 || Hv < 1 || Dv < 1) return -1;
-  return (((int64_t)norm_blocks(P * Hv) * Dv * 4 + 255) / 256) * 256;
+  return (((int64_t)norm_blocks(P * Hv, Dv, true) * Dv * 4 + 255) / 256) * 256;
 }
 
 int qb_gdn_gated_norm_bwd(int64_t P, int32_t Hv, int32_t Dv, float eps, int32_t dtype, const void* y, const void* z,
@@ -334,7 +341,7 @@ int qb_gdn_gated_norm_bwd(int64_t P, int32_t Hv, int32_t Dv, float eps, int32_t 
   a.part = dw ? static_cast<float*>(ws) : nullptr;
   cudaError_t e = dtype == QB_DTYPE_BF16 ? launch_norm<__nv_bfloat16>(true, a, st) : launch_norm<float>(true, a, st);
   if (e == cudaSuccess && dw) {
-    gdn_gated_norm_dw<<<Dv, 256, 0, st>>>(a.part, norm_blocks(a.rows), Dv, dw);
+    gdn_gated_norm_dw<<<Dv, 256, 0, st>>>(a.part, norm_blocks(a.rows, Dv, true), Dv, dw);
     note_launch();
     e = cudaGetLastError();
   }
