@@ -663,38 +663,17 @@ def _timed(step, steps, warmup, dev):
     return ms, {k: sum(v) / len(v) for k, v in per_op.items()}, launches, clocks
 
 
-def conv_norm_line(args, dev, hbm, src):
-    """The causal conv + SiLU (with the q/k/v split) and the gated RMSNorm, forward and backward, at the 4B
-    layer shape (Hk=16, Hv=32, Dk=Dv=128, conv_dim 8192, 4 taps) over B = 4 sequences of 2048 tokens: every
-    activation is 64-128 MB, so each op streams HBM.  The roofline is each op's algorithmic bytes (its
-    inputs read and outputs written once) over its CUDA-event time."""
-    from quotebound_b200 import _lib, conv, norm
-    B, T, Hk, Hv, D, K = 4, 2048, 16, 32, 128, 4
-    cdim = 2 * Hk * D + Hv * D
-    gen = torch.Generator(device=dev).manual_seed(0)
-    x = torch.randn(B, T, cdim, generator=gen, device=dev).to(torch.bfloat16)
-    w = (torch.randn(cdim, K, generator=gen, device=dev) * 0.5).to(torch.bfloat16)
-    st = torch.randn(B, K - 1, cdim, generator=gen, device=dev).to(torch.bfloat16)
-    dq = torch.randn(B, T, Hk, D, generator=gen, device=dev).to(torch.bfloat16)
-    dk = torch.randn(B, T, Hk, D, generator=gen, device=dev).to(torch.bfloat16)
-    dv = torch.randn(B, T, Hv, D, generator=gen, device=dev).to(torch.bfloat16)
-    y = torch.randn(B, T, Hv, D, generator=gen, device=dev).to(torch.bfloat16)
-    z = torch.randn(B, T, Hv, D, generator=gen, device=dev).to(torch.bfloat16)
-    do = torch.randn(B, T, Hv, D, generator=gen, device=dev).to(torch.bfloat16)
-    nw = torch.rand(D, generator=gen, device=dev) + 0.5
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
-
-    ops = (("conv_fwd", lambda: conv.conv_fwd(x, w, st, Hk=Hk, Dk=D, Hv=Hv, Dv=D)),
-           ("conv_bwd", lambda: conv.conv_bwd(x, w, st, dq, dk, dv, Hk=Hk, Dk=D, Hv=Hv, Dv=D)),
-           ("norm_fwd", lambda: norm.gated_norm_fwd(y, z, nw)),
-           ("norm_bwd", lambda: norm.gated_norm_bwd(y, z, nw, do)))
-    for _ in range(args.warmup):
+def _graph_ops_timed(ops, steps, warmup, dev, flush_bytes=256 * 1024 * 1024):
+    """Each (name, fn) of `ops` captured in its own CUDA graph (its host-side work -- argument checks, output
+    and workspace allocation, the ctypes call -- then stays out of its events) and replayed `steps` times,
+    L2 flushed before each replay, outside its events, so that each op's inputs come from HBM.  Returns the
+    mean device ms per op, the library launches in the timed replays and the clock record."""
+    from quotebound_b200 import _lib
+    flush = torch.empty(flush_bytes, dtype=torch.uint8, device=dev)
+    for _ in range(warmup):
         for _, fn in ops:
             fn()
     torch.cuda.synchronize()
-    # Each op captured in its own CUDA graph (its host-side work -- argument checks, output and workspace
-    # allocation, the ctypes call -- then stays out of its events); L2 flushed before each replay, outside
-    # its events, so each op's inputs come from HBM.
     graphs = []
     for name, fn in ops:
         side = torch.cuda.Stream()
@@ -713,7 +692,7 @@ def conv_norm_line(args, dev, hbm, src):
     sampler = ClockSampler(dev.index)
     sampler.start()
     evs = []
-    for _ in range(args.steps):
+    for _ in range(steps):
         for name, g, _ in graphs:
             flush.zero_()
             e0 = torch.cuda.Event(enable_timing=True)
@@ -724,11 +703,38 @@ def conv_norm_line(args, dev, hbm, src):
             evs.append((name, e0, e1))
     torch.cuda.synchronize()
     clocks = sampler.stop()
-    launches = sum(n for _, _, n in graphs) * args.steps
+    launches = sum(n for _, _, n in graphs) * steps
     per_op = {}
     for name, a, b in evs:
         per_op.setdefault(name, []).append(a.elapsed_time(b))
-    per_op = {k: sum(v) / len(v) for k, v in per_op.items()}
+    return {k: sum(v) / len(v) for k, v in per_op.items()}, launches, clocks
+
+
+def conv_norm_line(args, dev, hbm, src):
+    """The causal conv + SiLU (with the q/k/v split) and the gated RMSNorm, forward and backward, at the 4B
+    layer shape (Hk=16, Hv=32, Dk=Dv=128, conv_dim 8192, 4 taps) over B = 4 sequences of 2048 tokens: every
+    activation is 64-128 MB, so each op streams HBM.  The roofline is each op's algorithmic bytes (its
+    inputs read and outputs written once) over its CUDA-event time."""
+    from quotebound_b200 import conv, norm
+    B, T, Hk, Hv, D, K = 4, 2048, 16, 32, 128, 4
+    cdim = 2 * Hk * D + Hv * D
+    gen = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(B, T, cdim, generator=gen, device=dev).to(torch.bfloat16)
+    w = (torch.randn(cdim, K, generator=gen, device=dev) * 0.5).to(torch.bfloat16)
+    st = torch.randn(B, K - 1, cdim, generator=gen, device=dev).to(torch.bfloat16)
+    dq = torch.randn(B, T, Hk, D, generator=gen, device=dev).to(torch.bfloat16)
+    dk = torch.randn(B, T, Hk, D, generator=gen, device=dev).to(torch.bfloat16)
+    dv = torch.randn(B, T, Hv, D, generator=gen, device=dev).to(torch.bfloat16)
+    y = torch.randn(B, T, Hv, D, generator=gen, device=dev).to(torch.bfloat16)
+    z = torch.randn(B, T, Hv, D, generator=gen, device=dev).to(torch.bfloat16)
+    do = torch.randn(B, T, Hv, D, generator=gen, device=dev).to(torch.bfloat16)
+    nw = torch.rand(D, generator=gen, device=dev) + 0.5
+
+    ops = (("conv_fwd", lambda: conv.conv_fwd(x, w, st, Hk=Hk, Dk=D, Hv=Hv, Dv=D)),
+           ("conv_bwd", lambda: conv.conv_bwd(x, w, st, dq, dk, dv, Hk=Hk, Dk=D, Hv=Hv, Dv=D)),
+           ("norm_fwd", lambda: norm.gated_norm_fwd(y, z, nw)),
+           ("norm_bwd", lambda: norm.gated_norm_bwd(y, z, nw, do)))
+    per_op, launches, clocks = _graph_ops_timed(ops, args.steps, args.warmup, dev)
     ms = sum(per_op.values())  # the four ops' device time per step (the flushes between them excluded)
     act, row = B * T * cdim * 2, B * T * Hv * D * 2
     nbytes = {"conv_fwd": 2 * act, "conv_bwd": 3 * act, "norm_fwd": 3 * row, "norm_bwd": 5 * row}
@@ -748,6 +754,36 @@ def conv_norm_line(args, dev, hbm, src):
             "roofline": {"kernel": dom, "bound": "hbm", "achieved": roof[dom]["achieved_gbs"], "peak": hbm,
                          "unit": "GB/s", "frac": roof[dom]["frac"], "peak_source": src, "traffic": None,
                          "bytes_per_launch": nbytes[dom], "per_op": roof}}
+
+
+def decode_line(args, dev, hbm, N, V, Hk, Hv, D, rstates):
+    """The decode-time companions of the verify at config 4's shape: the conv's verify rows (V drafted
+    tokens of x through the conv + SiLU as V one-token steps, every token's conv window kept) and the two
+    selections after acceptance (keep_conv_rows, keep_rows: the states after keep[n] accepted tokens).
+    Each op a CUDA graph replay after an L2 flush; the roofline is each op's algorithmic bytes."""
+    from quotebound_b200 import conv, exact
+    K = 4
+    cdim = 2 * Hk * D + Hv * D
+    gen = torch.Generator(device=dev).manual_seed(3)
+    x = torch.randn(N, V, cdim, generator=gen, device=dev).to(torch.bfloat16)
+    w = (torch.randn(cdim, K, generator=gen, device=dev) * 0.5).to(torch.bfloat16)
+    st = torch.randn(N, K - 1, cdim, generator=gen, device=dev).to(torch.bfloat16)
+    cstates = conv.conv_verify(x, w, st, Hk=Hk, Dk=D, Hv=Hv, Dv=D)[3]
+    keep = torch.randint(1, V + 1, (N,), generator=gen, device=dev, dtype=torch.int32)
+    ops = (("conv_verify", lambda: conv.conv_verify(x, w, st, Hk=Hk, Dk=D, Hv=Hv, Dv=D)),
+           ("keep_conv_rows", lambda: conv.keep_conv_rows(cstates, keep)),
+           ("keep_rows", lambda: exact.keep_rows(rstates, keep)))
+    per_op, launches, clocks = _graph_ops_timed(ops, args.steps, args.warmup, dev)
+    nbytes = {"conv_verify": 2 * (2 * N * V * cdim + N * (K - 1) * cdim + N * V * (K - 1) * cdim) + cdim * K * 2,
+              "keep_conv_rows": 2 * 2 * N * (K - 1) * cdim,
+              "keep_rows": 2 * 4 * N * Hv * D * D}
+    return {"config": f"N={N} sequences x V={V} drafted tokens, conv_dim {cdim}, K={K} taps, Hv={Hv}, Dv=Dk={D}",
+            "per_op_ms": {k: round(v, 4) for k, v in per_op.items()},
+            "roofline": {k: {"achieved_gbs": round(nbytes[k] / (per_op[k] / 1e3) / 1e9, 1),
+                             "frac": round(nbytes[k] / (per_op[k] / 1e3) / 1e9 / hbm, 4), "bytes": nbytes[k]}
+                         for k in nbytes},
+            "gpu_launches": int(launches), "clocks": clocks,
+            "timing": "each op a CUDA graph replay after an L2 flush (256 MiB write, outside its events)"}
 
 
 def run_single(args):
@@ -801,6 +837,8 @@ def run_single(args):
                 events.append(("verify", e0, e1))
 
         ms, per_op, launches, clocks = _timed(step, args.steps, args.warmup, dev)
+        rstates = exact.verify(q, k, v, g, beta, state)[1]
+        decode = decode_line(args, dev, hbm, N, V, Hk, Hv, D, rstates)
         nbytes = (N * Hv * D * D * 4 + N * V * Hv * D * D * 4 + N * V * Hk * D * 2 * 2 + N * V * Hv * D * 2 * 2
                   + N * V * Hv * 4 * 2)
         ach = nbytes / (per_op["verify"] / 1e3) / 1e9
@@ -815,7 +853,8 @@ def run_single(args):
                 "roofline": {"kernel": "gdn_verify", "bound": "hbm", "achieved": round(ach, 1), "peak": hbm,
                              "unit": "GB/s", "frac": round(ach / hbm, 5), "peak_source": src,
                              "traffic": TRAFFIC.get(("c4", "verify")),
-                             "bytes_per_launch": nbytes}}
+                             "bytes_per_launch": nbytes},
+                "decode_integration": decode}
     print(json.dumps(line), flush=True)
 
 
