@@ -257,7 +257,10 @@ __global__ void __launch_bounds__(320, 1) gdn_chunk_bwd_state(const __grid_const
 #pragma unroll
       for (int j = 0; j < 8; ++j) o[j] = be * f8[j];
       if (L == C)  // a full chunk goes out by one TMA store after the barrier below
-        store_row8<Tout>(reinterpret_cast<Tout*>(smem + BW_DV) + i_row * DVT + 16 * half + 8 * hc, o);
+        store_row8<Tout>(sizeof(Tout) == 2  // bf16 rows in the 64-byte swizzle of the dv map (spread over the banks)
+                             ? reinterpret_cast<Tout*>(smem + BW_DV + i_row * 64 + (((2 * half + hc) ^ ((i_row >> 1) & 3)) << 4))
+                             : reinterpret_cast<Tout*>(smem + BW_DV) + i_row * DVT + 16 * half + 8 * hc,
+                         o);
       else if (i_row < L)  // the rows after a sequence's end belong to the next sequence: not written
         store_row8<Tout>(static_cast<Tout*>(a.dv) + ((tok0 + i_row) * Hv + hv) * (size_t)DV + dv0 + 16 * half + 8 * hc, o);
       const float h = -be * gi;

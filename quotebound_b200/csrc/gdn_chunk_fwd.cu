@@ -130,7 +130,13 @@ __global__ void __launch_bounds__(320, 1) gdn_chunk_fwd_state(const __grid_const
   auto put_rows = [&](const float (&y8)[8]) {
     const int hc = kside ? 0 : 1;
     if (prev_L == C) {
-      store_row8<Tout>(reinterpret_cast<Tout*>(smem + FW_Y) + i_row * DVT + 16 * half + 8 * hc, y8);
+      // bf16 rows (64 bytes) in the 64-byte swizzle of the output map: 16-byte chunk c of row r at
+      // c ^ ((r >> 1) & 3), which spreads a quarter-warp's eight rows over all banks
+      if constexpr (sizeof(Tout) == 2)
+        store_row8<Tout>(reinterpret_cast<Tout*>(smem + FW_Y + i_row * 64 + (((2 * half + hc) ^ ((i_row >> 1) & 3)) << 4)),
+                         y8);
+      else
+        store_row8<Tout>(reinterpret_cast<Tout*>(smem + FW_Y) + i_row * DVT + 16 * half + 8 * hc, y8);
     } else if (i_row < prev_L) {  // the rows after a sequence's end belong to the next sequence
       store_row8<Tout>(static_cast<Tout*>(a.y) + ((prev_tok + i_row) * Hv + hv) * (size_t)DV + dv0 + 16 * half + 8 * hc,
                        y8);
@@ -189,9 +195,11 @@ __global__ void __launch_bounds__(320, 1) gdn_chunk_fwd_state(const __grid_const
       float vr[16];  // this row's values (rows past the sequence's end read as zero)
       {
         Row16 raw;
-        const uint4* vp = reinterpret_cast<const uint4*>(smem + FW_V + buf * 4096 + i_row * 64 + 32 * half);
-        raw.w[0] = i_row < L ? vp[0] : make_uint4(0, 0, 0, 0);
-        raw.w[1] = i_row < L ? vp[1] : make_uint4(0, 0, 0, 0);
+        // the tile in the 64-byte swizzle of its map: 16-byte chunk c of row r at c ^ ((r >> 1) & 3)
+        const uint8_t* vrow = smem + FW_V + buf * 4096 + i_row * 64;
+        const int sw = (i_row >> 1) & 3;
+        raw.w[0] = i_row < L ? *reinterpret_cast<const uint4*>(vrow + (((2 * half) ^ sw) << 4)) : make_uint4(0, 0, 0, 0);
+        raw.w[1] = i_row < L ? *reinterpret_cast<const uint4*>(vrow + (((2 * half + 1) ^ sw) << 4)) : make_uint4(0, 0, 0, 0);
         cvt_row16(raw, vr);
       }
       ok = ok && tc::mbar_wait_or_drain(&bar_mma, ph, a.err, 11, s_hook);

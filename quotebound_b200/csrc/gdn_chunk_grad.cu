@@ -205,7 +205,9 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_bwd_grad(const __grid_consta
         const uint8_t* frow = buf + 32768 + r * 128;
         const float4 f0 = *reinterpret_cast<const float4*>(frow + (((4 * half + 2 * hc) ^ (r & 7)) << 4));
         const float4 f1 = *reinterpret_cast<const float4*>(frow + (((4 * half + 2 * hc + 1) ^ (r & 7)) << 4));
-        const uint4 w = rvalid ? reinterpret_cast<const uint4*>(buf + 57344 + i_row * 64 + 32 * half)[hc]
+        // (the V rows in the 64-byte swizzle of their map: chunk c of row r at c ^ ((r >> 1) & 3))
+        const uint4 w = rvalid ? *reinterpret_cast<const uint4*>(buf + 57344 + i_row * 64 +
+                                                                 (((2 * half + hc) ^ ((i_row >> 1) & 3)) << 4))
                                : make_uint4(0, 0, 0, 0);
         const float f[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
         const uint32_t u4[4] = {w.x, w.y, w.z, w.w};

@@ -180,7 +180,9 @@ cudaError_t chunked_fwd(const ChunkFwdArgs& a, void* ws, cudaStream_t st, int* s
     if ((e = launch_chunk_prep(kmap, qmap, pa, a.n_chunks, a.Hk, st)) != cudaSuccess) return e;
   }
   CUtensorMap vmap, ymap;
-  if (!map_rows(&vmap, a.v, rows, a.Hv, a.Dv, DVT, C) || !map_rows(&ymap, a.y, rows, a.Hv, a.Dv, DVT, C, !a.out_bf16))
+  // (bf16 tiles of 64-byte rows in the 64-byte swizzle: the walk's row reads and writes spread over the banks)
+  if (!map_rows(&vmap, a.v, rows, a.Hv, a.Dv, DVT, C, false, true) ||
+      !map_rows(&ymap, a.y, rows, a.Hv, a.Dv, DVT, C, !a.out_bf16, a.out_bf16))
     return cudaErrorInvalidValue;
   StateArgs sa{geo, a.v, gates, a.h0, a.y, a.hT, ckpt, Ti, Pi, KQi, a.saved ? sv.Ds : nullptr, err, a.ckpt_in,
                a.n_chunks};
@@ -213,8 +215,9 @@ cudaError_t chunked_bwd(const ChunkBwdArgs& a, void* ws, cudaStream_t st) {
   if (a.cu && (e = launch_chunk_offsets(a.cu, a.N, w.chunk_off, st)) != cudaSuccess) return e;
   Geo geo{a.T, a.Hk, a.Hv, a.N, (a.T + C - 1) / C, a.cu, a.cu ? w.chunk_off : nullptr};
   CUtensorMap dmap, vmap, dvmap;
-  if (!map_rows(&dmap, a.dy, rows, a.Hv, a.Dv, DVT, C, false, true) || !map_rows(&vmap, a.v, rows, a.Hv, a.Dv, DVT, C) ||
-      !map_rows(&dvmap, a.dv, rows, a.Hv, a.Dv, DVT, C, !a.out_bf16))
+  if (!map_rows(&dmap, a.dy, rows, a.Hv, a.Dv, DVT, C, false, true) ||
+      !map_rows(&vmap, a.v, rows, a.Hv, a.Dv, DVT, C, false, true) ||
+      !map_rows(&dvmap, a.dv, rows, a.Hv, a.Dv, DVT, C, !a.out_bf16, a.out_bf16))
     return cudaErrorInvalidValue;
   BwdStateArgs ba{geo, a.dy, sv.gates, a.dhT, a.dv, a.dh0, w.dsbuf, sv.Timg, sv.Pimg, sv.KQimg, w.Aimg, w.err};
   if ((e = launch_chunk_bwd_state(dmap, dvmap, ba, a.Hv, a.N, a.out_bf16, st)) != cudaSuccess) return e;
