@@ -195,7 +195,7 @@ class ClockSampler:
 class Work:
     """One rank's share of the workload, resident in HBM."""
 
-    def __init__(self, B, T, Hk, Hv, Dk, Dv, seed, device, algo, cu_seqlens=None):
+    def __init__(self, B, T, Hk, Hv, Dk, Dv, seed, device, algo, cu_seqlens=None, with_state=False):
         from quotebound_b200 import synthetic
         p = synthetic.make(B, T, Hk, Hv, Dk, Dv, seed=seed, device=device)
         self.cu = cu_seqlens
@@ -209,6 +209,11 @@ class Work:
         self.dy = p.dy.to(torch.bfloat16)
         self.shape = (B, T, Hk, Hv, Dk, Dv)
         self.algo = algo
+        # an initial state and a final-state gradient, both ~ N(0, 0.02) (config 3's long sequence)
+        self.h0 = self.dhT = None
+        if with_state:
+            self.h0 = torch.randn(B, Hv, Dv, Dk, generator=gen, device=device) * 0.02
+            self.dhT = torch.randn(B, Hv, Dv, Dk, generator=gen, device=device) * 0.02
 
     def step(self, events=None):
         """One fwd+bwd pass; returns (grads..., dA_log, ddt_bias).  `events`: list to append (name, ev0, ev1)."""
@@ -228,10 +233,11 @@ class Work:
         cu = getattr(self, "cu", None)
         if self.algo != 1:  # the fused layer path: norm, gates and recurrence in the chunked kernels
             from quotebound_b200 import layer
+            h0, dhT = getattr(self, "h0", None), getattr(self, "dhT", None)
             y, hT, saved = op("layer_fwd", lambda: layer.gated_delta_layer_fwd(
-                self.q, self.k, self.v, self.a, self.b, self.A_log, self.dt_bias, None, save=True, cu_seqlens=cu))
+                self.q, self.k, self.v, self.a, self.b, self.A_log, self.dt_bias, h0, save=True, cu_seqlens=cu))
             dq, dk, dv, da, db, dA, ddt, _ = op("layer_bwd", lambda: layer.gated_delta_layer_bwd(
-                self.q, self.k, self.v, self.a, self.b, self.A_log, self.dt_bias, None, self.dy, None, saved=saved,
+                self.q, self.k, self.v, self.a, self.b, self.A_log, self.dt_bias, h0, self.dy, dhT, saved=saved,
                 cu_seqlens=cu))
             return dq, dk, dv, da, db, dA, ddt
         qn, kn, g, beta = op("gate_fwd", lambda: gate.gate_fwd(self.q, self.k, self.a, self.b, self.A_log,
@@ -832,6 +838,20 @@ def run_single(args):
                 "clocks": clocks,
                 "roofline": {"kernel": dom, "bound": "tensor", "achieved": round(ach, 3), "peak": tf,
                              "unit": "TFLOP/s", "frac": round(ach / tf, 5), "peak_source": src, "traffic": None}}
+        # config 3's long sequence: T = 32768 with an initial state and a final-state gradient (dh0 out)
+        del W
+        TL = 32768
+        WL = Work(1, TL, 16, 32, 128, 128, 1, dev, args.algo, with_state=True)
+        ms_l, per_op_l, launches_l, clocks_l = _timed(WL.step, args.steps, args.warmup, dev)
+        dom_l = "layer_bwd" if "layer_bwd" in per_op_l else "gdn_bwd"
+        ach_l = 2 * fpt * TL * 32 / (per_op_l[dom_l] / 1e3) / 1e12
+        line["long_sequence"] = {
+            "config": "config3's long sequence: B=1, T=32768, Hk=16 Hv=32 Dk=Dv=128, h0 and dh_T ~ N(0, 0.02), "
+                      "dh0 returned", "value": round(TL / (ms_l / 1e3), 1), "unit": "tokens/s",
+            "ms_per_step": round(ms_l, 4), "per_op_ms": {k: round(v, 4) for k, v in per_op_l.items()},
+            "gpu_launches": int(launches_l), "clocks": clocks_l,
+            "roofline": {"kernel": dom_l, "bound": "tensor", "achieved": round(ach_l, 3), "peak": tf,
+                         "unit": "TFLOP/s", "frac": round(ach_l / tf, 5), "peak_source": src}}
     elif args.workload == "conv_norm":
         line = conv_norm_line(args, dev, hbm, src)
     else:
