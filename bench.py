@@ -336,6 +336,14 @@ def _measure(args, workload, world, rank, dev, dist, steps, warmup):
     if dist:
         torch.distributed.barrier()
     torch.cuda.synchronize()
+    if dist:
+        # The ranks' processes leave the barrier at different moments; a GPU whose timed steps start early
+        # would wait inside its first step's all-reduce for a peer whose host started late, and that wait
+        # would count in its events.  So the GPUs are aligned first: an all-reduce that all of them leave
+        # together, then a device sleep of about 20 ms during which every host enqueues its timed steps.
+        align = torch.zeros(1, device=dev)
+        torch.distributed.all_reduce(align)
+        torch.cuda._sleep(40_000_000)
     sampler.start()
     n0 = _lib.launches()
     step_events, op_events = [], []
@@ -369,14 +377,16 @@ def _measure(args, workload, world, rank, dev, dist, steps, warmup):
     for name, a, b in op_events:
         per_op.setdefault(name, []).append(a.elapsed_time(b))
     per_op = {k: sum(v) / len(v) for k, v in per_op.items()}
-    ms_max = ms
+    ms_max, ms_ranks = ms, [ms]
     if dist:
-        t = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms_max = float(t.item())
+        t = torch.zeros(world, device=dev)
+        t[rank] = ms
+        torch.distributed.all_reduce(t)  # every rank's time (the others contribute zeros)
+        ms_ranks = [round(float(x), 4) for x in t.tolist()]
+        ms_max = max(ms_ranks)
     total_tokens = world * B * T if workload == "c1" else 8 * 4096
     return {"W": W, "allreduce": allreduce, "graph": graph, "gout": gout, "graph_reduces": graph_reduces,
-            "ms_max": ms_max, "per_op": per_op, "launches": launches, "clocks": clocks, "B": B, "T": T, "Hk": Hk,
+            "ms_max": ms_max, "ms_ranks": ms_ranks, "per_op": per_op, "launches": launches, "clocks": clocks, "B": B, "T": T, "Hk": Hk,
             "Hv": Hv, "Dk": Dk, "Dv": Dv, "value": total_tokens / (ms_max / 1e3), "reduces": reduces,
             "flush": flush}
 
@@ -443,7 +453,8 @@ def run_ours(args):
             "metric": "GDN fwd+bwd tokens/s at 4B layer shape" if workload == "c1"
             else "GDN fwd+bwd tokens/s, B=8 T=4096 Hv=64 split over GPUs",
             "value": round(m["value"], 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(m["ms_max"], 4), "higher_is_better": True,
+            "warmup": args.warmup, "ms_per_step": round(m["ms_max"], 4), "ms_per_rank": m["ms_ranks"],
+            "higher_is_better": True,
             "scaling": "weak" if workload == "c1" else "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded; q,k,v,dO ~ N(0,1), q/k normalised, g = exp(-e^A_log softplus(a+dt_bias)))",
             "config": {"workload": "config1: B=1/GPU T=2048 Hk=16 Hv=32 Dk=Dv=128" if workload == "c1"
@@ -451,6 +462,8 @@ def run_ours(args):
                        "global_batch": world * m["B"] if workload == "c1" else 8, "seq_len": m["T"],
                        "parallelism": f"dp{world}" if workload == "c1" else f"bh{world}",
                        "l2": "flushed before every step (512 MiB write, outside the step events)",
+                       "ranks": "aligned before the timed steps (an all-reduce, then a device sleep while every "
+                                "host enqueues); the line's time is the slowest rank's" if world > 1 else "one",
                        "launch": "CUDA graph of the step" + (" and its all-reduce" if m["graph_reduces"] else "")
                        + ", replayed",
                        "algo": {0: "auto", 1: "rows", 2: "chunked"}[args.algo],
@@ -467,7 +480,7 @@ def run_ours(args):
             line["config2_strong"] = {
                 "metric": "GDN fwd+bwd tokens/s, config2 (B=8 T=4096 Hk=16 Hv=64) split over the GPUs",
                 "value": round(c2["value"], 1), "unit": "tokens/s", "n_gpus": world, "scaling": "strong",
-                "ms_per_step": round(c2["ms_max"], 4), "steps": max(3, args.steps // 2),
+                "ms_per_step": round(c2["ms_max"], 4), "ms_per_rank": c2["ms_ranks"], "steps": max(3, args.steps // 2),
                 "per_rank": {"batch_rows": c2["B"], "key_heads": c2["Hk"], "value_heads": c2["Hv"]},
                 "allreduce": c2["reduces"], "per_op_ms": {k: round(v, 4) for k, v in c2["per_op"].items()},
                 "gpu_launches": int(c2["launches"]), "clocks": c2["clocks"],
