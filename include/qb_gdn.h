@@ -227,7 +227,9 @@ int qb_gdn_keep_conv_rows(int32_t N, int32_t V, int32_t K, int32_t conv_dim, int
 
 /* The gated RMSNorm after the recurrence (src/deltanet.cpp:35-45, :122; Qwen3NextRMSNormGated): per
  * (token, value head) row, n = rms_norm(y, w, eps) rounded to dtype, o = silu(z) n in float32 rounded
- * to dtype.  y, z, o [P, Hv, Dv] (dtype), w [Dv] float32, Dv in {32, 64, 128, 256}. */
+ * to dtype.  y, z, o [P, Hv, Dv] (dtype), w [Dv] float32, Dv in {32, 64, 128, 256}; y, z, o (and in the
+ * backward dout, dy, dz) aligned to min(16, Dv / 32 x the element size) bytes (each lane moves its part of
+ * a row as one vector). */
 int qb_gdn_gated_norm_fwd(int64_t P, int32_t Hv, int32_t Dv, float eps, int32_t dtype, const void* y, const void* z,
                           const float* w, void* o, void* stream, char* err, int errlen);
 /* Workspace bytes of the backward's dw. */
