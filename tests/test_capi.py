@@ -115,6 +115,20 @@ def test_null_and_misaligned_pointers(L):
     assert rc == -1 and b"alignment" in err.value
 
 
+
+def test_gated_norm_refuses_misaligned_rows(L):
+    """Each lane of the gated norm moves its Dv / 32 elements of a row as one vector, so the rows' base
+    pointers must be aligned to min(16, Dv / 32 x element size) bytes; a misaligned one is refused on the
+    host, before anything is launched."""
+    err = _lib.err_buf()
+    fake, odd = 0x1000, 0x1008  # 0x1008: 8-byte aligned, not 16 (Dv = 128 in float32 needs 16)
+    rc = L.qb_gdn_gated_norm_fwd(4, 2, 128, 1e-6, _lib.QB_DTYPE_F32, odd, fake, fake, fake, None, err, len(err))
+    assert rc == -1 and b"alignment" in err.value
+    rc = L.qb_gdn_gated_norm_bwd(4, 2, 128, 1e-6, _lib.QB_DTYPE_BF16, fake, fake, fake, fake, fake, 0x1004, None,
+                                 None, 0, None, err, len(err))
+    assert rc == -1 and b"alignment" in err.value  # bf16 at Dv = 128: 8 bytes
+
+
 def test_workspace_too_small_is_refused(L):
     d = desc()
     need, _ = ws_or_err(L, d, _lib.QB_OP_BWD)
