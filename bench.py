@@ -377,7 +377,7 @@ def _measure(args, workload, world, rank, dev, dist, steps, warmup):
     for name, a, b in op_events:
         per_op.setdefault(name, []).append(a.elapsed_time(b))
     per_op = {k: sum(v) / len(v) for k, v in per_op.items()}
-    ms_max, ms_ranks = ms, [ms]
+    ms_max, ms_ranks = ms, [round(ms, 4)]
     if dist:
         t = torch.zeros(world, device=dev)
         t[rank] = ms
