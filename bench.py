@@ -13,15 +13,19 @@ Workloads (synthetic, seeded; shapes and value distributions of the measured con
   c1  Qwen3.5-4B layer: B=1 per GPU, T=2048, Hk=16, Hv=32, Dk=Dv=128, bf16 activations, fp32 g/beta/state.
       Weak scaling: GPU r runs batch row r (global batch = N).
   c2  B=8, T=4096, Hk=16, Hv=64 split over the GPUs by (batch x value-head group); strong scaling.
-  c3  16 sequences of U[128, 4096] tokens packed with cu_seqlens (one GPU).
-  c4  exact speculative verify of 8 drafted tokens for 32 sequences, every state kept (one GPU).
+  c3  16 sequences of U[128, 4096] tokens packed with cu_seqlens (one GPU); sub-result: one sequence of
+      T=32768 with an initial state and a final-state gradient.
+  c4  exact speculative verify of 8 drafted tokens for 32 sequences, every state kept (one GPU);
+      sub-result: the decode-time companions (the conv's verify rows, keep_conv_rows, keep_rows).
   conv_norm  the layer's steps either side of the recurrence at the 4B shape, 4 x 2048 tokens: the causal
       conv + SiLU with the q/k/v split and the gated RMSNorm, forward and backward (one GPU; HBM-bound).
 
 `value` is tokens/s of the whole job (tokens of all ranks / max over ranks of the device time);
 `e2e` is the same metric through the public API with host buffers: every step copies its inputs
-from pinned host memory and its gradients back.  L2 is flushed (a 512 MiB write) before each timed
-step and the flush is outside the step's events.
+from pinned host memory (packed in one buffer, one copy) and its gradients back.  L2 is flushed (a
+512 MiB write) before each timed step and the flush is outside the step's events.  With N ranks the
+GPUs are aligned before the timed steps (an all-reduce, then a short device sleep while every host
+enqueues), so that no rank's events include waiting for a peer whose process started late.
 """
 from __future__ import annotations
 
